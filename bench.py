@@ -1,0 +1,412 @@
+"""LLaMA-2-7B fp16 batch-1 decode benchmark of the vkllm-b200 C-ABI library.
+
+Workload: LLaMA-2-7B architecture (dim 4096, 32 layers, 32 heads of 128, SwiGLU 11008, vocab 32000,
+context 4096), fp16 weights random-initialised on the device (N(0, 0.02) counter-based generator;
+no checkpoint or dataset exists here, the data is synthetic), a 512-token seeded prompt prefilled
+through the drop-in API, then greedy decode. One bench "step" = one decode token at batch 1.
+
+  value : decode tok/s with the token feedback on the device (CUDA-Graph replay of the fused step),
+          timed with CUDA events on the library's stream; weights (13.2 GB) exceed L2, so every step
+          streams them from HBM.
+  e2e   : the same metric through the reference token loop of the C API
+          (tests/vkllm_test_infer_gguf.c:181-272): per token a new mapped input tensor (host write),
+          vkllm_graph_new / vkllm_models_llama2_build_graph / init / upload / run / post_run, read of
+          the mapped output (device -> host), vkllm_graph_free.
+  N > 1 : one process per GPU (torchrun), each decoding its own independent sequence (data
+          parallel, weak scaling); value = total tokens / max-over-ranks time.
+
+--impl reference runs the reference's algorithm on the host cores instead: the C++ oracle
+(oracle/, the CPU restatement of the reference shaders) on the same weights, because the reference
+itself (Vulkan) cannot run on these machines.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vkllm.c_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+CFG_7B = dict(block_count=32, context_length=4096, embedding_length=4096, head_count=32, ffn_length=11008,
+              vocab_size=32000, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
+PROMPT_LEN = 512
+SEED = 2024
+
+
+def weight_bytes(cfg):
+    D, F, V, L = cfg["embedding_length"], cfg["ffn_length"], cfg["vocab_size"], cfg["block_count"]
+    per_layer = (4 * D * D + 3 * F * D) * 2 + 2 * D * 4
+    return L * per_layer + V * D * 2 + D * 4 + D * 2  # layers + logits matrix + output norm + 1 embedding row
+
+
+def kv_bytes(cfg, lk):
+    D, L = cfg["embedding_length"], cfg["block_count"]
+    return L * 2 * D * 2 * lk  # K and V rows read per layer
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu}.csv")
+
+    def __enter__(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, v):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prompt_tokens(rank, n=PROMPT_LEN):
+    import numpy as np
+
+    return np.random.default_rng(SEED + 1000 * rank).integers(3, 32000, size=n, dtype=np.uint32)
+
+
+def download_weights(vk, ctx, model, cfg):
+    """Copies the model's weights to host numpy arrays (for the CPU oracle)."""
+    import numpy as np
+
+    w = {}
+    m = model.m.weights
+    w["token_embd.weight"] = vk.fetch(ctx, m.tok_embed_weights).reshape(cfg["vocab_size"], -1)
+    w["output.weight"] = vk.fetch(ctx, m.output_weight).reshape(cfg["vocab_size"], -1)
+    w["output_norm.weight"] = vk.fetch(ctx, m.output_norm_weight).reshape(-1)
+    names = {"attn_norm_weight": "attn_norm", "ffn_norm_weight": "ffn_norm", "WQ": "attn_q", "WK": "attn_k",
+             "WV": "attn_v", "WO": "attn_output", "WG": "ffn_gate", "WU": "ffn_up", "WD": "ffn_down"}
+    for l in range(cfg["block_count"]):
+        bw = model.block(l)
+        for f, n in names.items():
+            a = vk.fetch(ctx, getattr(bw, f))
+            w[f"blk.{l}.{n}.weight"] = a.reshape(-1) if "norm" in n else a.reshape(a.shape[2], a.shape[3])
+    return w
+
+
+def cpu_decode_sample(weights, cfg, n_steps=3, threads=0):
+    """Times n single-token decode steps of the oracle (reference algorithm on the CPU) at positions
+    0..n-1. Returns (tok/s, threads used)."""
+    import oracle
+
+    used = oracle.threads(threads or os.cpu_count() or 1)
+    ocfg = dict(D=cfg["embedding_length"], H=cfg["head_count"], F=cfg["ffn_length"], V=cfg["vocab_size"],
+                L=cfg["block_count"], ctx=64, eps=cfg["rms_eps"], rope_base=cfg["rope_freq_base"])
+    m = oracle.Llama2(ocfg, weights, ctx=64)
+    tok = 1
+    m.step([tok], 0)  # warm-up (page-in)
+    t0 = time.perf_counter()
+    for i in range(n_steps):
+        _, out = m.step([tok], i + 1)
+        tok = int(out[-1])
+    dt = time.perf_counter() - t0
+    m.close()
+    return n_steps / dt, used
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    import vkllm_b200 as vk
+
+    cfg = dict(CFG_7B)
+    ctx = vk.Context(local)
+    model = vk.Model(ctx).init_random(cfg, SEED)
+    l = vk.lib()
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    prompt = prompt_tokens(rank)
+
+    # Prefill through the drop-in API (timed separately, reported as prefill tok/s).
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = model.step(list(prompt), 0)
+    prefill_s = time.perf_counter() - t0
+    model.engine_prepare()
+    kps = l.vkllm_b200_engine_kernels_per_step(ctx.ptr, C.byref(model.m))
+
+    # ---- value: device-resident decode loop --------------------------------------------------
+    W, K = args.warmup, args.steps
+    vk.check(l.vkllm_b200_engine_set_state(ctx.ptr, C.byref(model.m), first, PROMPT_LEN), "set_state")
+    vk.check(l.vkllm_b200_engine_decode_steps(ctx.ptr, C.byref(model.m), W), "warmup")
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        vk.check(l.vkllm_b200_engine_decode_steps(ctx.ptr, C.byref(model.m), K), "decode_steps")
+        ev1.record(stream)
+        ev1.synchronize()
+        torch.cuda.synchronize()
+    dev_ms = ev0.elapsed_time(ev1)
+    toks = np.zeros(W + K, dtype=np.uint32)
+    vk.check(l.vkllm_b200_engine_read_tokens(ctx.ptr, C.byref(model.m), toks.ctypes.data, W + K), "read_tokens")
+    barrier(world)
+    t_max = max_over_ranks(world, dev_ms)
+    value = world * K / (t_max / 1000.0)
+
+    # ---- dominant-kernel roofline (FFN up/gate GEMV, the largest weight stream of a step) --------
+    us, nbytes = C.c_float(), C.c_uint64()
+    vk.check(l.vkllm_b200_engine_bench_kernel(ctx.ptr, C.byref(model.m), b"upgate", 64, C.byref(us),
+                                              C.byref(nbytes)), "bench_kernel")
+    kern = {}
+    for name in (b"qkv", b"wo", b"down", b"logits"):
+        u2, b2 = C.c_float(), C.c_uint64()
+        vk.check(l.vkllm_b200_engine_bench_kernel(ctx.ptr, C.byref(model.m), name, 32, C.byref(u2), C.byref(b2)), "k")
+        kern[name.decode()] = {"us": round(u2.value, 2), "GBps": round(b2.value / (u2.value * 1e-6) / 1e9, 1)}
+
+    # ---- e2e: reference token loop through the C API, host buffers --------------------------------
+    pos = PROMPT_LEN + W + K
+    tok = int(toks[-1])
+    n_e2e = max(2, min(K, 64))
+    for _ in range(2):  # warm the per-step allocations
+        tok = model.step([tok], pos)
+        pos += 1
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(n_e2e):
+        tok = model.step([tok], pos)
+        pos += 1
+    e1.record(stream)
+    e1.synchronize()
+    wall_e2e = time.perf_counter() - w0
+    e2e_ms = max(e0.elapsed_time(e1), wall_e2e * 1000.0)
+    e2e_max = max_over_ranks(world, e2e_ms)
+    e2e_value = world * n_e2e / (e2e_max / 1000.0)
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        mean_lk = PROMPT_LEN + W + (K + 1) / 2.0
+        step_bytes = weight_bytes(cfg) + kv_bytes(cfg, mean_lk)
+        ms_step = t_max / K
+        achieved = nbytes.value / (us.value * 1e-6) / 1e9
+        traffic = None
+        prof = os.path.join(ROOT, "profiles", "decode_upgate_gemv_7b.traffic.json")
+        if os.path.exists(prof):
+            with open(prof) as f:
+                traffic = json.load(f).get("bytes_per_launch")
+        result = {
+            "metric": "LLaMA2-7B fp16 decode tok/s (batch 1)",
+            "value": round(value, 2),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (random-init weights on device, seeded prompt ids)",
+            "config": {"workload": "llama2-7b fp16 batch-1 greedy decode after a 512-token prefill (BASELINE configs[2])",
+                       "model": "llama2-7b-arch", "global_batch": world, "seq_len": PROMPT_LEN,
+                       "positions": [PROMPT_LEN + W, PROMPT_LEN + W + K],
+                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (13.2 GB of weights streamed per step)"},
+            "step_roofline": {"bytes_per_token": int(step_bytes), "achieved_GBps": round(step_bytes / (ms_step * 1e-3) / 1e9, 1),
+                              "frac": round(step_bytes / (ms_step * 1e-3) / 1e9 / peak, 4),
+                              "ideal_tok_s": round(peak * 1e9 / step_bytes, 1)},
+            "roofline": {"kernel": "k_dec_upgate (ffn_norm + up/gate GEMV + SiLU gating)", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "bytes_per_launch": int(nbytes.value), "us_per_launch": round(us.value, 3),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6650 GB/s"},
+            "kernels": kern,
+            "prefill": {"tokens": PROMPT_LEN, "seconds": round(prefill_s, 4),
+                        "tok_s": round(PROMPT_LEN / prefill_s, 1), "path": "drop-in API"},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "steps": n_e2e, "path": "reference token loop through the C API (graph rebuilt per token)"},
+            "gpu_launches": int(kps * K),
+            "clocks": clk.summary(),
+        }
+    # ---- cpu baseline (rank 0, N == 1 only) ---------------------------------------------------
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            w = download_weights(vk, ctx, model, cfg)
+            tps, thr = cpu_decode_sample(w, cfg, n_steps=args.cpu_steps)
+            result["cpu_baseline"] = {"value": round(tps, 4), "unit": "tokens/s", "cores": thr, "kind": "port",
+                                      "sample": f"{args.cpu_steps} single-token decode steps of the same 7B weights at "
+                                                f"positions 1..{args.cpu_steps} (oracle/ C++ restatement of the reference "
+                                                f"shaders, OpenMP)"}
+            del w
+        except Exception as e:  # the baseline must not void the GPU measurement
+            result["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    model.free()
+    ctx.close()
+    return result
+
+
+def run_reference(args, world, rank, local):
+    """The reference's algorithm on the host cores (the oracle port; the Vulkan reference cannot run
+    here). Weights are the same generator's bits, rebuilt on the CPU."""
+    import numpy as np
+
+    import oracle
+
+    if rank != 0:
+        return None
+    cfg = dict(CFG_7B)
+    D, F, V, L = cfg["embedding_length"], cfg["ffn_length"], cfg["vocab_size"], cfg["block_count"]
+    oracle.threads(os.cpu_count() or 1)
+    w, tid = {}, 0
+
+    def mat(name, r, c):
+        nonlocal tid
+        w[name] = oracle.random_f16(SEED, tid, 0.02, 0, r * c).reshape(r, c)
+        tid += 1
+
+    def ones(name, n):
+        nonlocal tid
+        w[name] = np.ones(n, dtype=np.float32)
+        tid += 1
+
+    t_gen = time.perf_counter()
+    mat("token_embd.weight", V, D)
+    for l in range(L):
+        ones(f"blk.{l}.attn_norm.weight", D)
+        ones(f"blk.{l}.ffn_norm.weight", D)
+        for n in ("attn_q", "attn_k", "attn_v", "attn_output"):
+            mat(f"blk.{l}.{n}.weight", D, D)
+        mat(f"blk.{l}.ffn_gate.weight", F, D)
+        mat(f"blk.{l}.ffn_up.weight", F, D)
+        mat(f"blk.{l}.ffn_down.weight", D, F)
+    ones("output_norm.weight", D)
+    mat("output.weight", V, D)
+    gen_s = time.perf_counter() - t_gen
+    steps = max(1, min(args.steps, 4))
+    tps, thr = cpu_decode_sample(w, cfg, n_steps=steps)
+    return {
+        "impl": "reference",
+        "metric": "LLaMA2-7B fp16 decode tok/s (batch 1)",
+        "value": round(tps, 4),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": 1,
+        "ms_per_step": round(1000.0 / tps, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (same generator bits as the GPU arm)",
+        "config": {"workload": "llama2-7b fp16 batch-1 greedy decode (BASELINE configs[2])", "model": "llama2-7b-arch"},
+        "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": thr, "kind": "port",
+                         "sample": f"{steps} single-token decode steps at positions 1..{steps}; weights regenerated "
+                                   f"on the CPU in {gen_s:.1f} s (not timed)"},
+        "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "vkllm.c itself needs Vulkan, absent on this box; this is its algorithm restated in C++ (oracle/)",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_setup() if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
+                                                                    int(os.environ.get("RANK", "0")),
+                                                                    int(os.environ.get("LOCAL_RANK", "0")))
+    res = run_ours(args, world, rank, local) if args.impl == "ours" else run_reference(args, world, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if args.impl == "ours" and world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

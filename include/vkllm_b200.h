@@ -1,0 +1,106 @@
+/* B200-specific additions to the vkllm C API. None of these has a counterpart in the reference;
+ * they expose what the CUDA backend adds (device-side random init for benchmarks, execution-mode
+ * control, the fused decode engine's device-resident loop, tensor parallelism) without changing
+ * any reference signature. */
+#ifndef VKLLM_B200_H
+#define VKLLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "vkllm_errors.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct vkllm_context;
+struct vkllm_models_llama2;
+
+/* Library version string. */
+extern const char *vkllm_b200_version(void);
+
+/* ---- model construction without a GGUF file ------------------------------------------------ */
+
+struct vkllm_b200_llama2_config
+{
+    uint32_t block_count;
+    uint32_t context_length;
+    uint32_t embedding_length;
+    uint32_t head_count;
+    uint32_t ffn_length; /* SwiGLU hidden size */
+    uint32_t vocab_size;
+    float rope_freq_base; /* <= 0: 10000 */
+    float rms_eps;        /* <= 0: 1e-5 */
+    float init_std;       /* <= 0: 0.02 */
+};
+
+/* Fills `model` with the tensors vkllm_models_llama2_load would create for a GGUF of this shape
+ * (same names, shapes, dtypes), generated on the device: fp16 weights from a counter-based
+ * generator (Irwin-Hall sum of 12 uniforms, scaled to init_std; element i of the t-th tensor in
+ * GGUF order depends only on (seed, t, i)), f32 norm gains of 1. Used where writing a multi-GB
+ * GGUF is impractical (7B/13B benchmarks). */
+extern vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context *context,
+                                                        struct vkllm_models_llama2 *model,
+                                                        const struct vkllm_b200_llama2_config *cfg, uint64_t seed);
+
+/* Host-side twin of the device generator: the fp16 bit patterns of elements [first, first + n) of
+ * tensor `tensor_id` (for CPU references of randomly initialised models). */
+extern void vkllm_b200_random_f16_host(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t first, uint64_t n,
+                                       uint16_t *out);
+
+/* ---- execution control ---------------------------------------------------------------------- */
+
+enum
+{
+    VKLLM_B200_EXEC_FUSED = 0,  /* llama2 graphs run the fused engine (default) */
+    VKLLM_B200_EXEC_STRICT = 1, /* every graph runs one kernel per node, like the reference */
+};
+extern vkllm_err_t vkllm_b200_set_exec_mode(struct vkllm_context *context, int mode);
+extern int vkllm_b200_get_exec_mode(struct vkllm_context *context);
+
+/* The context's CUDA stream (cudaStream_t); all graph work is enqueued on it. */
+extern void *vkllm_b200_context_stream(struct vkllm_context *context);
+extern int vkllm_b200_context_device(struct vkllm_context *context);
+extern vkllm_err_t vkllm_b200_allocator_stats(struct vkllm_context *context, uint64_t *dev_in_use,
+                                              uint64_t *dev_cached, uint64_t *host_in_use);
+
+/* ---- fused decode engine: device-resident token loop ------------------------------------------
+ * The engine keeps a device "step state" (current token, position). One decode step reads it,
+ * runs the whole model for that token, writes the greedy next token back into it, appends the
+ * token to a device ring of generated tokens and advances the position, so steps can be enqueued
+ * back to back with no host round trip. */
+
+/* Builds the engine for `model` (workspace, kernel parameters, CUDA Graph of one decode step). */
+extern vkllm_err_t vkllm_b200_engine_prepare(struct vkllm_context *context, struct vkllm_models_llama2 *model);
+/* Enqueues: state.token = token, state.pos = pos, ring cleared. */
+extern vkllm_err_t vkllm_b200_engine_set_state(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                               uint32_t token, uint32_t pos);
+/* Enqueues n decode steps (CUDA Graph launches) on the context stream. */
+extern vkllm_err_t vkllm_b200_engine_decode_steps(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                  uint32_t n);
+/* Waits for the stream, then copies the first n generated tokens since set_state. */
+extern vkllm_err_t vkllm_b200_engine_read_tokens(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                 uint32_t *out, uint32_t n);
+/* Waits for the stream, then copies the fp16 logits of the last step ([vocab] halves). */
+extern vkllm_err_t vkllm_b200_engine_read_logits(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                 uint16_t *out, uint32_t n);
+/* Number of kernel launches in one decode step of the engine (for launch accounting). */
+extern uint32_t vkllm_b200_engine_kernels_per_step(struct vkllm_context *context, struct vkllm_models_llama2 *model);
+
+/* Times `iters` launches of one decode kernel of the engine ("qkv", "wo", "upgate", "down", "logits")
+ * on the context stream with CUDA events, cycling through the layers so every launch streams its
+ * own weights. Returns the mean microseconds per launch and the algorithmic bytes per launch
+ * (weights + activations read and written). Clobbers the engine's step state. */
+extern vkllm_err_t vkllm_b200_engine_bench_kernel(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                  const char *kernel, uint32_t iters, float *us_per_launch,
+                                                  uint64_t *bytes_per_launch);
+
+/* ---- struct layout queries (for FFI bindings that mirror the public structs) --------------- */
+extern size_t vkllm_b200_sizeof(const char *struct_name);
+extern size_t vkllm_b200_offsetof(const char *struct_name, const char *field);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,546 @@
+// Fused decode engine: owns the decode workspace of one model, captures one decode step as a CUDA
+// Graph, and runs it for vkllm_graph_run (graphs carrying a plan) and for the device-resident
+// token loop of vkllm_b200.h.
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "../runtime/internal.h"
+#include "decode_kernels.cuh"
+#include "plan.h"
+#include "vkllm_b200.h"
+#include "vkllm_kvcache.h"
+#include "vkllm_models_llama2.h"
+
+namespace vkb
+{
+
+struct Engine
+{
+    vkllm_context *ctx = nullptr;
+    DecodeDims dd{};
+    std::vector<LayerW> layers;
+    const __half *embed = nullptr, *wout = nullptr;
+    const float *out_norm = nullptr;
+    uint32_t unk = 0;
+    // workspace
+    void *ws = nullptr;
+    __half *x = nullptr, *q = nullptr, *attn = nullptr, *m = nullptr, *logits = nullptr, *scores = nullptr;
+    float2 *part = nullptr;
+    float *opart = nullptr;
+    uint32_t *counters = nullptr, *logit_counter = nullptr, *ring = nullptr;
+    StepState *state = nullptr;
+    // launch geometry
+    unsigned grid_qkv = 0, grid_wo = 0, grid_upgate = 0, grid_down = 0, grid_logits = 0, grid_embed = 0;
+    size_t smem_D = 0, smem_HD = 0, smem_F = 0;
+    // captured step
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint32_t kernels_per_step = 0;
+};
+
+namespace
+{
+
+unsigned gemv_grid(uint32_t groups, int sms)
+{
+    uint32_t need = (groups + kGemvWarps - 1) / kGemvWarps;
+    uint32_t cap = (uint32_t)sms * 4u;
+    return need < cap ? (need ? need : 1) : cap;
+}
+
+vkllm_err_t enqueue_step(Engine *e, cudaStream_t s)
+{
+    const DecodeDims &dd = e->dd;
+    k_dec_embed<<<e->grid_embed, 256, 0, s>>>(e->embed, dd.V, dd.D, e->unk, e->state, e->x);
+    dim3 agrid(dd.H, dd.nsplit);
+    for (const LayerW &lw : e->layers)
+    {
+        k_dec_qkv<<<e->grid_qkv, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->q, e->state);
+        k_dec_attn_scores<<<agrid, kAttnThreads, 0, s>>>(lw, dd, e->q, e->scores, e->part, e->state);
+        k_dec_attn_pv<<<agrid, kAttnThreads, 0, s>>>(lw, dd, e->scores, e->part, e->opart, e->counters, e->attn,
+                                                     e->state);
+        k_dec_wo<<<e->grid_wo, kGemvThreads, e->smem_HD, s>>>(lw, dd, e->attn, e->x);
+        k_dec_upgate<<<e->grid_upgate, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->m);
+        k_dec_down<<<e->grid_down, kGemvThreads, e->smem_F, s>>>(lw, dd, e->m, e->x);
+    }
+    k_dec_logits<<<e->grid_logits, kGemvThreads, e->smem_D, s>>>(e->wout, e->out_norm, dd, e->x, e->logits,
+                                                                 e->logit_counter, e->state, e->ring, dd.ctx);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess)
+        return cuda_check(err, "decode step launch", __FILE__, __LINE__);
+    return VKLLM_ERR_OK;
+}
+
+vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine **out)
+{
+    _CHECK_ARGS(model->weights.blocks && model->weights.kvcache && model->weights.tok_embed_weights &&
+                model->weights.output_weight && model->weights.output_norm_weight);
+    Engine *e = new Engine();
+    e->ctx = ctx;
+    DecodeDims &dd = e->dd;
+    dd.D = model->meta.embedding_length;
+    dd.H = model->meta.head_count;
+    dd.V = model->meta.vocab_size;
+    dd.ctx = model->meta.context_length;
+    dd.eps = model->meta.layer_norm_rms_epsilon;
+    dd.rope_base = model->meta.rope_freq_base;
+    block_weights *b0 = model->weights.blocks->data[0];
+    uint32_t HD = b0->WQ->shapes[2];
+    dd.hd = HD / dd.H;
+    dd.F = b0->WU->shapes[2];
+    dd.scale = 1.0f / sqrtf((float)dd.hd);
+    int sms = ctx->device->sm_count;
+    uint32_t ns = (uint32_t)((2 * sms + dd.H - 1) / dd.H);
+    dd.nsplit = ns < 1 ? 1 : (ns > 32 ? 32 : ns);
+    e->unk = model->meta.padding_token_id;
+    // Shape requirements of the fused kernels (anything else runs node by node).
+    bool ok = dd.D % 8 == 0 && dd.F % 8 == 0 && HD % 8 == 0 && dd.hd % 4 == 0 && dd.hd <= 256 && dd.D % 2 == 0 &&
+              HD == dd.D && model->weights.tok_embed_weights->shapes[3] == dd.D &&
+              model->weights.tok_embed_weights->dtype == vkllm_dtype_float16 &&
+              model->weights.output_weight->shapes[2] == dd.V && model->weights.output_weight->shapes[3] == dd.D &&
+              model->weights.output_weight->dtype == vkllm_dtype_float16 &&
+              model->weights.output_norm_weight->dtype == vkllm_dtype_float32 &&
+              model->weights.tok_embed_weights->shapes[2] == dd.V;
+    vkllm_kvcache *kv = model->weights.kvcache;
+    for (uint32_t l = 0; ok && l < model->meta.block_count; ++l)
+    {
+        block_weights *bw = model->weights.blocks->data[l];
+        ok = bw && bw->WQ && bw->WK && bw->WV && bw->WO && bw->WU && bw->WG && bw->WD && bw->attn_norm_weight &&
+             bw->ffn_norm_weight && bw->WQ->dtype == vkllm_dtype_float16 && bw->WK->dtype == vkllm_dtype_float16 &&
+             bw->WV->dtype == vkllm_dtype_float16 && bw->WO->dtype == vkllm_dtype_float16 &&
+             bw->WU->dtype == vkllm_dtype_float16 && bw->WG->dtype == vkllm_dtype_float16 &&
+             bw->WD->dtype == vkllm_dtype_float16 && bw->attn_norm_weight->dtype == vkllm_dtype_float32 &&
+             bw->ffn_norm_weight->dtype == vkllm_dtype_float32 && bw->WQ->shapes[2] == HD &&
+             bw->WQ->shapes[3] == dd.D && bw->WK->shapes[2] == HD && bw->WV->shapes[2] == HD &&
+             bw->WO->shapes[2] == dd.D && bw->WO->shapes[3] == HD && bw->WU->shapes[2] == dd.F &&
+             bw->WG->shapes[2] == dd.F && bw->WD->shapes[2] == dd.D && bw->WD->shapes[3] == dd.F &&
+             l < kv->kcaches->used_n && kv->kcaches->data[l]->shapes[3] == dd.hd &&
+             kv->kcaches->data[l]->shapes[1] == dd.H && kv->kcaches->data[l]->shapes[2] == dd.ctx;
+        if (!ok)
+            break;
+        LayerW lw;
+        lw.wq = (const __half *)dev_ptr(ctx, bw->WQ);
+        lw.wk = (const __half *)dev_ptr(ctx, bw->WK);
+        lw.wv = (const __half *)dev_ptr(ctx, bw->WV);
+        lw.wo = (const __half *)dev_ptr(ctx, bw->WO);
+        lw.wu = (const __half *)dev_ptr(ctx, bw->WU);
+        lw.wg = (const __half *)dev_ptr(ctx, bw->WG);
+        lw.wd = (const __half *)dev_ptr(ctx, bw->WD);
+        lw.attn_norm = (const float *)dev_ptr(ctx, bw->attn_norm_weight);
+        lw.ffn_norm = (const float *)dev_ptr(ctx, bw->ffn_norm_weight);
+        lw.kcache = (__half *)dev_ptr(ctx, kv->kcaches->data[l]);
+        lw.vcache = (__half *)dev_ptr(ctx, kv->vcaches->data[l]);
+        e->layers.push_back(lw);
+    }
+    if (!ok)
+    {
+        delete e;
+        log_info("model shape not covered by the fused decode engine; graphs run node by node");
+        return VKLLM_ERR_ARGS;
+    }
+    e->embed = (const __half *)dev_ptr(ctx, model->weights.tok_embed_weights);
+    e->wout = (const __half *)dev_ptr(ctx, model->weights.output_weight);
+    e->out_norm = (const float *)dev_ptr(ctx, model->weights.output_norm_weight);
+
+    // Workspace layout (256-byte aligned pieces).
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    size_t off_x = 0, off_q = off_x + al(dd.D * 2), off_attn = off_q + al(HD * 2), off_m = off_attn + al(HD * 2),
+           off_logits = off_m + al((size_t)dd.F * 2), off_scores = off_logits + al((size_t)dd.V * 2),
+           off_part = off_scores + al((size_t)dd.H * dd.ctx * 2), off_opart = off_part + al((size_t)dd.H * dd.nsplit * 8),
+           off_cnt = off_opart + al((size_t)dd.H * dd.nsplit * dd.hd * 4), off_lcnt = off_cnt + al(dd.H * 4),
+           off_ring = off_lcnt + al(4), off_state = off_ring + al((size_t)dd.ctx * 4),
+           total = off_state + al(sizeof(StepState));
+    if (cudaMalloc(&e->ws, total) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        delete e;
+        return VKLLM_ERR_ALLOC;
+    }
+    cudaMemsetAsync(e->ws, 0, total, ctx->runtime->stream);
+    char *w = (char *)e->ws;
+    e->x = (__half *)(w + off_x);
+    e->q = (__half *)(w + off_q);
+    e->attn = (__half *)(w + off_attn);
+    e->m = (__half *)(w + off_m);
+    e->logits = (__half *)(w + off_logits);
+    e->scores = (__half *)(w + off_scores);
+    e->part = (float2 *)(w + off_part);
+    e->opart = (float *)(w + off_opart);
+    e->counters = (uint32_t *)(w + off_cnt);
+    e->logit_counter = (uint32_t *)(w + off_lcnt);
+    e->ring = (uint32_t *)(w + off_ring);
+    e->state = (StepState *)(w + off_state);
+
+    e->grid_qkv = gemv_grid(3 * HD / 2, sms);
+    e->grid_wo = gemv_grid(dd.D / 2, sms);
+    e->grid_upgate = gemv_grid(dd.F, sms);
+    e->grid_down = gemv_grid(dd.D / 2, sms);
+    e->grid_logits = gemv_grid((dd.V + 1) / 2, sms);
+    e->grid_embed = (dd.D / 8 + 255) / 256;
+    e->smem_D = (size_t)dd.D * 2;
+    e->smem_HD = (size_t)HD * 2;
+    e->smem_F = (size_t)dd.F * 2;
+    size_t smax = e->smem_F > e->smem_D ? e->smem_F : e->smem_D;
+    if (smax > 48 * 1024)
+    {
+        cudaFuncSetAttribute(k_dec_qkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
+        cudaFuncSetAttribute(k_dec_wo, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
+        cudaFuncSetAttribute(k_dec_upgate, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
+        cudaFuncSetAttribute(k_dec_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
+        cudaFuncSetAttribute(k_dec_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
+    }
+    e->kernels_per_step = 2 + 6 * (uint32_t)e->layers.size();
+
+    // Capture one decode step.
+    cudaStream_t cs;
+    if (cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) != cudaSuccess)
+    {
+        cudaFree(e->ws);
+        delete e;
+        return VKLLM_ERR_VULKAN;
+    }
+    cudaStreamSynchronize(ctx->runtime->stream);
+    vkllm_err_t err = VKLLM_ERR_OK;
+    if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        err = VKLLM_ERR_VULKAN;
+    if (err == VKLLM_ERR_OK)
+    {
+        vkllm_err_t le = enqueue_step(e, cs);
+        cudaError_t ce = cudaStreamEndCapture(cs, &e->graph);
+        if (le != VKLLM_ERR_OK || ce != cudaSuccess)
+            err = VKLLM_ERR_VULKAN;
+    }
+    if (err == VKLLM_ERR_OK && cudaGraphInstantiate(&e->exec, e->graph, 0) != cudaSuccess)
+        err = VKLLM_ERR_VULKAN;
+    cudaStreamDestroy(cs);
+    if (err != VKLLM_ERR_OK)
+    {
+        log_error("capturing the decode step failed: %s", cudaGetErrorString(cudaGetLastError()));
+        if (e->graph)
+            cudaGraphDestroy(e->graph);
+        cudaFree(e->ws);
+        delete e;
+        return err;
+    }
+    *out = e;
+    return VKLLM_ERR_OK;
+}
+
+vkllm_err_t get_engine(vkllm_context *ctx, vkllm_models_llama2 *model, Engine **out)
+{
+    if (!model->b200.engine)
+    {
+        Engine *e = nullptr;
+        _CHECK(engine_create(ctx, model, &e));
+        model->b200.engine = e;
+    }
+    Engine *e = (Engine *)model->b200.engine;
+    if (e->ctx != ctx)
+        return VKLLM_ERR_ARGS;
+    *out = e;
+    return VKLLM_ERR_OK;
+}
+
+} // namespace
+
+void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
+{
+    (void)ctx;
+    Engine *e = (Engine *)model->b200.engine;
+    if (!e)
+        return;
+    if (e->ctx && e->ctx->runtime)
+        cudaStreamSynchronize(e->ctx->runtime->stream);
+    if (e->exec)
+        cudaGraphExecDestroy(e->exec);
+    if (e->graph)
+        cudaGraphDestroy(e->graph);
+    cudaFree(e->ws);
+    delete e;
+    model->b200.engine = nullptr;
+}
+
+vkllm_err_t plan_run(vkllm_context *ctx, vkllm_graph *graph)
+{
+    Plan *p = (Plan *)graph->b200_plan;
+    if (!p || p->seq_len != 1 || graph->output_node != p->output || graph->nodes->used_n != p->n_nodes)
+        return VKLLM_ERR_ARGS;
+    if (p->input_toks->dtype != vkllm_dtype_uint32 || !p->output->data.mapped)
+        return VKLLM_ERR_ARGS;
+    Engine *e = nullptr;
+    if (get_engine(ctx, p->model, &e) != VKLLM_ERR_OK)
+        return VKLLM_ERR_ARGS;
+    if (p->offsets >= e->dd.ctx)
+        return VKLLM_ERR_ARGS;
+    cudaStream_t s = (cudaStream_t)graph->commands->stream;
+    const uint32_t *tok = (const uint32_t *)dev_ptr(ctx, p->input_toks);
+    uint32_t *out = (uint32_t *)p->output->data.dev;
+    if (!tok || !out)
+        return VKLLM_ERR_ALLOC;
+    k_set_state<<<1, 1, 0, s>>>(e->state, tok, 0, p->offsets);
+    VKB_CUDA(cudaGraphLaunch(e->exec, s));
+    k_emit_token<<<1, 1, 0, s>>>(e->state, out);
+    VKB_CUDA(cudaGetLastError());
+    _CHECK(vkllm_commands_submit(ctx, graph->commands));
+    _CHECK(vkllm_commands_wait_exec(ctx, graph->commands));
+    return VKLLM_ERR_OK;
+}
+
+void plan_free(vkllm_graph *graph)
+{
+    free(graph->b200_plan);
+    graph->b200_plan = nullptr;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Counter-based generator for random weights: element i of tensor t is the Irwin-Hall sum of 12
+// 16-bit uniforms drawn from splitmix64(key + 3i + j), j = 0..2, centred and scaled to std_dev,
+// rounded to fp16. Integer sums are exact and the single fp32 product rounds identically on host
+// and device, so vkllm_b200_random_f16_host reproduces the device bits.
+__host__ __device__ inline uint64_t splitmix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__host__ __device__ inline float random_value(uint64_t key, uint64_t i, float scale)
+{
+    int64_t s = 0;
+    for (int j = 0; j < 3; ++j)
+    {
+        uint64_t h = splitmix64(key + 3 * i + (uint64_t)j);
+        s += (int64_t)(h & 0xffff) + (int64_t)((h >> 16) & 0xffff) + (int64_t)((h >> 32) & 0xffff) +
+             (int64_t)(h >> 48);
+    }
+    float t = (float)(int32_t)(s - 393210);
+    return t * scale;
+}
+
+__global__ void k_fill_random_f16(__half *dst, uint64_t n, uint64_t key, float scale)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2half_rn(random_value(key, i, scale));
+}
+
+__global__ void k_fill_const_f32(float *dst, uint64_t n, float v)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        dst[i] = v;
+}
+
+static uint64_t tensor_key(uint64_t seed, uint64_t tensor_id)
+{
+    return splitmix64(seed ^ splitmix64(tensor_id + 0x5851F42D4C957F2Dull));
+}
+
+vkllm_err_t fill_random_f16(vkllm_context *ctx, void *dst, uint64_t n, uint64_t seed, uint64_t tensor_id, float std_dev)
+{
+    float scale = std_dev * (1.0f / 65536.0f);
+    k_fill_random_f16<<<ctx->device->sm_count * 8, 256, 0, ctx->runtime->stream>>>((__half *)dst, n,
+                                                                                     tensor_key(seed, tensor_id), scale);
+    VKB_CUDA(cudaGetLastError());
+    return VKLLM_ERR_OK;
+}
+
+vkllm_err_t fill_const_f32(vkllm_context *ctx, void *dst, uint64_t n, float v)
+{
+    k_fill_const_f32<<<(unsigned)((n + 255) / 256 > 1024 ? 1024 : (n + 255) / 256), 256, 0, ctx->runtime->stream>>>(
+        (float *)dst, n, v);
+    VKB_CUDA(cudaGetLastError());
+    return VKLLM_ERR_OK;
+}
+
+static uint16_t f32_to_f16_rne(float f)
+{
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u, mant = x & 0x7fffffu;
+    int exp = (int)((x >> 23) & 0xff);
+    if (exp == 255)
+        return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+    int e = exp - 127 + 15;
+    if (e >= 31)
+        return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0)
+    {
+        if (e < -10)
+            return (uint16_t)sign;
+        mant |= 0x800000u;
+        int shift = 14 - e;
+        uint32_t hm = mant >> shift, rem = mant & ((1u << shift) - 1), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (hm & 1u)))
+            hm++;
+        return (uint16_t)(sign | hm);
+    }
+    uint32_t h = sign | ((uint32_t)e << 10) | (mant >> 13);
+    uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u)))
+        h++;
+    return (uint16_t)h;
+}
+
+} // namespace vkb
+
+using namespace vkb;
+
+extern "C" void vkllm_b200_random_f16_host(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t first,
+                                           uint64_t n, uint16_t *out)
+{
+    uint64_t key = tensor_key(seed, tensor_id);
+    float scale = std_dev * (1.0f / 65536.0f);
+    for (uint64_t i = 0; i < n; ++i)
+        out[i] = f32_to_f16_rne(random_value(key, first + i, scale));
+}
+
+extern "C" vkllm_err_t vkllm_b200_engine_prepare(struct vkllm_context *context, struct vkllm_models_llama2 *model)
+{
+    _CHECK_ARGS(context && model);
+    Engine *e;
+    return get_engine(context, model, &e);
+}
+
+extern "C" vkllm_err_t vkllm_b200_engine_set_state(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                   uint32_t token, uint32_t pos)
+{
+    _CHECK_ARGS(context && model);
+    Engine *e;
+    _CHECK(get_engine(context, model, &e));
+    _CHECK_ARGS(pos < e->dd.ctx);
+    k_set_state<<<1, 1, 0, context->runtime->stream>>>(e->state, nullptr, token, pos);
+    VKB_CUDA(cudaGetLastError());
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_engine_decode_steps(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                      uint32_t n)
+{
+    _CHECK_ARGS(context && model);
+    Engine *e;
+    _CHECK(get_engine(context, model, &e));
+    for (uint32_t i = 0; i < n; ++i)
+        VKB_CUDA(cudaGraphLaunch(e->exec, context->runtime->stream));
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_engine_read_tokens(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                     uint32_t *out, uint32_t n)
+{
+    _CHECK_ARGS(context && model && out);
+    Engine *e;
+    _CHECK(get_engine(context, model, &e));
+    _CHECK_ARGS(n <= e->dd.ctx);
+    VKB_CUDA(cudaStreamSynchronize(context->runtime->stream));
+    StepState st;
+    VKB_CUDA(cudaMemcpy(&st, e->state, sizeof(st), cudaMemcpyDeviceToHost));
+    if (st.error)
+    {
+        log_error("decode step refused: position past the KV cache");
+        return VKLLM_ERR_ARGS;
+    }
+    VKB_CUDA(cudaMemcpy(out, e->ring, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_engine_read_logits(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                     uint16_t *out, uint32_t n)
+{
+    _CHECK_ARGS(context && model && out);
+    Engine *e;
+    _CHECK(get_engine(context, model, &e));
+    _CHECK_ARGS(n <= e->dd.V);
+    VKB_CUDA(cudaStreamSynchronize(context->runtime->stream));
+    VKB_CUDA(cudaMemcpy(out, e->logits, (size_t)n * 2, cudaMemcpyDeviceToHost));
+    return VKLLM_ERR_OK;
+}
+
+extern "C" uint32_t vkllm_b200_engine_kernels_per_step(struct vkllm_context *context, struct vkllm_models_llama2 *model)
+{
+    if (!context || !model || !model->b200.engine)
+        return 0;
+    return ((Engine *)model->b200.engine)->kernels_per_step;
+}
+
+// Times `iters` back-to-back launches of one decode kernel (layers cycled so each launch streams
+// its own weights from HBM, as inside a step) with CUDA events on the context stream. Reports the
+// mean duration per launch and the algorithmic bytes one launch must move.
+extern "C" vkllm_err_t vkllm_b200_engine_bench_kernel(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                      const char *kernel, uint32_t iters, float *us_per_launch,
+                                                      uint64_t *bytes_per_launch)
+{
+    _CHECK_ARGS(context && model && kernel && iters > 0 && us_per_launch && bytes_per_launch);
+    Engine *e;
+    _CHECK(get_engine(context, model, &e));
+    const DecodeDims &dd = e->dd;
+    const uint64_t HD = (uint64_t)dd.H * dd.hd;
+    cudaStream_t s = context->runtime->stream;
+    int which = -1;
+    const char *names[] = {"qkv", "wo", "upgate", "down", "logits"};
+    for (int i = 0; i < 5; ++i)
+        if (strcmp(kernel, names[i]) == 0)
+            which = i;
+    _CHECK_ARGS(which >= 0);
+    uint64_t bytes = 0;
+    switch (which)
+    {
+    case 0:
+        bytes = 3 * HD * dd.D * 2 + dd.D * 2 + dd.D * 4 + 2 * HD * 2 + HD * 2;
+        break;
+    case 1:
+        bytes = (uint64_t)dd.D * HD * 2 + HD * 2 + 2ull * dd.D * 2;
+        break;
+    case 2:
+        bytes = 2ull * dd.F * dd.D * 2 + dd.D * 2 + dd.D * 4 + (uint64_t)dd.F * 2;
+        break;
+    case 3:
+        bytes = (uint64_t)dd.D * dd.F * 2 + (uint64_t)dd.F * 2 + 2ull * dd.D * 2;
+        break;
+    case 4:
+        bytes = (uint64_t)dd.V * dd.D * 2 + dd.D * 2 + dd.D * 4 + (uint64_t)dd.V * 2;
+        break;
+    }
+    k_set_state<<<1, 1, 0, s>>>(e->state, nullptr, 0, 0);
+    cudaEvent_t a, b;
+    VKB_CUDA(cudaEventCreate(&a));
+    VKB_CUDA(cudaEventCreate(&b));
+    auto launch = [&](uint32_t i) {
+        const LayerW &lw = e->layers[i % e->layers.size()];
+        switch (which)
+        {
+        case 0:
+            k_dec_qkv<<<e->grid_qkv, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->q, e->state);
+            break;
+        case 1:
+            k_dec_wo<<<e->grid_wo, kGemvThreads, e->smem_HD, s>>>(lw, dd, e->attn, e->x);
+            break;
+        case 2:
+            k_dec_upgate<<<e->grid_upgate, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->m);
+            break;
+        case 3:
+            k_dec_down<<<e->grid_down, kGemvThreads, e->smem_F, s>>>(lw, dd, e->m, e->x);
+            break;
+        case 4:
+            k_dec_logits<<<e->grid_logits, kGemvThreads, e->smem_D, s>>>(e->wout, e->out_norm, dd, e->x, e->logits,
+                                                                         e->logit_counter, e->state, e->ring, dd.ctx);
+            break;
+        }
+    };
+    for (uint32_t i = 0; i < 3; ++i)
+        launch(i);
+    VKB_CUDA(cudaEventRecord(a, s));
+    for (uint32_t i = 0; i < iters; ++i)
+        launch(i);
+    VKB_CUDA(cudaEventRecord(b, s));
+    VKB_CUDA(cudaEventSynchronize(b));
+    float ms = 0.f;
+    VKB_CUDA(cudaEventElapsedTime(&ms, a, b));
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    VKB_CUDA(cudaGetLastError());
+    *us_per_launch = ms * 1000.0f / (float)iters;
+    *bytes_per_launch = bytes;
+    return VKLLM_ERR_OK;
+}

@@ -1,0 +1,38 @@
+// Launchers shared by the op layer and the engine.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace vkb
+{
+
+// Batched C[z] = act(scale * A[z] . B[z]^T) for fp16 A [M, K] and B [N, K], both K-contiguous, C
+// [M, N] N-contiguous, fp32 accumulation; z enumerates the output's (b, c) batch with broadcast
+// offsets for A and B.
+struct GemmArgs
+{
+    const void *A, *B;
+    void *C;
+    uint32_t M, N, K;
+    uint64_t lda, ldb, ldc;           // row strides in elements
+    uint32_t batch_c;                 // output C extent (z = b * batch_c + c)
+    uint32_t batch;                   // output B * C
+    uint64_t a_sb, a_sc, b_sb, b_sc;  // batch strides in elements (0 where broadcast)
+    uint64_t c_sb, c_sc;
+    float scale;
+    int act;
+};
+
+// Fills `g` from 4-D descriptors when the tensor-core path applies (B read as [N, K] with unit
+// inner stride, all row strides multiples of 8 elements, 16-byte aligned bases). Returns false
+// otherwise.
+bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool trans_b, const void *a, const void *b,
+                    void *c, float scale, int act, GemmArgs *g);
+
+// Enqueues the tcgen05 GEMM; returns false when it cannot run on this device / shape.
+bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s);
+
+} // namespace vkb

@@ -1,0 +1,538 @@
+// LLaMA-2 model: GGUF load, free, graph build, tokenizer, and random initialisation on the device
+// (reference: src/models/vkllm_models_llama2.c).
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+
+#include "../engine/plan.h"
+#include "../runtime/internal.h"
+#include "gguf.h"
+#include "vkllm_b200.h"
+#include "vkllm_kvcache.h"
+#include "vkllm_models_llama2.h"
+#include "vkllm_op_matmul.h"
+#include "vkllm_op_rmsnorm.h"
+
+namespace vkb
+{
+void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model);
+vkllm_err_t fill_random_f16(vkllm_context *ctx, void *dst, uint64_t n, uint64_t seed, uint64_t tensor_id,
+                            float std_dev);
+vkllm_err_t fill_const_f32(vkllm_context *ctx, void *dst, uint64_t n, float v);
+} // namespace vkb
+
+namespace
+{
+
+// Defaults for metadata keys a file may omit (src/models/vkllm_models_llama2.c:224-241).
+void set_defaults(vkllm_models_llama2 *m)
+{
+    m->meta.block_count = 32;
+    m->meta.context_length = 2048;
+    m->meta.embedding_length = 4096;
+    m->meta.rope_freq_base = 10000.0f;
+    m->meta.layer_norm_rms_epsilon = 1e-6f;
+    m->meta.key_length = 128;
+    m->meta.value_length = 128;
+    m->meta.vocab_size = 32000;
+    m->meta.head_count = 32;
+    m->meta.head_count_kv = 32;
+    m->meta.bos_token_id = 1;
+    m->meta.eos_token_id = 2;
+    m->meta.padding_token_id = 0;
+    m->meta.add_bos_token = true;
+    m->meta.add_eos_token = true;
+}
+
+// Metadata keys and their typed targets (src/models/vkllm_models_llama2.c:67-187). A key only
+// takes effect with the expected GGUF type, as in the reference.
+void apply_kv(vkllm_models_llama2 *m, const vkb::GgufKV &kv)
+{
+    struct U32Key
+    {
+        const char *name;
+        uint32_t *dst;
+    };
+    const U32Key u32keys[] = {
+        {"llama.block_count", &m->meta.block_count},
+        {"llama.context_length", &m->meta.context_length},
+        {"llama.embedding_length", &m->meta.embedding_length},
+        {"llama.attention.key_length", &m->meta.key_length},
+        {"llama.attention.value_length", &m->meta.value_length},
+        {"llama.vocab_size", &m->meta.vocab_size},
+        {"llama.attention.head_count", &m->meta.head_count},
+        {"llama.attention.head_count_kv", &m->meta.head_count_kv},
+        {"tokenizer.ggml.bos_token_id", &m->meta.bos_token_id},
+        {"tokenizer.ggml.eos_token_id", &m->meta.eos_token_id},
+        {"tokenizer.ggml.padding_token_id", &m->meta.padding_token_id},
+    };
+    for (const auto &k : u32keys)
+        if (kv.key == k.name && kv.type == vkb::GGUF_U32)
+            *k.dst = (uint32_t)kv.u;
+    if (kv.key == "llama.rope.freq_base" && kv.type == vkb::GGUF_F32)
+        m->meta.rope_freq_base = (float)kv.f;
+    if (kv.key == "llama.attention.layer_norm_rms_epsilon" && kv.type == vkb::GGUF_F32)
+        m->meta.layer_norm_rms_epsilon = (float)kv.f;
+    if (kv.key == "tokenizer.ggml.add_bos_token" && kv.type == vkb::GGUF_BOOL)
+        m->meta.add_bos_token = kv.u != 0;
+    if (kv.key == "tokenizer.ggml.add_eos_token" && kv.type == vkb::GGUF_BOOL)
+        m->meta.add_eos_token = kv.u != 0;
+}
+
+vkllm_tensor **block_slot(block_weights *bw, const std::string &leaf)
+{
+    if (leaf == "attn_norm.weight")
+        return &bw->attn_norm_weight;
+    if (leaf == "ffn_norm.weight")
+        return &bw->ffn_norm_weight;
+    if (leaf == "attn_q.weight")
+        return &bw->WQ;
+    if (leaf == "attn_k.weight")
+        return &bw->WK;
+    if (leaf == "attn_v.weight")
+        return &bw->WV;
+    if (leaf == "attn_output.weight")
+        return &bw->WO;
+    if (leaf == "ffn_gate.weight")
+        return &bw->WG;
+    if (leaf == "ffn_up.weight")
+        return &bw->WU;
+    if (leaf == "ffn_down.weight")
+        return &bw->WD;
+    return nullptr;
+}
+
+vkllm_err_t ensure_blocks(vkllm_models_llama2 *m, size_t n)
+{
+    while (m->weights.blocks->used_n < n)
+    {
+        block_weights *bw = (block_weights *)calloc(1, sizeof(block_weights));
+        if (!bw)
+            return VKLLM_ERR_ALLOC;
+        _CHECK(vkllm_array_block_weights_append(m->weights.blocks, bw));
+    }
+    return VKLLM_ERR_OK;
+}
+
+// GGUF dims are innermost-first; the tensor shape is their reverse (src/models/vkllm_models_llama2.c:198-202).
+vkllm_err_t tensor_from_gguf(vkllm_context *ctx, const vkb::GgufTensor &gt, vkllm_tensor **out)
+{
+    if (gt.type != vkb::GGML_F32 && gt.type != vkb::GGML_F16)
+    {
+        log_error("tensor %s has GGML type %u; only F32 and F16 are supported", gt.name.c_str(), gt.type);
+        return VKLLM_ERR_ARGS;
+    }
+    vkllm_dtype_t dt = gt.type == vkb::GGML_F32 ? vkllm_dtype_float32 : vkllm_dtype_float16;
+    uint32_t shapes[4] = {1, 1, 1, 1};
+    for (uint32_t i = 0; i < gt.n_dims && i < 4; ++i)
+        shapes[3 - i] = (uint32_t)gt.dims[i];
+    _CHECK(vkllm_tensor_new(ctx, gt.name.c_str(), shapes, dt, VKLLM_OP_NONE, NULL, 0, NULL, 0, false, out));
+    void *d = vkb::dev_ptr(ctx, *out);
+    if (!d)
+        return VKLLM_ERR_ALLOC;
+    VKB_CUDA(cudaMemcpyAsync(d, gt.data, gt.bytes, cudaMemcpyHostToDevice, ctx->runtime->stream));
+    return VKLLM_ERR_OK;
+}
+
+vkllm_err_t create_kvcache(vkllm_context *ctx, vkllm_models_llama2 *m)
+{
+    _CHECK_ARGS(m->weights.blocks->used_n > 0 && m->weights.blocks->data[0]->WK && m->weights.blocks->data[0]->WV);
+    uint32_t H = m->meta.head_count;
+    uint32_t kd = m->weights.blocks->data[0]->WK->shapes[3] / H;
+    uint32_t vd = m->weights.blocks->data[0]->WV->shapes[3] / H;
+    uint32_t kshape[4] = {1, H, m->meta.context_length, kd};
+    uint32_t vshape[4] = {1, H, m->meta.context_length, vd};
+    return vkllm_kvcache_new(ctx, kshape, vshape, m->meta.block_count, &m->weights.kvcache);
+}
+
+} // namespace
+
+extern "C" vkllm_err_t vkllm_models_llama2_load(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                const char *file)
+{
+    _CHECK_ARGS(context && model && file);
+    memset(model, 0, sizeof(*model));
+    model->b200.tp_size = 1;
+    vkb::GgufFile gguf;
+    std::string err = gguf.open(file);
+    if (!err.empty())
+    {
+        log_error("failed to open gguf file %s: %s", file, err.c_str());
+        return VKLLM_ERR_ARGS;
+    }
+    set_defaults(model);
+    const vkb::GgufKV *tokens = nullptr, *scores = nullptr, *types = nullptr;
+    for (const auto &kv : gguf.kvs())
+    {
+        apply_kv(model, kv);
+        if (kv.key == "tokenizer.ggml.tokens" && kv.type == vkb::GGUF_ARRAY && kv.arr_type == vkb::GGUF_STRING)
+            tokens = &kv;
+        if (kv.key == "tokenizer.ggml.scores" && kv.type == vkb::GGUF_ARRAY && kv.arr_type == vkb::GGUF_F32)
+            scores = &kv;
+        if (kv.key == "tokenizer.ggml.token_type" && kv.type == vkb::GGUF_ARRAY && kv.arr_type == vkb::GGUF_I32)
+            types = &kv;
+    }
+    vkllm_err_t e = VKLLM_ERR_OK;
+    if (tokens)
+    {
+        _CHECK(vkllm_array_token_new(&model->meta.tokens, tokens->arr_str.size()));
+        for (size_t i = 0; i < tokens->arr_str.size(); ++i)
+        {
+            vkllm_token t;
+            t.text = strdup(tokens->arr_str[i].c_str());
+            t.score = scores && i < scores->arr_num.size() ? (float)scores->arr_num[i] : 0.0f;
+            t.type = types && i < types->arr_num.size() ? (int32_t)types->arr_num[i] : 0;
+            _CHECK(vkllm_array_token_append(model->meta.tokens, t));
+        }
+    }
+    _CHECK(vkllm_array_block_weights_new(&model->weights.blocks, model->meta.block_count));
+    for (const auto &t : gguf.tensors())
+    {
+        vkllm_tensor **slot = nullptr;
+        if (t.name == "token_embd.weight")
+            slot = &model->weights.tok_embed_weights;
+        else if (t.name == "output_norm.weight")
+            slot = &model->weights.output_norm_weight;
+        else if (t.name == "output.weight")
+            slot = &model->weights.output_weight;
+        else if (t.name.compare(0, 4, "blk.") == 0)
+        {
+            int idx = -1;
+            char leaf[96] = {0};
+            if (sscanf(t.name.c_str(), "blk.%d.%95s", &idx, leaf) == 2 && idx >= 0 && idx < 4096)
+            {
+                e = ensure_blocks(model, (size_t)idx + 1);
+                if (e != VKLLM_ERR_OK)
+                    goto fail;
+                slot = block_slot(model->weights.blocks->data[idx], leaf);
+            }
+        }
+        if (!slot)
+            continue;
+        if (*slot)
+            vkllm_tensor_free(context, *slot);
+        e = tensor_from_gguf(context, t, slot);
+        if (e != VKLLM_ERR_OK)
+            goto fail;
+    }
+    if (cudaStreamSynchronize(context->runtime->stream) != cudaSuccess)
+    {
+        e = VKLLM_ERR_VULKAN;
+        goto fail;
+    }
+    e = create_kvcache(context, model);
+    if (e != VKLLM_ERR_OK)
+        goto fail;
+    return VKLLM_ERR_OK;
+fail:
+    vkllm_models_llama2_free(context, model);
+    return e;
+}
+
+extern "C" vkllm_err_t vkllm_models_llama2_free(struct vkllm_context *context, struct vkllm_models_llama2 *model)
+{
+    _CHECK_ARGS(context && model);
+    vkb::engine_destroy(context, model);
+    if (model->meta.tokens)
+    {
+        for (size_t i = 0; i < model->meta.tokens->used_n; ++i)
+            free(model->meta.tokens->data[i].text);
+        vkllm_array_token_free(model->meta.tokens);
+        model->meta.tokens = NULL;
+    }
+    vkllm_tensor_free(context, model->weights.tok_embed_weights);
+    vkllm_tensor_free(context, model->weights.output_norm_weight);
+    vkllm_tensor_free(context, model->weights.output_weight);
+    model->weights.tok_embed_weights = model->weights.output_norm_weight = model->weights.output_weight = NULL;
+    if (model->weights.blocks)
+    {
+        for (size_t i = 0; i < model->weights.blocks->used_n; ++i)
+        {
+            block_weights *bw = model->weights.blocks->data[i];
+            if (!bw)
+                continue;
+            vkllm_tensor *ts[] = {bw->attn_norm_weight, bw->ffn_norm_weight, bw->WQ, bw->WK, bw->WV,
+                                  bw->WO,               bw->WU,              bw->WG, bw->WD};
+            for (vkllm_tensor *t : ts)
+                vkllm_tensor_free(context, t);
+            free(bw);
+        }
+        vkllm_array_block_weights_free(model->weights.blocks);
+        model->weights.blocks = NULL;
+    }
+    if (model->weights.kvcache)
+    {
+        vkllm_kvcache_free(context, model->weights.kvcache);
+        model->weights.kvcache = NULL;
+    }
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_models_llama2_build_graph(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                       struct vkllm_tensor *input_toks, struct vkllm_graph *graph,
+                                                       uint32_t offsets)
+{
+    _CHECK_ARGS(context && model && input_toks && graph);
+    _CHECK_ARGS(model->weights.tok_embed_weights && model->weights.output_norm_weight && model->weights.output_weight);
+    _CHECK_ARGS(model->weights.blocks && model->weights.blocks->used_n > 0 && model->weights.kvcache);
+    _CHECK_ARGS(input_toks->dtype == vkllm_dtype_uint32);
+    uint32_t B = input_toks->shapes[0], S = input_toks->shapes[3];
+    uint32_t D = model->meta.embedding_length, V = model->meta.vocab_size;
+    _CHECK_ARGS((uint64_t)offsets + S <= model->meta.context_length);
+
+    _CHECK(vkllm_graph_add_input(context, graph, input_toks));
+    uint32_t eshape[4] = {B, 1, S, D};
+    vkllm_tensor *esrcs[] = {input_toks, model->weights.tok_embed_weights};
+    uint32_t unk = model->meta.padding_token_id;
+    vkllm_tensor *embedded;
+    _CHECK(vkllm_tensor_new(context, "embedded", eshape, vkllm_dtype_float16, VKLLM_OP_EMBEDDING, esrcs, 2, &unk,
+                            sizeof(unk), false, &embedded));
+    vkllm_err_t e = vkllm_graph_add_node(context, graph, embedded);
+    if (e != VKLLM_ERR_OK)
+    {
+        vkllm_tensor_free(context, embedded);
+        return e;
+    }
+    vkllm_tensor *hidden = embedded;
+    for (uint32_t i = 0; i < model->meta.block_count && i < model->weights.blocks->used_n; ++i)
+    {
+        block_weights *bw = model->weights.blocks->data[i];
+        _CHECK_ARGS(bw);
+        vkllm_llama2_transformer_block_params bp;
+        memset(&bp, 0, sizeof(bp));
+        bp.attn.WK = bw->WK;
+        bp.attn.WQ = bw->WQ;
+        bp.attn.WV = bw->WV;
+        bp.attn.WO = bw->WO;
+        bp.attn.norm_weight = bw->attn_norm_weight;
+        bp.attn.norm_power = 2.0f;
+        bp.attn.norm_eps = model->meta.layer_norm_rms_epsilon;
+        bp.attn.freq_base = model->meta.rope_freq_base;
+        bp.attn.offsets = offsets;
+        bp.attn.num_head = model->meta.head_count;
+        bp.ffn.WU = bw->WU;
+        bp.ffn.WG = bw->WG;
+        bp.ffn.WD = bw->WD;
+        bp.ffn.norm_weight = bw->ffn_norm_weight;
+        bp.ffn.norm_power = 2.0f;
+        bp.ffn.norm_eps = model->meta.layer_norm_rms_epsilon;
+        _CHECK(vkllm_llama2_build_transformer_block(context, graph, model->weights.kvcache, hidden, bp, i));
+        hidden = graph->nodes->data[graph->nodes->used_n - 1];
+    }
+    vkllm_tensor *norm, *logits, *output;
+    vkllm_tensor *nsrcs[] = {hidden, model->weights.output_norm_weight};
+    vkllm_op_rmsnorm_params np = {2.0f, model->meta.layer_norm_rms_epsilon};
+    _CHECK(vkllm_tensor_new(context, "output_norm", hidden->shapes, hidden->dtype, VKLLM_OP_RMSNORM, nsrcs, 2, &np,
+                            sizeof(np), false, &norm));
+    _CHECK(vkllm_graph_add_node(context, graph, norm));
+    uint32_t lshape[4] = {B, 1, S, V};
+    vkllm_tensor *lsrcs[] = {norm, model->weights.output_weight};
+    vkllm_op_matmul_params mp = {1.0f, 0};
+    _CHECK(vkllm_tensor_new(context, "logits", lshape, norm->dtype, VKLLM_OP_MATMUL, lsrcs, 2, &mp, sizeof(mp), false,
+                            &logits));
+    _CHECK(vkllm_graph_add_node(context, graph, logits));
+    uint32_t oshape[4] = {B, 1, S, 1};
+    _CHECK(vkllm_tensor_new(context, "output", oshape, vkllm_dtype_uint32, VKLLM_OP_ARG_MAX, &logits, 1, NULL, 0, true,
+                            &output));
+    _CHECK(vkllm_graph_add_node(context, graph, output));
+    _CHECK(vkllm_graph_set_output(context, graph, output));
+
+    vkb::Plan *plan = (vkb::Plan *)calloc(1, sizeof(vkb::Plan));
+    if (plan)
+    {
+        plan->model = model;
+        plan->input_toks = input_toks;
+        plan->output = output;
+        plan->offsets = offsets;
+        plan->seq_len = S;
+        plan->n_nodes = graph->nodes->used_n;
+        free(graph->b200_plan);
+        graph->b200_plan = plan;
+    }
+    return VKLLM_ERR_OK;
+}
+
+// Tokenizer (src/models/vkllm_models_llama2.c:604-816): "▁" prefix and "▁" for every space, split
+// into UTF-8 characters, then repeatedly merge the adjacent pair whose concatenation is a vocabulary
+// entry with the highest score (first pair on ties), until no pair merges. Output: [bos] + ids of
+// the pieces found in the vocabulary (first entry with that text) + [eos].
+extern "C" vkllm_err_t vkllm_models_llama2_tokenize(struct vkllm_models_llama2 *model, const char *sentence,
+                                                    struct vkllm_array_token_id **token_ids)
+{
+    _CHECK_ARGS(model && sentence && token_ids);
+    _CHECK_ARGS(model->meta.tokens && model->meta.tokens->used_n > 0);
+    std::unordered_map<std::string, uint32_t> vocab;
+    vocab.reserve(model->meta.tokens->used_n * 2);
+    for (size_t i = 0; i < model->meta.tokens->used_n; ++i)
+        vocab.emplace(model->meta.tokens->data[i].text ? model->meta.tokens->data[i].text : "", (uint32_t)i);
+    size_t len = strlen(sentence);
+    if (len == 0)
+        return vkllm_array_token_id_new(token_ids, 1);
+    static const char kSpace[] = "\xE2\x96\x81";
+    std::string text = kSpace;
+    for (size_t i = 0; i < len; ++i)
+    {
+        if (sentence[i] == ' ')
+            text += kSpace;
+        else
+            text += sentence[i];
+    }
+    std::vector<std::string> pieces;
+    for (size_t i = 0; i < text.size();)
+    {
+        unsigned char c = (unsigned char)text[i];
+        size_t n = 1;
+        if (c >= 0x80)
+        {
+            if ((c & 0xE0) == 0xC0)
+                n = 2;
+            else if ((c & 0xF0) == 0xE0)
+                n = 3;
+            else if ((c & 0xF8) == 0xF0)
+                n = 4;
+        }
+        if (i + n > text.size())
+            n = text.size() - i;
+        pieces.push_back(text.substr(i, n));
+        i += n;
+    }
+    while (pieces.size() > 1)
+    {
+        float best = -INFINITY;
+        long best_i = -1;
+        for (size_t i = 0; i + 1 < pieces.size(); ++i)
+        {
+            auto it = vocab.find(pieces[i] + pieces[i + 1]);
+            if (it == vocab.end())
+                continue;
+            float sc = model->meta.tokens->data[it->second].score;
+            if (sc > best)
+            {
+                best = sc;
+                best_i = (long)i;
+            }
+        }
+        if (best_i < 0)
+            break;
+        pieces[best_i] += pieces[best_i + 1];
+        pieces.erase(pieces.begin() + best_i + 1);
+    }
+    _CHECK(vkllm_array_token_id_new(token_ids, pieces.size() + 2));
+    if (model->meta.add_bos_token)
+        _CHECK(vkllm_array_token_id_append(*token_ids, model->meta.bos_token_id));
+    for (const auto &p : pieces)
+    {
+        auto it = vocab.find(p);
+        if (it != vocab.end())
+            _CHECK(vkllm_array_token_id_append(*token_ids, it->second));
+    }
+    if (model->meta.add_eos_token)
+        _CHECK(vkllm_array_token_id_append(*token_ids, model->meta.eos_token_id));
+    return VKLLM_ERR_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Random initialisation on the device (no GGUF): same tensors, names and shapes as the GGUF loader
+// produces, fp16 weights ~ N(0, std) from a counter-based generator, f32 norm gains = 1.
+extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context *context,
+                                                            struct vkllm_models_llama2 *model,
+                                                            const struct vkllm_b200_llama2_config *cfg,
+                                                            uint64_t seed)
+{
+    _CHECK_ARGS(context && model && cfg);
+    _CHECK_ARGS(cfg->block_count > 0 && cfg->embedding_length > 0 && cfg->head_count > 0 && cfg->ffn_length > 0 &&
+                cfg->vocab_size > 0 && cfg->context_length > 0);
+    _CHECK_ARGS(cfg->embedding_length % cfg->head_count == 0);
+    memset(model, 0, sizeof(*model));
+    model->b200.tp_size = 1;
+    set_defaults(model);
+    model->meta.block_count = cfg->block_count;
+    model->meta.context_length = cfg->context_length;
+    model->meta.embedding_length = cfg->embedding_length;
+    model->meta.head_count = cfg->head_count;
+    model->meta.head_count_kv = cfg->head_count;
+    model->meta.key_length = model->meta.value_length = cfg->embedding_length / cfg->head_count;
+    model->meta.vocab_size = cfg->vocab_size;
+    model->meta.rope_freq_base = cfg->rope_freq_base > 0 ? cfg->rope_freq_base : 10000.0f;
+    model->meta.layer_norm_rms_epsilon = cfg->rms_eps > 0 ? cfg->rms_eps : 1e-5f;
+    uint32_t D = cfg->embedding_length, F = cfg->ffn_length, V = cfg->vocab_size;
+    float sd = cfg->init_std > 0 ? cfg->init_std : 0.02f;
+    uint64_t tid = 0;
+    vkllm_err_t e;
+    auto make16 = [&](const char *name, uint32_t rows, uint32_t cols, vkllm_tensor **out) -> vkllm_err_t {
+        uint32_t sh[4] = {1, 1, rows, cols};
+        _CHECK(vkllm_tensor_new(context, name, sh, vkllm_dtype_float16, VKLLM_OP_NONE, NULL, 0, NULL, 0, false, out));
+        void *d = vkb::dev_ptr(context, *out);
+        if (!d)
+            return VKLLM_ERR_ALLOC;
+        return vkb::fill_random_f16(context, d, (uint64_t)rows * cols, seed, tid++, sd);
+    };
+    auto make32 = [&](const char *name, uint32_t n, vkllm_tensor **out) -> vkllm_err_t {
+        uint32_t sh[4] = {1, 1, 1, n};
+        _CHECK(vkllm_tensor_new(context, name, sh, vkllm_dtype_float32, VKLLM_OP_NONE, NULL, 0, NULL, 0, false, out));
+        void *d = vkb::dev_ptr(context, *out);
+        if (!d)
+            return VKLLM_ERR_ALLOC;
+        tid++;
+        return vkb::fill_const_f32(context, d, n, 1.0f);
+    };
+    char name[128];
+    e = vkllm_array_block_weights_new(&model->weights.blocks, cfg->block_count);
+    if (e != VKLLM_ERR_OK)
+        return e;
+    // Tensor ids follow GGUF order: token_embd, blocks (attn_norm, ffn_norm, q, k, v, o, gate, up,
+    // down), output_norm, output.
+    if ((e = make16("token_embd.weight", V, D, &model->weights.tok_embed_weights)) != VKLLM_ERR_OK)
+        goto fail;
+    if ((e = ensure_blocks(model, cfg->block_count)) != VKLLM_ERR_OK)
+        goto fail;
+    for (uint32_t i = 0; i < cfg->block_count; ++i)
+    {
+        block_weights *bw = model->weights.blocks->data[i];
+        snprintf(name, sizeof(name), "blk.%u.attn_norm.weight", i);
+        if ((e = make32(name, D, &bw->attn_norm_weight)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.ffn_norm.weight", i);
+        if ((e = make32(name, D, &bw->ffn_norm_weight)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.attn_q.weight", i);
+        if ((e = make16(name, D, D, &bw->WQ)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.attn_k.weight", i);
+        if ((e = make16(name, D, D, &bw->WK)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.attn_v.weight", i);
+        if ((e = make16(name, D, D, &bw->WV)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.attn_output.weight", i);
+        if ((e = make16(name, D, D, &bw->WO)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.ffn_gate.weight", i);
+        if ((e = make16(name, F, D, &bw->WG)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.ffn_up.weight", i);
+        if ((e = make16(name, F, D, &bw->WU)) != VKLLM_ERR_OK)
+            goto fail;
+        snprintf(name, sizeof(name), "blk.%u.ffn_down.weight", i);
+        if ((e = make16(name, D, F, &bw->WD)) != VKLLM_ERR_OK)
+            goto fail;
+    }
+    if ((e = make32("output_norm.weight", D, &model->weights.output_norm_weight)) != VKLLM_ERR_OK)
+        goto fail;
+    if ((e = make16("output.weight", V, D, &model->weights.output_weight)) != VKLLM_ERR_OK)
+        goto fail;
+    if (cudaStreamSynchronize(context->runtime->stream) != cudaSuccess)
+    {
+        e = VKLLM_ERR_VULKAN;
+        goto fail;
+    }
+    if ((e = create_kvcache(context, model)) != VKLLM_ERR_OK)
+        goto fail;
+    return VKLLM_ERR_OK;
+fail:
+    vkllm_models_llama2_free(context, model);
+    return e;
+}
