@@ -305,8 +305,7 @@ def strided_from_dense(t, flat):
 
 def dense_from_strided(t, buf):
     tc = t.contents
-    es = np.dtype(NP_DTYPE[tc.dtype]).itemsize
-    view = np.lib.stride_tricks.as_strided(buf, shape=tuple(tc.shapes), strides=tuple(s * es for s in tc.strides))
+    view = np.lib.stride_tricks.as_strided(buf, shape=tuple(tc.shapes), strides=tuple(tc.strides))  # byte strides
     return np.array(view)
 
 
