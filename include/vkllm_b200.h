@@ -96,6 +96,24 @@ extern vkllm_err_t vkllm_b200_engine_bench_kernel(struct vkllm_context *context,
                                                   const char *kernel, uint32_t iters, float *us_per_launch,
                                                   uint64_t *bytes_per_launch);
 
+/* Decode attention for one token that allocates nothing. No counterpart in the reference (whose
+ * attention is three graph nodes: scores MATMUL, SOFTMAX, probs.V MATMUL); this computes the same
+ * result as those nodes for S = 1, in fp16 with fp32 arithmetic, for callers that cannot call
+ * cudaMalloc (inside stream capture, under a fixed memory budget, on real-time paths).
+ *   q       fp16 [heads, head_dim], the rotated query of the token
+ *   kcache  fp16 [heads, cache_rows, head_dim], vcache likewise; keys/values 0 .. n_keys-1 are used
+ *   out     fp16 [heads, head_dim]
+ *   scale   score scale (1/sqrt(head_dim) for LLaMA-2); stream is a cudaStream_t (NULL = legacy)
+ * All scratch lives in one static device array of about 1.1 MiB that every GPU loading the library
+ * holds until exit. Limits: heads <= 64, head_dim <= 256 and a multiple of 4,
+ * heads * cache_rows <= 262144; larger sizes return VKLLM_ERR_ARGS. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress, with that device current) and should
+ * come before any stream capture. Every call shares the array: calls that overlap on the GPU (two
+ * streams, or two host threads) race on it and must be serialised by the caller. */
+extern vkllm_err_t vkllm_b200_attention_decode_noalloc(const void *q, const void *kcache, const void *vcache,
+                                                       uint32_t heads, uint32_t head_dim, uint32_t cache_rows,
+                                                       uint32_t n_keys, float scale, void *out, void *stream);
+
 /* ---- struct layout queries (for FFI bindings that mirror the public structs) --------------- */
 extern size_t vkllm_b200_sizeof(const char *struct_name);
 extern size_t vkllm_b200_offsetof(const char *struct_name, const char *field);

@@ -544,3 +544,109 @@ extern "C" vkllm_err_t vkllm_b200_engine_bench_kernel(struct vkllm_context *cont
     *bytes_per_launch = bytes;
     return VKLLM_ERR_OK;
 }
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free decode attention.
+//
+// Some callers cannot allocate device memory at the point where they run attention: code that runs
+// while a CUDA stream is being captured into a graph (cudaMalloc is not allowed there), code inside
+// a memory-pool-managed or pre-budgeted runtime that forbids allocations after start-up, and
+// real-time paths that must not block on the driver's allocator. For them this entry point runs the
+// same split-key decode attention kernels as the fused engine (k_dec_attn_scores + k_dec_attn_pv),
+// with all their scratch memory (fp16 scores, per-split softmax statistics, per-split partial
+// outputs, completion counters, the step word) in one file-scope device array instead of a
+// workspace. The array is reserved when the library is loaded onto a device and stays there until
+// the process exits.
+namespace vkb
+{
+namespace
+{
+
+// Limits of the static scratch (about 1.1 MiB in total).
+constexpr uint32_t kNoAllocMaxHeads = 64;
+constexpr uint32_t kNoAllocMaxScoreRows = 262144; // heads * cache_rows
+constexpr uint32_t kNoAllocMaxHeadDim = 256;
+constexpr uint32_t kNoAllocSplits = 8;
+constexpr size_t kNoAllocScoresBytes = (size_t)kNoAllocMaxScoreRows * 2;
+constexpr size_t kNoAllocPartBytes = (size_t)kNoAllocMaxHeads * kNoAllocSplits * sizeof(float2);
+constexpr size_t kNoAllocOpartBytes = (size_t)kNoAllocMaxHeads * kNoAllocSplits * kNoAllocMaxHeadDim * 4;
+constexpr size_t kNoAllocCountersBytes = (size_t)kNoAllocMaxHeads * 4;
+constexpr size_t kNoAllocOffPart = kNoAllocScoresBytes;
+constexpr size_t kNoAllocOffOpart = kNoAllocOffPart + kNoAllocPartBytes;
+constexpr size_t kNoAllocOffCounters = kNoAllocOffOpart + kNoAllocOpartBytes;
+constexpr size_t kNoAllocOffState = kNoAllocOffCounters + kNoAllocCountersBytes;
+constexpr size_t kNoAllocBytes = kNoAllocOffState + 256;
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[64] = {};
+
+// Device address of the scratch array on the current device, looked up once per device (the
+// host-side symbol is only a stand-in and must never be handed to a kernel).
+vkllm_err_t noalloc_scratch(void **out)
+{
+    int dev = 0;
+    VKB_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64)
+        return VKLLM_ERR_DEV_NOT_FOUND;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev])
+    {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e != cudaSuccess)
+            return cuda_check(e, "cudaGetSymbolAddress(g_attn_noalloc_scratch)", __FILE__, __LINE__);
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return VKLLM_ERR_OK;
+}
+
+} // namespace
+} // namespace vkb
+
+extern "C" vkllm_err_t vkllm_b200_attention_decode_noalloc(const void *q, const void *kcache, const void *vcache,
+                                                           uint32_t heads, uint32_t head_dim, uint32_t cache_rows,
+                                                           uint32_t n_keys, float scale, void *out, void *stream)
+{
+    using namespace vkb;
+    _CHECK_ARGS(q && kcache && vcache && out);
+    _CHECK_ARGS(heads > 0 && head_dim > 0 && cache_rows > 0);
+    _CHECK_ARGS(n_keys >= 1 && n_keys <= cache_rows);
+    if (heads > kNoAllocMaxHeads || head_dim > kNoAllocMaxHeadDim || head_dim % 4 != 0 ||
+        (uint64_t)heads * cache_rows > kNoAllocMaxScoreRows)
+    {
+        log_error("vkllm_b200_attention_decode_noalloc: heads=%u head_dim=%u cache_rows=%u exceed the static scratch "
+                  "(heads <= %u, head_dim <= %u and a multiple of 4, heads * cache_rows <= %u)",
+                  heads, head_dim, cache_rows, kNoAllocMaxHeads, kNoAllocMaxHeadDim, kNoAllocMaxScoreRows);
+        return VKLLM_ERR_ARGS;
+    }
+    void *base = nullptr;
+    _CHECK(noalloc_scratch(&base));
+    char *sb = (char *)base;
+    cudaStream_t s = (cudaStream_t)stream;
+    LayerW lw;
+    memset(&lw, 0, sizeof(lw));
+    lw.kcache = (__half *)kcache;
+    lw.vcache = (__half *)vcache;
+    DecodeDims dd;
+    memset(&dd, 0, sizeof(dd));
+    dd.H = heads;
+    dd.hd = head_dim;
+    dd.ctx = cache_rows;
+    dd.nsplit = kNoAllocSplits;
+    dd.scale = scale;
+    StepState *st = (StepState *)(sb + kNoAllocOffState);
+    uint32_t *counters = (uint32_t *)(sb + kNoAllocOffCounters);
+    // The array keeps the previous call's contents: the completion counters must start at zero.
+    VKB_CUDA(cudaMemsetAsync(counters, 0, (size_t)heads * 4, s));
+    k_set_state<<<1, 1, 0, s>>>(st, nullptr, 0, n_keys - 1);
+    dim3 grid(heads, kNoAllocSplits);
+    k_dec_attn_scores<<<grid, kAttnThreads, 0, s>>>(lw, dd, (const __half *)q, (__half *)sb, (float2 *)(sb + kNoAllocOffPart),
+                                                   st);
+    k_dec_attn_pv<<<grid, kAttnThreads, 0, s>>>(lw, dd, (const __half *)sb, (const float2 *)(sb + kNoAllocOffPart),
+                                                (float *)(sb + kNoAllocOffOpart), counters, (__half *)out, st);
+    VKB_CUDA(cudaGetLastError());
+    return VKLLM_ERR_OK;
+}

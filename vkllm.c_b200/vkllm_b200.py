@@ -165,6 +165,8 @@ _SIGS = {
     "vkllm_b200_engine_kernels_per_step": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2)]),
     "vkllm_b200_engine_bench_kernel": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
                                                  C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
+    "vkllm_b200_attention_decode_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
+                                                      C.c_uint32, C.c_uint32, C.c_float, C.c_void_p, C.c_void_p]),
     "vkllm_b200_sizeof": (C.c_size_t, [C.c_char_p]),
     "vkllm_b200_offsetof": (C.c_size_t, [C.c_char_p, C.c_char_p]),
 }
