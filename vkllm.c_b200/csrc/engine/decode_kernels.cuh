@@ -10,6 +10,7 @@
 #include <cstdint>
 
 #include "../kernels/common.cuh"
+#include "gemv_stream.cuh"
 
 namespace vkb
 {
@@ -39,51 +40,6 @@ constexpr int kGemvThreads = 256;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kAttnThreads = 128;
 
-// ------------------------------------------------------------------------------------------------
-// Warp dot products of R weight rows against the fp16 vector staged in shared memory, fp32
-// accumulation, 16-byte streaming loads with U-way unrolling (R*U loads in flight per lane).
-template <int R, int U>
-__device__ __forceinline__ void warp_rows_dot(const uint4 *__restrict__ xs4, const __half *const *w, uint32_t nchunk,
-                                              float *acc)
-{
-    const uint32_t lane = threadIdx.x & 31;
-    const uint4 *wp[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-    {
-        acc[r] = 0.f;
-        wp[r] = reinterpret_cast<const uint4 *>(w[r]);
-    }
-    uint32_t i = lane;
-    for (; i + 32u * (U - 1) < nchunk; i += 32u * U)
-    {
-        uint4 wv[R][U];
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-                wv[r][u] = ldg_stream(wp[r] + i + 32u * u);
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-        {
-            uint4 xv = xs4[i + 32u * u];
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-                acc[r] = dot8_f16(xv, wv[r][u], acc[r]);
-        }
-    }
-    for (; i < nchunk; i += 32u)
-    {
-        uint4 xv = xs4[i];
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-            acc[r] = dot8_f16(xv, ldg_stream(wp[r] + i), acc[r]);
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-        acc[r] = warp_sum(acc[r]);
-}
-
 __device__ __forceinline__ float block_sum(float v, float *red)
 {
     v = warp_sum(v);
@@ -104,10 +60,11 @@ __device__ __forceinline__ float block_sum(float v, float *red)
     return r;
 }
 
-// Stages xs = fp16((x * g) * rsqrt(mean(x^2) + eps)) (the RMSNORM node, src/shaders/vkllm_rmsnorm.comp:48-81)
-// into shared memory. K % 8 == 0.
+// Stages the RMSNORM node's output fp16((x * g) * rsqrt(mean(x^2) + eps))
+// (src/shaders/vkllm_rmsnorm.comp:48-81) into shared memory as fp32 times kHalfBitsScale (the
+// streaming GEMV's activation format). K % 8 == 0.
 __device__ __forceinline__ void stage_rmsnorm(const __half *__restrict__ x, const float *__restrict__ g, uint32_t K,
-                                              float eps, uint4 *xs4, float *red)
+                                              float eps, float *xs, float *red)
 {
     const uint32_t nchunk = K / 8;
     const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
@@ -127,30 +84,41 @@ __device__ __forceinline__ void stage_rmsnorm(const __half *__restrict__ x, cons
     float tot = block_sum(s, red);
     float alpha = rsqrtf(tot / (float)K + eps);
     const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    float4 *xs4 = reinterpret_cast<float4 *>(xs);
     for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
     {
         uint4 v = x4[i];
         float4 ga = g4[2 * i], gb = g4[2 * i + 1];
         const __half2 *h = reinterpret_cast<const __half2 *>(&v);
         float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-        uint4 o;
-        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+        float o[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
         {
             float2 f = __half22float2(h[j]);
-            oh[j] = __floats2half2_rn((f.x * gg[2 * j]) * alpha, (f.y * gg[2 * j + 1]) * alpha);
+            o[2 * j] = round_f16((f.x * gg[2 * j]) * alpha) * kHalfBitsScale;
+            o[2 * j + 1] = round_f16((f.y * gg[2 * j + 1]) * alpha) * kHalfBitsScale;
         }
-        xs4[i] = o;
+        xs4[2 * i] = make_float4(o[0], o[1], o[2], o[3]);
+        xs4[2 * i + 1] = make_float4(o[4], o[5], o[6], o[7]);
     }
     __syncthreads();
 }
 
-__device__ __forceinline__ void stage_copy(const __half *__restrict__ x, uint32_t K, uint4 *xs4)
+// Stages an fp16 activation vector as fp32 times kHalfBitsScale.
+__device__ __forceinline__ void stage_copy(const __half *__restrict__ x, uint32_t K, float *xs)
 {
     const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+    float4 *xs4 = reinterpret_cast<float4 *>(xs);
     for (uint32_t i = threadIdx.x; i < K / 8; i += blockDim.x)
-        xs4[i] = x4[i];
+    {
+        uint4 v = x4[i];
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+        float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]), d = __half22float2(h[3]);
+        xs4[2 * i] = make_float4(a.x * kHalfBitsScale, a.y * kHalfBitsScale, b.x * kHalfBitsScale, b.y * kHalfBitsScale);
+        xs4[2 * i + 1] =
+            make_float4(c.x * kHalfBitsScale, c.y * kHalfBitsScale, d.x * kHalfBitsScale, d.y * kHalfBitsScale);
+    }
     __syncthreads();
 }
 
@@ -158,6 +126,8 @@ __device__ __forceinline__ void stage_copy(const __half *__restrict__ x, uint32_
 __global__ void k_dec_embed(const __half *__restrict__ table, uint32_t V, uint32_t D, uint32_t unk,
                             const StepState *__restrict__ st, __half *__restrict__ x)
 {
+    pdl_launch_dependents();
+    pdl_wait();
     uint32_t tok = st->token;
     if (tok >= V)
         tok = unk; // src/shaders/vkllm_embedding.comp:57-60
@@ -165,58 +135,6 @@ __global__ void k_dec_embed(const __half *__restrict__ table, uint32_t V, uint32
     uint4 *dst = reinterpret_cast<uint4 *>(x);
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < D / 8; i += gridDim.x * blockDim.x)
         dst[i] = src[i];
-}
-
-// attn.norm + Q/K/V projections + RoPE on Q and K + KV-cache row write at `pos`.
-// Row pairs (2i, 2i+1) of the stacked [Wq; Wk; Wv] are computed by one warp so the rotation of
-// each (even, odd) pair happens in registers: Q = fp16(acc), RQ = fp16(rot(Q)), as the Q -> ROPE
-// nodes round (src/shaders/vkllm_rope.comp:68-78).
-__global__ void __launch_bounds__(kGemvThreads) k_dec_qkv(LayerW lw, DecodeDims dd, const __half *__restrict__ x,
-                                                          __half *__restrict__ q_out, StepState *st)
-{
-    extern __shared__ uint4 xs4[];
-    __shared__ float red[32];
-    const uint32_t pos = st->pos;
-    if (pos >= dd.ctx)
-    {
-        if (blockIdx.x == 0 && threadIdx.x == 0)
-            st->error = 1;
-        return;
-    }
-    stage_rmsnorm(x, lw.attn_norm, dd.D, dd.eps, xs4, red);
-    const uint32_t HD = dd.H * dd.hd;
-    const uint32_t groups = 3 * HD / 2;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t g = blockIdx.x * kGemvWarps + warp; g < groups; g += gridDim.x * kGemvWarps)
-    {
-        uint32_t row = 2 * g;
-        uint32_t which = row / HD, r = row % HD;
-        const __half *base = which == 0 ? lw.wq : (which == 1 ? lw.wk : lw.wv);
-        const __half *rows[2] = {base + (uint64_t)r * dd.D, base + (uint64_t)(r + 1) * dd.D};
-        float acc[2];
-        warp_rows_dot<2, 4>(xs4, rows, dd.D / 8, acc);
-        if (lane != 0)
-            continue;
-        float v0 = round_f16(acc[0]), v1 = round_f16(acc[1]);
-        uint32_t head = r / dd.hd, d = r % dd.hd;
-        if (which < 2)
-        {
-            uint32_t w = d / 2;
-            float theta = (float)pos / powf(dd.rope_base, (float)(2 * w) / (float)dd.hd);
-            float c = cosf(theta), s = sinf(theta);
-            float o0 = c * v0 - s * v1, o1 = s * v0 + c * v1;
-            v0 = o0;
-            v1 = o1;
-        }
-        __half2 hv = __floats2half2_rn(v0, v1);
-        if (which == 0)
-            *reinterpret_cast<__half2 *>(q_out + r) = hv;
-        else
-        {
-            __half *cache = which == 1 ? lw.kcache : lw.vcache;
-            *reinterpret_cast<__half2 *>(cache + ((uint64_t)head * dd.ctx + pos) * dd.hd + d) = hv;
-        }
-    }
 }
 
 // Scores of one (head, key-split): s_j = fp16(scale * q.k_j) for keys j of this split (the scores
@@ -229,6 +147,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_dec_attn_scores(LayerW lw, Dec
     __shared__ float qs[256];
     __shared__ float red[32];
     __shared__ float smax[kAttnThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t pos = st->pos;
     if (pos >= dd.ctx)
         return;
@@ -293,6 +213,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_dec_attn_pv(LayerW lw, DecodeD
     __shared__ float acc_s[kAttnThreads / 32][256];
     __shared__ float ps[kAttnThreads];
     __shared__ uint32_t last;
+    pdl_launch_dependents();
+    pdl_wait();
     const uint32_t pos = st->pos;
     if (pos >= dd.ctx)
         return;
@@ -408,175 +330,245 @@ __global__ void __launch_bounds__(kAttnThreads) k_dec_attn_pv(LayerW lw, DecodeD
         counters[h] = 0;
 }
 
-// Wo projection + residual: x = fp16(x + fp16(attn . Wo^T)) (final_output and final_output_add nodes).
-__global__ void __launch_bounds__(kGemvThreads) k_dec_wo(LayerW lw, DecodeDims dd, const __half *__restrict__ attn,
-                                                         __half *__restrict__ x)
+
+// ------------------------------------------------------------------------------------------------
+// Epilogue ops of the weight-streaming GEMV (gemv_stream.cuh), one per projection of the step.
+
+// attn.norm + Q/K/V projections + RoPE on Q and K + KV-cache row write at `pos`. A unit is the row
+// pair (2i, 2i+1) of the stacked [Wq; Wk; Wv], so each (even, odd) pair is rotated in registers:
+// Q = fp16(acc), RQ = fp16(rot(Q)), as the Q -> ROPE nodes round (src/shaders/vkllm_rope.comp:68-78).
+struct QkvOp
 {
-    extern __shared__ uint4 xs4[];
-    const uint32_t HD = dd.H * dd.hd;
-    stage_copy(attn, HD, xs4);
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t g = blockIdx.x * kGemvWarps + warp; g < dd.D / 2; g += gridDim.x * kGemvWarps)
+    static constexpr int NM = 2;
+    LayerW lw;
+    DecodeDims dd;
+    const __half *x;
+    __half *q_out;
+    StepState *st;
+    __device__ const __half *row_ptr(uint32_t u, uint32_t m) const
     {
-        uint32_t r = 2 * g;
-        const __half *rows[2] = {lw.wo + (uint64_t)r * HD, lw.wo + (uint64_t)(r + 1) * HD};
-        float acc[2];
-        warp_rows_dot<2, 4>(xs4, rows, HD / 8, acc);
-        if (lane == 0)
+        const uint32_t HD = dd.H * dd.hd, row = 2 * u + m, which = row / HD, r = row % HD;
+        const __half *base = which == 0 ? lw.wq : (which == 1 ? lw.wk : lw.wv);
+        return base + (uint64_t)r * dd.D;
+    }
+    __device__ void prologue(float *xs, float *red) const
+    {
+        stage_rmsnorm(x, lw.attn_norm, dd.D, dd.eps, xs, red);
+    }
+    __device__ void epilogue(uint32_t u, const float *s) const
+    {
+        const uint32_t pos = st->pos;
+        if (pos >= dd.ctx)
         {
-            float2 xv = __half22float2(*reinterpret_cast<const __half2 *>(x + r));
-            *reinterpret_cast<__half2 *>(x + r) = __floats2half2_rn(xv.x + round_f16(acc[0]), xv.y + round_f16(acc[1]));
+            st->error = 1;
+            return;
+        }
+        const uint32_t HD = dd.H * dd.hd, row = 2 * u, which = row / HD, r = row % HD;
+        float v0 = round_f16(s[0]), v1 = round_f16(s[1]);
+        const uint32_t head = r / dd.hd, d = r % dd.hd;
+        if (which < 2)
+        {
+            const uint32_t w = d / 2;
+            const float theta = (float)pos / powf(dd.rope_base, (float)(2 * w) / (float)dd.hd);
+            const float c = cosf(theta), sn = sinf(theta);
+            const float o0 = c * v0 - sn * v1, o1 = sn * v0 + c * v1;
+            v0 = o0;
+            v1 = o1;
+        }
+        const __half2 hv = __floats2half2_rn(v0, v1);
+        if (which == 0)
+            *reinterpret_cast<__half2 *>(q_out + r) = hv;
+        else
+        {
+            __half *cache = which == 1 ? lw.kcache : lw.vcache;
+            *reinterpret_cast<__half2 *>(cache + ((uint64_t)head * dd.ctx + pos) * dd.hd + d) = hv;
         }
     }
-}
+    __device__ void finish() const
+    {
+    }
+};
+
+// Wo projection + residual: x = fp16(x + fp16(attn . Wo^T)) (final_output and final_output_add nodes).
+struct WoOp
+{
+    static constexpr int NM = 1;
+    LayerW lw;
+    DecodeDims dd;
+    const __half *attn;
+    __half *x;
+    __device__ const __half *row_ptr(uint32_t u, uint32_t) const
+    {
+        return lw.wo + (uint64_t)u * dd.H * dd.hd;
+    }
+    __device__ void prologue(float *xs, float *) const
+    {
+        stage_copy(attn, dd.H * dd.hd, xs);
+    }
+    __device__ void epilogue(uint32_t u, const float *s) const
+    {
+        x[u] = __float2half_rn(__half2float(x[u]) + round_f16(s[0]));
+    }
+    __device__ void finish() const
+    {
+    }
+};
 
 // ffn.norm + up / gate projections + SiLU gating: m = fp16(fp16(u) * fp16(silu(g))) (up, gate(act=1)
-// and mul nodes, src/models/vkllm_llama2_layers.c:36-60).
-__global__ void __launch_bounds__(kGemvThreads) k_dec_upgate(LayerW lw, DecodeDims dd, const __half *__restrict__ x,
-                                                             __half *__restrict__ m)
+// and mul nodes, src/models/vkllm_llama2_layers.c:36-60). A unit is one FFN column: its up row and
+// its gate row.
+struct UpGateOp
 {
-    extern __shared__ uint4 xs4[];
-    __shared__ float red[32];
-    stage_rmsnorm(x, lw.ffn_norm, dd.D, dd.eps, xs4, red);
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t r = blockIdx.x * kGemvWarps + warp; r < dd.F; r += gridDim.x * kGemvWarps)
+    static constexpr int NM = 2;
+    LayerW lw;
+    DecodeDims dd;
+    const __half *x;
+    __half *m;
+    __device__ const __half *row_ptr(uint32_t u, uint32_t k) const
     {
-        const __half *rows[2] = {lw.wu + (uint64_t)r * dd.D, lw.wg + (uint64_t)r * dd.D};
-        float acc[2];
-        warp_rows_dot<2, 4>(xs4, rows, dd.D / 8, acc);
-        if (lane == 0)
-        {
-            float u = round_f16(acc[0]);
-            float gt = round_f16(silu_f32(acc[1]));
-            m[r] = __float2half_rn(u * gt);
-        }
+        return (k == 0 ? lw.wu : lw.wg) + (uint64_t)u * dd.D;
     }
-}
+    __device__ void prologue(float *xs, float *red) const
+    {
+        stage_rmsnorm(x, lw.ffn_norm, dd.D, dd.eps, xs, red);
+    }
+    __device__ void epilogue(uint32_t u, const float *s) const
+    {
+        m[u] = __float2half_rn(round_f16(s[0]) * round_f16(silu_f32(s[1])));
+    }
+    __device__ void finish() const
+    {
+    }
+};
 
 // Down projection + residual: x = fp16(x + fp16(m . Wd^T)) (down and add nodes).
-__global__ void __launch_bounds__(kGemvThreads) k_dec_down(LayerW lw, DecodeDims dd, const __half *__restrict__ m,
-                                                           __half *__restrict__ x)
+struct DownOp
 {
-    extern __shared__ uint4 xs4[];
-    stage_copy(m, dd.F, xs4);
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (uint32_t g = blockIdx.x * kGemvWarps + warp; g < dd.D / 2; g += gridDim.x * kGemvWarps)
+    static constexpr int NM = 1;
+    LayerW lw;
+    DecodeDims dd;
+    const __half *m;
+    __half *x;
+    __device__ const __half *row_ptr(uint32_t u, uint32_t) const
     {
-        uint32_t r = 2 * g;
-        const __half *rows[2] = {lw.wd + (uint64_t)r * dd.F, lw.wd + (uint64_t)(r + 1) * dd.F};
-        float acc[2];
-        warp_rows_dot<2, 4>(xs4, rows, dd.F / 8, acc);
-        if (lane == 0)
-        {
-            float2 xv = __half22float2(*reinterpret_cast<const __half2 *>(x + r));
-            *reinterpret_cast<__half2 *>(x + r) = __floats2half2_rn(xv.x + round_f16(acc[0]), xv.y + round_f16(acc[1]));
-        }
+        return lw.wd + (uint64_t)u * dd.F;
     }
-}
+    __device__ void prologue(float *xs, float *) const
+    {
+        stage_copy(m, dd.F, xs);
+    }
+    __device__ void epilogue(uint32_t u, const float *s) const
+    {
+        x[u] = __float2half_rn(__half2float(x[u]) + round_f16(s[0]));
+    }
+    __device__ void finish() const
+    {
+    }
+};
 
-// output_norm + logits + ARG_MAX. Every block stores its fp16 logits; the last block to finish
-// computes the argmax over all of them with the reference tie rule
-// (src/shaders/vkllm_arg_max.comp:54-90): index i competes in class i mod 32 where the first
-// (smallest-index) strict maximum wins; classes are then reduced by the 16/8/4/2/1 tree that keeps
-// the left operand unless the right one is strictly greater. It then advances the step state.
-__global__ void __launch_bounds__(kGemvThreads) k_dec_logits(const __half *__restrict__ wout,
-                                                             const float *__restrict__ gnorm, DecodeDims dd,
-                                                             const __half *__restrict__ x, __half *__restrict__ logits,
-                                                             uint32_t *__restrict__ counter, StepState *st,
-                                                             uint32_t *__restrict__ ring, uint32_t ring_len)
+// output_norm + logits + ARG_MAX. Every CTA stores its fp16 logits; the last CTA to finish computes
+// the argmax over all of them with the reference tie rule (src/shaders/vkllm_arg_max.comp:54-90):
+// index i competes in class i mod 32 where the first (smallest-index) strict maximum wins; classes
+// are then reduced by the 16/8/4/2/1 tree that keeps the left operand unless the right one is
+// strictly greater. It then writes the token into the step state and advances it.
+struct LogitsOp
 {
-    extern __shared__ uint4 xs4[];
-    __shared__ float red[32];
-    __shared__ uint32_t last;
-    __shared__ float cls_v[kGemvWarps][32];
-    __shared__ uint32_t cls_i[kGemvWarps][32];
-    stage_rmsnorm(x, gnorm, dd.D, dd.eps, xs4, red);
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t V = dd.V;
-    for (uint32_t g = blockIdx.x * kGemvWarps + warp; g < (V + 1) / 2; g += gridDim.x * kGemvWarps)
+    static constexpr int NM = 1;
+    const __half *wout;
+    const float *gnorm;
+    DecodeDims dd;
+    const __half *x;
+    __half *logits;
+    uint32_t *counter;
+    StepState *st;
+    uint32_t *ring;
+    uint32_t ring_len;
+    __device__ const __half *row_ptr(uint32_t u, uint32_t) const
     {
-        uint32_t r = 2 * g;
-        uint32_t r1 = r + 1 < V ? r + 1 : r;
-        const __half *rows[2] = {wout + (uint64_t)r * dd.D, wout + (uint64_t)r1 * dd.D};
-        float acc[2];
-        warp_rows_dot<2, 4>(xs4, rows, dd.D / 8, acc);
-        if (lane == 0)
-        {
-            logits[r] = __float2half_rn(acc[0]);
-            if (r + 1 < V)
-                logits[r + 1] = __float2half_rn(acc[1]);
-        }
+        return wout + (uint64_t)u * dd.D;
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0)
-        last = atomicAdd(counter, 1u) == gridDim.x - 1 ? 1u : 0u;
-    __syncthreads();
-    if (!last)
-        return;
-    __threadfence();
-    // Class lane = i mod 32; warp w scans i = lane + 32 * (w + nw * k) ascending.
-    float bv = -FLT_MAX;
-    uint32_t bi = lane;
-    bool have = false;
-    for (uint32_t i = lane + 32 * warp; i < V; i += 32 * kGemvWarps)
+    __device__ void prologue(float *xs, float *red) const
     {
-        float v = __half2float(__ldcg(logits + i));
-        if (!have || v > bv)
-        {
-            bv = v;
-            bi = i;
-            have = true;
-        }
+        stage_rmsnorm(x, gnorm, dd.D, dd.eps, xs, red);
     }
-    cls_v[warp][lane] = have ? bv : -FLT_MAX;
-    cls_i[warp][lane] = have ? bi : 0xffffffffu;
-    __syncthreads();
-    if (warp == 0)
+    __device__ void epilogue(uint32_t u, const float *s) const
     {
-        // Combine the warps' subsets of class `lane`: larger value, smaller index on ties.
-        float v = -FLT_MAX;
-        uint32_t idx = 0xffffffffu;
-        for (int w = 0; w < kGemvWarps; ++w)
+        logits[u] = __float2half_rn(s[0]);
+    }
+    __device__ void finish() const
+    {
+        __shared__ uint32_t last;
+        __shared__ float cls_v[kStreamMaxWarps][32];
+        __shared__ uint32_t cls_i[kStreamMaxWarps][32];
+        const uint32_t nw = blockDim.x >> 5;
+        const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0)
+            last = atomicAdd(counter, 1u) == gridDim.x - 1 ? 1u : 0u;
+        __syncthreads();
+        if (!last)
+            return;
+        __threadfence();
+        const uint32_t V = dd.V;
+        float bv = -FLT_MAX;
+        uint32_t bi = 0xffffffffu;
+        for (uint32_t i = lane + 32 * warp; i < V; i += 32 * nw)
         {
-            float cv = cls_v[w][lane];
-            uint32_t ci = cls_i[w][lane];
-            if (ci == 0xffffffffu)
-                continue;
-            if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))
+            const float v = __half2float(__ldcg(logits + i));
+            if (bi == 0xffffffffu || v > bv)
             {
-                v = cv;
-                idx = ci;
+                bv = v;
+                bi = i;
             }
         }
-        if (idx == 0xffffffffu)
+        cls_v[warp][lane] = bv;
+        cls_i[warp][lane] = bi;
+        __syncthreads();
+        if (warp == 0)
         {
-            // Class with no entries (V < 32): the reference lane keeps -FLT_MAX and its own index.
-            v = -FLT_MAX;
-            idx = lane;
-        }
+            float v = -FLT_MAX;
+            uint32_t idx = 0xffffffffu;
+            for (uint32_t w = 0; w < nw; ++w)
+            {
+                const float cv = cls_v[w][lane];
+                const uint32_t ci = cls_i[w][lane];
+                if (ci == 0xffffffffu)
+                    continue;
+                if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))
+                {
+                    v = cv;
+                    idx = ci;
+                }
+            }
+            if (idx == 0xffffffffu)
+            {
+                v = -FLT_MAX; // empty class (V < 32): the reference lane keeps -FLT_MAX and its own index
+                idx = lane;
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-        {
-            float ov = __shfl_down_sync(0xffffffffu, v, o);
-            uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
-            if ((int)lane < o && ov > v)
+            for (int o = 16; o > 0; o >>= 1)
             {
-                v = ov;
-                idx = oi;
+                const float ov = __shfl_down_sync(0xffffffffu, v, o);
+                const uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
+                if ((int)lane < o && ov > v)
+                {
+                    v = ov;
+                    idx = oi;
+                }
+            }
+            if (lane == 0)
+            {
+                st->token = idx;
+                if (st->step < ring_len)
+                    ring[st->step] = idx;
+                st->step += 1;
+                st->pos += 1;
+                *counter = 0;
             }
         }
-        if (lane == 0)
-        {
-            st->token = idx;
-            if (st->step < ring_len)
-                ring[st->step] = idx;
-            st->step += 1;
-            st->pos += 1;
-            *counter = 0;
-        }
     }
-}
+};
 
 __global__ void k_set_state(StepState *st, const uint32_t *tok_src, uint32_t token, uint32_t pos)
 {

@@ -32,8 +32,8 @@ struct Engine
     uint32_t *counters = nullptr, *logit_counter = nullptr, *ring = nullptr;
     StepState *state = nullptr;
     // launch geometry
-    unsigned grid_qkv = 0, grid_wo = 0, grid_upgate = 0, grid_down = 0, grid_logits = 0, grid_embed = 0;
-    size_t smem_D = 0, smem_HD = 0, smem_F = 0;
+    unsigned grid_stream = 0, grid_embed = 0;
+    StreamGeom g_qkv{}, g_wo{}, g_upgate{}, g_down{}, g_logits{};
     // captured step
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -43,34 +43,86 @@ struct Engine
 namespace
 {
 
-unsigned gemv_grid(uint32_t groups, int sms)
+// Launch with Programmatic Dependent Launch enabled: the kernel may start while its predecessor in
+// the stream finishes; every decode kernel calls griddepcontrol.wait before reading its inputs.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args)
 {
-    uint32_t need = (groups + kGemvWarps - 1) / kGemvWarps;
-    uint32_t cap = (uint32_t)sms * 4u;
-    return need < cap ? (need ? need : 1) : cap;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+QkvOp op_qkv(Engine *e, const LayerW &lw)
+{
+    return QkvOp{lw, e->dd, e->x, e->q, e->state};
+}
+WoOp op_wo(Engine *e, const LayerW &lw)
+{
+    return WoOp{lw, e->dd, e->attn, e->x};
+}
+UpGateOp op_upgate(Engine *e, const LayerW &lw)
+{
+    return UpGateOp{lw, e->dd, e->x, e->m};
+}
+DownOp op_down(Engine *e, const LayerW &lw)
+{
+    return DownOp{lw, e->dd, e->m, e->x};
+}
+LogitsOp op_logits(Engine *e)
+{
+    return LogitsOp{e->wout, e->out_norm, e->dd, e->x, e->logits, e->logit_counter, e->state, e->ring, e->dd.ctx};
+}
+
+template <class Op> cudaError_t launch_stream(Engine *e, const Op &op, const StreamGeom &g, cudaStream_t s)
+{
+    return launch_pdl(k_gemv_stream<Op>, dim3(e->grid_stream), dim3(32 * g.warps), stream_smem_bytes(g), s, op, g,
+                      &e->state->error);
 }
 
 vkllm_err_t enqueue_step(Engine *e, cudaStream_t s)
 {
     const DecodeDims &dd = e->dd;
-    k_dec_embed<<<e->grid_embed, 256, 0, s>>>(e->embed, dd.V, dd.D, e->unk, e->state, e->x);
+    cudaError_t err = launch_pdl(k_dec_embed, dim3(e->grid_embed), dim3(256), 0, s, e->embed, dd.V, dd.D, e->unk,
+                                 (const StepState *)e->state, e->x);
     dim3 agrid(dd.H, dd.nsplit);
     for (const LayerW &lw : e->layers)
     {
-        k_dec_qkv<<<e->grid_qkv, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->q, e->state);
-        k_dec_attn_scores<<<agrid, kAttnThreads, 0, s>>>(lw, dd, e->q, e->scores, e->part, e->state);
-        k_dec_attn_pv<<<agrid, kAttnThreads, 0, s>>>(lw, dd, e->scores, e->part, e->opart, e->counters, e->attn,
-                                                     e->state);
-        k_dec_wo<<<e->grid_wo, kGemvThreads, e->smem_HD, s>>>(lw, dd, e->attn, e->x);
-        k_dec_upgate<<<e->grid_upgate, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->m);
-        k_dec_down<<<e->grid_down, kGemvThreads, e->smem_F, s>>>(lw, dd, e->m, e->x);
+        if (err == cudaSuccess)
+            err = launch_stream(e, op_qkv(e, lw), e->g_qkv, s);
+        if (err == cudaSuccess)
+            err = launch_pdl(k_dec_attn_scores, agrid, dim3(kAttnThreads), 0, s, lw, dd, (const __half *)e->q,
+                             e->scores, e->part, (const StepState *)e->state);
+        if (err == cudaSuccess)
+            err = launch_pdl(k_dec_attn_pv, agrid, dim3(kAttnThreads), 0, s, lw, dd, (const __half *)e->scores,
+                             (const float2 *)e->part, e->opart, e->counters, e->attn, (const StepState *)e->state);
+        if (err == cudaSuccess)
+            err = launch_stream(e, op_wo(e, lw), e->g_wo, s);
+        if (err == cudaSuccess)
+            err = launch_stream(e, op_upgate(e, lw), e->g_upgate, s);
+        if (err == cudaSuccess)
+            err = launch_stream(e, op_down(e, lw), e->g_down, s);
     }
-    k_dec_logits<<<e->grid_logits, kGemvThreads, e->smem_D, s>>>(e->wout, e->out_norm, dd, e->x, e->logits,
-                                                                 e->logit_counter, e->state, e->ring, dd.ctx);
-    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess)
+        err = launch_stream(e, op_logits(e), e->g_logits, s);
+    if (err == cudaSuccess)
+        err = cudaGetLastError();
     if (err != cudaSuccess)
         return cuda_check(err, "decode step launch", __FILE__, __LINE__);
     return VKLLM_ERR_OK;
+}
+
+template <class Op> void allow_smem(const StreamGeom &g)
+{
+    cudaFuncSetAttribute(k_gemv_stream<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stream_smem_bytes(g));
 }
 
 vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine **out)
@@ -173,24 +225,39 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->ring = (uint32_t *)(w + off_ring);
     e->state = (StepState *)(w + off_state);
 
-    e->grid_qkv = gemv_grid(3 * HD / 2, sms);
-    e->grid_wo = gemv_grid(dd.D / 2, sms);
-    e->grid_upgate = gemv_grid(dd.F, sms);
-    e->grid_down = gemv_grid(dd.D / 2, sms);
-    e->grid_logits = gemv_grid((dd.V + 1) / 2, sms);
-    e->grid_embed = (dd.D / 8 + 255) / 256;
-    e->smem_D = (size_t)dd.D * 2;
-    e->smem_HD = (size_t)HD * 2;
-    e->smem_F = (size_t)dd.F * 2;
-    size_t smax = e->smem_F > e->smem_D ? e->smem_F : e->smem_D;
-    if (smax > 48 * 1024)
+    // Streaming GEMV geometry: one CTA per SM; chunks of at most ~8 KB, one stage per warp and as
+    // many warps (<= 32) as ~220 KB of shared memory holds next to the fp32 input vector.
+    // Tuning overrides: VKLLM_B200_STREAM_SMEM_KB (shared memory per CTA), VKLLM_B200_STREAM_CHUNK_KB
+    // (target chunk), VKLLM_B200_STREAM_CTAS_PER_SM (grid = SMs x this).
+    auto env_u32 = [](const char *n, uint32_t d) {
+        const char *v = getenv(n);
+        return v && atoi(v) > 0 ? (uint32_t)atoi(v) : d;
+    };
+    const uint32_t kTarget = env_u32("VKLLM_B200_STREAM_CHUNK_KB", 8) * 1024;
+    const uint32_t kSmemCap = env_u32("VKLLM_B200_STREAM_SMEM_KB", 220) * 1024;
+    const uint32_t kSpw = env_u32("VKLLM_B200_STREAM_SPW", 1);
+    e->grid_stream = (unsigned)sms * env_u32("VKLLM_B200_STREAM_CTAS_PER_SM", 1);
+    e->g_qkv = make_stream_geom(3 * HD / 2, 2, dd.D, dd.D, kTarget, kSmemCap, kSpw);
+    e->g_wo = make_stream_geom(dd.D, 1, HD, HD, kTarget, kSmemCap, kSpw);
+    e->g_upgate = make_stream_geom(dd.F, 2, dd.D, dd.D, kTarget, kSmemCap, kSpw);
+    e->g_down = make_stream_geom(dd.D, 1, dd.F, dd.F, kTarget, kSmemCap, kSpw);
+    e->g_logits = make_stream_geom(dd.V, 1, dd.D, dd.D, kTarget, kSmemCap, kSpw);
+    for (const StreamGeom *g : {&e->g_qkv, &e->g_wo, &e->g_upgate, &e->g_down, &e->g_logits})
     {
-        cudaFuncSetAttribute(k_dec_qkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
-        cudaFuncSetAttribute(k_dec_wo, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
-        cudaFuncSetAttribute(k_dec_upgate, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
-        cudaFuncSetAttribute(k_dec_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
-        cudaFuncSetAttribute(k_dec_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smax);
+        if (g->warps < 4 || stream_smem_bytes(*g) > ctx->device->smem_optin)
+        {
+            log_info("model rows too long for the streaming GEMV's shared memory; graphs run node by node");
+            cudaFree(e->ws);
+            delete e;
+            return VKLLM_ERR_ARGS;
+        }
     }
+    allow_smem<QkvOp>(e->g_qkv);
+    allow_smem<WoOp>(e->g_wo);
+    allow_smem<UpGateOp>(e->g_upgate);
+    allow_smem<DownOp>(e->g_down);
+    allow_smem<LogitsOp>(e->g_logits);
+    e->grid_embed = (dd.D / 8 + 255) / 256;
     e->kernels_per_step = 2 + 6 * (uint32_t)e->layers.size();
 
     // Capture one decode step.
@@ -511,20 +578,19 @@ extern "C" vkllm_err_t vkllm_b200_engine_bench_kernel(struct vkllm_context *cont
         switch (which)
         {
         case 0:
-            k_dec_qkv<<<e->grid_qkv, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->q, e->state);
+            launch_stream(e, op_qkv(e, lw), e->g_qkv, s);
             break;
         case 1:
-            k_dec_wo<<<e->grid_wo, kGemvThreads, e->smem_HD, s>>>(lw, dd, e->attn, e->x);
+            launch_stream(e, op_wo(e, lw), e->g_wo, s);
             break;
         case 2:
-            k_dec_upgate<<<e->grid_upgate, kGemvThreads, e->smem_D, s>>>(lw, dd, e->x, e->m);
+            launch_stream(e, op_upgate(e, lw), e->g_upgate, s);
             break;
         case 3:
-            k_dec_down<<<e->grid_down, kGemvThreads, e->smem_F, s>>>(lw, dd, e->m, e->x);
+            launch_stream(e, op_down(e, lw), e->g_down, s);
             break;
         case 4:
-            k_dec_logits<<<e->grid_logits, kGemvThreads, e->smem_D, s>>>(e->wout, e->out_norm, dd, e->x, e->logits,
-                                                                         e->logit_counter, e->state, e->ring, dd.ctx);
+            launch_stream(e, op_logits(e), e->g_logits, s);
             break;
         }
     };

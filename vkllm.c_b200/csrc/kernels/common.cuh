@@ -112,4 +112,35 @@ __device__ __forceinline__ float dot8_f16(const uint4 &a, const uint4 &b, float 
     return acc;
 }
 
+// fp16 -> fp32 without the conversion pipe: placing the fp16 exponent/mantissa bits of a half at
+// fp32 bit 13 (sign at bit 31) gives exactly h * 2^-112 for every finite half, subnormals included
+// (they become fp32 denormals with the same ratio). Two halves packed in a word take a shift and a
+// LOP3 each. Multiplying by an operand pre-scaled by 2^112 then yields exactly the fp32 product of
+// the original values, so sums are bit-identical to fma(float(x), float(h), acc).
+constexpr float kHalfBitsScale = 0x1p112f;
+
+__device__ __forceinline__ float2 half2_bits_scaled(uint32_t v)
+{
+    const float lo = __uint_as_float(((v << 13) & 0x0fffe000u) | ((v << 16) & 0x80000000u));
+    const float hi = __uint_as_float(((v >> 3) & 0x0fffe000u) | (v & 0x80000000u));
+    return make_float2(lo, hi);
+}
+
+// acc + sum_i xs[i] * w[i] for 8 fp16 weights `w` and 8 staged activations `xs` that were
+// multiplied by kHalfBitsScale (xs0 holds elements 0-3, xs1 elements 4-7).
+__device__ __forceinline__ float dot8_scaled(const float4 &xs0, const float4 &xs1, const uint4 &w, float acc)
+{
+    const float2 w0 = half2_bits_scaled(w.x), w1 = half2_bits_scaled(w.y), w2 = half2_bits_scaled(w.z),
+                 w3 = half2_bits_scaled(w.w);
+    acc = fmaf(xs0.x, w0.x, acc);
+    acc = fmaf(xs0.y, w0.y, acc);
+    acc = fmaf(xs0.z, w1.x, acc);
+    acc = fmaf(xs0.w, w1.y, acc);
+    acc = fmaf(xs1.x, w2.x, acc);
+    acc = fmaf(xs1.y, w2.y, acc);
+    acc = fmaf(xs1.z, w3.x, acc);
+    acc = fmaf(xs1.w, w3.y, acc);
+    return acc;
+}
+
 } // namespace vkb
