@@ -85,8 +85,33 @@ extern vkllm_err_t vkllm_b200_engine_read_tokens(struct vkllm_context *context, 
 /* Waits for the stream, then copies the fp16 logits of the last step ([vocab] halves). */
 extern vkllm_err_t vkllm_b200_engine_read_logits(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                                  uint16_t *out, uint32_t n);
-/* Number of kernel launches in one decode step of the engine (for launch accounting). */
+/* Kernel launches per decode step of the engine's current mode: the persistent cooperative
+ * kernel (one launch runs up to 64 steps) reports 1; the CUDA-Graph fallback (environment
+ * VKLLM_B200_DECODE=graph, or devices without cooperative launch) 2 + 6 * layers. */
 extern uint32_t vkllm_b200_engine_kernels_per_step(struct vkllm_context *context, struct vkllm_models_llama2 *model);
+/* Kernel launches enqueued by the last vkllm_b200_engine_decode_steps call. */
+extern uint32_t vkllm_b200_engine_last_launches(struct vkllm_context *context, struct vkllm_models_llama2 *model);
+/* Tracing: with the environment variable VKLLM_B200_TRACE=1 set when the engine is built, the
+ * persistent kernel's CTA 0 records %globaltimer (ns) at its start and at every grid barrier
+ * arrival and release. Copies up to `cap` entries of the last launch; returns the count copied
+ * (0 when tracing is off). Per step the barriers are, per layer: after QKV, scores, probs.V, Wo,
+ * up/gate, down; then after the logits and after the argmax. A single mark (no pair) follows each
+ * GEMV phase's input staging (before QKV, Wo, up/gate, down and logits). */
+extern uint32_t vkllm_b200_engine_read_trace(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                             uint64_t *out, uint32_t cap);
+/* Tracing: for each grid barrier of the last persistent launch, %globaltimer (ns) when the last
+ * CTA arrived, stored at the index of the barrier's release entry in vkllm_b200_engine_read_trace's
+ * layout (other entries undefined). Returns the count copied, 0 when tracing is off. */
+extern uint32_t vkllm_b200_engine_read_trace_last(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                  uint64_t *out, uint32_t cap);
+/* Tracing: CTA 0's per-warp weight-pipeline accounting, in SM cycles, summed over every persistent
+ * launch since the engine was built: out[(warp * 5 + kind) * 4 + {0: mbarrier wait, 1: consume
+ * (compute + refill issue), 2: chunks, 3: compute}], kind 0..4 = QKV, Wo, up/gate, down, logits.
+ * Needs cap >= 640; returns 640, or 0 when tracing is off. */
+extern uint32_t vkllm_b200_engine_read_warp_trace(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                  uint64_t *out, uint32_t cap);
+/* 1 when the engine runs the persistent decode kernel. */
+extern int vkllm_b200_engine_is_persistent(struct vkllm_context *context, struct vkllm_models_llama2 *model);
 
 /* Times `iters` launches of one decode kernel of the engine ("qkv", "wo", "upgate", "down", "logits")
  * on the context stream with CUDA events, cycling through the layers so every launch streams its

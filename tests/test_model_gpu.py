@@ -83,7 +83,11 @@ def test_device_loop_matches_api_loop(vk, ctx, tiny_gguf, reference_run):
         out = np.zeros(40, dtype=np.uint32)
         vk.check(l.vkllm_b200_engine_read_tokens(ctx.ptr, C.byref(model.m), out.ctypes.data, 40), "read_tokens")
         assert list(out) == ref_toks[1:41]
-        assert l.vkllm_b200_engine_kernels_per_step(ctx.ptr, C.byref(model.m)) == 2 + 6 * 6
+        kps = l.vkllm_b200_engine_kernels_per_step(ctx.ptr, C.byref(model.m))
+        if l.vkllm_b200_engine_is_persistent(ctx.ptr, C.byref(model.m)):
+            assert kps == 1 and l.vkllm_b200_engine_last_launches(ctx.ptr, C.byref(model.m)) == 1  # 40 steps, 1 launch
+        else:
+            assert kps == 2 + 6 * 6
     finally:
         model.free()
 

@@ -71,7 +71,7 @@ __device__ __forceinline__ void stage_rmsnorm(const __half *__restrict__ x, cons
     float s = 0.f;
     for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
     {
-        uint4 v = x4[i];
+        uint4 v = __ldcg(x4 + i); // L2: x may have been written by other CTAs of a persistent kernel
         const __half2 *h = reinterpret_cast<const __half2 *>(&v);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -87,7 +87,7 @@ __device__ __forceinline__ void stage_rmsnorm(const __half *__restrict__ x, cons
     float4 *xs4 = reinterpret_cast<float4 *>(xs);
     for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
     {
-        uint4 v = x4[i];
+        uint4 v = __ldcg(x4 + i);
         float4 ga = g4[2 * i], gb = g4[2 * i + 1];
         const __half2 *h = reinterpret_cast<const __half2 *>(&v);
         float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
@@ -112,7 +112,7 @@ __device__ __forceinline__ void stage_copy(const __half *__restrict__ x, uint32_
     float4 *xs4 = reinterpret_cast<float4 *>(xs);
     for (uint32_t i = threadIdx.x; i < K / 8; i += blockDim.x)
     {
-        uint4 v = x4[i];
+        uint4 v = __ldcg(x4 + i);
         const __half2 *h = reinterpret_cast<const __half2 *>(&v);
         float2 a = __half22float2(h[0]), b = __half22float2(h[1]), c = __half22float2(h[2]), d = __half22float2(h[3]);
         xs4[2 * i] = make_float4(a.x * kHalfBitsScale, a.y * kHalfBitsScale, b.x * kHalfBitsScale, b.y * kHalfBitsScale);

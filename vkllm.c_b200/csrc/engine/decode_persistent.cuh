@@ -1,0 +1,983 @@
+// Persistent LLaMA-2 decode: one cooperative launch runs whole decode steps.
+//
+// One CTA per SM. Every warp of every CTA streams its share of ALL the step's weights, in step
+// order (per layer: QKV, Wo, up/gate, down; then the logits matrix), through its private
+// shared-memory stages with cp.async.bulk, and keeps streaming across matrix boundaries: while the
+// CTA waits at a grid barrier, or computes attention, the next matrix's weights are already
+// landing. Activations are exchanged through global memory between grid barriers.
+//
+// Weight tiles: a CTA owns a contiguous range of output rows of each matrix; they are cut into
+// tiles of 16 rows x 256 columns (one 512 B bulk copy per row, rows 528 B apart in shared memory
+// so that ldmatrix reads are free of bank conflicts). A warp reduces a tile against the staged
+// fp16 input vector with mma.sync m16n8k16 (the vector is the B operand, replicated over the 8
+// columns; products exact, fp32 accumulation), so shared memory sees each weight byte once per
+// write and once per read, and the warp issues ~4 instructions per 512 B. The tile partials land
+// in a per-CTA [segment][row] buffer that is summed in a fixed order after the phase.
+//
+// Phases:
+//
+//   [embed rows]  per layer: rmsnorm+QKV+RoPE+KV write | scores | probs.V | Wo+residual |
+//                 rmsnorm+up/gate+SiLU | down+residual   then: rmsnorm+logits | argmax
+//
+// Every node output is rounded to fp16 where the reference graph materialises it
+// (src/models/vkllm_llama2_layers.c:13-340), arithmetic is fp32. Every spin (mbarrier waits, grid
+// barriers) is bounded (~2 s on %globaltimer); on expiry or when another CTA reported an error the
+// kernel records it, drains its own bulk copies still in flight and returns.
+#pragma once
+
+#include "decode_kernels.cuh"
+#include "gemv_stream.cuh"
+
+namespace vkb
+{
+
+enum PhaseKind : uint32_t
+{
+    PK_QKV = 0,
+    PK_WO = 1,
+    PK_UPGATE = 2,
+    PK_DOWN = 3,
+    PK_LOGITS = 4,
+    PK_COUNT = 5
+};
+
+constexpr uint32_t kErrBarrierTimeout = 0x200;
+constexpr uint32_t kErrPosition = 0x1;
+
+constexpr uint32_t kTileRows = 16;                        // MMA M
+constexpr uint32_t kSegHalves = 256;                      // columns per tile
+constexpr uint32_t kRowPitch = 2 * kSegHalves + 16;       // bytes between tile rows in shared memory
+constexpr uint32_t kTileBytes = kTileRows * kRowPitch;    // one stage
+
+// Geometry of one GEMV phase kind: `units` outputs of `nm` rows each, rows of K columns cut into
+// Ks segments of kSegHalves (the last one `last` wide, a multiple of 16).
+struct TileGeom
+{
+    uint32_t units, nm, K, Ks, last;
+};
+
+struct PersistParams
+{
+    DecodeDims dd;
+    const LayerW *layers; // device array [L]
+    uint32_t L;
+    const __half *embed, *wout;
+    const float *out_norm;
+    uint32_t unk;
+    __half *x, *q, *m, *logits, *scores;
+    float2 *part;
+    float *opart;
+    float *am_val;     // per-CTA argmax partials [grid][32]
+    uint32_t *am_idx;  // [grid][32]
+    StepState *st;
+    uint32_t *ring;
+    uint32_t ring_len;
+    uint32_t *bar_count;    // grid barrier arrivals (zeroed before each launch, with the two below)
+    uint32_t *head_cnt;     // [H] attention splits that published their softmax statistics
+    uint32_t *head_done;    // [H] attention splits that published their partial outputs
+    __half *attn;           // [H * hd] attention output (the combined splits)
+    uint32_t att_groups;    // key groups of the attention phase (bounded by the scratch)
+    uint32_t *err;
+    TileGeom tg[PK_COUNT];
+    uint32_t spw, warps;    // stages per warp, warps per CTA
+    uint32_t xs_bytes;      // fp16 input staging (>= 2 * max K)
+    uint32_t part_bytes;    // tile partials; xs + part also serve as the attention scratch
+    uint32_t n_steps;
+    uint32_t att_split;     // key splits per head in the attention phases
+    uint64_t *trace;        // optional: CTA 0 records %globaltimer at every barrier arrival/release
+    uint32_t trace_cap;     // entries available in `trace`
+    unsigned long long *wtrace; // optional: CTA 0 per (warp, kind): wait, consume, chunks, compute part
+    uint64_t *trace_last;       // optional: per trace entry, %globaltimer when the last CTA arrived
+    uint32_t l2_bytes;          // per CTA: next-phase weights prefetched into L2 at each barrier
+    uint32_t l2_hint;           // 1: stage loads mark their lines evict-first in L2
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Barrier and trace bookkeeping of thread 0 of a CTA.
+struct SyncState
+{
+    uint32_t n;     // trace entries so far
+    uint32_t epoch; // grid barriers passed so far
+};
+
+// Grid-wide barrier for a cooperative launch (all CTAs co-resident): one release-add per CTA on a
+// counter that only grows during the launch (zeroed before it); barrier n completes when the
+// counter reaches n * gridDim.x. Bounded: false when it timed out or another CTA reported an error.
+__device__ __forceinline__ bool grid_sync(const PersistParams &P, SyncState &tr)
+{
+    __shared__ uint32_t ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        if (P.trace && blockIdx.x == 0 && tr.n < P.trace_cap)
+            P.trace[tr.n] = global_ns();
+        ++tr.n;
+        bool ok = true;
+        const uint32_t target = (++tr.epoch) * gridDim.x;
+        uint32_t prev;
+        asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.bar_count) : "memory");
+        if (prev + 1 == target)
+        {
+            if (P.trace_last && tr.n < P.trace_cap)
+                P.trace_last[tr.n] = global_ns();
+        }
+        else
+        {
+            const uint64_t t0 = global_ns();
+            while (ld_acquire_u32(P.bar_count) < target)
+            {
+                if (ld_acquire_u32(P.err) != 0)
+                {
+                    ok = false;
+                    break;
+                }
+                if (global_ns() - t0 > kWaitLimitNs)
+                {
+                    atomicOr(P.err, kErrBarrierTimeout);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (P.trace && blockIdx.x == 0 && tr.n < P.trace_cap)
+            P.trace[tr.n] = global_ns();
+        ++tr.n;
+        ok_s = ok ? 1u : 0u;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+// Trace point of CTA 0 (after a staging prologue); `tr` counts entries on every CTA.
+__device__ __forceinline__ void trace_mark(const PersistParams &P, SyncState &tr)
+{
+    if (threadIdx.x == 0)
+    {
+        if (P.trace && blockIdx.x == 0 && tr.n < P.trace_cap)
+            P.trace[tr.n] = global_ns();
+        ++tr.n;
+    }
+}
+
+// The weight row `m` of unit `u` of phase (kind, layer).
+__device__ __forceinline__ const __half *persist_row(const PersistParams &P, uint32_t kind, const LayerW &lw,
+                                                     uint32_t u, uint32_t m)
+{
+    const DecodeDims &dd = P.dd;
+    switch (kind)
+    {
+    case PK_QKV: {
+        const uint32_t HD = dd.H * dd.hd, row = 2 * u + m, which = row / HD, r = row % HD;
+        const __half *base = which == 0 ? lw.wq : (which == 1 ? lw.wk : lw.wv);
+        return base + (uint64_t)r * dd.D;
+    }
+    case PK_WO:
+        return lw.wo + (uint64_t)u * dd.H * dd.hd;
+    case PK_UPGATE:
+        return (m == 0 ? lw.wu : lw.wg) + (uint64_t)u * dd.D;
+    case PK_DOWN:
+        return lw.wd + (uint64_t)u * dd.F;
+    default:
+        return P.wout + (uint64_t)u * dd.D;
+    }
+}
+
+struct UnitRange
+{
+    uint32_t u0, count;
+};
+
+__device__ __forceinline__ UnitRange cta_units(uint32_t units)
+{
+    const uint32_t base = units / gridDim.x, rem = units % gridDim.x;
+    return UnitRange{blockIdx.x * base + min(blockIdx.x, rem), base + (blockIdx.x < rem ? 1u : 0u)};
+}
+
+// Producer cursor of one warp over its chunk sequence (step, layer, kind, k).
+struct Cursor
+{
+    uint32_t step, layer, kind, k;
+    bool done;
+};
+
+// Tiles of this CTA in a phase: ceil(rows / 16) row groups x Ks segments, tile t = group * Ks + segment.
+__device__ __forceinline__ uint32_t cta_tiles(const TileGeom &g, uint32_t count)
+{
+    return (count * g.nm + kTileRows - 1) / kTileRows * g.Ks;
+}
+
+// Tiles of warp w (tiles w, w + warps, ...).
+__device__ __forceinline__ uint32_t kind_chunks(const PersistParams &P, uint32_t kind, uint32_t w)
+{
+    const uint32_t T = cta_tiles(P.tg[kind], cta_units(P.tg[kind].units).count);
+    return T > w ? (T - w + P.warps - 1) / P.warps : 0;
+}
+
+__device__ __forceinline__ void cursor_settle(const PersistParams &P, Cursor &c, uint32_t w)
+{
+    // Skip phases where this warp has no chunk.
+    while (!c.done && c.k >= kind_chunks(P, c.kind, w))
+    {
+        c.k = 0;
+        if (c.kind == PK_LOGITS)
+        {
+            c.kind = PK_QKV;
+            c.layer = 0;
+            if (++c.step >= P.n_steps)
+                c.done = true;
+        }
+        else if (c.kind == PK_DOWN)
+        {
+            if (++c.layer >= P.L)
+                c.kind = PK_LOGITS;
+            else
+                c.kind = PK_QKV;
+        }
+        else
+            ++c.kind;
+    }
+}
+
+// Issues the copies of the cursor's tile into `dst` (whole warp: lane i copies row i); with
+// dst == nullptr, prefetches the tile into L2 instead.
+__device__ __forceinline__ void cursor_issue(const PersistParams &P, const Cursor &c, uint32_t w, unsigned char *dst,
+                                             uint64_t *bar, uint64_t policy)
+{
+    const uint32_t lane = threadIdx.x & 31;
+    const TileGeom &g = P.tg[c.kind];
+    const UnitRange r = cta_units(g.units);
+    const LayerW &lw = P.layers[c.kind == PK_LOGITS ? 0 : c.layer];
+    const uint32_t t = w + P.warps * c.k, grp = t / g.Ks, ks = t % g.Ks;
+    const uint32_t r0 = grp * kTileRows, nvalid = min(kTileRows, r.count * g.nm - r0);
+    const uint32_t bytes = 2 * (ks + 1 == g.Ks ? g.last : kSegHalves);
+    if (dst && lane == 0)
+        mbar_arrive_expect_tx(bar, nvalid * bytes);
+    __syncwarp();
+    if (lane < nvalid)
+    {
+        const uint32_t row = r0 + lane;
+        const __half *src = persist_row(P, c.kind, lw, r.u0 + row / g.nm, row % g.nm) + (size_t)ks * kSegHalves;
+        if (dst)
+        {
+            fence_proxy_async(); // this warp's earlier reads of the stage precede the async refill
+            if (policy)
+                bulk_g2s_hint(dst + lane * kRowPitch, src, bytes, bar, policy);
+            else
+                bulk_g2s(dst + lane * kRowPitch, src, bytes, bar);
+        }
+        else
+            bulk_prefetch_l2(src, bytes);
+    }
+}
+
+// Per-warp pipeline state.
+struct WarpPipe
+{
+    uint64_t *bar;        // spw barriers
+    unsigned char *stage; // spw stages of kTileBytes
+    uint32_t consumed;    // chunks consumed so far (global count)
+    uint32_t issued;      // chunks issued so far
+    Cursor cur;           // next chunk to issue (warp-uniform)
+    uint64_t policy;      // L2 policy of the stage loads (0: default)
+};
+
+// Issues the next tile into its stage.
+__device__ __forceinline__ void pipe_advance(const PersistParams &P, WarpPipe &wp, uint32_t warp)
+{
+    cursor_issue(P, wp.cur, warp, wp.stage + (size_t)(wp.issued % P.spw) * kTileBytes, &wp.bar[wp.issued % P.spw],
+                 wp.policy);
+    ++wp.issued;
+    ++wp.cur.k;
+    cursor_settle(P, wp.cur, warp);
+}
+
+// Prefetches into L2 this CTA's rows of phase (kind, layer) beyond the tiles the warps' stages take
+// first (up to l2_bytes): each CTA's rows of a matrix are contiguous, so a few large requests cover
+// them. Issued when the CTA reaches a grid barrier, it keeps HBM streaming through the barrier,
+// the next input staging and the attention phases. One thread.
+__device__ __forceinline__ void prefetch_slice(const PersistParams &P, uint32_t kind, uint32_t layer)
+{
+    if (P.l2_bytes == 0)
+        return;
+    const TileGeom &g = P.tg[kind];
+    const UnitRange r = cta_units(g.units);
+    const LayerW &lw = P.layers[kind == PK_LOGITS ? 0 : layer];
+    const uint32_t row_bytes = g.K * 2, unit_bytes = g.nm * row_bytes;
+    const uint32_t staged_rows = (P.warps * P.spw + g.Ks - 1) / g.Ks * kTileRows;
+    const uint32_t skip = (staged_rows + g.nm - 1) / g.nm;
+    if (skip >= r.count)
+        return;
+    uint32_t n = min(r.count - skip, P.l2_bytes / unit_bytes);
+    uint32_t u = r.u0 + skip;
+    constexpr uint32_t kPiece = 64 * 1024;
+    auto run = [&](const __half *p, uint32_t bytes) {
+        const char *c = reinterpret_cast<const char *>(p);
+        for (uint32_t o = 0; o < bytes; o += kPiece)
+            bulk_prefetch_l2(c + o, min(kPiece, bytes - o));
+    };
+    if (kind == PK_QKV)
+    {
+        // unit u = rows 2u, 2u+1 of [Wq; Wk; Wv], split where the matrix changes
+        const uint32_t HD = P.dd.H * P.dd.hd;
+        uint32_t row = 2 * u, end = 2 * (u + n);
+        while (row < end)
+        {
+            const uint32_t which = row / HD, stop = min(end, (which + 1) * HD);
+            run(persist_row(P, kind, lw, row / 2, row % 2), (stop - row) * row_bytes);
+            row = stop;
+        }
+    }
+    else if (kind == PK_UPGATE)
+    {
+        run(persist_row(P, kind, lw, u, 0), n * row_bytes);
+        run(persist_row(P, kind, lw, u, 1), n * row_bytes);
+    }
+    else
+        run(persist_row(P, kind, lw, u, 0), n * row_bytes);
+}
+
+// Epilogue of one unit of a GEMV phase (executed by one lane).
+__device__ __forceinline__ void persist_epilogue(const PersistParams &P, uint32_t kind, const LayerW &lw, uint32_t u,
+                                                 const float *s, uint32_t pos)
+{
+    const DecodeDims &dd = P.dd;
+    switch (kind)
+    {
+    case PK_QKV: {
+        const uint32_t HD = dd.H * dd.hd, row = 2 * u, which = row / HD, r = row % HD;
+        float v0 = round_f16(s[0]), v1 = round_f16(s[1]);
+        const uint32_t head = r / dd.hd, d = r % dd.hd;
+        if (which < 2)
+        {
+            const uint32_t w = d / 2;
+            const float theta = (float)pos / powf(dd.rope_base, (float)(2 * w) / (float)dd.hd);
+            const float c = cosf(theta), sn = sinf(theta);
+            const float o0 = c * v0 - sn * v1, o1 = sn * v0 + c * v1;
+            v0 = o0;
+            v1 = o1;
+        }
+        const __half2 hv = __floats2half2_rn(v0, v1);
+        if (which == 0)
+            *reinterpret_cast<__half2 *>(P.q + r) = hv;
+        else
+        {
+            __half *cache = which == 1 ? lw.kcache : lw.vcache;
+            *reinterpret_cast<__half2 *>(cache + ((uint64_t)head * dd.ctx + pos) * dd.hd + d) = hv;
+        }
+        break;
+    }
+    case PK_WO:
+    case PK_DOWN:
+        P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(s[0]));
+        break;
+    case PK_UPGATE:
+        P.m[u] = __float2half_rn(round_f16(s[0]) * round_f16(silu_f32(s[1])));
+        break;
+    default:
+        P.logits[u] = __float2half_rn(s[0]);
+        break;
+    }
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+
+// c += A(16x16, row) * B(16x8, col), fp16 inputs, fp32 accumulation.
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One GEMV phase: consumes this warp's tiles (partials to `part`), then the CTA sums the partials
+// of each of its units in segment order and runs the epilogue. Returns false when a wait timed out
+// in any warp of the CTA.
+template <int NM>
+__device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t kind, uint32_t layer, WarpPipe &wp,
+                                             const __half *xs, float *part, uint32_t pos, SyncState &tr)
+{
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const TileGeom &g = P.tg[kind];
+    const UnitRange r = cta_units(g.units);
+    const uint32_t groups = (r.count * NM + kTileRows - 1) / kTileRows, pitch = groups * kTileRows;
+    const uint32_t T = groups * g.Ks;
+    const uint32_t nk = T > warp ? (T - warp + P.warps - 1) / P.warps : 0;
+    const LayerW &lw = P.layers[kind == PK_LOGITS ? 0 : layer];
+    const bool wt = P.wtrace && blockIdx.x == 0 && lane == 0;
+    unsigned long long t_wait = 0, t_cons = 0, t_comp = 0;
+    bool ok = true;
+    for (uint32_t k = 0; k < nk; ++k)
+    {
+        const uint32_t gi = wp.consumed, s = gi % P.spw;
+        const long long c0 = wt ? clock64() : 0;
+        const bool okw = mbar_wait_bounded(&wp.bar[s], (gi / P.spw) & 1u, kWaitLimitNs);
+        if (__any_sync(0xffffffffu, !okw))
+        {
+            ok = false;
+            break;
+        }
+        const long long c1 = wt ? clock64() : 0;
+        t_wait += (unsigned long long)(c1 - c0);
+        const uint32_t t = warp + P.warps * k, grp = t / g.Ks, ks = t % g.Ks;
+        const uint32_t width = ks + 1 == g.Ks ? g.last : kSegHalves;
+        const unsigned char *st = wp.stage + (size_t)s * kTileBytes;
+        const uint32_t a_addr = smem_u32(st + (lane & 15) * kRowPitch + (lane >> 4) * 16);
+        const uint32_t *xk = reinterpret_cast<const uint32_t *>(xs + ks * kSegHalves + 2 * (lane & 3));
+        // two accumulator chains (even / odd k-steps) halve the dependent MMA latency
+        float c[4] = {0.f, 0.f, 0.f, 0.f}, d[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t kk = 0;
+#pragma unroll 2
+        for (; kk + 32 <= width; kk += 32)
+        {
+            uint32_t a0, a1, a2, a3, e0, e1, e2, e3;
+            ldsm_x4(a_addr + kk * 2, a0, a1, a2, a3);
+            ldsm_x4(a_addr + kk * 2 + 32, e0, e1, e2, e3);
+            mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
+            mma_16816(d, e0, e1, e2, e3, xk[kk / 2 + 8], xk[kk / 2 + 12]);
+        }
+        if (kk < width)
+        {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(a_addr + kk * 2, a0, a1, a2, a3);
+            mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
+        }
+        if ((lane & 3) == 0)
+        {
+            const uint32_t row = grp * kTileRows + (lane >> 2);
+            part[ks * pitch + row] = c[0] + d[0];
+            part[ks * pitch + row + 8] = c[2] + d[2];
+        }
+        __syncwarp();
+        const long long c2 = wt ? clock64() : 0;
+        t_comp += (unsigned long long)(c2 - c1);
+        if (!wp.cur.done)
+            pipe_advance(P, wp, warp);
+        ++wp.consumed;
+        if (wt)
+            t_cons += (unsigned long long)(clock64() - c1);
+    }
+    if (wt)
+    {
+        unsigned long long *o = P.wtrace + ((size_t)warp * PK_COUNT + kind) * 4;
+        atomicAdd(o, t_wait);
+        atomicAdd(o + 1, t_cons);
+        atomicAdd(o + 2, (unsigned long long)nk);
+        atomicAdd(o + 3, t_comp);
+    }
+    if (!__syncthreads_and(ok))
+        return false;
+    trace_mark(P, tr);
+    // Unit sums over the segments in order, a thread per unit.
+    for (uint32_t ul = threadIdx.x; ul < r.count; ul += blockDim.x)
+    {
+        float sums[NM];
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+        {
+            float a = 0.f;
+            for (uint32_t ks = 0; ks < g.Ks; ++ks)
+                a += part[ks * pitch + ul * NM + m];
+            sums[m] = a;
+        }
+        persist_epilogue(P, kind, lw, r.u0 + ul, sums, pos);
+    }
+    (void)nw;
+    return true;
+}
+
+// Attention of one layer over (head, key-split) items, at most one per CTA: the scores node
+// s_j = fp16(scale * q.k_j), the softmax node p_j = fp16(exp(s_j - M) / L) with M, L over the
+// whole head, and the attention output fp16(sum_j p_j v_j). A split publishes its (max, sum exp)
+// and waits (bounded) for its sibling splits' statistics on a per-head counter instead of a grid
+// barrier; the last split of a head to publish its partial output combines the splits in order.
+// Keys are read `lpk` lanes per key (8 fp16 per lane). For Lk == hd the reference reads V as
+// [hd, Lk] (src/core/vkllm_op_matmul.c:14-30): split 0 then computes o[w] = sum_k p_k V[w][k] from
+// the stored scores and the other splits contribute 0. `aepoch` counts the attention phases of
+// this launch. Returns false on a timed-out wait or a reported error.
+__device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32_t layer, uint32_t pos,
+                                                  uint32_t aepoch, float *scratch, float *red)
+{
+    const DecodeDims &dd = P.dd;
+    const LayerW &lw = P.layers[layer];
+    const uint32_t tid = threadIdx.x, nt = blockDim.x;
+    const uint32_t Lk = pos + 1, ns = P.att_split, hd = dd.hd, pieces = hd / 8;
+    uint32_t lpk = 1;
+    while (lpk < pieces)
+        lpk <<= 1;
+    const uint32_t G = min(P.att_groups, nt / lpk), gi = tid / lpk, pc = tid % lpk;
+    const bool lane_on = gi < G && pc < pieces;
+    const uint32_t chunk = (Lk + ns - 1) / ns, hd_al = (hd + 31) & ~31u;
+    float *qs = scratch;             // [hd]
+    float *sc = qs + hd_al;          // [chunk] this split's scores
+    float *acc = sc + ((chunk + 31) & ~31u); // [G][hd] per-group partial outputs
+    __shared__ uint32_t flag_s;
+    const uint32_t target = ns * (aepoch + 1);
+    for (uint32_t it = blockIdx.x; it < dd.H * ns; it += gridDim.x)
+    {
+        const uint32_t h = it / ns, split = it % ns;
+        const uint32_t j0 = split * chunk, j1 = min(Lk, j0 + chunk);
+        const uint32_t nkeys = j1 > j0 ? j1 - j0 : 0, rounds = (nkeys + G - 1) / G;
+        for (uint32_t d = tid; d < hd; d += nt)
+            qs[d] = __half2float(__ldcg(P.q + h * hd + d));
+        __syncthreads();
+        const __half *kb = lw.kcache + (uint64_t)h * dd.ctx * hd;
+        float mx = -FLT_MAX;
+        for (uint32_t rr = 0; rr < rounds; ++rr)
+        {
+            const uint32_t j = j0 + gi + G * rr;
+            const bool valid = lane_on && j < j1;
+            float a = 0.f;
+            if (valid)
+            {
+                const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(kb + (uint64_t)j * hd) + pc);
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                {
+                    const float2 f = __half22float2(hh[e]);
+                    a = fmaf(qs[8 * pc + 2 * e], f.x, a);
+                    a = fmaf(qs[8 * pc + 2 * e + 1], f.y, a);
+                }
+            }
+            for (uint32_t o = lpk / 2; o > 0; o >>= 1)
+                a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (valid)
+            {
+                const float s = round_f16(a * dd.scale);
+                if (pc == 0)
+                {
+                    sc[j - j0] = s;
+                    P.scores[(uint64_t)h * dd.ctx + j] = __float2half_rn(s);
+                }
+                mx = fmaxf(mx, s);
+            }
+        }
+        // this split's max and sum of exp (the reference's reductions over the whole row, in parts)
+        mx = warp_max(mx);
+        if ((tid & 31) == 0)
+            red[tid >> 5] = mx;
+        __syncthreads();
+        float m = -FLT_MAX;
+        for (uint32_t w = 0; w < (nt >> 5); ++w)
+            m = fmaxf(m, red[w]);
+        float l = 0.f;
+        for (uint32_t j = tid; j < nkeys; j += nt)
+            l += expf(sc[j] - m);
+        __syncthreads();
+        l = block_sum(l, red);
+        if (tid == 0)
+        {
+            bool ok = true;
+            P.part[h * ns + split] = make_float2(nkeys ? m : -FLT_MAX, nkeys ? l : 0.f);
+            uint32_t prev;
+            asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.head_cnt + h) : "memory");
+            if (prev + 1 < target)
+            {
+                const uint64_t t0 = global_ns();
+                while (ld_acquire_u32(P.head_cnt + h) < target)
+                {
+                    if (ld_acquire_u32(P.err) != 0)
+                    {
+                        ok = false;
+                        break;
+                    }
+                    if (global_ns() - t0 > kWaitLimitNs)
+                    {
+                        atomicOr(P.err, kErrBarrierTimeout);
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            flag_s = ok ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!flag_s)
+            return false;
+        float M = -FLT_MAX, L = 0.f;
+        for (uint32_t c = 0; c < ns; ++c)
+            M = fmaxf(M, __ldcg(P.part + h * ns + c).x);
+        for (uint32_t c = 0; c < ns; ++c)
+        {
+            const float2 pl = __ldcg(P.part + h * ns + c);
+            if (pl.y > 0.f)
+                L += pl.y * expf(pl.x - M);
+        }
+        const __half *vb = lw.vcache + (uint64_t)h * dd.ctx * hd;
+        float *op = P.opart + ((uint64_t)h * ns + split) * hd;
+        if (Lk == hd)
+        {
+            for (uint32_t w = tid; w < hd; w += nt)
+            {
+                float o = 0.f;
+                if (split == 0)
+                {
+                    const __half *vr = vb + (uint64_t)w * hd;
+                    const __half *sr = P.scores + (uint64_t)h * dd.ctx;
+                    for (uint32_t k = 0; k < Lk; ++k)
+                        o = fmaf(round_f16(expf(__half2float(__ldcg(sr + k)) - M) / L), __half2float(__ldcg(vr + k)),
+                                 o);
+                }
+                op[w] = o;
+            }
+        }
+        else
+        {
+            float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (uint32_t rr = 0; rr < rounds; ++rr)
+            {
+                const uint32_t j = j0 + gi + G * rr;
+                if (lane_on && j < j1)
+                {
+                    const float pj = round_f16(expf(sc[j - j0] - M) / L);
+                    const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(vb + (uint64_t)j * hd) + pc);
+                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                    {
+                        const float2 f = __half22float2(hh[e]);
+                        a[2 * e] = fmaf(pj, f.x, a[2 * e]);
+                        a[2 * e + 1] = fmaf(pj, f.y, a[2 * e + 1]);
+                    }
+                }
+            }
+            if (lane_on)
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    acc[gi * hd + 8 * pc + e] = a[e];
+            __syncthreads();
+            for (uint32_t d = tid; d < hd; d += nt)
+            {
+                float o = 0.f;
+                for (uint32_t g = 0; g < G; ++g)
+                    o += acc[g * hd + d];
+                op[d] = o;
+            }
+        }
+        __syncthreads();
+        if (tid == 0)
+        {
+            uint32_t prev;
+            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.head_done + h) : "memory");
+            flag_s = prev + 1 == target ? 1u : 0u; // the head's last split combines
+        }
+        __syncthreads();
+        if (flag_s)
+            for (uint32_t d = tid; d < hd; d += nt)
+            {
+                float o = 0.f;
+                for (uint32_t c = 0; c < ns; ++c)
+                    o += __ldcg(P.opart + ((uint64_t)h * ns + c) * hd + d);
+                P.attn[h * hd + d] = __float2half_rn(o);
+            }
+        __syncthreads();
+    }
+    return true;
+}
+
+// Stages the RMSNORM node's output fp16((x * g) * rsqrt(mean(x^2) + eps)) as fp16 (x read from L2).
+__device__ __forceinline__ void stage_rmsnorm_h(const __half *__restrict__ x, const float *__restrict__ g, uint32_t K,
+                                                float eps, __half *xs, float *red)
+{
+    const uint32_t nchunk = K / 8;
+    const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+    float s = 0.f;
+    for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
+    {
+        const uint4 v = __ldcg(x4 + i);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+        {
+            const float2 f = __half22float2(h[j]);
+            s = fmaf(f.x, f.x, s);
+            s = fmaf(f.y, f.y, s);
+        }
+    }
+    const float alpha = rsqrtf(block_sum(s, red) / (float)K + eps);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    uint4 *xs4 = reinterpret_cast<uint4 *>(xs);
+    for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
+    {
+        const uint4 v = __ldcg(x4 + i);
+        const float4 ga = g4[2 * i], gb = g4[2 * i + 1];
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+        const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+        {
+            const float2 f = __half22float2(h[j]);
+            oh[j] = __floats2half2_rn((f.x * gg[2 * j]) * alpha, (f.y * gg[2 * j + 1]) * alpha);
+        }
+        xs4[i] = o;
+    }
+    __syncthreads();
+}
+
+// Stages an fp16 vector written by other CTAs (read from L2).
+__device__ __forceinline__ void stage_copy_h(const __half *__restrict__ x, uint32_t K, __half *xs)
+{
+    const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+    uint4 *xs4 = reinterpret_cast<uint4 *>(xs);
+    for (uint32_t i = threadIdx.x; i < K / 8; i += blockDim.x)
+        xs4[i] = __ldcg(x4 + i);
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(PersistParams P)
+{
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    __half *xs = reinterpret_cast<__half *>(smem + kStreamBarBytes);
+    float *part = reinterpret_cast<float *>(smem + kStreamBarBytes + P.xs_bytes);
+    float *scratch = reinterpret_cast<float *>(smem + kStreamBarBytes); // attention phases: xs + part
+    unsigned char *stages = smem + kStreamBarBytes + P.xs_bytes + P.part_bytes;
+    __shared__ float sred[32];
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const DecodeDims &dd = P.dd;
+    WarpPipe wp;
+    wp.bar = bars + warp * P.spw;
+    wp.stage = stages + (size_t)warp * P.spw * kTileBytes;
+    wp.consumed = 0;
+    wp.issued = 0;
+    wp.cur = Cursor{0, 0, PK_QKV, 0, P.n_steps == 0};
+    bool ok = true;
+    SyncState tr{1, 0}; // thread 0: trace entry 0 is the start
+    if (P.trace && blockIdx.x == 0 && threadIdx.x == 0 && P.trace_cap > 0)
+        P.trace[0] = global_ns();
+    if (lane == 0)
+    {
+        for (uint32_t s = 0; s < P.spw; ++s)
+            mbar_init(&wp.bar[s], 1);
+        fence_barrier_init();
+        fence_proxy_async();
+    }
+    __syncwarp();
+    wp.policy = P.l2_hint ? l2_evict_first_policy() : 0;
+    cursor_settle(P, wp.cur, warp);
+    // Fill every stage: the first weights do not depend on anything.
+    while (!wp.cur.done && wp.issued < P.spw)
+    {
+        cursor_issue(P, wp.cur, warp, wp.stage + (size_t)wp.issued * kTileBytes, &wp.bar[wp.issued], wp.policy);
+        ++wp.issued;
+        ++wp.cur.k;
+        cursor_settle(P, wp.cur, warp);
+    }
+
+    // Every CTA tracks the token and position itself (each computes the same argmax); CTA 0
+    // publishes them to the step state for the host.
+    uint32_t pos = __ldcg(&P.st->pos), tok0 = __ldcg(&P.st->token);
+    for (uint32_t step = 0; ok && step < P.n_steps; ++step)
+    {
+        if (pos >= dd.ctx)
+        {
+            if (blockIdx.x == 0 && threadIdx.x == 0)
+                atomicOr(P.err, kErrPosition);
+            ok = false;
+            break;
+        }
+        const uint32_t tok = tok0 < dd.V ? tok0 : P.unk; // src/shaders/vkllm_embedding.comp:57-60
+        // The residual rows this CTA owns (the Wo / down output rows) start as the embedding.
+        {
+            const UnitRange r = cta_units(P.tg[PK_WO].units);
+            for (uint32_t i = threadIdx.x; i < r.count; i += blockDim.x)
+                P.x[r.u0 + i] = P.embed[(uint64_t)tok * dd.D + r.u0 + i];
+        }
+        for (uint32_t l = 0; ok && l < P.L; ++l)
+        {
+            const LayerW &lw = P.layers[l];
+            if (l == 0)
+                stage_rmsnorm_h(P.embed + (uint64_t)tok * dd.D, lw.attn_norm, dd.D, dd.eps, xs, sred);
+            else
+                stage_rmsnorm_h(P.x, lw.attn_norm, dd.D, dd.eps, xs, sred);
+            trace_mark(P, tr);
+            ok = persist_gemv<2>(P, PK_QKV, l, wp, xs, part, pos, tr);
+            if (threadIdx.x == 0)
+                prefetch_slice(P, PK_WO, l);
+            if (!__syncthreads_and(ok) || !grid_sync(P, tr))
+            {
+                ok = false;
+                break;
+            }
+            if (!persist_attention(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
+            {
+                ok = false;
+                break;
+            }
+            stage_copy_h(P.attn, dd.H * dd.hd, xs);
+            trace_mark(P, tr);
+            ok = persist_gemv<1>(P, PK_WO, l, wp, xs, part, pos, tr);
+            if (threadIdx.x == 0)
+                prefetch_slice(P, PK_UPGATE, l);
+            if (!__syncthreads_and(ok) || !grid_sync(P, tr))
+            {
+                ok = false;
+                break;
+            }
+            stage_rmsnorm_h(P.x, lw.ffn_norm, dd.D, dd.eps, xs, sred);
+            trace_mark(P, tr);
+            ok = persist_gemv<2>(P, PK_UPGATE, l, wp, xs, part, pos, tr);
+            if (threadIdx.x == 0)
+                prefetch_slice(P, PK_DOWN, l);
+            if (!__syncthreads_and(ok) || !grid_sync(P, tr))
+            {
+                ok = false;
+                break;
+            }
+            stage_copy_h(P.m, dd.F, xs);
+            trace_mark(P, tr);
+            ok = persist_gemv<1>(P, PK_DOWN, l, wp, xs, part, pos, tr);
+            if (threadIdx.x == 0)
+                prefetch_slice(P, l + 1 < P.L ? PK_QKV : PK_LOGITS, l + 1 < P.L ? l + 1 : 0);
+            if (!__syncthreads_and(ok) || !grid_sync(P, tr))
+            {
+                ok = false;
+                break;
+            }
+        }
+        if (!ok)
+            break;
+        stage_rmsnorm_h(P.x, P.out_norm, dd.D, dd.eps, xs, sred);
+        trace_mark(P, tr);
+        ok = persist_gemv<1>(P, PK_LOGITS, 0, wp, xs, part, pos, tr);
+        if (threadIdx.x == 0 && step + 1 < P.n_steps)
+            prefetch_slice(P, PK_QKV, 0);
+        if (!__syncthreads_and(ok))
+        {
+            ok = false;
+            break;
+        }
+        // Per-CTA argmax partials over its logits rows, per class i mod 32: the first (smallest
+        // index) strict maximum (src/shaders/vkllm_arg_max.comp:54-69).
+        {
+            const UnitRange r = cta_units(P.tg[PK_LOGITS].units);
+            if (warp == 0)
+            {
+                float bv = -FLT_MAX;
+                uint32_t bi = 0xffffffffu;
+                const uint32_t first = r.u0 + ((lane + 32 - (r.u0 & 31)) & 31);
+                for (uint32_t i = first; i < r.u0 + r.count; i += 32)
+                {
+                    const float v = __half2float(__ldcg(P.logits + i));
+                    if (bi == 0xffffffffu || v > bv)
+                    {
+                        bv = v;
+                        bi = i;
+                    }
+                }
+                P.am_val[blockIdx.x * 32 + lane] = bv;
+                P.am_idx[blockIdx.x * 32 + lane] = bi;
+            }
+        }
+        if (!grid_sync(P, tr))
+        {
+            ok = false;
+            break;
+        }
+        // Every CTA combines the partials: class `lane` over the CTAs (warps take CTAs w, w + nw,
+        // ...; the largest value wins, ties to the smallest index, which is the in-order scan's
+        // result since a class's indices grow with the CTA), then the 16/8/4/2/1 tree over the
+        // classes that keeps the left operand unless the right one is strictly greater
+        // (vkllm_arg_max.comp:77-90).
+        {
+            float *cv_s = scratch;                                              // [nw][32]
+            uint32_t *ci_s = reinterpret_cast<uint32_t *>(scratch + 32 * 32); // [nw][32]
+            const uint32_t nw = blockDim.x >> 5;
+            float v = -FLT_MAX;
+            uint32_t idx = 0xffffffffu;
+            for (uint32_t b = warp; b < gridDim.x; b += nw)
+            {
+                const uint32_t ci = __ldcg(P.am_idx + b * 32 + lane);
+                const float cv = __ldcg(P.am_val + b * 32 + lane);
+                if (ci == 0xffffffffu)
+                    continue;
+                if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))
+                {
+                    v = cv;
+                    idx = ci;
+                }
+            }
+            cv_s[warp * 32 + lane] = v;
+            ci_s[warp * 32 + lane] = idx;
+            __syncthreads();
+            if (warp == 0)
+            {
+                v = -FLT_MAX;
+                idx = 0xffffffffu;
+                for (uint32_t w = 0; w < nw; ++w)
+                {
+                    const uint32_t ci = ci_s[w * 32 + lane];
+                    const float cv = cv_s[w * 32 + lane];
+                    if (ci == 0xffffffffu)
+                        continue;
+                    if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))
+                    {
+                        v = cv;
+                        idx = ci;
+                    }
+                }
+                if (idx == 0xffffffffu)
+                {
+                    v = -FLT_MAX; // empty class (V < 32): the reference lane keeps -FLT_MAX and its own index
+                    idx = lane;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                {
+                    const float ov = __shfl_down_sync(0xffffffffu, v, o);
+                    const uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
+                    if ((int)lane < o && ov > v)
+                    {
+                        v = ov;
+                        idx = oi;
+                    }
+                }
+                if (lane == 0)
+                {
+                    ci_s[0] = idx;
+                    if (blockIdx.x == 0)
+                    {
+                        P.st->token = idx;
+                        if (P.st->step < P.ring_len)
+                            P.ring[P.st->step] = idx;
+                        P.st->step += 1;
+                        P.st->pos = pos + 1;
+                    }
+                }
+            }
+            __syncthreads();
+            tok0 = ci_s[0];
+            pos += 1;
+            __syncthreads();
+        }
+    }
+    if (!ok)
+    {
+        if (threadIdx.x == 0)
+            atomicOr(P.err, kErrMbarTimeout);
+    }
+    // Copies this warp issued and did not consume must land before the shared memory is released
+    // (none on the normal path: the cursor stops after the last step).
+    for (uint32_t gi = wp.consumed; gi < wp.issued; ++gi)
+        (void)mbar_wait_bounded(&wp.bar[gi % P.spw], (gi / P.spw) & 1u, kWaitLimitNs / 4);
+    __syncwarp();
+}
+
+} // namespace vkb

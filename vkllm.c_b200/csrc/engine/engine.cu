@@ -8,6 +8,7 @@
 
 #include "../runtime/internal.h"
 #include "decode_kernels.cuh"
+#include "decode_persistent.cuh"
 #include "plan.h"
 #include "vkllm_b200.h"
 #include "vkllm_kvcache.h"
@@ -38,6 +39,14 @@ struct Engine
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     uint32_t kernels_per_step = 0;
+    // persistent decode (one cooperative launch runs n steps)
+    bool persistent = false;
+    PersistParams pp{};
+    size_t pp_smem = 0;
+    LayerW *d_layers = nullptr;
+    float *am_val = nullptr;
+    uint32_t *am_idx = nullptr, *bar = nullptr; // bar[0] = barrier arrivals, then 2 x H attention counters
+    uint32_t launches = 0;                      // kernel launches enqueued by the last decode call
 };
 
 namespace
@@ -125,6 +134,180 @@ template <class Op> void allow_smem(const StreamGeom &g)
     cudaFuncSetAttribute(k_gemv_stream<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stream_smem_bytes(g));
 }
 
+// Persistent decode geometry: every phase kind shares the block size and stage layout.
+void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_t spw, uint32_t l2_kb)
+{
+    const char *mode = getenv("VKLLM_B200_DECODE");
+    if (mode && strcmp(mode, "graph") == 0)
+        return;
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device->ordinal);
+    if (!coop)
+        return;
+    const DecodeDims &dd = e->dd;
+    const uint32_t HD = dd.H * dd.hd;
+    PersistParams &P = e->pp;
+    P.dd = dd;
+    P.L = (uint32_t)e->layers.size();
+    P.embed = e->embed;
+    P.wout = e->wout;
+    P.out_norm = e->out_norm;
+    P.unk = e->unk;
+    P.x = e->x;
+    P.q = e->q;
+    P.m = e->m;
+    P.logits = e->logits;
+    P.scores = e->scores;
+    P.part = e->part;
+    P.opart = e->opart;
+    P.am_val = e->am_val;
+    P.am_idx = e->am_idx;
+    P.st = e->state;
+    P.ring = e->ring;
+    P.ring_len = dd.ctx;
+    P.bar_count = e->bar;
+    P.head_cnt = e->bar + 1;
+    P.head_done = e->bar + 1 + dd.H;
+    P.attn = e->attn;
+    P.err = &e->state->error;
+    P.att_split = att_split;
+    P.l2_bytes = l2_kb * 1024;
+    const char *hint = getenv("VKLLM_B200_PERSIST_L2_HINT");
+    P.l2_hint = hint ? (uint32_t)atoi(hint) : 0u;
+    // Weight tiles of 16 rows x 256 columns; every K must be a multiple of 16 (MMA k-step).
+    if (dd.D % 16 != 0 || HD % 16 != 0 || dd.F % 16 != 0)
+        return;
+    auto tile_geom = [](uint32_t units, uint32_t nm, uint32_t K) {
+        TileGeom g;
+        g.units = units;
+        g.nm = nm;
+        g.K = K;
+        g.Ks = (K + kSegHalves - 1) / kSegHalves;
+        g.last = K - kSegHalves * (g.Ks - 1);
+        return g;
+    };
+    P.tg[PK_QKV] = tile_geom(3 * HD / 2, 2, dd.D);
+    P.tg[PK_WO] = tile_geom(dd.D, 1, HD);
+    P.tg[PK_UPGATE] = tile_geom(dd.F, 2, dd.D);
+    P.tg[PK_DOWN] = tile_geom(dd.D, 1, dd.F);
+    P.tg[PK_LOGITS] = tile_geom(dd.V, 1, dd.D);
+    const uint32_t grid = (uint32_t)ctx->device->sm_count;
+    uint32_t maxk = dd.D > HD ? dd.D : HD;
+    if (dd.F > maxk)
+        maxk = dd.F;
+    size_t part_floats = 0;
+    for (int k = 0; k < PK_COUNT; ++k)
+    {
+        const TileGeom &g = P.tg[k];
+        const uint32_t rows = (g.units + grid - 1) / grid * g.nm;
+        const size_t need = (size_t)(rows + kTileRows - 1) / kTileRows * kTileRows * g.Ks;
+        part_floats = need > part_floats ? need : part_floats;
+    }
+    P.spw = spw < 1 ? 1 : (spw > kStreamMaxSpw ? kStreamMaxSpw : spw);
+    P.xs_bytes = (maxk * 2 + 127) / 128 * 128;
+    P.part_bytes = (uint32_t)((part_floats * 4 + 127) / 128 * 128);
+    // Attention scratch (aliases xs + part): q, the split's scores, and per key-group partial
+    // outputs [groups][hd]; at least 8 key groups, up to one per lpk threads of a full CTA. The
+    // argmax combine needs 2 x 32 x 32 words of it.
+    const uint32_t hd_al = (dd.hd + 31) & ~31u, chunk = (dd.ctx + att_split - 1) / att_split,
+                   chunk_al = (chunk + 31) & ~31u;
+    uint32_t lpk = 1;
+    while (lpk < dd.hd / 8)
+        lpk <<= 1;
+    const uint32_t groups_full = 1024 / lpk;
+    {
+        const uint32_t min_floats = hd_al + chunk_al + 8 * dd.hd, argmax_floats = 2048;
+        const uint32_t need = 4 * (min_floats > argmax_floats ? min_floats : argmax_floats);
+        if (need > P.xs_bytes + P.part_bytes)
+            P.part_bytes = (need - P.xs_bytes + 127) / 128 * 128;
+        const uint32_t avail = (P.xs_bytes + P.part_bytes) / 4 - hd_al - chunk_al;
+        P.att_groups = avail / dd.hd < groups_full ? avail / dd.hd : groups_full;
+    }
+    if (dd.hd % 8 != 0 || dd.hd > 256)
+        return;
+    const size_t optin = ctx->device->smem_optin;
+    const size_t fixed = kStreamBarBytes + P.xs_bytes + P.part_bytes;
+    uint32_t warps = optin > fixed ? (uint32_t)((optin - fixed) / ((size_t)P.spw * kTileBytes)) : 0;
+    if (warps > (uint32_t)kStreamMaxWarps)
+        warps = kStreamMaxWarps;
+    if (warps < 8)
+        return;
+    P.warps = warps;
+    e->pp_smem = fixed + (size_t)warps * P.spw * kTileBytes;
+    const char *trace = getenv("VKLLM_B200_TRACE");
+    if (trace && atoi(trace) != 0)
+    {
+        P.trace_cap = 1u << 16;
+        if (cudaMalloc(&P.trace, sizeof(uint64_t) * P.trace_cap) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            P.trace = nullptr;
+            P.trace_cap = 0;
+        }
+        if (cudaMalloc(&P.trace_last, sizeof(uint64_t) * P.trace_cap) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            P.trace_last = nullptr;
+        }
+        const size_t wbytes = sizeof(unsigned long long) * kStreamMaxWarps * PK_COUNT * 4;
+        if (cudaMalloc(&P.wtrace, wbytes) != cudaSuccess || cudaMemset(P.wtrace, 0, wbytes) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            P.wtrace = nullptr;
+        }
+    }
+    if (cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->pp_smem) !=
+        cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return;
+    }
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_decode_persistent, 32 * warps, e->pp_smem) !=
+            cudaSuccess ||
+        blocks < 1)
+    {
+        (void)cudaGetLastError();
+        return;
+    }
+    if (cudaMalloc(&e->d_layers, sizeof(LayerW) * e->layers.size()) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return;
+    }
+    cudaMemcpy(e->d_layers, e->layers.data(), sizeof(LayerW) * e->layers.size(), cudaMemcpyHostToDevice);
+    P.layers = e->d_layers;
+    e->persistent = true;
+}
+
+// Enqueues n decode steps as cooperative persistent launches (at most 64 steps per launch).
+vkllm_err_t run_persistent(Engine *e, uint32_t n, cudaStream_t s)
+{
+    e->launches = 0;
+    while (n > 0)
+    {
+        const uint32_t k = n > 64 ? 64 : n;
+        // barrier arrivals and per-head attention counters (they only grow during a launch)
+        VKB_CUDA(cudaMemsetAsync(e->bar, 0, 4 * (1 + 2 * (size_t)e->dd.H), s));
+        PersistParams P = e->pp;
+        P.n_steps = k;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)e->ctx->device->sm_count); // one co-resident CTA per SM
+        cfg.blockDim = dim3(32 * P.warps);
+        cfg.dynamicSmemBytes = e->pp_smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        VKB_CUDA(cudaLaunchKernelEx(&cfg, k_decode_persistent, P));
+        e->launches += 1;
+        n -= k;
+    }
+    return VKLLM_ERR_OK;
+}
+
 vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine **out)
 {
     _CHECK_ARGS(model->weights.blocks && model->weights.kvcache && model->weights.tok_embed_weights &&
@@ -196,14 +379,18 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->wout = (const __half *)dev_ptr(ctx, model->weights.output_weight);
     e->out_norm = (const float *)dev_ptr(ctx, model->weights.output_norm_weight);
 
+    // Attention key splits of the persistent path: about one (head, split) item per SM.
+    const uint32_t att_split = (uint32_t)sms / dd.H > 0 ? ((uint32_t)sms / dd.H > 32 ? 32 : (uint32_t)sms / dd.H) : 1;
+    const uint32_t max_split = att_split > dd.nsplit ? att_split : dd.nsplit;
     // Workspace layout (256-byte aligned pieces).
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
     size_t off_x = 0, off_q = off_x + al(dd.D * 2), off_attn = off_q + al(HD * 2), off_m = off_attn + al(HD * 2),
            off_logits = off_m + al((size_t)dd.F * 2), off_scores = off_logits + al((size_t)dd.V * 2),
-           off_part = off_scores + al((size_t)dd.H * dd.ctx * 2), off_opart = off_part + al((size_t)dd.H * dd.nsplit * 8),
-           off_cnt = off_opart + al((size_t)dd.H * dd.nsplit * dd.hd * 4), off_lcnt = off_cnt + al(dd.H * 4),
+           off_part = off_scores + al((size_t)dd.H * dd.ctx * 2), off_opart = off_part + al((size_t)dd.H * max_split * 8),
+           off_cnt = off_opart + al((size_t)dd.H * max_split * dd.hd * 4), off_lcnt = off_cnt + al(dd.H * 4),
            off_ring = off_lcnt + al(4), off_state = off_ring + al((size_t)dd.ctx * 4),
-           total = off_state + al(sizeof(StepState));
+           off_amv = off_state + al(sizeof(StepState)), off_ami = off_amv + al((size_t)sms * 32 * 4),
+           off_bar = off_ami + al((size_t)sms * 32 * 4), total = off_bar + al(4 * (1 + 2 * (size_t)dd.H));
     if (cudaMalloc(&e->ws, total) != cudaSuccess)
     {
         (void)cudaGetLastError();
@@ -224,6 +411,9 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->logit_counter = (uint32_t *)(w + off_lcnt);
     e->ring = (uint32_t *)(w + off_ring);
     e->state = (StepState *)(w + off_state);
+    e->am_val = (float *)(w + off_amv);
+    e->am_idx = (uint32_t *)(w + off_ami);
+    e->bar = (uint32_t *)(w + off_bar);
 
     // Streaming GEMV geometry: one CTA per SM; chunks of at most ~8 KB, one stage per warp and as
     // many warps (<= 32) as ~220 KB of shared memory holds next to the fp32 input vector.
@@ -259,6 +449,10 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     allow_smem<LogitsOp>(e->g_logits);
     e->grid_embed = (dd.D / 8 + 255) / 256;
     e->kernels_per_step = 2 + 6 * (uint32_t)e->layers.size();
+    // Persistent kernel: VKLLM_B200_PERSIST_SPW overrides the weight-tile stages per warp,
+    // VKLLM_B200_PERSIST_L2_KB the next-phase weights per CTA prefetched into L2 at each barrier.
+    const char *l2kb = getenv("VKLLM_B200_PERSIST_L2_KB");
+    setup_persistent(e, ctx, att_split, env_u32("VKLLM_B200_PERSIST_SPW", 1), l2kb ? (uint32_t)atoi(l2kb) : 0u);
 
     // Capture one decode step.
     cudaStream_t cs;
@@ -325,6 +519,14 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
     if (e->graph)
         cudaGraphDestroy(e->graph);
     cudaFree(e->ws);
+    if (e->d_layers)
+        cudaFree(e->d_layers);
+    if (e->pp.trace)
+        cudaFree(e->pp.trace);
+    if (e->pp.wtrace)
+        cudaFree(e->pp.wtrace);
+    if (e->pp.trace_last)
+        cudaFree(e->pp.trace_last);
     delete e;
     model->b200.engine = nullptr;
 }
@@ -347,7 +549,10 @@ vkllm_err_t plan_run(vkllm_context *ctx, vkllm_graph *graph)
     if (!tok || !out)
         return VKLLM_ERR_ALLOC;
     k_set_state<<<1, 1, 0, s>>>(e->state, tok, 0, p->offsets);
-    VKB_CUDA(cudaGraphLaunch(e->exec, s));
+    if (e->persistent)
+        _CHECK(run_persistent(e, 1, s));
+    else
+        VKB_CUDA(cudaGraphLaunch(e->exec, s));
     k_emit_token<<<1, 1, 0, s>>>(e->state, out);
     VKB_CUDA(cudaGetLastError());
     _CHECK(vkllm_commands_submit(ctx, graph->commands));
@@ -488,8 +693,11 @@ extern "C" vkllm_err_t vkllm_b200_engine_decode_steps(struct vkllm_context *cont
     _CHECK_ARGS(context && model);
     Engine *e;
     _CHECK(get_engine(context, model, &e));
+    if (e->persistent)
+        return run_persistent(e, n, context->runtime->stream);
     for (uint32_t i = 0; i < n; ++i)
         VKB_CUDA(cudaGraphLaunch(e->exec, context->runtime->stream));
+    e->launches = n * e->kernels_per_step;
     return VKLLM_ERR_OK;
 }
 
@@ -505,8 +713,9 @@ extern "C" vkllm_err_t vkllm_b200_engine_read_tokens(struct vkllm_context *conte
     VKB_CUDA(cudaMemcpy(&st, e->state, sizeof(st), cudaMemcpyDeviceToHost));
     if (st.error)
     {
-        log_error("decode step refused: position past the KV cache");
-        return VKLLM_ERR_ARGS;
+        log_error("decode step failed on the device (error word 0x%x: 0x1 position past the KV cache, "
+                  "0x100 copy wait timed out, 0x200 grid barrier timed out)", st.error);
+        return (st.error & ~1u) ? VKLLM_ERR_VULKAN : VKLLM_ERR_ARGS;
     }
     VKB_CUDA(cudaMemcpy(out, e->ring, (size_t)n * 4, cudaMemcpyDeviceToHost));
     return VKLLM_ERR_OK;
@@ -528,7 +737,8 @@ extern "C" uint32_t vkllm_b200_engine_kernels_per_step(struct vkllm_context *con
 {
     if (!context || !model || !model->b200.engine)
         return 0;
-    return ((Engine *)model->b200.engine)->kernels_per_step;
+    Engine *e = (Engine *)model->b200.engine;
+    return e->persistent ? 1u : e->kernels_per_step;
 }
 
 // Times `iters` back-to-back launches of one decode kernel (layers cycled so each launch streams
@@ -715,4 +925,72 @@ extern "C" vkllm_err_t vkllm_b200_attention_decode_noalloc(const void *q, const 
                                                 (float *)(sb + kNoAllocOffOpart), counters, (__half *)out, st);
     VKB_CUDA(cudaGetLastError());
     return VKLLM_ERR_OK;
+}
+
+extern "C" uint32_t vkllm_b200_engine_last_launches(struct vkllm_context *context, struct vkllm_models_llama2 *model)
+{
+    if (!context || !model || !model->b200.engine)
+        return 0;
+    return ((Engine *)model->b200.engine)->launches;
+}
+
+extern "C" int vkllm_b200_engine_is_persistent(struct vkllm_context *context, struct vkllm_models_llama2 *model)
+{
+    if (!context || !model || !model->b200.engine)
+        return 0;
+    return ((Engine *)model->b200.engine)->persistent ? 1 : 0;
+}
+
+// Copies the barrier timestamps of the last persistent launch (CTA 0, %globaltimer ns): entry 0 is
+// the kernel start, then one (arrival, release) pair per grid barrier. Returns the entry count.
+extern "C" uint32_t vkllm_b200_engine_read_trace(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                 uint64_t *out, uint32_t cap)
+{
+    if (!context || !model || !model->b200.engine || !out)
+        return 0;
+    Engine *e = (Engine *)model->b200.engine;
+    if (!e->pp.trace)
+        return 0;
+    cudaStreamSynchronize(context->runtime->stream);
+    uint32_t n = cap < e->pp.trace_cap ? cap : e->pp.trace_cap;
+    if (cudaMemcpy(out, e->pp.trace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+// %globaltimer of the last CTA's arrival per trace entry (at the release entry index of each grid
+// barrier; other entries undefined). Returns the entry count, 0 when tracing is off.
+extern "C" uint32_t vkllm_b200_engine_read_trace_last(struct vkllm_context *context,
+                                                      struct vkllm_models_llama2 *model, uint64_t *out,
+                                                      uint32_t cap)
+{
+    if (!context || !model || !model->b200.engine || !out)
+        return 0;
+    Engine *e = (Engine *)model->b200.engine;
+    if (!e->pp.trace_last)
+        return 0;
+    cudaStreamSynchronize(context->runtime->stream);
+    uint32_t n = cap < e->pp.trace_cap ? cap : e->pp.trace_cap;
+    if (cudaMemcpy(out, e->pp.trace_last, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+// Per-warp pipeline accounting of CTA 0 accumulated over all persistent launches since the engine
+// was built (SM cycles): [warp][kind QKV, Wo, up/gate, down, logits][wait, consume, chunks, the
+// compute share of consume]. Returns the entry count (32 * 5 * 4), 0 when tracing is off.
+extern "C" uint32_t vkllm_b200_engine_read_warp_trace(struct vkllm_context *context,
+                                                      struct vkllm_models_llama2 *model, uint64_t *out,
+                                                      uint32_t cap)
+{
+    const uint32_t n = kStreamMaxWarps * PK_COUNT * 4;
+    if (!context || !model || !model->b200.engine || !out || cap < n)
+        return 0;
+    Engine *e = (Engine *)model->b200.engine;
+    if (!e->pp.wtrace)
+        return 0;
+    cudaStreamSynchronize(context->runtime->stream);
+    if (cudaMemcpy(out, e->pp.wtrace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    return n;
 }

@@ -163,6 +163,11 @@ _SIGS = {
     "vkllm_b200_engine_read_tokens": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
     "vkllm_b200_engine_read_logits": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
     "vkllm_b200_engine_kernels_per_step": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2)]),
+    "vkllm_b200_engine_last_launches": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2)]),
+    "vkllm_b200_engine_is_persistent": (C.c_int, [C.c_void_p, C.POINTER(Llama2)]),
+    "vkllm_b200_engine_read_trace": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
+    "vkllm_b200_engine_read_warp_trace": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
+    "vkllm_b200_engine_read_trace_last": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
     "vkllm_b200_engine_bench_kernel": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
                                                  C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
     "vkllm_b200_attention_decode_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
