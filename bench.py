@@ -193,6 +193,8 @@ def run_ours(args, world, rank, local):
     import vkllm_b200 as vk
 
     cfg = dict(CFG_7B)
+    if args.layers:
+        cfg["block_count"] = args.layers
     ctx = vk.Context(local)
     model = vk.Model(ctx).init_random(cfg, SEED)
     l = vk.lib()
@@ -202,7 +204,10 @@ def run_ours(args, world, rank, local):
     # Prefill through the drop-in API (timed separately, reported as prefill tok/s).
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    first = model.step(list(prompt), 0)
+    if args.no_extras:  # profiling case: skip the prefill graph; decode starts at position PROMPT_LEN anyway
+        first = int(prompt[-1])
+    else:
+        first = model.step(list(prompt), 0)
     prefill_s = time.perf_counter() - t0
     model.engine_prepare()
     kps = l.vkllm_b200_engine_kernels_per_step(ctx.ptr, C.byref(model.m))
@@ -229,6 +234,15 @@ def run_ours(args, world, rank, local):
     barrier(world)
     t_max = max_over_ranks(world, dev_ms)
     value = world * K / (t_max / 1000.0)
+
+    if args.no_extras:
+        if rank == 0:
+            print(json.dumps({"profile_case": True, "layers": cfg["block_count"], "steps": K, "warmup": W,
+                              "ms_per_step": round(t_max / K, 4), "persistent": persistent, "launches": launches}),
+                  flush=True)
+        model.free()
+        ctx.close()
+        return None
 
     # ---- dominant-kernel roofline (FFN up/gate GEMV, the largest weight stream of a step) --------
     us, nbytes = C.c_float(), C.c_uint64()
@@ -409,6 +423,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # Profiling case only (ncu): fewer layers, no prefill / e2e / per-kernel extras, no JSON result line.
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--no-extras", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_setup() if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
