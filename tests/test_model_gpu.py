@@ -105,3 +105,30 @@ def test_random_init_matches_host_generator(vk, ctx):
         assert np.array_equal(wq, vk.random_f16_host(99, 3, 0.02, 0, wq.size))
     finally:
         model.free()
+
+
+def test_gguf_loader_matches_the_gguf_reader(vk, ctx, tiny_gguf):
+    """The C++ GGUF loader (the gguf-tools call sites of src/models/vkllm_models_llama2.c:185-392)
+    against the `gguf` package's reader on the same file: every tensor's bytes, after upload and
+    download, are identical."""
+    import gguf
+
+    path, _ = tiny_gguf
+    rd = gguf.GGUFReader(path)
+    want = {t.name: np.asarray(t.data).reshape(-1) for t in rd.tensors}
+    model = vk.Model(ctx).load(path)
+    try:
+        w = model.m.weights
+        got = {"token_embd.weight": vk.fetch(ctx, w.tok_embed_weights), "output.weight": vk.fetch(ctx, w.output_weight),
+               "output_norm.weight": vk.fetch(ctx, w.output_norm_weight)}
+        names = {"attn_norm_weight": "attn_norm", "ffn_norm_weight": "ffn_norm", "WQ": "attn_q", "WK": "attn_k",
+                 "WV": "attn_v", "WO": "attn_output", "WG": "ffn_gate", "WU": "ffn_up", "WD": "ffn_down"}
+        for l in range(model.meta.block_count):
+            bw = model.block(l)
+            for f, n in names.items():
+                got[f"blk.{l}.{n}.weight"] = vk.fetch(ctx, getattr(bw, f))
+    finally:
+        model.free()
+    assert set(got) == set(want)
+    for n, a in want.items():
+        assert got[n].reshape(-1).tobytes() == a.tobytes(), n
