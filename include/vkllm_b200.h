@@ -110,6 +110,18 @@ extern uint32_t vkllm_b200_engine_read_trace_last(struct vkllm_context *context,
  * Needs cap >= 640; returns 640, or 0 when tracing is off. */
 extern uint32_t vkllm_b200_engine_read_warp_trace(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                                   uint64_t *out, uint32_t cap);
+/* Tensor-core GEMM (tcgen05 + TMEM, TMA-fed): C = act(scale * A . B^T) for fp16 A [M, K] (row
+ * stride lda elements), B [N, K] (row stride ldb), C [M, N] (row stride ldc), fp32 accumulation,
+ * act 1 = SiLU. Device pointers, 16-byte aligned; K, lda and ldb multiples of 8. Enqueued on
+ * `stream` (a cudaStream_t, NULL = default stream). Returns VKLLM_ERR_ARGS when the shape or the
+ * alignment does not fit, VKLLM_ERR_VULKAN on a launch error. It is the kernel behind
+ * VKLLM_OP_MATMUL (src/core/vkllm_op_matmul.c:212-315) for fp16 operands with M > 1 and B [N, K]. */
+extern vkllm_err_t vkllm_b200_gemm_f16(const void *A, const void *B, void *C, uint32_t M, uint32_t N, uint32_t K,
+                                       uint64_t lda, uint64_t ldb, uint64_t ldc, float scale, int act, void *stream);
+/* Sticky error word of the tensor-core GEMM on the current device: 0, or bit 0 when one of its
+ * bounded waits expired (the results of that launch are not valid). */
+extern uint32_t vkllm_b200_gemm_f16_error(void);
+
 /* 1 when the engine runs the persistent decode kernel. */
 extern int vkllm_b200_engine_is_persistent(struct vkllm_context *context, struct vkllm_models_llama2 *model);
 

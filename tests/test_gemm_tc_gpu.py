@@ -1,0 +1,71 @@
+"""The tcgen05 tensor-core GEMM (vkllm_b200_gemm_f16, the kernel behind VKLLM_OP_MATMUL for fp16
+M > 1) against a plain PyTorch fp32 reference of the same op: C = act(scale * A . B^T), fp16 out.
+
+Shapes: the BASELINE prefill GEMMs (M 512 x (N, K) in {(4096, 4096), (11008, 4096), (4096, 11008)}),
+the batched-decode M = 64, odd tails in M, N and K (TMA zero fill), SiLU and a scale. Tolerance:
+fp16 output rounding plus fp32 accumulation-order differences, |d| <= 1e-2 * max|ref| + 2 fp16 ulps.
+The kernel's sticky error word must stay 0 (no bounded wait expired)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def run_gemm(vk, torch, M, N, K, scale=1.0, act=0, lda=None, ldb=None, ldc=None, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    lda, ldb, ldc = lda or K, ldb or K, ldc or N
+    A = (torch.rand((M, lda), generator=g, device="cuda") * 2 - 1).half()
+    B = (torch.rand((N, ldb), generator=g, device="cuda") * 2 - 1).half()
+    Cm = torch.full((M, ldc), float("nan"), device="cuda", dtype=torch.float16)
+    s = torch.cuda.current_stream().cuda_stream
+    err = vk.lib().vkllm_b200_gemm_f16(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, N, K, lda, ldb, ldc, scale, act, s)
+    assert err == vk.OK
+    torch.cuda.synchronize()
+    assert vk.lib().vkllm_b200_gemm_f16_error() == 0
+    ref = (A[:, :K].float() @ B[:, :K].float().T) * scale
+    if act:
+        ref = ref / (1.0 + torch.exp(-ref))
+    return Cm[:, :N].float(), ref, Cm
+
+
+def check(got, ref):
+    tol = 1e-2 * ref.abs().max().item() + 2 * 2.0 ** -10 * ref.abs()
+    bad = (got - ref).abs() > tol
+    assert not bool(bad.any()), f"{int(bad.sum())} of {bad.numel()} off; max diff {(got - ref).abs().max().item()}"
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return torch
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (128, 128, 128), (512, 4096, 4096), (512, 11008, 4096),
+                                   (512, 4096, 11008), (64, 4096, 4096), (33, 65, 264), (300, 1000, 1032),
+                                   (1, 512, 512), (700, 384, 96)])
+def test_gemm_matches_torch_fp32(vk, torch_cuda, M, N, K):
+    got, ref, _ = run_gemm(vk, torch_cuda, M, N, K, seed=M + N + K)
+    check(got, ref)
+
+
+def test_gemm_scale_and_silu(vk, torch_cuda):
+    got, ref, _ = run_gemm(vk, torch_cuda, 200, 520, 320, scale=0.125, act=1, seed=5)
+    check(got, ref)
+
+
+def test_gemm_strided_operands_leave_padding_untouched(vk, torch_cuda):
+    got, ref, Cm = run_gemm(vk, torch_cuda, 96, 200, 128, lda=136, ldb=144, ldc=208, seed=9)
+    check(got, ref)
+    assert bool(torch_cuda.isnan(Cm[:, 200:]).all())  # columns past N are not written
+
+
+def test_gemm_rejects_unaligned_k(vk, torch_cuda):
+    lib = vk.lib()
+    buf = torch_cuda.zeros(4096, device="cuda", dtype=torch_cuda.float16)
+    p = buf.data_ptr()
+    assert lib.vkllm_b200_gemm_f16(p, p, p, 4, 4, 12, 12, 12, 4, 1.0, 0, None) == vk.ARGS  # K % 8 != 0

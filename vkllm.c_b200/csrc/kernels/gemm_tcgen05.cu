@@ -1,21 +1,494 @@
-// Tensor-core GEMM for sm_100a (tcgen05). Placeholder dispatch: the tensor-core kernel is not
-// enabled yet, so every GEMM runs on the CUDA-core kernel of ops/op_matmul.cu.
+// Tensor-core GEMM for sm_100a: C[z] = act(scale * A[z] . B[z]^T), fp16 A [M, K] and B [N, K]
+// (both K-contiguous), fp32 accumulation in tensor memory, fp16 C [M, N].
+//
+// One CTA computes a 128 x BN tile of C:
+//   warp 4 (one lane)  TMA producer: 2-D boxes of 64 K-elements (128 B, 128-byte swizzle) x 128 rows
+//                      of A and x BN rows of B into a ring of shared-memory stages (full barriers);
+//   warp 5             allocates BN tensor-memory columns; one lane issues tcgen05.mma
+//                      (kind::f16, M = 128, N = BN, K = 16 per instruction, 4 per stage) and
+//                      tcgen05.commit frees each stage (empty barriers) and finally signals `done`;
+//   warps 0-3          epilogue: tcgen05.ld of their 32 accumulator lanes (rows), scale, SiLU,
+//                      fp16 stores with bounds checks.
+// Rows and K beyond the operands are zero-filled by TMA, so any M, N and K (K a multiple of 8)
+// work. Every wait is bounded (2 s of %globaltimer): on expiry the CTA records an error, lets the
+// copies and MMAs it issued complete (bounded again), frees its tensor memory and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "kernels.h"
 
 namespace vkb
 {
+namespace
+{
+
+constexpr uint32_t kBM = 128, kBK = 64;
+constexpr uint64_t kTcWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t su32(const void *p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t gtime()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool try_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.b32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok)
+                 : "r"(su32(bar)), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, uint64_t limit)
+{
+    if (try_wait(bar, parity))
+        return true;
+    const uint64_t t0 = gtime();
+    while (!try_wait(bar, parity))
+        if (gtime() - t0 > limit)
+            return false;
+    return true;
+}
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose 8-row groups are
+// 1024 B apart (the layout TMA writes for a 64 x rows fp16 box): start address >> 4 in bits
+// [0, 14), leading byte offset 1 (unused for swizzled K-major), stride byte offset 1024 >> 4 in
+// bits [32, 46), descriptor version 1 in bits [46, 48), layout SWIZZLE_128B (2) in bits [61, 64).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of kind::f16: D fp32 (bits [4, 6) = 1), A and B fp16 (formats 0), both
+// K-major, N >> 3 in bits [17, 23), M >> 4 in bits [24, 29).
+__host__ __device__ constexpr uint32_t f16_idesc(uint32_t M, uint32_t N)
+{
+    return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1, int32_t c2,
+                                            int32_t c3, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+                 "%4, %5}], [%6];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(su32(bar))
+                 : "memory");
+}
+
+template <int N> struct TileCfg
+{
+    static constexpr uint32_t kStages = N == 256 ? 4 : 6;
+    static constexpr uint32_t kABytes = kBM * kBK * 2;
+    static constexpr uint32_t kBBytes = (uint32_t)N * kBK * 2;
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kSmem = 1024 /* alignment slack */ + kStages * kStageBytes + 256 /* barriers */;
+};
+
+struct TcParams
+{
+    uint32_t M, N, K;
+    uint64_t ldc;
+    uint32_t batch_c;
+    uint32_t a_bc, a_cc, b_bc, b_cc; // 1 where the operand's b / c index is broadcast (use 0)
+    uint64_t c_sb, c_sc;
+    float scale;
+    int act;
+    __half *C;
+    uint32_t *err;
+};
+
+// Epilogue of 32 consecutive accumulator columns of one row: scale, SiLU when act, fp16.
+__device__ __forceinline__ void store_row32(__half *crow, uint32_t nb, const uint32_t (&r)[32], const TcParams &p)
+{
+    __half h[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+    {
+        float v = __uint_as_float(r[j]) * p.scale;
+        if (p.act)
+            v = v / (1.0f + expf(-v)); // SiLU as the reference evaluates it
+        h[j] = __float2half_rn(v);
+    }
+    if (nb + 32 <= p.N && (p.ldc % 8) == 0 && ((reinterpret_cast<uintptr_t>(crow) & 15) == 0))
+    {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            reinterpret_cast<uint4 *>(crow + nb)[j] = reinterpret_cast<const uint4 *>(h)[j];
+    }
+    else
+    {
+        for (uint32_t j = 0; j < 32 && nb + j < p.N; ++j)
+            crow[nb + j] = h[j];
+    }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
+                                                     const __grid_constant__ CUtensorMap tmB, TcParams p)
+{
+    using Cfg = TileCfg<BN>;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t base = (su32(smem_raw) + 1023u) & ~1023u; // 1024-B aligned stages (swizzle atoms)
+    unsigned char *smem = smem_raw + (base - su32(smem_raw));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + Cfg::kStages * Cfg::kStageBytes);
+    uint64_t *empty = full + Cfg::kStages;
+    uint64_t *done = empty + Cfg::kStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    __shared__ uint32_t fail_s;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM, z = blockIdx.z;
+    const uint32_t zb = z / p.batch_c, zc = z % p.batch_c;
+    const uint32_t kb_n = (p.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0)
+    {
+        for (uint32_t s = 0; s < Cfg::kStages; ++s)
+        {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&full[s])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&empty[s])));
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(done)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fail_s = 0;
+    }
+    if (warp == 5)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                     "r"((uint32_t)BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4 && lane == 0)
+    {
+        // Producer.
+        const int32_t ca = p.a_cc ? 0 : (int32_t)zc, ba = p.a_bc ? 0 : (int32_t)zb;
+        const int32_t cb = p.b_cc ? 0 : (int32_t)zc, bb = p.b_bc ? 0 : (int32_t)zb;
+        uint32_t issued = 0;
+        bool ok = true;
+        for (uint32_t kb = 0; kb < kb_n; ++kb)
+        {
+            const uint32_t s = kb % Cfg::kStages, n = kb / Cfg::kStages;
+            if (n > 0 && !wait_bounded(&empty[s], (n - 1) & 1u, kTcWaitNs))
+            {
+                ok = false;
+                break;
+            }
+            const uint32_t sa = base + s * Cfg::kStageBytes, sb = sa + Cfg::kABytes;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])),
+                         "r"(Cfg::kStageBytes)
+                         : "memory");
+            tma_load_4d(sa, &tmA, (int32_t)(kb * kBK), (int32_t)m0, ca, ba, &full[s]);
+            tma_load_4d(sb, &tmB, (int32_t)(kb * kBK), (int32_t)n0, cb, bb, &full[s]);
+            ++issued;
+        }
+        if (!ok)
+        {
+            atomicOr(p.err, 1u);
+            fail_s = 1;
+            // the stages issued and not yet consumed must land before the CTA exits
+            for (uint32_t kb = issued > Cfg::kStages ? issued - Cfg::kStages : 0; kb < issued; ++kb)
+                (void)wait_bounded(&full[kb % Cfg::kStages], (kb / Cfg::kStages) & 1u, kTcWaitNs / 4);
+        }
+    }
+    else if (warp == 5 && lane == 0)
+    {
+        // MMA issuer.
+        constexpr uint32_t idesc = f16_idesc(kBM, BN);
+        bool ok = true;
+        for (uint32_t kb = 0; kb < kb_n; ++kb)
+        {
+            const uint32_t s = kb % Cfg::kStages;
+            if (!wait_bounded(&full[s], (kb / Cfg::kStages) & 1u, kTcWaitNs))
+            {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t sa = base + s * Cfg::kStageBytes, sb = sa + Cfg::kABytes;
+#pragma unroll
+            for (uint32_t k = 0; k < kBK / 16; ++k)
+            {
+                const uint64_t da = sw128_desc(sa + 32 * k), db = sw128_desc(sb + 32 * k);
+                const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+                             "l"(da), "l"(db), "r"(idesc), "r"(acc));
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             su32(&empty[s]))
+                         : "memory");
+        }
+        if (!ok)
+        {
+            atomicOr(p.err, 1u);
+            fail_s = 1;
+        }
+        // Signals the epilogue once every MMA issued above has completed (also on the error path,
+        // so that the tensor memory is idle before it is freed).
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(done))
+                     : "memory");
+    }
+    else if (warp < 4)
+    {
+        // Epilogue: row m0 + 32 * warp + lane of the tile, 32 accumulator columns per load.
+        const bool ok = wait_bounded(done, 0, 2 * kTcWaitNs);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (__all_sync(0xffffffffu, ok) && !fail_s)
+        {
+            const uint32_t row = m0 + 32 * warp + lane;
+            __half *crow = p.C + zb * p.c_sb + zc * p.c_sc + (uint64_t)row * p.ldc;
+            const uint32_t taddr = tmem + ((32 * warp) << 16);
+#pragma unroll 1
+            for (uint32_t c = 0; c < (uint32_t)BN; c += 32)
+            {
+                uint32_t r[32];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+                             "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+                             "%28, %29, %30, %31}, [%32];"
+                             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                               "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                               "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+                               "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+                               "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                             : "r"(taddr + c));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                const uint32_t nb = n0 + c;
+                if (row < p.M && nb < p.N)
+                    store_row32(crow, nb, r, p);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 5)
+    {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            (void)cudaGetLastError();
+    });
+    return fn;
+}
+
+// 4-D map {K, rows, C, B} of an fp16 operand (K innermost), box {64, box_rows, 1, 1}, 128-byte
+// swizzle, zero fill outside. Broadcast dimensions get extent 1.
+bool encode_operand(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, uint64_t ld, uint32_t ext_c,
+                    uint64_t sc, uint32_t ext_b, uint64_t sb, uint32_t box_rows)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+    if (!fn)
+        return false;
+    const uint64_t row_b = ld * 2;
+    const uint64_t c_b = ext_c > 1 ? sc * 2 : row_b * rows;
+    const uint64_t b_b = ext_b > 1 ? sb * 2 : c_b * ext_c;
+    cuuint64_t dims[4] = {K, rows, ext_c, ext_b};
+    cuuint64_t strides[3] = {row_b, c_b, b_b};
+    cuuint32_t box[4] = {kBK, box_rows, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (row_b % 16 || c_b % 16 || b_b % 16 || (reinterpret_cast<uintptr_t>(ptr) & 15))
+        return false;
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+uint32_t *error_word(int dev)
+{
+    static uint32_t *words[64] = {};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64)
+        return nullptr;
+    if (!words[dev])
+    {
+        if (cudaMalloc(&words[dev], sizeof(uint32_t)) != cudaSuccess || cudaMemset(words[dev], 0, 4) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            words[dev] = nullptr;
+        }
+    }
+    return words[dev];
+}
+
+template <int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
+{
+    using Cfg = TileCfg<BN>;
+    int dev = 0, cc = 0, optin = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return false;
+    cudaDeviceGetAttribute(&cc, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (cc != 10 || (uint32_t)optin < Cfg::kSmem)
+        return false;
+    static bool attr_set[64] = {};
+    if (dev < 64 && !attr_set[dev])
+    {
+        if (cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) !=
+            cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            return false;
+        }
+        attr_set[dev] = true;
+    }
+    const uint32_t batch_b = g.batch / g.batch_c;
+    CUtensorMap ma, mb;
+    // broadcast dimensions (stride 0) are described with extent 1 and indexed 0 by the kernel
+    if (!encode_operand(&ma, g.A, g.K, g.M, g.lda, g.a_sc ? g.batch_c : 1, g.a_sc, g.a_sb ? batch_b : 1, g.a_sb, kBM))
+        return false;
+    if (!encode_operand(&mb, g.B, g.K, g.N, g.ldb, g.b_sc ? g.batch_c : 1, g.b_sc, g.b_sb ? batch_b : 1, g.b_sb, BN))
+        return false;
+    TcParams p{};
+    p.M = g.M;
+    p.N = g.N;
+    p.K = g.K;
+    p.ldc = g.ldc;
+    p.batch_c = g.batch_c;
+    p.a_bc = g.a_sb == 0;
+    p.a_cc = g.a_sc == 0;
+    p.b_bc = g.b_sb == 0;
+    p.b_cc = g.b_sc == 0;
+    p.c_sb = g.c_sb;
+    p.c_sc = g.c_sc;
+    p.scale = g.scale;
+    p.act = g.act;
+    p.C = (__half *)g.C;
+    p.err = error_word(dev);
+    if (!p.err)
+        return false;
+    dim3 grid((g.N + BN - 1) / BN, (g.M + kBM - 1) / kBM, g.batch);
+    k_gemm_tc<BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
+    return cudaGetLastError() == cudaSuccess;
+}
+
+} // namespace
 
 bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool trans_b, const void *a, const void *b,
                     void *c, float scale, int act, GemmArgs *g)
 {
-    (void)da, (void)db, (void)dc, (void)trans_b, (void)a, (void)b, (void)c, (void)scale, (void)act, (void)g;
-    return false;
+    // A [Ba, Ca, M, K], B [Bb, Cb, N, K] (trans_b), C [B, C, M, N]; unit inner strides; row and batch
+    // strides multiples of 8 elements; 16-byte aligned bases.
+    if (!trans_b)
+        return false;
+    if (da.stride[3] != 1 || db.stride[3] != 1 || dc.stride[3] != 1)
+        return false;
+    const uint32_t M = dc.shape[2], N = dc.shape[3], K = da.shape[3];
+    if (db.shape[3] != K || db.shape[2] != N || da.shape[2] != M || K == 0 || M == 0 || N == 0)
+        return false;
+    if (K % 8 || da.stride[2] % 8 || db.stride[2] % 8)
+        return false;
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!al16(a) || !al16(b) || !al16(c))
+        return false;
+    const uint32_t Bc = dc.shape[0], Cc = dc.shape[1];
+    for (int i = 0; i < 2; ++i)
+    {
+        if ((da.shape[i] != 1 && da.shape[i] != dc.shape[i]) || (db.shape[i] != 1 && db.shape[i] != dc.shape[i]))
+            return false;
+        if (da.stride[i] % 8 || db.stride[i] % 8)
+            return false;
+    }
+    g->A = a;
+    g->B = b;
+    g->C = c;
+    g->M = M;
+    g->N = N;
+    g->K = K;
+    g->lda = da.stride[2];
+    g->ldb = db.stride[2];
+    g->ldc = dc.stride[2];
+    g->batch_c = Cc;
+    g->batch = Bc * Cc;
+    g->a_sb = da.shape[0] == 1 ? 0 : da.stride[0];
+    g->a_sc = da.shape[1] == 1 ? 0 : da.stride[1];
+    g->b_sb = db.shape[0] == 1 ? 0 : db.stride[0];
+    g->b_sc = db.shape[1] == 1 ? 0 : db.stride[1];
+    g->c_sb = dc.stride[0];
+    g->c_sc = dc.stride[1];
+    g->scale = scale;
+    g->act = act;
+    return true;
 }
 
 bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
 {
-    (void)g, (void)s;
-    return false;
+    if (g.batch == 0 || g.batch_c == 0)
+        return false;
+    // 128 x 256 tiles when they still cover the SMs, 128 x 128 otherwise.
+    const uint64_t tiles256 = (uint64_t)((g.N + 255) / 256) * ((g.M + kBM - 1) / kBM) * g.batch;
+    if (tiles256 >= 148)
+        return launch_tc<256>(g, s);
+    return launch_tc<128>(g, s);
+}
+
+uint32_t gemm_tcgen05_error(int dev)
+{
+    uint32_t *w = error_word(dev), v = 0;
+    if (!w || cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0xffffffffu;
+    return v;
 }
 
 } // namespace vkb
+
+// ------------------------------------------------------------------------------------------------
+// C-ABI: the tensor-core GEMM on raw device pointers (declared in include/vkllm_b200.h).
+#include "vkllm_errors.h"
+
+extern "C" vkllm_err_t vkllm_b200_gemm_f16(const void *A, const void *B, void *C, uint32_t M, uint32_t N, uint32_t K,
+                                           uint64_t lda, uint64_t ldb, uint64_t ldc, float scale, int act,
+                                           void *stream)
+{
+    if (!A || !B || !C || M == 0 || N == 0 || K == 0 || lda < K || ldb < K || ldc < N)
+        return VKLLM_ERR_ARGS;
+    vkb::Desc4 da{{1, 1, M, K}, {0, 0, (uint32_t)lda, 1}};
+    vkb::Desc4 db{{1, 1, N, K}, {0, 0, (uint32_t)ldb, 1}};
+    vkb::Desc4 dc{{1, 1, M, N}, {0, 0, (uint32_t)ldc, 1}};
+    vkb::GemmArgs g;
+    if (lda > 0xffffffffull || ldb > 0xffffffffull || ldc > 0xffffffffull ||
+        !vkb::make_gemm_args(da, db, dc, true, A, B, C, scale, act, &g))
+        return VKLLM_ERR_ARGS;
+    if (!vkb::gemm_tcgen05_launch(g, (cudaStream_t)stream))
+    {
+        (void)cudaGetLastError();
+        return VKLLM_ERR_VULKAN;
+    }
+    return VKLLM_ERR_OK;
+}
+
+extern "C" uint32_t vkllm_b200_gemm_f16_error(void)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return 0xffffffffu;
+    return vkb::gemm_tcgen05_error(dev);
+}

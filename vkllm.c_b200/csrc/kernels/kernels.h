@@ -35,4 +35,7 @@ bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool tran
 // Enqueues the tcgen05 GEMM; returns false when it cannot run on this device / shape.
 bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s);
 
+// Sticky error word of the tcgen05 GEMM on device `dev` (bit 0: a bounded wait expired).
+uint32_t gemm_tcgen05_error(int dev);
+
 } // namespace vkb
