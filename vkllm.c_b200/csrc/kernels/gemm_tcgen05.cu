@@ -15,6 +15,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "kernels.h"
@@ -24,7 +26,7 @@ namespace vkb
 namespace
 {
 
-constexpr uint32_t kBM = 128, kBK = 64;
+constexpr uint32_t kBK = 64;
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t su32(const void *p)
@@ -86,12 +88,16 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
                  : "memory");
 }
 
-template <int N> struct TileCfg
+// Tile BM x N: BM = 128 (one accumulator) or 256 (two M = 128 accumulators side by side in tensor
+// memory, sharing each B tile, which halves the operand bytes per flop of a 128 x N tile).
+template <int BM, int N> struct TileCfg
 {
-    static constexpr uint32_t kStages = N == 256 ? 4 : 6;
-    static constexpr uint32_t kABytes = kBM * kBK * 2;
+    static constexpr uint32_t kAcc = BM / 128;
+    static constexpr uint32_t kABytes = (uint32_t)BM * kBK * 2;
     static constexpr uint32_t kBBytes = (uint32_t)N * kBK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kStages = (200u * 1024u) / kStageBytes;
+    static constexpr uint32_t kTmemCols = kAcc * N;
     static constexpr uint32_t kSmem = 1024 /* alignment slack */ + kStages * kStageBytes + 256 /* barriers */;
 };
 
@@ -133,11 +139,11 @@ __device__ __forceinline__ void store_row32(__half *crow, uint32_t nb, const uin
     }
 }
 
-template <int BN>
+template <int BM, int BN>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                      const __grid_constant__ CUtensorMap tmB, TcParams p)
 {
-    using Cfg = TileCfg<BN>;
+    using Cfg = TileCfg<BM, BN>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t base = (su32(smem_raw) + 1023u) & ~1023u; // 1024-B aligned stages (swizzle atoms)
     unsigned char *smem = smem_raw + (base - su32(smem_raw));
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     __shared__ uint32_t fail_s;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM, z = blockIdx.z;
+    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
     const uint32_t zb = z / p.batch_c, zc = z % p.batch_c;
     const uint32_t kb_n = (p.K + kBK - 1) / kBK;
 
@@ -166,7 +172,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     if (warp == 5)
     {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
-                     "r"((uint32_t)BN));
+                     "r"(Cfg::kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     }
@@ -193,7 +199,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])),
                          "r"(Cfg::kStageBytes)
                          : "memory");
-            tma_load_4d(sa, &tmA, (int32_t)(kb * kBK), (int32_t)m0, ca, ba, &full[s]);
+            tma_load_4d(sa, &tmA, (int32_t)(kb * kBK), (int32_t)m0, ca, ba, &full[s]); // BM rows
             tma_load_4d(sb, &tmB, (int32_t)(kb * kBK), (int32_t)n0, cb, bb, &full[s]);
             ++issued;
         }
@@ -209,7 +215,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     else if (warp == 5 && lane == 0)
     {
         // MMA issuer.
-        constexpr uint32_t idesc = f16_idesc(kBM, BN);
+        constexpr uint32_t idesc = f16_idesc(128, BN);
         bool ok = true;
         for (uint32_t kb = 0; kb < kb_n; ++kb)
         {
@@ -224,11 +230,17 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
 #pragma unroll
             for (uint32_t k = 0; k < kBK / 16; ++k)
             {
-                const uint64_t da = sw128_desc(sa + 32 * k), db = sw128_desc(sb + 32 * k);
+                const uint64_t db = sw128_desc(sb + 32 * k);
                 const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
-                             "l"(da), "l"(db), "r"(idesc), "r"(acc));
+#pragma unroll
+                for (uint32_t h = 0; h < Cfg::kAcc; ++h)
+                {
+                    // rows 128 h .. 128 h + 127 of the A tile (16 KB further per half) -> accumulator h
+                    const uint64_t da = sw128_desc(sa + h * (128 * 128) + 32 * k);
+                    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + h * BN),
+                                 "l"(da), "l"(db), "r"(idesc), "r"(acc));
+                }
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              su32(&empty[s]))
@@ -250,10 +262,12 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         const bool ok = wait_bounded(done, 0, 2 * kTcWaitNs);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (__all_sync(0xffffffffu, ok) && !fail_s)
+#pragma unroll 1
+            for (uint32_t h = 0; h < Cfg::kAcc; ++h)
         {
-            const uint32_t row = m0 + 32 * warp + lane;
+            const uint32_t row = m0 + 128 * h + 32 * warp + lane;
             __half *crow = p.C + zb * p.c_sb + zc * p.c_sc + (uint64_t)row * p.ldc;
-            const uint32_t taddr = tmem + ((32 * warp) << 16);
+            const uint32_t taddr = tmem + ((32 * warp) << 16) + h * BN;
 #pragma unroll 1
             for (uint32_t c = 0; c < (uint32_t)BN; c += 32)
             {
@@ -279,7 +293,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     if (warp == 5)
     {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols));
     }
 }
 
@@ -339,9 +353,9 @@ uint32_t *error_word(int dev)
     return words[dev];
 }
 
-template <int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
+template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
 {
-    using Cfg = TileCfg<BN>;
+    using Cfg = TileCfg<BM, BN>;
     int dev = 0, cc = 0, optin = 0;
     if (cudaGetDevice(&dev) != cudaSuccess)
         return false;
@@ -352,7 +366,7 @@ template <int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev])
     {
-        if (cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) !=
+        if (cudaFuncSetAttribute(k_gemm_tc<BM, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) !=
             cudaSuccess)
         {
             (void)cudaGetLastError();
@@ -363,7 +377,7 @@ template <int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
     const uint32_t batch_b = g.batch / g.batch_c;
     CUtensorMap ma, mb;
     // broadcast dimensions (stride 0) are described with extent 1 and indexed 0 by the kernel
-    if (!encode_operand(&ma, g.A, g.K, g.M, g.lda, g.a_sc ? g.batch_c : 1, g.a_sc, g.a_sb ? batch_b : 1, g.a_sb, kBM))
+    if (!encode_operand(&ma, g.A, g.K, g.M, g.lda, g.a_sc ? g.batch_c : 1, g.a_sc, g.a_sb ? batch_b : 1, g.a_sb, BM))
         return false;
     if (!encode_operand(&mb, g.B, g.K, g.N, g.ldb, g.b_sc ? g.batch_c : 1, g.b_sc, g.b_sb ? batch_b : 1, g.b_sb, BN))
         return false;
@@ -385,8 +399,8 @@ template <int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
     p.err = error_word(dev);
     if (!p.err)
         return false;
-    dim3 grid((g.N + BN - 1) / BN, (g.M + kBM - 1) / kBM, g.batch);
-    k_gemm_tc<BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+    k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
     return cudaGetLastError() == cudaSuccess;
 }
 
@@ -443,11 +457,35 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
 {
     if (g.batch == 0 || g.batch_c == 0)
         return false;
-    // 128 x 256 tiles when they still cover the SMs, 128 x 128 otherwise.
-    const uint64_t tiles256 = (uint64_t)((g.N + 255) / 256) * ((g.M + kBM - 1) / kBM) * g.batch;
-    if (tiles256 >= 148)
-        return launch_tc<256>(g, s);
-    return launch_tc<128>(g, s);
+    // The largest tile that still gives every SM a tile: 256 x 256, then 128 x 256, then 128 x 128.
+    auto tiles = [&](uint32_t bm, uint32_t bn) {
+        return (uint64_t)((g.N + bn - 1) / bn) * ((g.M + bm - 1) / bm) * g.batch;
+    };
+    const char *force = getenv("VKLLM_B200_GEMM_TILE");
+    if (force)
+    {
+        if (!strcmp(force, "256x256"))
+            return launch_tc<256, 256>(g, s);
+        if (!strcmp(force, "128x256"))
+            return launch_tc<128, 256>(g, s);
+        if (!strcmp(force, "128x128"))
+            return launch_tc<128, 128>(g, s);
+    }
+    // Pick the tile minimising waves x time per tile. Per K step, a 128 x 128 tile takes ~0.85 and a
+    // 256 x 256 tile ~1.64 of the time of a 128 x 256 tile (L2-to-SM operand bandwidth, measured on
+    // B200), so larger tiles win unless they leave SMs idle in the last wave.
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto cost = [&](uint32_t bm, uint32_t bn, double per_tile) {
+        return (double)((tiles(bm, bn) + sms - 1) / sms) * per_tile;
+    };
+    const double c128 = cost(128, 128, 0.85), c256 = cost(128, 256, 1.0), c2x = g.M > 128 ? cost(256, 256, 1.64) : 1e30;
+    if (c2x < c256 && c2x < c128)
+        return launch_tc<256, 256>(g, s);
+    if (c256 < c128)
+        return launch_tc<128, 256>(g, s);
+    return launch_tc<128, 128>(g, s);
 }
 
 uint32_t gemm_tcgen05_error(int dev)
