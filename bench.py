@@ -186,6 +186,47 @@ def cpu_decode_sample(weights, cfg, n_steps=3, threads=0):
     return n_steps / dt, used
 
 
+def prefill_gemm_roofline(vk, l, model, cfg, stream):
+    """Times the prefill GEMM shapes (M = prompt length) of one layer and the logits on the tensor-core
+    GEMM (vkllm_b200_gemm_f16) with the model's weights as B; TF/s against MEASURED_PEAKS bf16 burst."""
+    import torch
+
+    D, F, V = cfg["embedding_length"], cfg["ffn_length"], cfg["vocab_size"]
+    bw = model.block(0)
+    shapes = {"qkv/wo (4096x4096)": (bw.WQ, D, D), "up/gate (11008x4096)": (bw.WU, F, D),
+              "down (4096x11008)": (bw.WD, D, F), "logits (32000x4096)": (model.m.weights.output_weight, V, D)}
+    peak = 1656.1
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak = json.load(f).get("bf16_tflops", peak)
+    out = {}
+    M = PROMPT_LEN
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for name, (w, N, K) in shapes.items():
+        A = (torch.rand((M, K), generator=g, device="cuda") * 0.2 - 0.1).half()
+        Cm = torch.empty((M, N), device="cuda", dtype=torch.float16)
+        B = w.contents.data.dev
+        args = (A.data_ptr(), B, Cm.data_ptr(), M, N, K, K, K, N, 1.0, 0, stream.cuda_stream)
+        for _ in range(3):
+            vk.check(l.vkllm_b200_gemm_f16(*args), "gemm")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 10
+        e0.record(stream)
+        for _ in range(n):
+            l.vkllm_b200_gemm_f16(*args)
+        e1.record(stream)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / n
+        tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+        out[name] = {"M": M, "N": N, "K": K, "us": round(us, 2), "tflops": round(tf, 1), "frac": round(tf / peak, 4)}
+    if l.vkllm_b200_gemm_f16_error() != 0:
+        raise RuntimeError("tensor-core GEMM reported a timed-out wait")
+    out["peak_tflops"] = peak
+    out["peak_source"] = "MEASURED_PEAKS.json bf16_tflops (burst)"
+    return out
+
+
 def run_ours(args, world, rank, local):
     import numpy as np
     import torch
@@ -201,14 +242,18 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
     prompt = prompt_tokens(rank)
 
-    # Prefill through the drop-in API (timed separately, reported as prefill tok/s).
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
+    # Prefill through the drop-in API (timed separately, reported as prefill tok/s): one untimed
+    # warm-up prefill (first-use costs: kernel attributes, tensor maps, allocator growth), then the
+    # timed one over the same prompt and positions (it rewrites the same KV rows).
     if args.no_extras:  # profiling case: skip the prefill graph; decode starts at position PROMPT_LEN anyway
-        first = int(prompt[-1])
+        first, prefill_s = int(prompt[-1]), float("nan")
     else:
+        model.step(list(prompt), 0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
         first = model.step(list(prompt), 0)
-    prefill_s = time.perf_counter() - t0
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
     model.engine_prepare()
     kps = l.vkllm_b200_engine_kernels_per_step(ctx.ptr, C.byref(model.m))
 
@@ -253,6 +298,9 @@ def run_ours(args, world, rank, local):
         u2, b2 = C.c_float(), C.c_uint64()
         vk.check(l.vkllm_b200_engine_bench_kernel(ctx.ptr, C.byref(model.m), name, 32, C.byref(u2), C.byref(b2)), "k")
         kern[name.decode()] = {"us": round(u2.value, 2), "GBps": round(b2.value / (u2.value * 1e-6) / 1e9, 1)}
+
+    # ---- prefill GEMMs on the tensor cores (tcgen05), on the model's own weights --------------------
+    prefill_gemms = prefill_gemm_roofline(vk, l, model, cfg, stream)
 
     # ---- e2e: reference token loop through the C API, host buffers --------------------------------
     pos = PROMPT_LEN + W + K
@@ -330,7 +378,8 @@ def run_ours(args, world, rank, local):
             "decode_path": "persistent cooperative kernel" if persistent else "CUDA-graph of per-op kernels",
             "graph_path_kernels": kern,
             "prefill": {"tokens": PROMPT_LEN, "seconds": round(prefill_s, 4),
-                        "tok_s": round(PROMPT_LEN / prefill_s, 1), "path": "drop-in API"},
+                        "tok_s": round(PROMPT_LEN / prefill_s, 1), "path": "drop-in API (graph of op kernels, tcgen05 GEMMs)",
+                        "gemms": prefill_gemms},
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                     "steps": n_e2e, "path": "reference token loop through the C API (graph rebuilt per token)"},
             "gpu_launches": int(launches if persistent else kps * K),

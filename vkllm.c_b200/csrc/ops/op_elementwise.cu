@@ -204,6 +204,37 @@ template <typename TI, typename TO> __global__ void k_bin(const TI *a, const TI 
     }
 }
 
+// Dense fp16 operands, 8 elements per thread (16-byte loads and stores).
+template <typename TO> __global__ void k_bin_h8(const __half *a, const __half *bb, TO *out, uint64_t n8, int op)
+{
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < n8; t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint4 va = reinterpret_cast<const uint4 *>(a)[t], vb = reinterpret_cast<const uint4 *>(bb)[t];
+        const __half *ha = reinterpret_cast<const __half *>(&va), *hb = reinterpret_cast<const __half *>(&vb);
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            const float x = __half2float(ha[i]), y = __half2float(hb[i]);
+            r[i] = op == 0 ? x + y : (op == 1 ? x - y : (op == 2 ? x * y : x / y));
+        }
+        if constexpr (sizeof(TO) == 2)
+        {
+            uint4 o;
+            __half *ho = reinterpret_cast<__half *>(&o);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                ho[i] = __float2half_rn(r[i]);
+            reinterpret_cast<uint4 *>(out)[t] = o;
+        }
+        else
+        {
+            reinterpret_cast<float4 *>(out)[2 * t] = make_float4(r[0], r[1], r[2], r[3]);
+            reinterpret_cast<float4 *>(out)[2 * t + 1] = make_float4(r[4], r[5], r[6], r[7]);
+        }
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // EMBEDDING (src/shaders/vkllm_embedding.comp:41-70): one block per id. The reference addresses the
 // output with strides shifted by one axis (out = c*s0 + h*s1 + w*s2), which for ids [1,1,1,S] and
@@ -543,7 +574,19 @@ extern "C" vkllm_err_t vkllm_op_bin_run(vkllm_context *context, vkllm_commands *
     Desc4 d = desc_of(tensor);
     unsigned grid = grid_1d(d4_count(d), 256);
     timing_begin(context, tensor->pipeline, s);
-    if (in0->dtype == vkllm_dtype_float16)
+    const uint64_t n = d4_count(d);
+    const bool dense = d.stride[3] == 1 && d.stride[2] == d.shape[3] && d.stride[1] == (uint64_t)d.shape[2] * d.shape[3] &&
+                       d.stride[0] == (uint64_t)d.shape[1] * d.shape[2] * d.shape[3] && n % 8 == 0 &&
+                       (((uintptr_t)a | (uintptr_t)b | (uintptr_t)y) & 15) == 0;
+    if (in0->dtype == vkllm_dtype_float16 && dense)
+    {
+        const unsigned g8 = grid_1d(n / 8, 256);
+        if (tensor->dtype == vkllm_dtype_float16)
+            k_bin_h8<__half><<<g8, 256, 0, s>>>((const __half *)a, (const __half *)b, (__half *)y, n / 8, op);
+        else
+            k_bin_h8<float><<<g8, 256, 0, s>>>((const __half *)a, (const __half *)b, (float *)y, n / 8, op);
+    }
+    else if (in0->dtype == vkllm_dtype_float16)
     {
         if (tensor->dtype == vkllm_dtype_float16)
             k_bin<__half, __half><<<grid, 256, 0, s>>>((const __half *)a, (const __half *)b, (__half *)y, d, op);

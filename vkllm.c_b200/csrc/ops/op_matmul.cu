@@ -253,6 +253,60 @@ extern "C" vkllm_err_t vkllm_op_matmul_init(vkllm_context *context, vkllm_comman
     return dev_ptr(context, tensor) ? VKLLM_ERR_OK : VKLLM_ERR_ALLOC;
 }
 
+// B [Bb, Cb, K, N] (N contiguous) -> dense Bt [Bb * Cb][N][K]: 32 x 32 tiles through shared memory.
+__global__ void k_transpose_kn(const __half *__restrict__ b, Desc4 db, __half *__restrict__ bt)
+{
+    __shared__ __half tile[32][33];
+    const uint32_t K = db.shape[2], N = db.shape[3], z = blockIdx.z;
+    const uint32_t zb = z / db.shape[1], zc = z % db.shape[1];
+    const __half *src = b + (uint64_t)zb * db.stride[0] + (uint64_t)zc * db.stride[1];
+    __half *dst = bt + (uint64_t)z * N * K;
+    const uint32_t k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    for (uint32_t i = threadIdx.y; i < 32; i += blockDim.y)
+    {
+        const uint32_t k = k0 + i, n = n0 + threadIdx.x;
+        tile[i][threadIdx.x] = (k < K && n < N) ? src[(uint64_t)k * db.stride[2] + (uint64_t)n * db.stride[3]]
+                                                : __float2half(0.f);
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.y; i < 32; i += blockDim.y)
+    {
+        const uint32_t n = n0 + i, k = k0 + threadIdx.x;
+        if (n < N && k < K)
+            dst[(uint64_t)n * K + k] = tile[threadIdx.x][i];
+    }
+}
+
+// C = A . B for B read as [K, N] (the attention probs . V product): B is transposed into a dense
+// [N, K] scratch from the context's allocator, then the tensor-core GEMM runs with B^T. The scratch
+// goes back to the cache right after the enqueue; the context's single stream orders its reuse.
+bool matmul_tc_via_transpose(vkllm_context *context, const Desc4 &da, const Desc4 &db, const Desc4 &dc, const void *a,
+                             const void *b, void *c, float scale, int act, cudaStream_t s)
+{
+    const uint32_t K = db.shape[2], N = db.shape[3], zn = db.shape[0] * db.shape[1];
+    if (K % 8 != 0 || K != da.shape[3] || N != dc.shape[3] || zn == 0)
+        return false;
+    size_t cap = 0;
+    const size_t bytes = (size_t)zn * N * K * sizeof(__half);
+    void *bt = context->runtime->dev_alloc->alloc(bytes, &cap);
+    if (!bt)
+        return false;
+    k_transpose_kn<<<dim3((N + 31) / 32, (K + 31) / 32, zn), dim3(32, 8), 0, s>>>((const __half *)b, db, (__half *)bt);
+    Desc4 dbt;
+    dbt.shape[0] = db.shape[0];
+    dbt.shape[1] = db.shape[1];
+    dbt.shape[2] = N;
+    dbt.shape[3] = K;
+    dbt.stride[3] = 1;
+    dbt.stride[2] = K;
+    dbt.stride[1] = N * K;
+    dbt.stride[0] = db.shape[1] * N * K;
+    GemmArgs g;
+    bool ok = make_gemm_args(da, dbt, dc, true, a, bt, c, scale, act, &g) && gemm_tcgen05_launch(g, s);
+    context->runtime->dev_alloc->release(bt);
+    return ok;
+}
+
 extern "C" vkllm_err_t vkllm_op_matmul_run(vkllm_context *context, vkllm_commands *commands, vkllm_tensor *tensor)
 {
     _CHECK_ARGS(context && commands && tensor && tensor->srcs[0] && tensor->srcs[1]);
@@ -291,10 +345,12 @@ extern "C" vkllm_err_t vkllm_op_matmul_run(vkllm_context *context, vkllm_command
         bool done = false;
         if (f16)
         {
-            // Tensor-core path: A [M,K] and B [N,K] (or [K,N]) with unit inner stride.
+            // Tensor-core path: A [M,K] and B [N,K] with unit inner stride.
             GemmArgs g;
-            if (make_gemm_args(da, db, dc, tb, a, b, c, p->scale, p->act, &g))
+            if (tb && make_gemm_args(da, db, dc, tb, a, b, c, p->scale, p->act, &g))
                 done = gemm_tcgen05_launch(g, s);
+            else if (!tb)
+                done = matmul_tc_via_transpose(context, da, db, dc, a, b, c, p->scale, p->act, s);
         }
         if (!done)
         {
