@@ -44,8 +44,11 @@ enum PhaseKind : uint32_t
 constexpr uint32_t kErrBarrierTimeout = 0x200;
 constexpr uint32_t kErrPosition = 0x1;
 
+#ifndef VKB_PERSIST_SEG
+#define VKB_PERSIST_SEG 256
+#endif
 constexpr uint32_t kTileRows = 16;                        // MMA M
-constexpr uint32_t kSegHalves = 256;                      // columns per tile
+constexpr uint32_t kSegHalves = VKB_PERSIST_SEG;          // columns per tile (one bulk copy per row)
 constexpr uint32_t kRowPitch = 2 * kSegHalves + 16;       // bytes between tile rows in shared memory
 constexpr uint32_t kTileBytes = kTileRows * kRowPitch;    // one stage
 

@@ -112,7 +112,29 @@ struct TcParams
     int act;
     __half *C;
     uint32_t *err;
+    // Split-K: `splits` CTAs share a tile, each over kb_per k-blocks, writing fp32 partials to
+    // `ws` [split][z][M][N]; k_splitk_reduce sums them in split order and applies the epilogue.
+    uint32_t splits, kb_per;
+    float *ws;
 };
+
+// Split-K epilogue part: 32 fp32 partial columns of one row to the workspace.
+__device__ __forceinline__ void store_part32(float *wrow, uint32_t nb, const uint32_t (&r)[32], const TcParams &p)
+{
+    if (nb + 32 <= p.N && (p.N % 4) == 0)
+    {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            reinterpret_cast<float4 *>(wrow + nb)[j] =
+                make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                            __uint_as_float(r[4 * j + 3]));
+    }
+    else
+    {
+        for (uint32_t j = 0; j < 32 && nb + j < p.N; ++j)
+            wrow[nb + j] = __uint_as_float(r[j]);
+    }
+}
 
 // Epilogue of 32 consecutive accumulator columns of one row: scale, SiLU when act, fp16.
 __device__ __forceinline__ void store_row32(__half *crow, uint32_t nb, const uint32_t (&r)[32], const TcParams &p)
@@ -154,9 +176,10 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     __shared__ uint32_t fail_s;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z;
+    const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z / p.splits, split = blockIdx.z % p.splits;
     const uint32_t zb = z / p.batch_c, zc = z % p.batch_c;
-    const uint32_t kb_n = (p.K + kBK - 1) / kBK;
+    const uint32_t kb_all = (p.K + kBK - 1) / kBK;
+    const uint32_t kb_lo = split * p.kb_per, kb_n = min(kb_all, kb_lo + p.kb_per) - kb_lo; // >= 1 (host)
 
     if (threadIdx.x == 0)
     {
@@ -199,8 +222,8 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[s])),
                          "r"(Cfg::kStageBytes)
                          : "memory");
-            tma_load_4d(sa, &tmA, (int32_t)(kb * kBK), (int32_t)m0, ca, ba, &full[s]); // BM rows
-            tma_load_4d(sb, &tmB, (int32_t)(kb * kBK), (int32_t)n0, cb, bb, &full[s]);
+            tma_load_4d(sa, &tmA, (int32_t)((kb_lo + kb) * kBK), (int32_t)m0, ca, ba, &full[s]); // BM rows
+            tma_load_4d(sb, &tmB, (int32_t)((kb_lo + kb) * kBK), (int32_t)n0, cb, bb, &full[s]);
             ++issued;
         }
         if (!ok)
@@ -284,7 +307,13 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 const uint32_t nb = n0 + c;
                 if (row < p.M && nb < p.N)
-                    store_row32(crow, nb, r, p);
+                {
+                    if (p.splits > 1)
+                        store_part32(p.ws + (((uint64_t)split * gridDim.z / p.splits + z) * p.M + row) * p.N, nb, r,
+                                     p);
+                    else
+                        store_row32(crow, nb, r, p);
+                }
             }
         }
     }
@@ -295,6 +324,73 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Cfg::kTmemCols));
     }
+}
+
+// Sums the split-K partials in split order, then scale, SiLU and fp16 store (the epilogue of the
+// unsplit kernel). One thread per 4 columns.
+__global__ void k_splitk_reduce(const float *__restrict__ ws, TcParams p, uint32_t batch)
+{
+    const uint32_t n4 = (p.N + 3) / 4;
+    const uint64_t total = (uint64_t)batch * p.M * n4;
+    const uint64_t plane = (uint64_t)batch * p.M * p.N;
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t c4 = (uint32_t)(t % n4);
+        const uint64_t rz = t / n4;
+        const uint32_t row = (uint32_t)(rz % p.M), z = (uint32_t)(rz / p.M);
+        const uint32_t zb = z / p.batch_c, zc = z % p.batch_c;
+        __half *crow = p.C + zb * p.c_sb + zc * p.c_sc + (uint64_t)row * p.ldc;
+        const uint64_t off = ((uint64_t)z * p.M + row) * p.N;
+        for (uint32_t j = 0; j < 4; ++j)
+        {
+            const uint32_t n = 4 * c4 + j;
+            if (n >= p.N)
+                break;
+            float v = 0.f;
+            for (uint32_t sidx = 0; sidx < p.splits; ++sidx)
+                v += ws[sidx * plane + off + n];
+            v *= p.scale;
+            if (p.act)
+                v = v / (1.0f + expf(-v));
+            crow[n] = __float2half_rn(v);
+        }
+    }
+}
+
+// Per-device split-K workspace, grown on demand (never inside stream capture: growth fails there and
+// the caller runs without splitting).
+float *splitk_workspace(int dev, size_t bytes, cudaStream_t s)
+{
+    static float *ws[64] = {};
+    static size_t cap[64] = {};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64)
+        return nullptr;
+    if (cap[dev] >= bytes)
+        return ws[dev];
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &st) != cudaSuccess || st != cudaStreamCaptureStatusNone)
+    {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    (void)cudaGetLastError();
+    float *p = nullptr;
+    const size_t want = bytes < ((size_t)32 << 20) ? ((size_t)32 << 20) : bytes;
+    if (cudaMalloc(&p, want) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    if (ws[dev])
+    {
+        cudaDeviceSynchronize();
+        cudaFree(ws[dev]);
+    }
+    ws[dev] = p;
+    cap[dev] = want;
+    return p;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
@@ -353,7 +449,7 @@ uint32_t *error_word(int dev)
     return words[dev];
 }
 
-template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
+template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1)
 {
     using Cfg = TileCfg<BM, BN>;
     int dev = 0, cc = 0, optin = 0;
@@ -399,8 +495,29 @@ template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s)
     p.err = error_word(dev);
     if (!p.err)
         return false;
-    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch);
+    const uint32_t kb_all = (g.K + kBK - 1) / kBK;
+    if (splits > kb_all)
+        splits = kb_all;
+    p.kb_per = (kb_all + splits - 1) / splits;
+    p.splits = splits > 1 ? (kb_all + p.kb_per - 1) / p.kb_per : 1; // every split gets >= 1 k-block
+    p.ws = nullptr;
+    if (p.splits > 1)
+    {
+        p.ws = splitk_workspace(dev, (size_t)p.splits * g.batch * g.M * g.N * sizeof(float), s);
+        if (!p.ws)
+        {
+            p.splits = 1;
+            p.kb_per = kb_all;
+        }
+    }
+    dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch * p.splits);
     k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
+    if (p.splits > 1)
+    {
+        const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 3) / 4);
+        const unsigned blocks = (unsigned)((work + 255) / 256 < 148u * 8u ? (work + 255) / 256 : 148u * 8u);
+        k_splitk_reduce<<<blocks, 256, 0, s>>>(p.ws, p, g.batch);
+    }
     return cudaGetLastError() == cudaSuccess;
 }
 
@@ -480,6 +597,13 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
     auto cost = [&](uint32_t bm, uint32_t bn, double per_tile) {
         return (double)((tiles(bm, bn) + sms - 1) / sms) * per_tile;
     };
+    // Small M (GEMM-shaped decode): few tiles, weights-bound; split K so that every SM streams.
+    const uint64_t t128 = tiles(128, 128);
+    if (g.M <= 128 && t128 * 2 <= (uint64_t)sms)
+    {
+        const uint32_t splits = (uint32_t)((uint64_t)sms / t128) > 8 ? 8 : (uint32_t)((uint64_t)sms / t128);
+        return launch_tc<128, 128>(g, s, splits);
+    }
     const double c128 = cost(128, 128, 0.85), c256 = cost(128, 256, 1.0), c2x = g.M > 128 ? cost(256, 256, 1.64) : 1e30;
     if (c2x < c256 && c2x < c128)
         return launch_tc<256, 256>(g, s);

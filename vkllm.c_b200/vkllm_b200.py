@@ -11,7 +11,7 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libvkllm_b200.so")
+LIB_PATH = os.environ.get("VKLLM_B200_LIB_PATH") or os.path.join(HERE, "lib", "libvkllm_b200.so")
 
 OK, ALLOC, VULKAN, DEV_NOT_FOUND, PIPELINE_NOT_FOUND, ARGS = 1, 2, 3, 4, 5, 6
 F32, F16, I8, U32 = 1, 2, 3, 4
