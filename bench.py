@@ -227,6 +227,44 @@ def prefill_gemm_roofline(vk, l, model, cfg, stream):
     return out
 
 
+def batched_decode_leg(vk, model, args, world, rank, stream):
+    """64 independent sequences with their own 128-token seeded prompts, greedy
+    decode on the tensor-core GEMM path, sequences split evenly over the ranks (data parallel).
+    Returns aggregate tokens/s over all ranks (max-over-ranks device time)."""
+    import numpy as np
+    import torch
+
+    n_local = max(1, args.batch_seqs // world)
+    P, cap = 128, 384
+    rng = np.random.default_rng(SEED + 7)
+    prompts = [rng.integers(3, 32000, size=P, dtype=np.uint32) for _ in range(args.batch_seqs)]
+    mine = prompts[rank * n_local:(rank + 1) * n_local]
+    b = vk.Batch(model, len(mine), cap)
+    try:
+        for i, p in enumerate(mine):
+            b.add_prompt(i, p)
+        b.decode(3)  # warm-up (graph capture) at positions 128..130
+        K = args.batch_steps
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        b.decode(K)
+        e1.record(stream)
+        e1.synchronize()
+        ms = max_over_ranks(world, e0.elapsed_time(e1))
+    finally:
+        b.free()
+    D, L = 4096, 32
+    mean_lk = P + 3 + (K + 1) / 2.0
+    step_bytes = weight_bytes(CFG_7B) + n_local * L * 2 * D * 2 * mean_lk
+    peak, _ = measured_peaks()
+    return {"sequences": n_local * world, "per_rank": n_local, "steps": K, "prompt": P, "kv_rows": cap,
+            "tok_s": round(n_local * world * K / (ms / 1000.0), 1), "ms_per_step": round(ms / K, 4),
+            "hbm_frac_per_rank": round(step_bytes / (ms / K * 1e-3) / 1e9 / peak, 4),
+            "path": "tcgen05 GEMMs (M = sequences per rank, split-K) + per-sequence RoPE/KV/attention kernels, CUDA graph per step"}
+
+
 def run_ours(args, world, rank, local):
     import numpy as np
     import torch
@@ -301,6 +339,11 @@ def run_ours(args, world, rank, local):
 
     # ---- prefill GEMMs on the tensor cores (tcgen05), on the model's own weights --------------------
     prefill_gemms = prefill_gemm_roofline(vk, l, model, cfg, stream)
+
+    # ---- batched decode: 64 sequences split over the ranks -------------------
+    batched = None
+    if args.batch_seqs > 0:
+        batched = batched_decode_leg(vk, model, args, world, rank, stream)
 
     # ---- e2e: reference token loop through the C API, host buffers --------------------------------
     pos = PROMPT_LEN + W + K
@@ -380,6 +423,7 @@ def run_ours(args, world, rank, local):
             "prefill": {"tokens": PROMPT_LEN, "seconds": round(prefill_s, 4),
                         "tok_s": round(PROMPT_LEN / prefill_s, 1), "path": "drop-in API (graph of op kernels, tcgen05 GEMMs)",
                         "gemms": prefill_gemms},
+            "batched": batched,
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                     "steps": n_e2e, "path": "reference token loop through the C API (graph rebuilt per token)"},
             "gpu_launches": int(launches if persistent else kps * K),
@@ -472,6 +516,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch-seqs", type=int, default=64)
+    ap.add_argument("--batch-steps", type=int, default=32)
     # Profiling case only (ncu): fewer layers, no prefill / e2e / per-kernel extras, no JSON result line.
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-extras", action="store_true")

@@ -122,6 +122,32 @@ extern vkllm_err_t vkllm_b200_gemm_f16(const void *A, const void *B, void *C, ui
  * bounded waits expired (the results of that launch are not valid). */
 extern uint32_t vkllm_b200_gemm_f16_error(void);
 
+/* Batched greedy decode of independent sequences sharing the model's weights (no reference
+ * counterpart; the reference decodes one sequence per graph). Each sequence has its own KV cache of
+ * `kv_rows` rows per layer and head inside the batch. A step of all sequences runs the reference
+ * graph's nodes with S = 1 per sequence: projections as tensor-core GEMMs with M = n_seqs, RoPE /
+ * KV rows / attention / argmax per sequence, fp16 at every node.
+ *   vkllm_b200_batch_new            allocates the caches and activations (zeroed).
+ *   vkllm_b200_batch_load_sequence  copies rows [0, n_rows) of the model's own KV cache (written by a
+ *                                   prefill through vkllm_graph_run) into slot `seq`, whose next input
+ *                                   token is `next_token` at position n_rows.
+ *   vkllm_b200_batch_decode_steps   n greedy steps of every sequence (n <= 1024); VKLLM_ERR_ARGS if a
+ *                                   sequence would pass its KV capacity.
+ *   vkllm_b200_batch_read_tokens    tokens of the last decode call, [step][seq].
+ *   vkllm_b200_batch_read_logits    fp16 logits of the last step, [seq][vocab]. */
+struct vkllm_b200_batch;
+extern vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                        uint32_t n_seqs, uint32_t kv_rows, struct vkllm_b200_batch **out);
+extern vkllm_err_t vkllm_b200_batch_load_sequence(struct vkllm_context *context, struct vkllm_b200_batch *batch,
+                                                  uint32_t seq, uint32_t next_token, uint32_t n_rows);
+extern vkllm_err_t vkllm_b200_batch_decode_steps(struct vkllm_context *context, struct vkllm_b200_batch *batch,
+                                                 uint32_t n_steps);
+extern vkllm_err_t vkllm_b200_batch_read_tokens(struct vkllm_context *context, struct vkllm_b200_batch *batch,
+                                                uint32_t *out, uint32_t n_steps);
+extern vkllm_err_t vkllm_b200_batch_read_logits(struct vkllm_context *context, struct vkllm_b200_batch *batch,
+                                                uint16_t *out);
+extern void vkllm_b200_batch_free(struct vkllm_context *context, struct vkllm_b200_batch *batch);
+
 /* 1 when the engine runs the persistent decode kernel. */
 extern int vkllm_b200_engine_is_persistent(struct vkllm_context *context, struct vkllm_models_llama2 *model);
 

@@ -1,0 +1,571 @@
+// Batched greedy decode of independent sequences that share one model's weights (
+// 64 sequences, each with its own prompt and KV cache). One decode step of all sequences is the
+// reference graph of vkllm_llama2_layers.c with S = 1 per sequence, evaluated for B sequences at
+// once: the projections become GEMMs with M = B on the tensor cores (tcgen05, split-K when M is
+// small), the weights stream once per step for all sequences, and the per-sequence parts (RoPE at
+// each sequence's own position, KV rows, attention over its own cache, argmax) run as small kernels.
+// Every node output is rounded to fp16 where the reference materialises it; arithmetic is fp32.
+//
+// Sequences are prefilled through the drop-in graph API (the model's own KV cache) and their rows
+// copied into the batch (vkllm_b200_batch_load_sequence). One step is captured as a CUDA graph.
+#include <cfloat>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "../kernels/kernels.h"
+#include "../runtime/internal.h"
+#include "vkllm_b200.h"
+#include "vkllm_kvcache.h"
+#include "vkllm_models_llama2.h"
+
+namespace vkb
+{
+struct BatchDims
+{
+    uint32_t D, H, hd, F, V, ctx;
+    float eps, rope_base, scale;
+};
+
+struct BatchLayer
+{
+    const __half *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    const float *attn_norm, *ffn_norm;
+};
+} // namespace vkb
+
+struct vkllm_b200_batch
+{
+    vkllm_context *ctx = nullptr;
+    vkllm_models_llama2 *model = nullptr;
+    uint32_t B = 0, cap = 0, L = 0, HD = 0, unk = 0;
+    vkb::BatchDims dd{};
+    std::vector<vkb::BatchLayer> layers;
+    const __half *embed = nullptr, *wout = nullptr;
+    const float *out_norm = nullptr;
+    void *ws = nullptr;
+    __half *kv = nullptr; // [L][2][B][H][cap][hd]
+    __half *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *t0 = nullptr,
+           *up = nullptr, *gate = nullptr, *logits = nullptr;
+    uint32_t *tok = nullptr, *pos = nullptr, *ring = nullptr, *err = nullptr;
+    uint32_t ring_steps = 0, last_steps = 0;
+    std::vector<uint32_t> host_pos; // positions as the host knows them (load + steps)
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+namespace vkb
+{
+namespace
+{
+
+constexpr int kBT = 256;
+
+__device__ __forceinline__ float bsum(float v, float *red)
+{
+    v = warp_sum(v);
+    const uint32_t w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0)
+        red[w] = v;
+    __syncthreads();
+    if (w == 0)
+    {
+        float t = l < (blockDim.x >> 5) ? red[l] : 0.f;
+        t = warp_sum(t);
+        if (l == 0)
+            red[0] = t;
+    }
+    __syncthreads();
+    const float r = red[0];
+    __syncthreads();
+    return r;
+}
+
+__global__ void k_b_embed(const __half *__restrict__ table, uint32_t V, uint32_t D, uint32_t unk,
+                          const uint32_t *__restrict__ tok, __half *__restrict__ x)
+{
+    uint32_t t = tok[blockIdx.x];
+    if (t >= V)
+        t = unk; // src/shaders/vkllm_embedding.comp:57-60
+    const uint4 *src = reinterpret_cast<const uint4 *>(table + (uint64_t)t * D);
+    uint4 *dst = reinterpret_cast<uint4 *>(x + (uint64_t)blockIdx.x * D);
+    for (uint32_t i = threadIdx.x; i < D / 8; i += blockDim.x)
+        dst[i] = src[i];
+}
+
+// RMSNORM node per row: fp16((x * g) * rsqrt(mean(x^2) + eps)).
+__global__ void k_b_rmsnorm(const __half *__restrict__ x, const float *__restrict__ g, uint32_t D, float eps,
+                            __half *__restrict__ y)
+{
+    __shared__ float red[32];
+    const __half *xr = x + (uint64_t)blockIdx.x * D;
+    float s = 0.f;
+    for (uint32_t i = threadIdx.x; i < D; i += blockDim.x)
+    {
+        const float f = __half2float(xr[i]);
+        s = fmaf(f, f, s);
+    }
+    const float alpha = rsqrtf(bsum(s, red) / (float)D + eps);
+    __half *yr = y + (uint64_t)blockIdx.x * D;
+    for (uint32_t i = threadIdx.x; i < D; i += blockDim.x)
+        yr[i] = __float2half_rn((__half2float(xr[i]) * g[i]) * alpha);
+}
+
+// ROPE of q and k at each sequence's position (theta = pos / base^(2w / hd)), then the k and v rows
+// written at that position of the sequence's caches (the UPDATE_ROWS nodes). q is rotated in place.
+__global__ void k_b_rope_kv(__half *__restrict__ q, const __half *__restrict__ k, const __half *__restrict__ v,
+                            const uint32_t *__restrict__ pos, uint32_t H, uint32_t hd, uint32_t cap, float base,
+                            __half *__restrict__ kc, __half *__restrict__ vc, uint32_t B)
+{
+    const uint32_t b = blockIdx.x, HD = H * hd, p = pos[b];
+    if (p >= cap)
+        return; // flagged by k_b_check_pos; no write outside the sequence's rows
+    __half *qr = q + (uint64_t)b * HD;
+    const __half *kr = k + (uint64_t)b * HD, *vr = v + (uint64_t)b * HD;
+    for (uint32_t i = threadIdx.x; i < HD / 2; i += blockDim.x)
+    {
+        const uint32_t h = (2 * i) / hd, d = (2 * i) % hd, w = d / 2;
+        const float theta = (float)p / powf(base, (float)(2 * w) / (float)hd);
+        const float c = cosf(theta), s = sinf(theta);
+        const float q0 = __half2float(qr[2 * i]), q1 = __half2float(qr[2 * i + 1]);
+        qr[2 * i] = __float2half_rn(c * q0 - s * q1);
+        qr[2 * i + 1] = __float2half_rn(s * q0 + c * q1);
+        const float k0 = __half2float(kr[2 * i]), k1 = __half2float(kr[2 * i + 1]);
+        const uint64_t row = (((uint64_t)b * H + h) * cap + p) * hd + d;
+        kc[row] = __float2half_rn(c * k0 - s * k1);
+        kc[row + 1] = __float2half_rn(s * k0 + c * k1);
+        vc[row] = vr[2 * i];
+        vc[row + 1] = vr[2 * i + 1];
+    }
+}
+
+// Attention of one (head, sequence): scores s_j = fp16(scale * q.k_j) over the sequence's Lk = pos + 1
+// keys, softmax p_j = fp16(exp(s_j - max) / sum) (max over all entries, vkllm_softmax.comp), output
+// fp16(sum_j p_j v_j). For Lk == hd the reference reads V as [hd, Lk] (src/core/vkllm_op_matmul.c:14-30):
+// o[w] = sum_k p_k V[w][k].
+__global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ q, const __half *__restrict__ kc,
+                                                     const __half *__restrict__ vc, const uint32_t *__restrict__ pos,
+                                                     uint32_t H, uint32_t hd, uint32_t cap, float scale,
+                                                     __half *__restrict__ out)
+{
+    extern __shared__ float sm[];
+    float *qs = sm;           // [hd]
+    float *sc = sm + 256;     // [Lk]
+    __shared__ float red[32];
+    const uint32_t h = blockIdx.x, b = blockIdx.y, HD = H * hd;
+    if (pos[b] >= cap)
+        return; // flagged by k_b_check_pos
+    const uint32_t Lk = pos[b] + 1;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x)
+        qs[d] = __half2float(q[(uint64_t)b * HD + h * hd + d]);
+    __syncthreads();
+    const __half *kb = kc + ((uint64_t)b * H + h) * cap * hd;
+    const __half *vb = vc + ((uint64_t)b * H + h) * cap * hd;
+    float mx = -FLT_MAX;
+    for (uint32_t j = warp; j < Lk; j += nw)
+    {
+        const __half *kr = kb + (uint64_t)j * hd;
+        float a = 0.f;
+        for (uint32_t d = lane; d < hd; d += 32)
+            a = fmaf(qs[d], __half2float(kr[d]), a);
+        a = warp_sum(a);
+        const float s = round_f16(a * scale);
+        if (lane == 0)
+            sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    if (lane == 0)
+        red[warp] = mx;
+    __syncthreads();
+    float m = -FLT_MAX;
+    for (uint32_t w = 0; w < nw; ++w)
+        m = fmaxf(m, red[w]);
+    __syncthreads();
+    float l = 0.f;
+    for (uint32_t j = threadIdx.x; j < Lk; j += blockDim.x)
+        l += expf(sc[j] - m);
+    l = bsum(l, red);
+    for (uint32_t j = threadIdx.x; j < Lk; j += blockDim.x)
+        sc[j] = round_f16(expf(sc[j] - m) / l);
+    __syncthreads();
+    __half *o = out + (uint64_t)b * HD + h * hd;
+    if (Lk == hd)
+    {
+        for (uint32_t w = threadIdx.x; w < hd; w += blockDim.x)
+        {
+            float a = 0.f;
+            for (uint32_t kk = 0; kk < Lk; ++kk)
+                a = fmaf(sc[kk], __half2float(vb[(uint64_t)w * hd + kk]), a);
+            o[w] = __float2half_rn(a);
+        }
+        return;
+    }
+    // thread (d, part): dims d, keys j = part, part + parts, ...; partial sums combined in smem
+    const uint32_t parts = blockDim.x / hd > 0 ? blockDim.x / hd : 1;
+    float *acc = sc + ((Lk + 31) & ~31u); // [parts][hd]
+    for (uint32_t t = threadIdx.x; t < parts * hd; t += blockDim.x)
+    {
+        const uint32_t d = t % hd, part = t / hd;
+        float a = 0.f;
+        for (uint32_t j = part; j < Lk; j += parts)
+            a = fmaf(sc[j], __half2float(vb[(uint64_t)j * hd + d]), a);
+        acc[part * hd + d] = a;
+    }
+    __syncthreads();
+    for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x)
+    {
+        float a = 0.f;
+        for (uint32_t part = 0; part < parts; ++part)
+            a += acc[part * hd + d];
+        o[d] = __float2half_rn(a);
+    }
+}
+
+// x = fp16(x + t) (the residual BIN add) or m = fp16(a * b) (the gate BIN mul), 8 halves per thread.
+__global__ void k_b_bin8(__half *__restrict__ out, const __half *__restrict__ a, const __half *__restrict__ b,
+                         uint64_t n8, int mul)
+{
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < n8; t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint4 va = reinterpret_cast<const uint4 *>(a)[t], vb = reinterpret_cast<const uint4 *>(b)[t];
+        const __half *ha = reinterpret_cast<const __half *>(&va), *hb = reinterpret_cast<const __half *>(&vb);
+        uint4 o;
+        __half *ho = reinterpret_cast<__half *>(&o);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            const float x = __half2float(ha[i]), y = __half2float(hb[i]);
+            ho[i] = __float2half_rn(mul ? x * y : x + y);
+        }
+        reinterpret_cast<uint4 *>(out)[t] = o;
+    }
+}
+
+// ARG_MAX per sequence with the reference rule (src/shaders/vkllm_arg_max.comp:54-90): lane l keeps
+// the first strict maximum of i = l, l + 32, ...; a 16/8/4/2/1 tree keeps the left operand unless the
+// right one is strictly greater. Then the token feeds back and the position advances.
+__global__ void k_b_argmax(const __half *__restrict__ logits, uint32_t V, uint32_t *__restrict__ tok,
+                           uint32_t *__restrict__ pos, uint32_t *__restrict__ ring, uint32_t ring_steps,
+                           uint32_t *__restrict__ step_ctr, uint32_t B)
+{
+    const uint32_t b = blockIdx.x, lane = threadIdx.x;
+    const __half *row = logits + (uint64_t)b * V;
+    float v = -FLT_MAX;
+    uint32_t idx = lane;
+    if (lane < V)
+        v = __half2float(row[lane]);
+    for (uint32_t i = lane + 32; i < V; i += 32)
+    {
+        const float c = __half2float(row[i]);
+        if (c > v)
+        {
+            v = c;
+            idx = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float ov = __shfl_down_sync(0xffffffffu, v, o);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
+        if ((int)lane < o && ov > v)
+        {
+            v = ov;
+            idx = oi;
+        }
+    }
+    if (lane == 0)
+    {
+        tok[b] = idx;
+        const uint32_t st = *step_ctr;
+        if (st < ring_steps)
+            ring[(uint64_t)st * B + b] = idx;
+        pos[b] += 1;
+    }
+}
+
+__global__ void k_b_step_done(uint32_t *step_ctr)
+{
+    *step_ctr += 1;
+}
+
+__global__ void k_b_check_pos(const uint32_t *pos, uint32_t cap, uint32_t B, uint32_t *err)
+{
+    for (uint32_t b = threadIdx.x; b < B; b += blockDim.x)
+        if (pos[b] >= cap)
+            atomicOr(err, 1u);
+}
+
+bool gemm(const __half *A, const __half *W, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s)
+{
+    GemmArgs g{};
+    g.A = A;
+    g.B = W;
+    g.C = C;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.lda = K;
+    g.ldb = K;
+    g.ldc = N;
+    g.batch = 1;
+    g.batch_c = 1;
+    g.scale = 1.0f;
+    g.act = act;
+    return gemm_tcgen05_launch(g, s);
+}
+
+vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
+{
+    const BatchDims &dd = bt->dd;
+    const uint32_t B = bt->B, D = dd.D, HD = bt->HD, F = dd.F, H = dd.H, hd = dd.hd;
+    k_b_check_pos<<<1, 64, 0, s>>>(bt->pos, bt->cap, B, bt->err);
+    k_b_embed<<<B, kBT, 0, s>>>(bt->embed, dd.V, D, bt->unk, bt->tok, bt->x);
+    const size_t att_smem = (256 + ((bt->cap + 31) & ~31u) + (size_t)(kBT / hd > 0 ? kBT / hd : 1) * hd) * 4;
+    for (uint32_t l = 0; l < bt->L; ++l)
+    {
+        const BatchLayer &w = bt->layers[l];
+        __half *kc = bt->kv + ((uint64_t)l * 2 + 0) * B * H * bt->cap * hd;
+        __half *vc = bt->kv + ((uint64_t)l * 2 + 1) * B * H * bt->cap * hd;
+        k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
+        if (!gemm(bt->xn, w.wq, bt->q, B, HD, D, 0, s) || !gemm(bt->xn, w.wk, bt->k, B, HD, D, 0, s) ||
+            !gemm(bt->xn, w.wv, bt->v, B, HD, D, 0, s))
+            return VKLLM_ERR_VULKAN;
+        k_b_rope_kv<<<B, kBT, 0, s>>>(bt->q, bt->k, bt->v, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
+        k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->q, kc, vc, bt->pos, H, hd, bt->cap, dd.scale, bt->attn);
+        if (!gemm(bt->attn, w.wo, bt->t0, B, D, HD, 0, s))
+            return VKLLM_ERR_VULKAN;
+        k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
+        k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.ffn_norm, D, dd.eps, bt->xn);
+        if (!gemm(bt->xn, w.wu, bt->up, B, F, D, 0, s) || !gemm(bt->xn, w.wg, bt->gate, B, F, D, 1, s))
+            return VKLLM_ERR_VULKAN;
+        k_b_bin8<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->up, bt->up, bt->gate, (uint64_t)B * F / 8, 1);
+        if (!gemm(bt->up, w.wd, bt->t0, B, D, F, 0, s))
+            return VKLLM_ERR_VULKAN;
+        k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
+    }
+    k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, bt->out_norm, D, dd.eps, bt->xn);
+    if (!gemm(bt->xn, bt->wout, bt->logits, B, dd.V, D, 0, s))
+        return VKLLM_ERR_VULKAN;
+    k_b_argmax<<<B, 32, 0, s>>>(bt->logits, dd.V, bt->tok, bt->pos, bt->ring, bt->ring_steps, bt->err + 1, B);
+    k_b_step_done<<<1, 1, 0, s>>>(bt->err + 1);
+    return cudaGetLastError() == cudaSuccess ? VKLLM_ERR_OK : VKLLM_ERR_VULKAN;
+}
+
+} // namespace
+} // namespace vkb
+
+using namespace vkb;
+
+extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vkllm_models_llama2 *model,
+                                            uint32_t n_seqs, uint32_t kv_rows, struct vkllm_b200_batch **out)
+{
+    _CHECK_ARGS(ctx && model && out && n_seqs > 0 && kv_rows > 0);
+    _CHECK_ARGS(model->weights.blocks && model->weights.tok_embed_weights && model->weights.output_weight);
+    block_weights *b0 = model->weights.blocks->data[0];
+    auto *bt = new vkllm_b200_batch();
+    bt->ctx = ctx;
+    bt->model = model;
+    BatchDims &dd = bt->dd;
+    dd.D = model->meta.embedding_length;
+    dd.H = model->meta.head_count;
+    dd.V = model->meta.vocab_size;
+    dd.ctx = model->meta.context_length;
+    dd.eps = model->meta.layer_norm_rms_epsilon;
+    dd.rope_base = model->meta.rope_freq_base;
+    bt->HD = b0->WQ->shapes[2];
+    dd.hd = bt->HD / dd.H;
+    dd.F = b0->WU->shapes[2];
+    dd.scale = 1.0f / sqrtf((float)dd.hd);
+    bt->B = n_seqs;
+    bt->cap = kv_rows < dd.ctx ? kv_rows : dd.ctx;
+    bt->L = model->meta.block_count;
+    bt->unk = model->meta.padding_token_id;
+    bt->host_pos.assign(n_seqs, 0);
+    if (dd.D % 8 || dd.F % 8 || bt->HD % 8 || dd.hd > 256 || dd.hd % 2 || bt->cap > 8192 - 256)
+    {
+        delete bt;
+        return VKLLM_ERR_ARGS;
+    }
+    for (uint32_t l = 0; l < bt->L; ++l)
+    {
+        block_weights *bw = model->weights.blocks->data[l];
+        BatchLayer w{};
+        w.wq = (const __half *)dev_ptr(ctx, bw->WQ);
+        w.wk = (const __half *)dev_ptr(ctx, bw->WK);
+        w.wv = (const __half *)dev_ptr(ctx, bw->WV);
+        w.wo = (const __half *)dev_ptr(ctx, bw->WO);
+        w.wu = (const __half *)dev_ptr(ctx, bw->WU);
+        w.wg = (const __half *)dev_ptr(ctx, bw->WG);
+        w.wd = (const __half *)dev_ptr(ctx, bw->WD);
+        w.attn_norm = (const float *)dev_ptr(ctx, bw->attn_norm_weight);
+        w.ffn_norm = (const float *)dev_ptr(ctx, bw->ffn_norm_weight);
+        bt->layers.push_back(w);
+    }
+    bt->embed = (const __half *)dev_ptr(ctx, model->weights.tok_embed_weights);
+    bt->wout = (const __half *)dev_ptr(ctx, model->weights.output_weight);
+    bt->out_norm = (const float *)dev_ptr(ctx, model->weights.output_norm_weight);
+    const uint32_t B = n_seqs, D = dd.D, HD = bt->HD, F = dd.F;
+    bt->ring_steps = 1024;
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t kv_bytes = al((size_t)bt->L * 2 * B * dd.H * bt->cap * dd.hd * 2);
+    const size_t act = al((size_t)B * D * 2) * 3 + al((size_t)B * HD * 2) * 4 + al((size_t)B * F * 2) * 2 +
+                       al((size_t)B * dd.V * 2);
+    const size_t small = al((size_t)B * 4) * 2 + al((size_t)bt->ring_steps * B * 4) + al(16);
+    if (cudaMalloc(&bt->ws, kv_bytes + act + small) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        delete bt;
+        return VKLLM_ERR_ALLOC;
+    }
+    char *p = (char *)bt->ws;
+    auto take = [&](size_t b) {
+        char *r = p;
+        p += al(b);
+        return r;
+    };
+    bt->kv = (__half *)take(kv_bytes);
+    bt->x = (__half *)take((size_t)B * D * 2);
+    bt->xn = (__half *)take((size_t)B * D * 2);
+    bt->t0 = (__half *)take((size_t)B * D * 2);
+    bt->q = (__half *)take((size_t)B * HD * 2);
+    bt->k = (__half *)take((size_t)B * HD * 2);
+    bt->v = (__half *)take((size_t)B * HD * 2);
+    bt->attn = (__half *)take((size_t)B * HD * 2);
+    bt->up = (__half *)take((size_t)B * F * 2);
+    bt->gate = (__half *)take((size_t)B * F * 2);
+    bt->logits = (__half *)take((size_t)B * dd.V * 2);
+    bt->tok = (uint32_t *)take((size_t)B * 4);
+    bt->pos = (uint32_t *)take((size_t)B * 4);
+    bt->ring = (uint32_t *)take((size_t)bt->ring_steps * B * 4);
+    bt->err = (uint32_t *)take(16); // [0] error bits, [1] step counter
+    cudaStream_t s = ctx->runtime->stream;
+    if (cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
+        cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        cudaFree(bt->ws);
+        delete bt;
+        return VKLLM_ERR_VULKAN;
+    }
+    *out = bt;
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_batch_load_sequence(struct vkllm_context *ctx, struct vkllm_b200_batch *bt,
+                                                      uint32_t seq, uint32_t next_token, uint32_t n_rows)
+{
+    _CHECK_ARGS(ctx && bt && seq < bt->B && n_rows < bt->cap && n_rows <= bt->dd.ctx);
+    vkllm_kvcache *kv = bt->model->weights.kvcache;
+    _CHECK_ARGS(kv && kv->kcaches && kv->vcaches);
+    cudaStream_t s = ctx->runtime->stream;
+    const BatchDims &dd = bt->dd;
+    const size_t row = (size_t)dd.hd * 2;
+    for (uint32_t l = 0; l < bt->L; ++l)
+        for (int which = 0; which < 2; ++which)
+        {
+            const __half *src = (const __half *)dev_ptr(ctx, which == 0 ? kv->kcaches->data[l] : kv->vcaches->data[l]);
+            __half *dst = bt->kv + (((uint64_t)l * 2 + which) * bt->B + seq) * dd.H * bt->cap * dd.hd;
+            if (n_rows > 0)
+                VKB_CUDA(cudaMemcpy2DAsync(dst, bt->cap * row, src, (size_t)dd.ctx * row, n_rows * row, dd.H,
+                                           cudaMemcpyDeviceToDevice, s));
+        }
+    VKB_CUDA(cudaMemcpyAsync(bt->tok + seq, &next_token, 4, cudaMemcpyHostToDevice, s));
+    VKB_CUDA(cudaMemcpyAsync(bt->pos + seq, &n_rows, 4, cudaMemcpyHostToDevice, s));
+    VKB_CUDA(cudaStreamSynchronize(s));
+    bt->host_pos[seq] = n_rows;
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_batch_decode_steps(struct vkllm_context *ctx, struct vkllm_b200_batch *bt,
+                                                     uint32_t n_steps)
+{
+    _CHECK_ARGS(ctx && bt && n_steps <= bt->ring_steps);
+    for (uint32_t b = 0; b < bt->B; ++b)
+        if (bt->host_pos[b] + n_steps > bt->cap)
+        {
+            log_error("batched decode: sequence %u would pass its %u KV rows", b, bt->cap);
+            return VKLLM_ERR_ARGS;
+        }
+    cudaStream_t s = ctx->runtime->stream;
+    const uint32_t total = n_steps;
+    VKB_CUDA(cudaMemsetAsync(bt->err, 0, 8, s));
+    if (!bt->exec && n_steps > 0)
+    {
+        // First step eagerly (first-use allocations of the GEMM: kernel attributes, split-K workspace),
+        // then capture one step as a graph for the rest.
+        _CHECK(enqueue_batch_step(bt, s));
+        n_steps -= 1;
+        cudaStream_t cs;
+        VKB_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+        VKB_CUDA(cudaStreamSynchronize(s));
+        vkllm_err_t err = VKLLM_ERR_OK;
+        if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+            err = VKLLM_ERR_VULKAN;
+        if (err == VKLLM_ERR_OK)
+        {
+            vkllm_err_t le = enqueue_batch_step(bt, cs);
+            if (cudaStreamEndCapture(cs, &bt->graph) != cudaSuccess || le != VKLLM_ERR_OK)
+                err = VKLLM_ERR_VULKAN;
+        }
+        if (err == VKLLM_ERR_OK && cudaGraphInstantiate(&bt->exec, bt->graph, 0) != cudaSuccess)
+            err = VKLLM_ERR_VULKAN;
+        cudaStreamDestroy(cs);
+        if (err != VKLLM_ERR_OK)
+        {
+            (void)cudaGetLastError();
+            return err;
+        }
+    }
+    for (uint32_t i = 0; i < n_steps; ++i)
+        VKB_CUDA(cudaGraphLaunch(bt->exec, s));
+    bt->last_steps = total;
+    for (uint32_t b = 0; b < bt->B; ++b)
+        bt->host_pos[b] += total;
+    uint32_t e[2] = {0, 0};
+    VKB_CUDA(cudaMemcpyAsync(e, bt->err, 8, cudaMemcpyDeviceToHost, s));
+    VKB_CUDA(cudaStreamSynchronize(s));
+    if (e[0] != 0 || gemm_tcgen05_error(ctx->device->ordinal) != 0)
+    {
+        log_error("batched decode: %s", e[0] ? "a sequence reached its KV capacity" : "tensor-core GEMM wait expired");
+        return VKLLM_ERR_ARGS;
+    }
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_batch_read_tokens(struct vkllm_context *ctx, struct vkllm_b200_batch *bt,
+                                                    uint32_t *out, uint32_t n_steps)
+{
+    _CHECK_ARGS(ctx && bt && out && n_steps <= bt->ring_steps);
+    VKB_CUDA(cudaMemcpy(out, bt->ring, (size_t)n_steps * bt->B * 4, cudaMemcpyDeviceToHost));
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_batch_read_logits(struct vkllm_context *ctx, struct vkllm_b200_batch *bt,
+                                                    uint16_t *out)
+{
+    _CHECK_ARGS(ctx && bt && out);
+    VKB_CUDA(cudaMemcpy(out, bt->logits, (size_t)bt->B * bt->dd.V * 2, cudaMemcpyDeviceToHost));
+    return VKLLM_ERR_OK;
+}
+
+extern "C" void vkllm_b200_batch_free(struct vkllm_context *ctx, struct vkllm_b200_batch *bt)
+{
+    (void)ctx;
+    if (!bt)
+        return;
+    if (bt->exec)
+        cudaGraphExecDestroy(bt->exec);
+    if (bt->graph)
+        cudaGraphDestroy(bt->graph);
+    if (bt->ws)
+    {
+        cudaDeviceSynchronize();
+        cudaFree(bt->ws);
+    }
+    delete bt;
+}

@@ -171,6 +171,12 @@ _SIGS = {
     "vkllm_b200_gemm_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
                                       C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_int, C.c_void_p]),
     "vkllm_b200_gemm_f16_error": (C.c_uint32, []),
+    "vkllm_b200_batch_new": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_uint32, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "vkllm_b200_batch_load_sequence": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32]),
+    "vkllm_b200_batch_decode_steps": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
+    "vkllm_b200_batch_read_tokens": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32]),
+    "vkllm_b200_batch_read_logits": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "vkllm_b200_batch_free": (None, [C.c_void_p, C.c_void_p]),
     "vkllm_b200_engine_bench_kernel": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
                                                  C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
     "vkllm_b200_attention_decode_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
@@ -471,3 +477,37 @@ def random_f16_host(seed, tensor_id, std, first, n):
     out = np.empty(n, dtype=np.uint16)
     lib().vkllm_b200_random_f16_host(seed, tensor_id, std, first, n, out.ctypes.data)
     return out
+
+
+class Batch:
+    """Batched greedy decode of independent sequences on one model (vkllm_b200_batch_*)."""
+
+    def __init__(self, model, n_seqs, kv_rows):
+        self.model, self.ctx, self.n = model, model.ctx, n_seqs
+        self.ptr = C.c_void_p()
+        check(lib().vkllm_b200_batch_new(self.ctx.ptr, C.byref(model.m), n_seqs, kv_rows, C.byref(self.ptr)),
+              "batch_new")
+
+    def add_prompt(self, seq, prompt):
+        """Prefills `prompt` through the drop-in graph API (the model's KV cache) and moves its KV rows
+        into slot `seq`. Returns the prefill's predicted token (the slot's next input)."""
+        first = self.model.step(list(prompt), 0)
+        check(lib().vkllm_b200_batch_load_sequence(self.ctx.ptr, self.ptr, seq, first, len(prompt)), "load_sequence")
+        return first
+
+    def decode(self, n_steps):
+        check(lib().vkllm_b200_batch_decode_steps(self.ctx.ptr, self.ptr, n_steps), "batch_decode_steps")
+        out = np.zeros((n_steps, self.n), dtype=np.uint32)
+        check(lib().vkllm_b200_batch_read_tokens(self.ctx.ptr, self.ptr, out.ctypes.data, n_steps), "read_tokens")
+        return out
+
+    def logits(self):
+        V = self.model.meta.vocab_size
+        out = np.zeros((self.n, V), dtype=np.uint16)
+        check(lib().vkllm_b200_batch_read_logits(self.ctx.ptr, self.ptr, out.ctypes.data), "read_logits")
+        return out.view(np.float16)
+
+    def free(self):
+        if self.ptr:
+            lib().vkllm_b200_batch_free(self.ctx.ptr, self.ptr)
+            self.ptr = C.c_void_p()
