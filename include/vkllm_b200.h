@@ -44,6 +44,32 @@ extern vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context *co
                                                         struct vkllm_models_llama2 *model,
                                                         const struct vkllm_b200_llama2_config *cfg, uint64_t seed);
 
+/* Tensor-parallel shard `tp_rank` of `tp_size` (<= 8) of the same random model: Wq, Wk, Wv, Wgate,
+ * Wup and the output matrix keep rows [r n/N, (r+1) n/N), Wo and Wdown keep the matching columns
+ * (attention heads and FFN columns sharded), the embedding and the
+ * norm gains stay whole, and the KV cache holds head_count / tp_size heads. Every shard element has
+ * the bits of the same element of the unsharded model. head_count, ffn_length and vocab_size must
+ * be multiples of tp_size. Such a model decodes only through the engine entry points
+ * (vkllm_b200_engine_*) after vkllm_b200_tp_connect. */
+extern vkllm_err_t vkllm_b200_models_llama2_init_random_tp(struct vkllm_context *context,
+                                                           struct vkllm_models_llama2 *model,
+                                                           const struct vkllm_b200_llama2_config *cfg, uint64_t seed,
+                                                           uint32_t tp_rank, uint32_t tp_size);
+
+/* Tensor parallelism over peer memory (one process per GPU, every rank with its shard from
+ * vkllm_b200_models_llama2_init_random_tp). Each rank calls vkllm_b200_tp_init, which allocates its
+ * exchange buffer and writes its 64-byte CUDA IPC handle to handle_out; the caller gathers the
+ * handles of all ranks (rank order, 64 bytes each, e.g. with torch.distributed.all_gather_object)
+ * and passes them to vkllm_b200_tp_connect, which maps the peers' buffers. Then the engine entry
+ * points decode on every rank in lockstep: the Wo and down projections of each layer exchange
+ * their partial sums inside the decode kernel (NVLink stores + release flags, bounded waits), and
+ * the argmax of the vocabulary shards is combined with the reference tie rule. Every rank must make
+ * the same engine calls in the same order. Call both before the first decode. */
+extern vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                      void *handle_out);
+extern vkllm_err_t vkllm_b200_tp_connect(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                         const void *handles);
+
 /* Host-side twin of the device generator: the fp16 bit patterns of elements [first, first + n) of
  * tensor `tensor_id` (for CPU references of randomly initialised models). */
 extern void vkllm_b200_random_f16_host(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t first, uint64_t n,

@@ -77,7 +77,7 @@ struct vkllm_models_llama2
         void *engine;      /* fused decode engine (opaque), created on first fused run */
         uint32_t tp_rank;  /* tensor-parallel shard of this replica (0 when not sharded) */
         uint32_t tp_size;  /* 1 when not sharded */
-        void *tp_comm;     /* NCCL communicator (opaque) when tp_size > 1 */
+        void *tp_comm;     /* peer-memory exchange of the tensor-parallel ranks (opaque) when tp_size > 1 */
     } b200;
 };
 

@@ -42,6 +42,9 @@ enum PhaseKind : uint32_t
 };
 
 constexpr uint32_t kErrBarrierTimeout = 0x200;
+constexpr uint32_t kErrPeerTimeout = 0x400;
+constexpr uint32_t kTpMax = 8;     // ranks
+constexpr uint32_t kTpCtas = 256;  // flag slots per site (>= CTAs of the grid)
 constexpr uint32_t kErrPosition = 0x1;
 
 #ifndef VKB_PERSIST_SEG
@@ -93,6 +96,15 @@ struct PersistParams
     uint64_t *trace_last;       // optional: per trace entry, %globaltimer when the last CTA arrived
     uint32_t l2_bytes;          // per CTA: next-phase weights prefetched into L2 at each barrier
     uint32_t l2_hint;           // 1: stage loads mark their lines evict-first in L2
+    // Tensor parallelism over peer memory (tp_size 1: off). Each rank owns H / N heads, F / N FFN
+    // rows and V / N vocabulary rows (from v0); the Wo and down outputs are partial sums that every
+    // rank writes, per output row, into every peer's receive area, then raises a flag per CTA.
+    uint32_t tp_size, tp_rank, v0, Vg;
+    float *tp_x[kTpMax];          // rank q's receive area [2 sites][N ranks][D] fp32
+    uint32_t *tp_flag[kTpMax];    // rank q's flags [3 sites][kTpCtas][N ranks]
+    float *tp_amv[kTpMax];        // rank q's argmax class slots [N ranks][32]
+    uint32_t *tp_ami[kTpMax];
+    uint32_t tp_base[3];          // exchanges done per site before this launch (flags only grow)
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p)
@@ -168,6 +180,18 @@ __device__ __forceinline__ void trace_mark(const PersistParams &P, SyncState &tr
     }
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // The weight row `m` of unit `u` of phase (kind, layer).
 __device__ __forceinline__ const __half *persist_row(const PersistParams &P, uint32_t kind, const LayerW &lw,
                                                      uint32_t u, uint32_t m)
@@ -200,6 +224,57 @@ __device__ __forceinline__ UnitRange cta_units(uint32_t units)
 {
     const uint32_t base = units / gridDim.x, rem = units % gridDim.x;
     return UnitRange{blockIdx.x * base + min(blockIdx.x, rem), base + (blockIdx.x < rem ? 1u : 0u)};
+}
+
+// Tensor-parallel allreduce of this CTA's output rows of the Wo (site 0) or down (site 1) phase:
+// the epilogue wrote each row's partial into every rank's receive area; here thread 0 publishes a
+// flag to the same CTA index of every rank and waits (bounded) for theirs; then each row is summed
+// over the ranks in rank order (fp32), rounded to fp16 (the projection node) and added to the
+// residual: x = fp16(x + fp16(sum)). Returns false on a timed-out wait or a reported error.
+__device__ __forceinline__ bool tp_allreduce_rows(const PersistParams &P, uint32_t site, uint32_t epoch)
+{
+    __shared__ uint32_t ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        __threadfence_system(); // this CTA's partial stores to the peers precede the flags
+        const uint32_t slot = (site * kTpCtas + blockIdx.x) * kTpMax + P.tp_rank;
+        for (uint32_t q = 0; q < P.tp_size; ++q)
+            st_release_sys_u32(P.tp_flag[q] + slot, epoch);
+        bool ok = true;
+        const uint32_t *mine = P.tp_flag[P.tp_rank] + (site * kTpCtas + blockIdx.x) * kTpMax;
+        const uint64_t t0 = global_ns();
+        for (uint32_t q = 0; q < P.tp_size && ok; ++q)
+            while (ld_acquire_sys_u32(mine + q) < epoch)
+            {
+                if (ld_acquire_u32(P.err) != 0)
+                {
+                    ok = false;
+                    break;
+                }
+                if (global_ns() - t0 > kWaitLimitNs)
+                {
+                    atomicOr(P.err, kErrPeerTimeout);
+                    ok = false;
+                    break;
+                }
+            }
+        ok_s = ok ? 1u : 0u;
+    }
+    __syncthreads();
+    if (!ok_s)
+        return false;
+    const UnitRange r = cta_units(P.tg[site == 0 ? PK_WO : PK_DOWN].units);
+    const float *rx = P.tp_x[P.tp_rank] + (uint64_t)site * P.tp_size * P.dd.D;
+    for (uint32_t i = threadIdx.x; i < r.count; i += blockDim.x)
+    {
+        const uint32_t u = r.u0 + i;
+        float t = 0.f;
+        for (uint32_t q = 0; q < P.tp_size; ++q)
+            t += __ldcg(rx + (uint64_t)q * P.dd.D + u);
+        P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(t));
+    }
+    return true;
 }
 
 // Producer cursor of one warp over its chunk sequence (step, layer, kind, k).
@@ -377,7 +452,15 @@ __device__ __forceinline__ void persist_epilogue(const PersistParams &P, uint32_
     }
     case PK_WO:
     case PK_DOWN:
-        P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(s[0]));
+        if (P.tp_size > 1)
+        {
+            // partial over this rank's K slice -> every rank's receive area (site 0 = Wo, 1 = down)
+            const uint32_t site = kind == PK_WO ? 0u : 1u;
+            for (uint32_t q = 0; q < P.tp_size; ++q)
+                P.tp_x[q][((uint64_t)site * P.tp_size + P.tp_rank) * dd.D + u] = s[0];
+        }
+        else
+            P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(s[0]));
         break;
     case PK_UPGATE:
         P.m[u] = __float2half_rn(round_f16(s[0]) * round_f16(silu_f32(s[1])));
@@ -752,6 +835,7 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
     float *scratch = reinterpret_cast<float *>(smem + kStreamBarBytes); // attention phases: xs + part
     unsigned char *stages = smem + kStreamBarBytes + P.xs_bytes + P.part_bytes;
     __shared__ float sred[32];
+    __shared__ uint32_t xfail_s; // the tensor-parallel argmax exchange timed out
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const DecodeDims &dd = P.dd;
@@ -763,6 +847,8 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
     wp.cur = Cursor{0, 0, PK_QKV, 0, P.n_steps == 0};
     bool ok = true;
     SyncState tr{1, 0}; // thread 0: trace entry 0 is the start
+    if (threadIdx.x == 0)
+        xfail_s = 0;
     if (P.trace && blockIdx.x == 0 && threadIdx.x == 0 && P.trace_cap > 0)
         P.trace[0] = global_ns();
     if (lane == 0)
@@ -796,7 +882,7 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
             ok = false;
             break;
         }
-        const uint32_t tok = tok0 < dd.V ? tok0 : P.unk; // src/shaders/vkllm_embedding.comp:57-60
+        const uint32_t tok = tok0 < P.Vg ? tok0 : P.unk; // src/shaders/vkllm_embedding.comp:57-60
         // The residual rows this CTA owns (the Wo / down output rows) start as the embedding.
         {
             const UnitRange r = cta_units(P.tg[PK_WO].units);
@@ -829,6 +915,8 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
             ok = persist_gemv<1>(P, PK_WO, l, wp, xs, part, pos, tr);
             if (threadIdx.x == 0)
                 prefetch_slice(P, PK_UPGATE, l);
+            if (P.tp_size > 1 && __syncthreads_and(ok))
+                ok = tp_allreduce_rows(P, 0, P.tp_base[0] + step * P.L + l + 1);
             if (!__syncthreads_and(ok) || !grid_sync(P, tr))
             {
                 ok = false;
@@ -849,6 +937,8 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
             ok = persist_gemv<1>(P, PK_DOWN, l, wp, xs, part, pos, tr);
             if (threadIdx.x == 0)
                 prefetch_slice(P, l + 1 < P.L ? PK_QKV : PK_LOGITS, l + 1 < P.L ? l + 1 : 0);
+            if (P.tp_size > 1 && __syncthreads_and(ok))
+                ok = tp_allreduce_rows(P, 1, P.tp_base[1] + step * P.L + l + 1);
             if (!__syncthreads_and(ok) || !grid_sync(P, tr))
             {
                 ok = false;
@@ -873,16 +963,17 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
             const UnitRange r = cta_units(P.tg[PK_LOGITS].units);
             if (warp == 0)
             {
+                // class of a row = its vocabulary index (v0 + local row) mod 32
                 float bv = -FLT_MAX;
                 uint32_t bi = 0xffffffffu;
-                const uint32_t first = r.u0 + ((lane + 32 - (r.u0 & 31)) & 31);
+                const uint32_t first = r.u0 + ((lane + 32 - ((P.v0 + r.u0) & 31)) & 31);
                 for (uint32_t i = first; i < r.u0 + r.count; i += 32)
                 {
                     const float v = __half2float(__ldcg(P.logits + i));
                     if (bi == 0xffffffffu || v > bv)
                     {
                         bv = v;
-                        bi = i;
+                        bi = P.v0 + i;
                     }
                 }
                 P.am_val[blockIdx.x * 32 + lane] = bv;
@@ -936,6 +1027,60 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
                         idx = ci;
                     }
                 }
+                if (P.tp_size > 1)
+                {
+                    // this rank's class results -> every rank (CTA 0 sends), then every CTA combines the
+                    // ranks' results per class with the same rule (indices grow with the rank)
+                    const uint32_t epoch = P.tp_base[2] + step + 1;
+                    if (blockIdx.x == 0)
+                    {
+                        for (uint32_t q = 0; q < P.tp_size; ++q)
+                        {
+                            P.tp_amv[q][P.tp_rank * 32 + lane] = v;
+                            P.tp_ami[q][P.tp_rank * 32 + lane] = idx;
+                        }
+                        __syncwarp();
+                        if (lane == 0)
+                        {
+                            __threadfence_system();
+                            for (uint32_t q = 0; q < P.tp_size; ++q)
+                                st_release_sys_u32(P.tp_flag[q] + (2 * kTpCtas) * kTpMax + P.tp_rank, epoch);
+                        }
+                    }
+                    bool okw = true;
+                    if (lane == 0)
+                    {
+                        const uint32_t *mine = P.tp_flag[P.tp_rank] + (2 * kTpCtas) * kTpMax;
+                        const uint64_t t0 = global_ns();
+                        for (uint32_t q = 0; q < P.tp_size && okw; ++q)
+                            while (ld_acquire_sys_u32(mine + q) < epoch)
+                            {
+                                if (ld_acquire_u32(P.err) != 0 || global_ns() - t0 > kWaitLimitNs)
+                                {
+                                    atomicOr(P.err, kErrPeerTimeout);
+                                    okw = false;
+                                    break;
+                                }
+                            }
+                    }
+                    okw = __shfl_sync(0xffffffffu, okw, 0);
+                    v = -FLT_MAX;
+                    idx = 0xffffffffu;
+                    for (uint32_t q = 0; okw && q < P.tp_size; ++q)
+                    {
+                        const uint32_t ci = __ldcg(P.tp_ami[P.tp_rank] + q * 32 + lane);
+                        const float cv = __ldcg(P.tp_amv[P.tp_rank] + q * 32 + lane);
+                        if (ci == 0xffffffffu)
+                            continue;
+                        if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))
+                        {
+                            v = cv;
+                            idx = ci;
+                        }
+                    }
+                    if (!okw && lane == 0)
+                        xfail_s = 1u;
+                }
                 if (idx == 0xffffffffu)
                 {
                     v = -FLT_MAX; // empty class (V < 32): the reference lane keeps -FLT_MAX and its own index
@@ -968,7 +1113,13 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
             __syncthreads();
             tok0 = ci_s[0];
             pos += 1;
+            const bool xfail = xfail_s != 0;
             __syncthreads();
+            if (xfail)
+            {
+                ok = false;
+                break;
+            }
         }
     }
     if (!ok)

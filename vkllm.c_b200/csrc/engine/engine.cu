@@ -17,6 +17,8 @@
 namespace vkb
 {
 
+struct TpComm;
+
 struct Engine
 {
     vkllm_context *ctx = nullptr;
@@ -47,7 +49,38 @@ struct Engine
     float *am_val = nullptr;
     uint32_t *am_idx = nullptr, *bar = nullptr; // bar[0] = barrier arrivals, then 2 x H attention counters
     uint32_t launches = 0;                      // kernel launches enqueued by the last decode call
+    TpComm *tp = nullptr;                       // tensor-parallel exchange (shards only)
 };
+
+// Peer-memory exchange of a tensor-parallel rank: one device buffer, exported with CUDA IPC, holding
+// the receive areas and flags its peers write into (layout in tp_layout), plus the peers' buffers
+// opened from their handles.
+struct TpComm
+{
+    uint32_t rank = 0, world = 1, D = 0;
+    void *buf = nullptr;
+    size_t bytes = 0;
+    void *peer[kTpMax] = {};
+    bool connected = false;
+    uint32_t base[3] = {0, 0, 0}; // exchanges done per site (Wo, down, argmax)
+};
+
+struct TpLayout
+{
+    size_t x, flag, amv, ami, total;
+};
+
+inline TpLayout tp_layout(uint32_t world, uint32_t D)
+{
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    TpLayout t;
+    t.x = 0;
+    t.flag = t.x + al((size_t)2 * world * D * 4);
+    t.amv = t.flag + al((size_t)3 * kTpCtas * kTpMax * 4);
+    t.ami = t.amv + al((size_t)kTpMax * 32 * 4);
+    t.total = t.ami + al((size_t)kTpMax * 32 * 4);
+    return t;
+}
 
 namespace
 {
@@ -291,6 +324,15 @@ vkllm_err_t run_persistent(Engine *e, uint32_t n, cudaStream_t s)
         VKB_CUDA(cudaMemsetAsync(e->bar, 0, 4 * (1 + 2 * (size_t)e->dd.H), s));
         PersistParams P = e->pp;
         P.n_steps = k;
+        if (e->tp)
+        {
+            // every rank runs the same launches, so the per-site exchange counts stay in step
+            for (int i = 0; i < 3; ++i)
+                P.tp_base[i] = e->tp->base[i];
+            e->tp->base[0] += k * P.L;
+            e->tp->base[1] += k * P.L;
+            e->tp->base[2] += k;
+        }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)e->ctx->device->sm_count); // one co-resident CTA per SM
         cfg.blockDim = dim3(32 * P.warps);
@@ -315,9 +357,10 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     Engine *e = new Engine();
     e->ctx = ctx;
     DecodeDims &dd = e->dd;
+    const uint32_t tp = model->b200.tp_size > 1 ? model->b200.tp_size : 1;
     dd.D = model->meta.embedding_length;
-    dd.H = model->meta.head_count;
-    dd.V = model->meta.vocab_size;
+    dd.H = model->meta.head_count / tp;            // heads of this shard
+    dd.V = model->weights.output_weight->shapes[2]; // vocabulary rows of this shard
     dd.ctx = model->meta.context_length;
     dd.eps = model->meta.layer_norm_rms_epsilon;
     dd.rope_base = model->meta.rope_freq_base;
@@ -332,12 +375,12 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->unk = model->meta.padding_token_id;
     // Shape requirements of the fused kernels (anything else runs node by node).
     bool ok = dd.D % 8 == 0 && dd.F % 8 == 0 && HD % 8 == 0 && dd.hd % 4 == 0 && dd.hd <= 256 && dd.D % 2 == 0 &&
-              HD == dd.D && model->weights.tok_embed_weights->shapes[3] == dd.D &&
+              HD * tp == dd.D && model->weights.tok_embed_weights->shapes[3] == dd.D &&
               model->weights.tok_embed_weights->dtype == vkllm_dtype_float16 &&
               model->weights.output_weight->shapes[2] == dd.V && model->weights.output_weight->shapes[3] == dd.D &&
               model->weights.output_weight->dtype == vkllm_dtype_float16 &&
               model->weights.output_norm_weight->dtype == vkllm_dtype_float32 &&
-              model->weights.tok_embed_weights->shapes[2] == dd.V;
+              model->weights.tok_embed_weights->shapes[2] == dd.V * tp;
     vkllm_kvcache *kv = model->weights.kvcache;
     for (uint32_t l = 0; ok && l < model->meta.block_count; ++l)
     {
@@ -453,6 +496,37 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     // VKLLM_B200_PERSIST_L2_KB the next-phase weights per CTA prefetched into L2 at each barrier.
     const char *l2kb = getenv("VKLLM_B200_PERSIST_L2_KB");
     setup_persistent(e, ctx, att_split, env_u32("VKLLM_B200_PERSIST_SPW", 1), l2kb ? (uint32_t)atoi(l2kb) : 0u);
+    e->pp.tp_size = tp;
+    e->pp.tp_rank = tp > 1 ? model->b200.tp_rank : 0;
+    e->pp.v0 = e->pp.tp_rank * dd.V;
+    e->pp.Vg = dd.V * tp;
+    if (tp > 1)
+    {
+        // Tensor-parallel shards decode only on the persistent kernel, whose Wo / down epilogues
+        // exchange the partial sums over peer memory.
+        TpComm *c = (TpComm *)model->b200.tp_comm;
+        if (!e->persistent || !c || !c->connected || (uint32_t)sms > kTpCtas)
+        {
+            log_error("tensor-parallel decode needs the persistent kernel and vkllm_b200_tp_connect first");
+            if (e->d_layers)
+                cudaFree(e->d_layers);
+            cudaFree(e->ws);
+            delete e;
+            return VKLLM_ERR_ARGS;
+        }
+        const TpLayout t = tp_layout(c->world, dd.D);
+        for (uint32_t q = 0; q < c->world; ++q)
+        {
+            char *b = (char *)c->peer[q];
+            e->pp.tp_x[q] = (float *)(b + t.x);
+            e->pp.tp_flag[q] = (uint32_t *)(b + t.flag);
+            e->pp.tp_amv[q] = (float *)(b + t.amv);
+            e->pp.tp_ami[q] = (uint32_t *)(b + t.ami);
+        }
+        e->tp = c;
+        *out = e;
+        return VKLLM_ERR_OK; // no CUDA-graph path for shards
+    }
 
     // Capture one decode step.
     cudaStream_t cs;
@@ -598,6 +672,19 @@ __global__ void k_fill_random_f16(__half *dst, uint64_t n, uint64_t key, float s
         dst[i] = __float2half_rn(random_value(key, i, scale));
 }
 
+// Shard [rows, cols] of a [*, full_cols] matrix at (row0, col0): element (i, c) is element
+// (row0 + i) * full_cols + col0 + c of the full tensor, so shards hold exactly the full matrix's bits.
+__global__ void k_fill_random_f16_2d(__half *dst, uint64_t rows, uint64_t cols, uint64_t full_cols, uint64_t row0,
+                                     uint64_t col0, uint64_t key, float scale)
+{
+    const uint64_t n = rows * cols;
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < n; t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint64_t i = t / cols, c = t % cols;
+        dst[t] = __float2half_rn(random_value(key, (row0 + i) * full_cols + col0 + c, scale));
+    }
+}
+
 __global__ void k_fill_const_f32(float *dst, uint64_t n, float v)
 {
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
@@ -614,6 +701,16 @@ vkllm_err_t fill_random_f16(vkllm_context *ctx, void *dst, uint64_t n, uint64_t 
     float scale = std_dev * (1.0f / 65536.0f);
     k_fill_random_f16<<<ctx->device->sm_count * 8, 256, 0, ctx->runtime->stream>>>((__half *)dst, n,
                                                                                      tensor_key(seed, tensor_id), scale);
+    VKB_CUDA(cudaGetLastError());
+    return VKLLM_ERR_OK;
+}
+
+vkllm_err_t fill_random_f16_shard(vkllm_context *ctx, void *dst, uint64_t rows, uint64_t cols, uint64_t full_cols,
+                                  uint64_t row0, uint64_t col0, uint64_t seed, uint64_t tensor_id, float std_dev)
+{
+    float scale = std_dev * (1.0f / 65536.0f);
+    k_fill_random_f16_2d<<<ctx->device->sm_count * 8, 256, 0, ctx->runtime->stream>>>(
+        (__half *)dst, rows, cols, full_cols, row0, col0, tensor_key(seed, tensor_id), scale);
     VKB_CUDA(cudaGetLastError());
     return VKLLM_ERR_OK;
 }
@@ -993,4 +1090,87 @@ extern "C" uint32_t vkllm_b200_engine_read_warp_trace(struct vkllm_context *cont
     if (cudaMemcpy(out, e->pp.wtrace, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
         return 0;
     return n;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Tensor parallelism: the peer-memory exchange between the ranks of a sharded model.
+
+namespace vkb
+{
+void tp_comm_free(vkllm_models_llama2 *model)
+{
+    TpComm *c = (TpComm *)model->b200.tp_comm;
+    if (!c)
+        return;
+    cudaDeviceSynchronize();
+    for (uint32_t q = 0; q < c->world; ++q)
+        if (q != c->rank && c->peer[q])
+            cudaIpcCloseMemHandle(c->peer[q]);
+    if (c->buf)
+        cudaFree(c->buf);
+    delete c;
+    model->b200.tp_comm = nullptr;
+}
+} // namespace vkb
+
+extern "C" vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                          void *handle_out)
+{
+    _CHECK_ARGS(context && model && handle_out);
+    _CHECK_ARGS(model->b200.tp_size > 1 && model->b200.tp_size <= kTpMax && model->b200.tp_rank < model->b200.tp_size);
+    _CHECK_ARGS(!model->b200.tp_comm && !model->b200.engine);
+    auto *c = new TpComm();
+    c->rank = model->b200.tp_rank;
+    c->world = model->b200.tp_size;
+    c->D = model->meta.embedding_length;
+    const TpLayout t = tp_layout(c->world, c->D);
+    c->bytes = t.total;
+    if (cudaMalloc(&c->buf, c->bytes) != cudaSuccess || cudaMemset(c->buf, 0, c->bytes) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        delete c;
+        return VKLLM_ERR_ALLOC;
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, c->buf) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        cudaFree(c->buf);
+        delete c;
+        return VKLLM_ERR_VULKAN;
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    c->peer[c->rank] = c->buf;
+    model->b200.tp_comm = c;
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_tp_connect(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                             const void *handles)
+{
+    _CHECK_ARGS(context && model && handles && model->b200.tp_comm);
+    TpComm *c = (TpComm *)model->b200.tp_comm;
+    _CHECK_ARGS(!c->connected);
+    const cudaIpcMemHandle_t *hs = (const cudaIpcMemHandle_t *)handles;
+    for (uint32_t q = 0; q < c->world; ++q)
+    {
+        if (q == c->rank)
+            continue;
+        void *p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, hs[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        {
+            log_error("tensor parallel: opening the buffer of rank %u failed: %s", q,
+                      cudaGetErrorString(cudaGetLastError()));
+            for (uint32_t r = 0; r < q; ++r)
+                if (r != c->rank && c->peer[r])
+                {
+                    cudaIpcCloseMemHandle(c->peer[r]);
+                    c->peer[r] = nullptr;
+                }
+            return VKLLM_ERR_VULKAN;
+        }
+        c->peer[q] = p;
+    }
+    c->connected = true;
+    return VKLLM_ERR_OK;
 }

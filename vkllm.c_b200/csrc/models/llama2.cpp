@@ -19,6 +19,9 @@
 namespace vkb
 {
 void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model);
+void tp_comm_free(vkllm_models_llama2 *model);
+vkllm_err_t fill_random_f16_shard(vkllm_context *ctx, void *dst, uint64_t rows, uint64_t cols, uint64_t full_cols,
+                                  uint64_t row0, uint64_t col0, uint64_t seed, uint64_t tensor_id, float std_dev);
 vkllm_err_t fill_random_f16(vkllm_context *ctx, void *dst, uint64_t n, uint64_t seed, uint64_t tensor_id,
                             float std_dev);
 vkllm_err_t fill_const_f32(vkllm_context *ctx, void *dst, uint64_t n, float v);
@@ -140,9 +143,11 @@ vkllm_err_t tensor_from_gguf(vkllm_context *ctx, const vkb::GgufTensor &gt, vkll
 vkllm_err_t create_kvcache(vkllm_context *ctx, vkllm_models_llama2 *m)
 {
     _CHECK_ARGS(m->weights.blocks->used_n > 0 && m->weights.blocks->data[0]->WK && m->weights.blocks->data[0]->WV);
-    uint32_t H = m->meta.head_count;
-    uint32_t kd = m->weights.blocks->data[0]->WK->shapes[3] / H;
-    uint32_t vd = m->weights.blocks->data[0]->WV->shapes[3] / H;
+    // a tensor-parallel shard holds head_count / tp_size heads (its rows of Wk / Wv)
+    uint32_t H = m->meta.head_count / (m->b200.tp_size > 0 ? m->b200.tp_size : 1);
+    // head size = rows of Wk / Wv (heads x head_dim of this shard)
+    uint32_t kd = m->weights.blocks->data[0]->WK->shapes[2] / H;
+    uint32_t vd = m->weights.blocks->data[0]->WV->shapes[2] / H;
     uint32_t kshape[4] = {1, H, m->meta.context_length, kd};
     uint32_t vshape[4] = {1, H, m->meta.context_length, vd};
     return vkllm_kvcache_new(ctx, kshape, vshape, m->meta.block_count, &m->weights.kvcache);
@@ -236,6 +241,7 @@ extern "C" vkllm_err_t vkllm_models_llama2_free(struct vkllm_context *context, s
 {
     _CHECK_ARGS(context && model);
     vkb::engine_destroy(context, model);
+    vkb::tp_comm_free(model);
     if (model->meta.tokens)
     {
         for (size_t i = 0; i < model->meta.tokens->used_n; ++i)
@@ -442,12 +448,23 @@ extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context
                                                             const struct vkllm_b200_llama2_config *cfg,
                                                             uint64_t seed)
 {
+    return vkllm_b200_models_llama2_init_random_tp(context, model, cfg, seed, 0, 1);
+}
+
+extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random_tp(struct vkllm_context *context,
+                                                               struct vkllm_models_llama2 *model,
+                                                               const struct vkllm_b200_llama2_config *cfg,
+                                                               uint64_t seed, uint32_t tp_rank, uint32_t tp_size)
+{
     _CHECK_ARGS(context && model && cfg);
     _CHECK_ARGS(cfg->block_count > 0 && cfg->embedding_length > 0 && cfg->head_count > 0 && cfg->ffn_length > 0 &&
                 cfg->vocab_size > 0 && cfg->context_length > 0);
     _CHECK_ARGS(cfg->embedding_length % cfg->head_count == 0);
+    _CHECK_ARGS(tp_size >= 1 && tp_size <= 8 && tp_rank < tp_size);
+    _CHECK_ARGS(cfg->head_count % tp_size == 0 && cfg->ffn_length % tp_size == 0 && cfg->vocab_size % tp_size == 0);
     memset(model, 0, sizeof(*model));
-    model->b200.tp_size = 1;
+    model->b200.tp_size = tp_size;
+    model->b200.tp_rank = tp_rank;
     set_defaults(model);
     model->meta.block_count = cfg->block_count;
     model->meta.context_length = cfg->context_length;
@@ -462,13 +479,23 @@ extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context
     float sd = cfg->init_std > 0 ? cfg->init_std : 0.02f;
     uint64_t tid = 0;
     vkllm_err_t e;
-    auto make16 = [&](const char *name, uint32_t rows, uint32_t cols, vkllm_tensor **out) -> vkllm_err_t {
-        uint32_t sh[4] = {1, 1, rows, cols};
+    // The tensor-parallel shard of rank r of N: rows [r rows/N, (r+1) rows/N) (split = 1: Wq/Wk/Wv,
+    // Wgate/Wup, output) or columns [r cols/N, ...) (split = 2: Wo, Wdown) of the full matrix, with the
+    // full matrix's element bits; split = 0 keeps the whole tensor (embedding).
+    auto make16s = [&](const char *name, uint32_t rows, uint32_t cols, int split, vkllm_tensor **out) -> vkllm_err_t {
+        const uint32_t lr = split == 1 ? rows / tp_size : rows, lc = split == 2 ? cols / tp_size : cols;
+        const uint32_t r0 = split == 1 ? tp_rank * lr : 0, c0 = split == 2 ? tp_rank * lc : 0;
+        uint32_t sh[4] = {1, 1, lr, lc};
         _CHECK(vkllm_tensor_new(context, name, sh, vkllm_dtype_float16, VKLLM_OP_NONE, NULL, 0, NULL, 0, false, out));
         void *d = vkb::dev_ptr(context, *out);
         if (!d)
             return VKLLM_ERR_ALLOC;
-        return vkb::fill_random_f16(context, d, (uint64_t)rows * cols, seed, tid++, sd);
+        if (tp_size == 1)
+            return vkb::fill_random_f16(context, d, (uint64_t)rows * cols, seed, tid++, sd);
+        return vkb::fill_random_f16_shard(context, d, lr, lc, cols, r0, c0, seed, tid++, sd);
+    };
+    auto make16 = [&](const char *name, uint32_t rows, uint32_t cols, vkllm_tensor **out) -> vkllm_err_t {
+        return make16s(name, rows, cols, 0, out);
     };
     auto make32 = [&](const char *name, uint32_t n, vkllm_tensor **out) -> vkllm_err_t {
         uint32_t sh[4] = {1, 1, 1, n};
@@ -499,30 +526,30 @@ extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context
         if ((e = make32(name, D, &bw->ffn_norm_weight)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.attn_q.weight", i);
-        if ((e = make16(name, D, D, &bw->WQ)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, D, D, 1, &bw->WQ)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.attn_k.weight", i);
-        if ((e = make16(name, D, D, &bw->WK)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, D, D, 1, &bw->WK)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.attn_v.weight", i);
-        if ((e = make16(name, D, D, &bw->WV)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, D, D, 1, &bw->WV)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.attn_output.weight", i);
-        if ((e = make16(name, D, D, &bw->WO)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, D, D, 2, &bw->WO)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.ffn_gate.weight", i);
-        if ((e = make16(name, F, D, &bw->WG)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, F, D, 1, &bw->WG)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.ffn_up.weight", i);
-        if ((e = make16(name, F, D, &bw->WU)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, F, D, 1, &bw->WU)) != VKLLM_ERR_OK)
             goto fail;
         snprintf(name, sizeof(name), "blk.%u.ffn_down.weight", i);
-        if ((e = make16(name, D, F, &bw->WD)) != VKLLM_ERR_OK)
+        if ((e = make16s(name, D, F, 2, &bw->WD)) != VKLLM_ERR_OK)
             goto fail;
     }
     if ((e = make32("output_norm.weight", D, &model->weights.output_norm_weight)) != VKLLM_ERR_OK)
         goto fail;
-    if ((e = make16("output.weight", V, D, &model->weights.output_weight)) != VKLLM_ERR_OK)
+    if ((e = make16s("output.weight", V, D, 1, &model->weights.output_weight)) != VKLLM_ERR_OK)
         goto fail;
     if (cudaStreamSynchronize(context->runtime->stream) != cudaSuccess)
     {

@@ -177,6 +177,10 @@ _SIGS = {
     "vkllm_b200_batch_read_tokens": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32]),
     "vkllm_b200_batch_read_logits": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "vkllm_b200_batch_free": (None, [C.c_void_p, C.c_void_p]),
+    "vkllm_b200_models_llama2_init_random_tp": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.POINTER(Llama2Config),
+                                                          C.c_uint64, C.c_uint32, C.c_uint32]),
+    "vkllm_b200_tp_init": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
+    "vkllm_b200_tp_connect": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
     "vkllm_b200_engine_bench_kernel": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
                                                  C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
     "vkllm_b200_attention_decode_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
@@ -396,6 +400,23 @@ class Model:
               "llama2_init_random")
         self.loaded = True
         return self
+
+    def init_random_tp(self, cfg: dict, seed: int, rank: int, world: int):
+        """Tensor-parallel shard `rank` of `world` of the random model of init_random."""
+        c = Llama2Config(**cfg)
+        check(lib().vkllm_b200_models_llama2_init_random_tp(self.ctx.ptr, C.byref(self.m), C.byref(c), seed, rank,
+                                                             world), "llama2_init_random_tp")
+        self.loaded = True
+        return self
+
+    def tp_connect(self, all_gather):
+        """Sets up the peer-memory exchange: `all_gather(bytes) -> list of bytes` (rank order) is the
+        caller's collective, e.g. torch.distributed.all_gather_object."""
+        h = (C.c_char * 64)()
+        check(lib().vkllm_b200_tp_init(self.ctx.ptr, C.byref(self.m), h), "tp_init")
+        handles = all_gather(bytes(h))
+        buf = (C.c_char * (64 * len(handles))).from_buffer_copy(b"".join(handles))
+        check(lib().vkllm_b200_tp_connect(self.ctx.ptr, C.byref(self.m), buf), "tp_connect")
 
     def free(self):
         if self.loaded:
