@@ -265,6 +265,67 @@ def batched_decode_leg(vk, model, args, world, rank, stream):
             "path": "tcgen05 GEMMs (M = sequences per rank, split-K) + per-sequence RoPE/KV/attention kernels, CUDA graph per step"}
 
 
+CFG_13B = dict(block_count=40, context_length=4096, embedding_length=5120, head_count=40, ffn_length=13824,
+               vocab_size=32000, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
+
+
+def tp13b_leg(vk, ctx, args, world, rank, stream):
+    """LLaMA-2-13B, tensor parallel over the ranks (heads / FFN rows / vocabulary
+    sharded; the Wo and down partial sums exchanged inside the persistent decode kernel over peer
+    memory). Batch-1 greedy decode at positions 2048.. (the prompt length of the config); the KV rows
+    before 2048 are the zeroed cache, since only decode throughput is measured here (a 2048-token TP
+    prefill is not part of this leg). Returns tokens/s (max-over-ranks device time)."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    cfg = dict(CFG_13B)
+    l = vk.lib()
+    m = vk.Model(ctx)
+    if world > 1:
+        m.init_random_tp(cfg, SEED, rank, world)
+
+        def gather(b):
+            got = [None] * world
+            dist.all_gather_object(got, b)
+            return got
+
+        m.tp_connect(gather)
+    else:
+        m.init_random(cfg, SEED)
+    try:
+        P, K, W = 2048, args.tp_steps, 3
+        vk.check(l.vkllm_b200_engine_set_state(ctx.ptr, C.byref(m.m), 1, P), "set_state")
+        vk.check(l.vkllm_b200_engine_decode_steps(ctx.ptr, C.byref(m.m), W), "warmup")
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        vk.check(l.vkllm_b200_engine_decode_steps(ctx.ptr, C.byref(m.m), K), "decode")
+        e1.record(stream)
+        e1.synchronize()
+        toks = np.zeros(W + K, dtype=np.uint32)
+        vk.check(l.vkllm_b200_engine_read_tokens(ctx.ptr, C.byref(m.m), toks.ctypes.data, W + K), "tokens")
+        ms = max_over_ranks(world, e0.elapsed_time(e1))
+        persistent = bool(l.vkllm_b200_engine_is_persistent(ctx.ptr, C.byref(m.m)))
+    finally:
+        m.free()
+    D, F, V, L = cfg["embedding_length"], cfg["ffn_length"], cfg["vocab_size"], cfg["block_count"]
+    w_rank = (L * ((4 * D * D + 3 * F * D) * 2) + V * D * 2) / world + L * 2 * D * 4 + D * 4 + D * 2
+    mean_lk = P + W + (K + 1) / 2.0
+    kv_rank = L * 2 * D * 2 * mean_lk / world
+    peak, _ = measured_peaks()
+    ms_tok = ms / K
+    return {"model": "llama2-13b-arch", "tp": world, "tok_s": round(K / (ms / 1000.0), 2),
+            "ms_per_token": round(ms_tok, 4), "positions": [P + W, P + W + K],
+            "bytes_per_token_per_rank": int(w_rank + kv_rank),
+            "hbm_frac_per_rank": round((w_rank + kv_rank) / (ms_tok * 1e-3) / 1e9 / peak, 4),
+            "allreduce": "fused in the decode kernel: per layer 2 x D fp32 row partials over NVLink peer memory" if world > 1 else "none (1 GPU)",
+            "path": "persistent kernel" if persistent else "graph", "kv": "zeroed cache below position 2048 (decode-only leg)"}
+
+
 def run_ours(args, world, rank, local):
     import numpy as np
     import torch
@@ -442,6 +503,11 @@ def run_ours(args, world, rank, local):
         except Exception as e:  # the baseline must not void the GPU measurement
             result["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     model.free()
+    # ---- 13B tensor parallel ---------------------------------------------------
+    if args.tp_steps > 0:
+        tp = tp13b_leg(vk, ctx, args, world, rank, stream)
+        if result is not None:
+            result["tp13b"] = tp
     ctx.close()
     return result
 
@@ -518,6 +584,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch-seqs", type=int, default=64)
     ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--tp-steps", type=int, default=32, help="13B tensor-parallel decode leg (0: skip)")
     # Profiling case only (ncu): fewer layers, no prefill / e2e / per-kernel extras, no JSON result line.
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-extras", action="store_true")

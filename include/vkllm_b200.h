@@ -70,6 +70,16 @@ extern vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct vkll
 extern vkllm_err_t vkllm_b200_tp_connect(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                          const void *handles);
 
+/* The shard of a rows x cols matrix held by tensor-parallel rank tp_rank of tp_size: split 1 = rows
+ * (Wq, Wk, Wv, Wgate, Wup, output), 2 = columns (Wo, Wdown), 0 = whole (embedding). out = {row0, rows,
+ * col0, cols} of the shard in the unsharded matrix. Host only. */
+extern vkllm_err_t vkllm_b200_tp_shard(uint32_t rows, uint32_t cols, int split, uint32_t tp_rank, uint32_t tp_size,
+                                       uint32_t *out);
+/* Host twin of a shard of the device generator: element (i, c) is element (row0 + i) * full_cols +
+ * col0 + c of tensor `tensor_id` (what init_random_tp writes on the device). */
+extern void vkllm_b200_random_f16_host_shard(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t full_cols,
+                                             uint32_t row0, uint32_t rows, uint32_t col0, uint32_t cols, uint16_t *out);
+
 /* Host-side twin of the device generator: the fp16 bit patterns of elements [first, first + n) of
  * tensor `tensor_id` (for CPU references of randomly initialised models). */
 extern void vkllm_b200_random_f16_host(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t first, uint64_t n,

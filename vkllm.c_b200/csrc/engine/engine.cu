@@ -258,7 +258,14 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     }
     if (dd.hd % 8 != 0 || dd.hd > 256)
         return;
-    const size_t optin = ctx->device->smem_optin;
+    // dynamic shared memory may use the opt-in limit minus the kernel's static shared memory
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, k_decode_persistent) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return;
+    }
+    const size_t optin = ctx->device->smem_optin > fa.sharedSizeBytes ? ctx->device->smem_optin - fa.sharedSizeBytes : 0;
     const size_t fixed = kStreamBarBytes + P.xs_bytes + P.part_bytes;
     uint32_t warps = optin > fixed ? (uint32_t)((optin - fixed) / ((size_t)P.spw * kTileBytes)) : 0;
     if (warps > (uint32_t)kStreamMaxWarps)
@@ -755,6 +762,17 @@ static uint16_t f32_to_f16_rne(float f)
 } // namespace vkb
 
 using namespace vkb;
+
+extern "C" void vkllm_b200_random_f16_host_shard(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t full_cols,
+                                                 uint32_t row0, uint32_t rows, uint32_t col0, uint32_t cols,
+                                                 uint16_t *out)
+{
+    const float scale = std_dev * (1.0f / 65536.0f);
+    const uint64_t key = tensor_key(seed, tensor_id);
+    for (uint64_t i = 0; i < rows; ++i)
+        for (uint64_t c = 0; c < cols; ++c)
+            out[i * cols + c] = f32_to_f16_rne(random_value(key, (row0 + i) * full_cols + col0 + c, scale));
+}
 
 extern "C" void vkllm_b200_random_f16_host(uint64_t seed, uint64_t tensor_id, float std_dev, uint64_t first,
                                            uint64_t n, uint16_t *out)

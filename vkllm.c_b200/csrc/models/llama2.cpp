@@ -443,6 +443,22 @@ extern "C" vkllm_err_t vkllm_models_llama2_tokenize(struct vkllm_models_llama2 *
 // ------------------------------------------------------------------------------------------------
 // Random initialisation on the device (no GGUF): same tensors, names and shapes as the GGUF loader
 // produces, fp16 weights ~ N(0, std) from a counter-based generator, f32 norm gains = 1.
+// Tensor-parallel shard of one matrix (rows x cols of the unsharded model) for rank r of N:
+// split 1 = rows, split 2 = columns, 0 = whole. out = {row0, rows, col0, cols}.
+extern "C" vkllm_err_t vkllm_b200_tp_shard(uint32_t rows, uint32_t cols, int split, uint32_t tp_rank,
+                                           uint32_t tp_size, uint32_t *out)
+{
+    _CHECK_ARGS(out && tp_size >= 1 && tp_rank < tp_size && split >= 0 && split <= 2);
+    _CHECK_ARGS(split != 1 || rows % tp_size == 0);
+    _CHECK_ARGS(split != 2 || cols % tp_size == 0);
+    const uint32_t lr = split == 1 ? rows / tp_size : rows, lc = split == 2 ? cols / tp_size : cols;
+    out[0] = split == 1 ? tp_rank * lr : 0;
+    out[1] = lr;
+    out[2] = split == 2 ? tp_rank * lc : 0;
+    out[3] = lc;
+    return VKLLM_ERR_OK;
+}
+
 extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random(struct vkllm_context *context,
                                                             struct vkllm_models_llama2 *model,
                                                             const struct vkllm_b200_llama2_config *cfg,
@@ -483,8 +499,9 @@ extern "C" vkllm_err_t vkllm_b200_models_llama2_init_random_tp(struct vkllm_cont
     // Wgate/Wup, output) or columns [r cols/N, ...) (split = 2: Wo, Wdown) of the full matrix, with the
     // full matrix's element bits; split = 0 keeps the whole tensor (embedding).
     auto make16s = [&](const char *name, uint32_t rows, uint32_t cols, int split, vkllm_tensor **out) -> vkllm_err_t {
-        const uint32_t lr = split == 1 ? rows / tp_size : rows, lc = split == 2 ? cols / tp_size : cols;
-        const uint32_t r0 = split == 1 ? tp_rank * lr : 0, c0 = split == 2 ? tp_rank * lc : 0;
+        uint32_t sp[4];
+        _CHECK(vkllm_b200_tp_shard(rows, cols, split, tp_rank, tp_size, sp));
+        const uint32_t r0 = sp[0], lr = sp[1], c0 = sp[2], lc = sp[3];
         uint32_t sh[4] = {1, 1, lr, lc};
         _CHECK(vkllm_tensor_new(context, name, sh, vkllm_dtype_float16, VKLLM_OP_NONE, NULL, 0, NULL, 0, false, out));
         void *d = vkb::dev_ptr(context, *out);

@@ -180,6 +180,9 @@ _SIGS = {
     "vkllm_b200_models_llama2_init_random_tp": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.POINTER(Llama2Config),
                                                           C.c_uint64, C.c_uint32, C.c_uint32]),
     "vkllm_b200_tp_init": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
+    "vkllm_b200_tp_shard": (C.c_int, [C.c_uint32, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "vkllm_b200_random_f16_host_shard": (None, [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint32, C.c_uint32,
+                                                C.c_uint32, C.c_uint32, C.c_void_p]),
     "vkllm_b200_tp_connect": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
     "vkllm_b200_engine_bench_kernel": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
                                                  C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
