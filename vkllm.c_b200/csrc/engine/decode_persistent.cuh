@@ -6,12 +6,14 @@
 // CTA waits at a grid barrier, or computes attention, the next matrix's weights are already
 // landing. Activations are exchanged through global memory between grid barriers.
 //
-// Weight tiles: a CTA owns a contiguous range of output rows of each matrix; they are cut into
-// tiles of 16 rows x 256 columns (one 512 B bulk copy per row, rows 528 B apart in shared memory
-// so that ldmatrix reads are free of bank conflicts). A warp reduces a tile against the staged
+// Weight tiles: a CTA owns a contiguous range of output rows of each matrix, cut into tiles of 16
+// rows x 256 columns. The engine keeps a decode copy of the weights in which every tile is
+// contiguous in HBM (tiles in the order the CTA consumes them, each CTA's tiles where its rows are
+// in the row-major matrix) with the 16-byte chunks of tile row r XOR-swizzled by r & 7, so a tile is
+// ONE bulk copy (the bulk-copy request rate of one SM, not HBM, limits 512 B row copies) and the
+// ldmatrix reads of 8 rows hit 8 different bank groups. A warp reduces a tile against the staged
 // fp16 input vector with mma.sync m16n8k16 (the vector is the B operand, replicated over the 8
-// columns; products exact, fp32 accumulation), so shared memory sees each weight byte once per
-// write and once per read, and the warp issues ~4 instructions per 512 B. The tile partials land
+// columns; products exact, fp32 accumulation): ~4 instructions per 512 B. The tile partials land
 // in a per-CTA [segment][row] buffer that is summed in a fixed order after the phase.
 //
 // Phases:
@@ -52,8 +54,14 @@ constexpr uint32_t kErrPosition = 0x1;
 #endif
 constexpr uint32_t kTileRows = 16;                        // MMA M
 constexpr uint32_t kSegHalves = VKB_PERSIST_SEG;          // columns per tile (one bulk copy per row)
-constexpr uint32_t kRowPitch = 2 * kSegHalves + 16;       // bytes between tile rows in shared memory
-constexpr uint32_t kTileBytes = kTileRows * kRowPitch;    // one stage
+constexpr uint32_t kTileBytes = kTileRows * kSegHalves * 2; // one stage (a full tile)
+
+// Physical 16-byte chunk of logical chunk c in row r of a tile whose rows hold nchunks chunks:
+// swizzled within aligned groups of 8 (the tail of a row that is not a whole group stays in place).
+__host__ __device__ __forceinline__ uint32_t tile_chunk(uint32_t c, uint32_t r, uint32_t nchunks)
+{
+    return ((c | 7u) < nchunks) ? (c ^ (r & 7u)) : c;
+}
 
 // Geometry of one GEMV phase kind: `units` outputs of `nm` rows each, rows of K columns cut into
 // Ks segments of kSegHalves (the last one `last` wide, a multiple of 16).
@@ -90,6 +98,8 @@ struct PersistParams
     uint32_t part_bytes;    // tile partials; xs + part also serve as the attention scratch
     uint32_t n_steps;
     uint32_t att_split;     // key splits per head in the attention phases
+    const __half *const *tiled; // decode copy of the weights: [layer * 4 + kind] (QKV, Wo, up/gate, down)
+    const __half *tiled_logits; // decode copy of the output matrix
     uint64_t *trace;        // optional: CTA 0 records %globaltimer at every barrier arrival/release
     uint32_t trace_cap;     // entries available in `trace`
     unsigned long long *wtrace; // optional: CTA 0 per (warp, kind): wait, consume, chunks, compute part
@@ -190,29 +200,6 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p)
 __device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v)
 {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// The weight row `m` of unit `u` of phase (kind, layer).
-__device__ __forceinline__ const __half *persist_row(const PersistParams &P, uint32_t kind, const LayerW &lw,
-                                                     uint32_t u, uint32_t m)
-{
-    const DecodeDims &dd = P.dd;
-    switch (kind)
-    {
-    case PK_QKV: {
-        const uint32_t HD = dd.H * dd.hd, row = 2 * u + m, which = row / HD, r = row % HD;
-        const __half *base = which == 0 ? lw.wq : (which == 1 ? lw.wk : lw.wv);
-        return base + (uint64_t)r * dd.D;
-    }
-    case PK_WO:
-        return lw.wo + (uint64_t)u * dd.H * dd.hd;
-    case PK_UPGATE:
-        return (m == 0 ? lw.wu : lw.wg) + (uint64_t)u * dd.D;
-    case PK_DOWN:
-        return lw.wd + (uint64_t)u * dd.F;
-    default:
-        return P.wout + (uint64_t)u * dd.D;
-    }
 }
 
 struct UnitRange
@@ -322,36 +309,34 @@ __device__ __forceinline__ void cursor_settle(const PersistParams &P, Cursor &c,
     }
 }
 
-// Issues the copies of the cursor's tile into `dst` (whole warp: lane i copies row i); with
-// dst == nullptr, prefetches the tile into L2 instead.
+// This CTA's region of a phase matrix in the decode copy: its rows' bytes of the row-major matrix.
+__device__ __forceinline__ const __half *tiled_region(const PersistParams &P, uint32_t kind, uint32_t layer,
+                                                      const TileGeom &g, const UnitRange &r)
+{
+    const __half *base = kind == PK_LOGITS ? P.tiled_logits : P.tiled[layer * 4 + kind];
+    return base + (uint64_t)r.u0 * g.nm * g.K;
+}
+
+// Issues the single bulk copy of the cursor's tile into `dst` (lane 0).
 __device__ __forceinline__ void cursor_issue(const PersistParams &P, const Cursor &c, uint32_t w, unsigned char *dst,
                                              uint64_t *bar, uint64_t policy)
 {
     const uint32_t lane = threadIdx.x & 31;
+    if (lane != 0)
+        return;
     const TileGeom &g = P.tg[c.kind];
     const UnitRange r = cta_units(g.units);
-    const LayerW &lw = P.layers[c.kind == PK_LOGITS ? 0 : c.layer];
     const uint32_t t = w + P.warps * c.k, grp = t / g.Ks, ks = t % g.Ks;
     const uint32_t r0 = grp * kTileRows, nvalid = min(kTileRows, r.count * g.nm - r0);
-    const uint32_t bytes = 2 * (ks + 1 == g.Ks ? g.last : kSegHalves);
-    if (dst && lane == 0)
-        mbar_arrive_expect_tx(bar, nvalid * bytes);
-    __syncwarp();
-    if (lane < nvalid)
-    {
-        const uint32_t row = r0 + lane;
-        const __half *src = persist_row(P, c.kind, lw, r.u0 + row / g.nm, row % g.nm) + (size_t)ks * kSegHalves;
-        if (dst)
-        {
-            fence_proxy_async(); // this warp's earlier reads of the stage precede the async refill
-            if (policy)
-                bulk_g2s_hint(dst + lane * kRowPitch, src, bytes, bar, policy);
-            else
-                bulk_g2s(dst + lane * kRowPitch, src, bytes, bar);
-        }
-        else
-            bulk_prefetch_l2(src, bytes);
-    }
+    const uint32_t width = ks + 1 == g.Ks ? g.last : kSegHalves;
+    const __half *src = tiled_region(P, c.kind, c.layer, g, r) + (uint64_t)r0 * g.K + (uint64_t)ks * nvalid * kSegHalves;
+    const uint32_t bytes = nvalid * width * 2;
+    mbar_arrive_expect_tx(bar, bytes);
+    fence_proxy_async(); // this warp's earlier reads of the stage precede the async refill
+    if (policy)
+        bulk_g2s_hint(dst, src, bytes, bar, policy);
+    else
+        bulk_g2s(dst, src, bytes, bar);
 }
 
 // Per-warp pipeline state.
@@ -385,39 +370,13 @@ __device__ __forceinline__ void prefetch_slice(const PersistParams &P, uint32_t 
         return;
     const TileGeom &g = P.tg[kind];
     const UnitRange r = cta_units(g.units);
-    const LayerW &lw = P.layers[kind == PK_LOGITS ? 0 : layer];
-    const uint32_t row_bytes = g.K * 2, unit_bytes = g.nm * row_bytes;
-    const uint32_t staged_rows = (P.warps * P.spw + g.Ks - 1) / g.Ks * kTileRows;
-    const uint32_t skip = (staged_rows + g.nm - 1) / g.nm;
-    if (skip >= r.count)
+    const uint64_t region = (uint64_t)r.count * g.nm * g.K * 2, staged = (uint64_t)P.warps * P.spw * kTileBytes;
+    if (staged >= region)
         return;
-    uint32_t n = min(r.count - skip, P.l2_bytes / unit_bytes);
-    uint32_t u = r.u0 + skip;
-    constexpr uint32_t kPiece = 64 * 1024;
-    auto run = [&](const __half *p, uint32_t bytes) {
-        const char *c = reinterpret_cast<const char *>(p);
-        for (uint32_t o = 0; o < bytes; o += kPiece)
-            bulk_prefetch_l2(c + o, min(kPiece, bytes - o));
-    };
-    if (kind == PK_QKV)
-    {
-        // unit u = rows 2u, 2u+1 of [Wq; Wk; Wv], split where the matrix changes
-        const uint32_t HD = P.dd.H * P.dd.hd;
-        uint32_t row = 2 * u, end = 2 * (u + n);
-        while (row < end)
-        {
-            const uint32_t which = row / HD, stop = min(end, (which + 1) * HD);
-            run(persist_row(P, kind, lw, row / 2, row % 2), (stop - row) * row_bytes);
-            row = stop;
-        }
-    }
-    else if (kind == PK_UPGATE)
-    {
-        run(persist_row(P, kind, lw, u, 0), n * row_bytes);
-        run(persist_row(P, kind, lw, u, 1), n * row_bytes);
-    }
-    else
-        run(persist_row(P, kind, lw, u, 0), n * row_bytes);
+    const char *c = reinterpret_cast<const char *>(tiled_region(P, kind, layer, g, r)) + staged;
+    const uint64_t n = min((uint64_t)P.l2_bytes, region - staged);
+    for (uint64_t o = 0; o < n; o += 65536)
+        bulk_prefetch_l2(c + o, (uint32_t)min((uint64_t)65536, n - o));
 }
 
 // Epilogue of one unit of a GEMV phase (executed by one lane).
@@ -521,7 +480,9 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
         const uint32_t t = warp + P.warps * k, grp = t / g.Ks, ks = t % g.Ks;
         const uint32_t width = ks + 1 == g.Ks ? g.last : kSegHalves;
         const unsigned char *st = wp.stage + (size_t)s * kTileBytes;
-        const uint32_t a_addr = smem_u32(st + (lane & 15) * kRowPitch + (lane >> 4) * 16);
+        // ldmatrix rows: lanes 0-15 -> tile rows 0-15 at chunk 2j, lanes 16-31 -> rows 0-15 at chunk 2j + 1
+        const uint32_t tr = lane & 15, half = lane >> 4, nchunks = width >> 3;
+        const uint32_t row_addr = smem_u32(st + tr * width * 2);
         const uint32_t *xk = reinterpret_cast<const uint32_t *>(xs + ks * kSegHalves + 2 * (lane & 3));
         // two accumulator chains (even / odd k-steps) halve the dependent MMA latency
         float c[4] = {0.f, 0.f, 0.f, 0.f}, d[4] = {0.f, 0.f, 0.f, 0.f};
@@ -530,15 +491,15 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
         for (; kk + 32 <= width; kk += 32)
         {
             uint32_t a0, a1, a2, a3, e0, e1, e2, e3;
-            ldsm_x4(a_addr + kk * 2, a0, a1, a2, a3);
-            ldsm_x4(a_addr + kk * 2 + 32, e0, e1, e2, e3);
+            ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + half, tr, nchunks), a0, a1, a2, a3);
+            ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + 2 + half, tr, nchunks), e0, e1, e2, e3);
             mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
             mma_16816(d, e0, e1, e2, e3, xk[kk / 2 + 8], xk[kk / 2 + 12]);
         }
         if (kk < width)
         {
             uint32_t a0, a1, a2, a3;
-            ldsm_x4(a_addr + kk * 2, a0, a1, a2, a3);
+            ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + half, tr, nchunks), a0, a1, a2, a3);
             mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
         }
         if ((lane & 3) == 0)

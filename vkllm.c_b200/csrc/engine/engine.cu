@@ -50,6 +50,8 @@ struct Engine
     uint32_t *am_idx = nullptr, *bar = nullptr; // bar[0] = barrier arrivals, then 2 x H attention counters
     uint32_t launches = 0;                      // kernel launches enqueued by the last decode call
     TpComm *tp = nullptr;                       // tensor-parallel exchange (shards only)
+    __half *tiled = nullptr;                    // decode copy of the weights (persistent kernel's tile layout)
+    void *d_tiled_ptrs = nullptr;               // [layer * 4 + phase] pointers into `tiled`
 };
 
 // Peer-memory exchange of a tensor-parallel rank: one device buffer, exported with CUDA IPC, holding
@@ -168,6 +170,43 @@ template <class Op> void allow_smem(const StreamGeom &g)
 }
 
 // Persistent decode geometry: every phase kind shares the block size and stage layout.
+// Decode copy of one phase matrix (the persistent kernel's tile layout): logical row R (mode 0: rows
+// of s0, then s1, then s2; mode 1: rows alternate s0, s1, i.e. up/gate pairs) belongs to the CTA
+// owning unit R / nm; within that CTA's rows, 16-row groups, then K segments, are contiguous tiles
+// whose rows hold the segment's chunks swizzled by tile_chunk.
+__global__ void k_relayout(__half *__restrict__ dst, const __half *s0, const __half *s1, const __half *s2,
+                           uint32_t rows0, uint32_t rows1, int mode, uint32_t K, uint32_t total_rows, uint32_t nm,
+                           uint32_t units, uint32_t grid)
+{
+    const uint32_t nch = K / 8;
+    const uint64_t n = (uint64_t)total_rows * nch;
+    const uint32_t base = units / grid, rem = units % grid;
+    const uint32_t Ks = (K + kSegHalves - 1) / kSegHalves, last = K - kSegHalves * (Ks - 1);
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < n; t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t R = (uint32_t)(t / nch), c = (uint32_t)(t % nch);
+        const __half *src;
+        if (mode == 1)
+            src = ((R & 1u) ? s1 : s0) + (uint64_t)(R >> 1) * K;
+        else if (R < rows0)
+            src = s0 + (uint64_t)R * K;
+        else if (R < rows0 + rows1)
+            src = s1 + (uint64_t)(R - rows0) * K;
+        else
+            src = s2 + (uint64_t)(R - rows0 - rows1) * K;
+        const uint32_t u = R / nm;
+        const uint32_t b = u < rem * (base + 1) ? u / (base + 1) : rem + (u - rem * (base + 1)) / base;
+        const uint32_t u0 = b * base + min(b, rem), cnt = base + (b < rem ? 1u : 0u);
+        const uint32_t rl = R - u0 * nm, rows_b = cnt * nm;
+        const uint32_t g = rl / kTileRows, r = rl % kTileRows, nv = min(kTileRows, rows_b - g * kTileRows);
+        const uint32_t ks = c / (kSegHalves / 8), cc = c % (kSegHalves / 8);
+        const uint32_t width = ks + 1 == Ks ? last : kSegHalves;
+        const uint64_t off = (uint64_t)u0 * nm * K + (uint64_t)g * kTileRows * K + (uint64_t)ks * nv * kSegHalves +
+                             (uint64_t)r * width + (uint64_t)tile_chunk(cc, r, width / 8) * 8;
+        *reinterpret_cast<uint4 *>(dst + off) = *reinterpret_cast<const uint4 *>(src + (uint64_t)c * 8);
+    }
+}
+
 void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_t spw, uint32_t l2_kb)
 {
     const char *mode = getenv("VKLLM_B200_DECODE");
@@ -310,6 +349,51 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
         (void)cudaGetLastError();
         return;
     }
+    // Decode copy of the weights in the tile layout (one bulk copy per tile).
+    const uint32_t L = (uint32_t)e->layers.size();
+    const size_t per_layer = (size_t)3 * HD * dd.D + (size_t)dd.D * HD + (size_t)2 * dd.F * dd.D + (size_t)dd.D * dd.F;
+    const size_t halves = per_layer * L + (size_t)dd.V * dd.D;
+    if (cudaMalloc(&e->tiled, halves * sizeof(__half)) != cudaSuccess ||
+        cudaMalloc(&e->d_tiled_ptrs, sizeof(__half *) * 4 * L) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        log_info("no room for the decode copy of the weights (%zu MB); decode runs on the CUDA-graph path",
+                 halves * 2 >> 20);
+        if (e->tiled)
+            cudaFree(e->tiled);
+        e->tiled = nullptr;
+        return;
+    }
+    std::vector<const __half *> ptrs(4 * L);
+    cudaStream_t st = ctx->runtime->stream;
+    const unsigned rb = (unsigned)ctx->device->sm_count * 8;
+    __half *cur = e->tiled;
+    for (uint32_t l = 0; l < L; ++l)
+    {
+        const LayerW &w = e->layers[l];
+        ptrs[4 * l + PK_QKV] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wq, w.wk, w.wv, HD, HD, 0, dd.D, 3 * HD, 2, 3 * HD / 2, grid);
+        cur += (size_t)3 * HD * dd.D;
+        ptrs[4 * l + PK_WO] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wo, nullptr, nullptr, dd.D, 0, 0, HD, dd.D, 1, dd.D, grid);
+        cur += (size_t)dd.D * HD;
+        ptrs[4 * l + PK_UPGATE] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wu, w.wg, nullptr, 0, 0, 1, dd.D, 2 * dd.F, 2, dd.F, grid);
+        cur += (size_t)2 * dd.F * dd.D;
+        ptrs[4 * l + PK_DOWN] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wd, nullptr, nullptr, dd.D, 0, 0, dd.F, dd.D, 1, dd.D, grid);
+        cur += (size_t)dd.D * dd.F;
+    }
+    k_relayout<<<rb, 256, 0, st>>>(cur, e->wout, nullptr, nullptr, dd.V, 0, 0, dd.D, dd.V, 1, dd.V, grid);
+    P.tiled_logits = cur;
+    if (cudaMemcpyAsync(e->d_tiled_ptrs, ptrs.data(), sizeof(__half *) * 4 * L, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return;
+    }
+    P.tiled = (const __half *const *)e->d_tiled_ptrs;
     if (cudaMalloc(&e->d_layers, sizeof(LayerW) * e->layers.size()) != cudaSuccess)
     {
         (void)cudaGetLastError();
@@ -602,6 +686,10 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
     cudaFree(e->ws);
     if (e->d_layers)
         cudaFree(e->d_layers);
+    if (e->tiled)
+        cudaFree(e->tiled);
+    if (e->d_tiled_ptrs)
+        cudaFree(e->d_tiled_ptrs);
     if (e->pp.trace)
         cudaFree(e->pp.trace);
     if (e->pp.wtrace)
