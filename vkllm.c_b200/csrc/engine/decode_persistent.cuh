@@ -583,14 +583,19 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
         __syncthreads();
         const __half *kb = lw.kcache + (uint64_t)h * dd.ctx * hd;
         float mx = -FLT_MAX;
+        // one round of key rows loads ahead of the round being reduced
+        uint4 nxt = (lane_on && j0 + gi < j1) ? __ldcg(reinterpret_cast<const uint4 *>(kb + (uint64_t)(j0 + gi) * hd) + pc)
+                                              : make_uint4(0, 0, 0, 0);
         for (uint32_t rr = 0; rr < rounds; ++rr)
         {
             const uint32_t j = j0 + gi + G * rr;
             const bool valid = lane_on && j < j1;
+            const uint4 raw = nxt;
+            if (rr + 1 < rounds && lane_on && j + G < j1)
+                nxt = __ldcg(reinterpret_cast<const uint4 *>(kb + (uint64_t)(j + G) * hd) + pc);
             float a = 0.f;
             if (valid)
             {
-                const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(kb + (uint64_t)j * hd) + pc);
                 const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
@@ -655,15 +660,20 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
         __syncthreads();
         if (!flag_s)
             return false;
-        float M = -FLT_MAX, L = 0.f;
-        for (uint32_t c = 0; c < ns; ++c)
-            M = fmaxf(M, __ldcg(P.part + h * ns + c).x);
-        for (uint32_t c = 0; c < ns; ++c)
+        // the head's max and sum over its splits (ns <= 32: one lane per split), broadcast in smem
+        if (tid < 32)
         {
-            const float2 pl = __ldcg(P.part + h * ns + c);
-            if (pl.y > 0.f)
-                L += pl.y * expf(pl.x - M);
+            const float2 pl = tid < ns ? __ldcg(P.part + h * ns + tid) : make_float2(-FLT_MAX, 0.f);
+            const float Mw = warp_max(pl.x);
+            const float Lw = warp_sum(pl.y > 0.f ? pl.y * expf(pl.x - Mw) : 0.f);
+            if (tid == 0)
+            {
+                red[0] = Mw;
+                red[1] = Lw;
+            }
         }
+        __syncthreads();
+        const float M = red[0], L = red[1];
         const __half *vb = lw.vcache + (uint64_t)h * dd.ctx * hd;
         float *op = P.opart + ((uint64_t)h * ns + split) * hd;
         if (Lk == hd)
@@ -685,13 +695,17 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
         else
         {
             float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            uint4 vn = (lane_on && j0 + gi < j1) ? __ldcg(reinterpret_cast<const uint4 *>(vb + (uint64_t)(j0 + gi) * hd) + pc)
+                                                 : make_uint4(0, 0, 0, 0);
             for (uint32_t rr = 0; rr < rounds; ++rr)
             {
                 const uint32_t j = j0 + gi + G * rr;
+                const uint4 raw = vn;
+                if (rr + 1 < rounds && lane_on && j + G < j1)
+                    vn = __ldcg(reinterpret_cast<const uint4 *>(vb + (uint64_t)(j + G) * hd) + pc);
                 if (lane_on && j < j1)
                 {
                     const float pj = round_f16(expf(sc[j - j0] - M) / L);
-                    const uint4 raw = __ldcg(reinterpret_cast<const uint4 *>(vb + (uint64_t)j * hd) + pc);
                     const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
@@ -702,16 +716,23 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                     }
                 }
             }
-            if (lane_on)
+            // the key groups of a warp (32 / lpk of them) are summed with shuffles, then the warps'
+            // sums in smem, in warp order
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                for (uint32_t o = lpk; o < 32; o <<= 1)
+                    a[e] += __shfl_xor_sync(0xffffffffu, a[e], o);
+            const uint32_t lane = tid & 31, nwarp = nt >> 5;
+            if (lane < lpk && pc < pieces)
 #pragma unroll
                 for (int e = 0; e < 8; ++e)
-                    acc[gi * hd + 8 * pc + e] = a[e];
+                    acc[(tid >> 5) * hd + 8 * pc + e] = a[e];
             __syncthreads();
             for (uint32_t d = tid; d < hd; d += nt)
             {
                 float o = 0.f;
-                for (uint32_t g = 0; g < G; ++g)
-                    o += acc[g * hd + d];
+                for (uint32_t w = 0; w < nwarp; ++w)
+                    o += acc[w * hd + d];
                 op[d] = o;
             }
         }
@@ -727,6 +748,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
             for (uint32_t d = tid; d < hd; d += nt)
             {
                 float o = 0.f;
+#pragma unroll 4
                 for (uint32_t c = 0; c < ns; ++c)
                     o += __ldcg(P.opart + ((uint64_t)h * ns + c) * hd + d);
                 P.attn[h * hd + d] = __float2half_rn(o);

@@ -309,7 +309,7 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     uint32_t warps = optin > fixed ? (uint32_t)((optin - fixed) / ((size_t)P.spw * kTileBytes)) : 0;
     if (warps > (uint32_t)kStreamMaxWarps)
         warps = kStreamMaxWarps;
-    if (warps < 8)
+    if (warps < 8 || P.att_groups < warps) // attention sums one partial row per warp in the scratch
         return;
     P.warps = warps;
     e->pp_smem = fixed + (size_t)warps * P.spw * kTileBytes;
