@@ -100,6 +100,7 @@ struct PersistParams
     uint32_t att_split;     // key splits per head in the attention phases
     const __half *const *tiled; // decode copy of the weights: [layer * 4 + kind] (QKV, Wo, up/gate, down)
     const __half *tiled_logits; // decode copy of the output matrix
+    const float *rope_den;      // [hd / 2] RoPE denominators base^(2w / hd)
     uint64_t *trace;        // optional: CTA 0 records %globaltimer at every barrier arrival/release
     uint32_t trace_cap;     // entries available in `trace`
     unsigned long long *wtrace; // optional: CTA 0 per (warp, kind): wait, consume, chunks, compute part
@@ -393,7 +394,8 @@ __device__ __forceinline__ void persist_epilogue(const PersistParams &P, uint32_
         if (which < 2)
         {
             const uint32_t w = d / 2;
-            const float theta = (float)pos / powf(dd.rope_base, (float)(2 * w) / (float)dd.hd);
+            // rope_den[w] = powf(base, 2w / hd), computed once on the device
+            const float theta = (float)pos / __ldg(P.rope_den + w);
             const float c = cosf(theta), sn = sinf(theta);
             const float o0 = c * v0 - sn * v1, o1 = sn * v0 + c * v1;
             v0 = o0;
@@ -455,7 +457,7 @@ template <int NM>
 __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t kind, uint32_t layer, WarpPipe &wp,
                                              const __half *xs, float *part, uint32_t pos, SyncState &tr)
 {
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom &g = P.tg[kind];
     const UnitRange r = cta_units(g.units);
     const uint32_t groups = (r.count * NM + kTileRows - 1) / kTileRows, pitch = groups * kTileRows;
@@ -542,7 +544,6 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
         }
         persist_epilogue(P, kind, lw, r.u0 + ul, sums, pos);
     }
-    (void)nw;
     return true;
 }
 
@@ -764,10 +765,13 @@ __device__ __forceinline__ void stage_rmsnorm_h(const __half *__restrict__ x, co
 {
     const uint32_t nchunk = K / 8;
     const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+    // one 16-byte chunk per thread is kept in registers between the two passes (K <= 8 * threads)
+    const bool one = nchunk <= blockDim.x;
+    const uint4 v0 = (one && threadIdx.x < nchunk) ? __ldcg(x4 + threadIdx.x) : make_uint4(0, 0, 0, 0);
     float s = 0.f;
     for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
     {
-        const uint4 v = __ldcg(x4 + i);
+        const uint4 v = one ? v0 : __ldcg(x4 + i);
         const __half2 *h = reinterpret_cast<const __half2 *>(&v);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -782,7 +786,7 @@ __device__ __forceinline__ void stage_rmsnorm_h(const __half *__restrict__ x, co
     uint4 *xs4 = reinterpret_cast<uint4 *>(xs);
     for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
     {
-        const uint4 v = __ldcg(x4 + i);
+        const uint4 v = one ? v0 : __ldcg(x4 + i);
         const float4 ga = g4[2 * i], gb = g4[2 * i + 1];
         const __half2 *h = reinterpret_cast<const __half2 *>(&v);
         const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};

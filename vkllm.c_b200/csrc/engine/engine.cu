@@ -52,6 +52,7 @@ struct Engine
     TpComm *tp = nullptr;                       // tensor-parallel exchange (shards only)
     __half *tiled = nullptr;                    // decode copy of the weights (persistent kernel's tile layout)
     void *d_tiled_ptrs = nullptr;               // [layer * 4 + phase] pointers into `tiled`
+    float *rope_den = nullptr;                  // RoPE denominators of the persistent kernel
 };
 
 // Peer-memory exchange of a tensor-parallel rank: one device buffer, exported with CUDA IPC, holding
@@ -205,6 +206,12 @@ __global__ void k_relayout(__half *__restrict__ dst, const __half *s0, const __h
                              (uint64_t)r * width + (uint64_t)tile_chunk(cc, r, width / 8) * 8;
         *reinterpret_cast<uint4 *>(dst + off) = *reinterpret_cast<const uint4 *>(src + (uint64_t)c * 8);
     }
+}
+
+__global__ void k_rope_den(float *den, uint32_t half_hd, uint32_t hd, float base)
+{
+    for (uint32_t w = threadIdx.x; w < half_hd; w += blockDim.x)
+        den[w] = powf(base, (float)(2 * w) / (float)hd);
 }
 
 void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_t spw, uint32_t l2_kb)
@@ -394,6 +401,13 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
         return;
     }
     P.tiled = (const __half *const *)e->d_tiled_ptrs;
+    if (cudaMalloc(&e->rope_den, sizeof(float) * 128) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return;
+    }
+    k_rope_den<<<1, 128, 0, st>>>(e->rope_den, dd.hd / 2, dd.hd, dd.rope_base);
+    P.rope_den = e->rope_den;
     if (cudaMalloc(&e->d_layers, sizeof(LayerW) * e->layers.size()) != cudaSuccess)
     {
         (void)cudaGetLastError();
@@ -690,6 +704,8 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
         cudaFree(e->tiled);
     if (e->d_tiled_ptrs)
         cudaFree(e->d_tiled_ptrs);
+    if (e->rope_den)
+        cudaFree(e->rope_den);
     if (e->pp.trace)
         cudaFree(e->pp.trace);
     if (e->pp.wtrace)
