@@ -143,7 +143,10 @@ extern uint32_t vkllm_b200_engine_read_trace_last(struct vkllm_context *context,
 /* Tracing: CTA 0's per-warp weight-pipeline accounting, in SM cycles, summed over every persistent
  * launch since the engine was built: out[(warp * 5 + kind) * 4 + {0: mbarrier wait, 1: consume
  * (compute + refill issue), 2: chunks, 3: compute}], kind 0..4 = QKV, Wo, up/gate, down, logits.
- * Needs cap >= 640; returns 640, or 0 when tracing is off. */
+ * With cap >= 648, out[640..647] adds CTA 0's attention sub-steps in SM cycles: 0 q load, 1 key
+ * scores, 2 split statistics, 3 wait for the sibling splits, 4 head statistics, 5 probs . V, 6 the
+ * combine of the splits, 7 attention items. Needs cap >= 640; returns 640 or 648, or 0 when tracing
+ * is off. */
 extern uint32_t vkllm_b200_engine_read_warp_trace(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                                   uint64_t *out, uint32_t cap);
 /* Tensor-core GEMM (tcgen05 + TMEM, TMA-fed): C = act(scale * A . B^T) for fp16 A [M, K] (row

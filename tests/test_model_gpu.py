@@ -48,6 +48,41 @@ def test_tiny_token_loop_parity(vk, ctx, tiny_gguf, reference_run, mode):
         assert d.mean() <= 2e-3, f"step {i}: mean-abs {d.mean()}"
 
 
+# Long-context shape for the persistent kernel's attention phase: 8 heads of 128 split 18 ways, 24
+# key groups per split (F = 6144 sizes the shared scratch for them), so a decode at position ~1800
+# reduces ~100 keys per split in 5 rounds, past its 4-round load window (the tiny model needs 1).
+LONG = dict(D=1024, L=1, H=8, F=6144, V=512, ctx=2048, eps=1e-5, rope_base=10000.0)
+LONG_PROMPT, LONG_STEPS = 1800, 9
+
+
+def test_long_context_decode_parity(vk, ctx, orc, tmp_path):
+    import ctypes as C
+
+    import gen_gguf
+
+    path = str(tmp_path / "long.gguf")
+    weights = gen_gguf.write_gguf(path, LONG, seed=99)
+    prompt = gen_gguf.prompt(5, LONG_PROMPT, vocab=LONG["V"])
+    model = vk.Model(ctx).load(path)
+    try:
+        logits = []
+        toks = model.generate(prompt, LONG_STEPS, logits)
+        assert vk.lib().vkllm_b200_engine_is_persistent(ctx.ptr, C.byref(model.m))
+    finally:
+        model.free()
+    m = orc.Llama2(dict(LONG), weights)
+    ref_toks, ref_logits = m.generate(prompt, LONG_STEPS)
+    m.close()
+    n_same = next((i for i in range(LONG_STEPS) if toks[i] != ref_toks[i]), LONG_STEPS)
+    for i in range(min(n_same + 1, LONG_STEPS)):
+        r = np.asarray(ref_logits[i], dtype=np.float32)
+        d = np.abs(logits[i].astype(np.float32) - r)
+        assert d.max() <= 2e-2 and d.mean() <= 2e-3, (i, d.max(), d.mean())
+    if n_same < LONG_STEPS:  # a divergence only at a near tie of the reference's logits
+        r = np.asarray(ref_logits[n_same], dtype=np.float32)
+        assert r[ref_toks[n_same]] - r[toks[n_same]] <= 2e-2, (n_same, toks, ref_toks)
+
+
 def test_tokenizer_and_metadata(vk, ctx, tiny_gguf):
     import ctypes as C
 

@@ -55,6 +55,12 @@ constexpr uint32_t kErrPosition = 0x1;
 constexpr uint32_t kTileRows = 16;                        // MMA M
 constexpr uint32_t kSegHalves = VKB_PERSIST_SEG;          // columns per tile (one bulk copy per row)
 constexpr uint32_t kTileBytes = kTileRows * kSegHalves * 2; // one stage (a full tile)
+// At most 24 warps per CTA, so that the launch bound leaves each thread 80 registers (65536 / 768);
+// shared memory limits the 7B and 13B shapes to 23 and 22 warps of one 8 KB stage each anyway.
+constexpr int kPersistMaxWarps = 24;
+constexpr uint32_t kAttWindow = 4; // attention key rounds whose K (then V) rows are loaded at once
+// Trace slots after the per-warp pipeline accounting: CTA 0's attention sub-steps (SM cycles).
+constexpr uint32_t kAttTraceBase = kStreamMaxWarps * PK_COUNT * 4, kAttTraceSlots = 8;
 
 // Physical 16-byte chunk of logical chunk c in row r of a tile whose rows hold nchunks chunks:
 // swizzled within aligned groups of 8 (the tail of a row that is not a whole group stays in place).
@@ -270,6 +276,11 @@ struct Cursor
 {
     uint32_t step, layer, kind, k;
     bool done;
+    // geometry of the current phase for this warp, set when the cursor enters the phase
+    uint32_t nk;         // tiles of this warp in the phase
+    uint32_t Ks, K, rows, last;
+    uint32_t grp, ks;    // the next tile: row group and K segment (tile t = w + warps * k)
+    const __half *base;  // this CTA's region of the phase matrix in the decode copy
 };
 
 // Tiles of this CTA in a phase: ceil(rows / 16) row groups x Ks segments, tile t = group * Ks + segment.
@@ -278,17 +289,45 @@ __device__ __forceinline__ uint32_t cta_tiles(const TileGeom &g, uint32_t count)
     return (count * g.nm + kTileRows - 1) / kTileRows * g.Ks;
 }
 
-// Tiles of warp w (tiles w, w + warps, ...).
-__device__ __forceinline__ uint32_t kind_chunks(const PersistParams &P, uint32_t kind, uint32_t w)
+// This CTA's region of a phase matrix in the decode copy: its rows' bytes of the row-major matrix.
+__device__ __forceinline__ const __half *tiled_region(const PersistParams &P, uint32_t kind, uint32_t layer,
+                                                      const TileGeom &g, const UnitRange &r)
 {
-    const uint32_t T = cta_tiles(P.tg[kind], cta_units(P.tg[kind].units).count);
-    return T > w ? (T - w + P.warps - 1) / P.warps : 0;
+    const __half *base = kind == PK_LOGITS ? P.tiled_logits : P.tiled[layer * 4 + kind];
+    return base + (uint64_t)r.u0 * g.nm * g.K;
+}
+
+// Loads the geometry of the cursor's (kind, layer) phase; the per-tile advance is then divisions-free.
+__device__ __forceinline__ void cursor_enter(const PersistParams &P, Cursor &c, uint32_t w)
+{
+    const TileGeom &g = P.tg[c.kind];
+    const UnitRange r = cta_units(g.units);
+    const uint32_t T = cta_tiles(g, r.count);
+    c.nk = T > w ? (T - w + P.warps - 1) / P.warps : 0;
+    c.Ks = g.Ks;
+    c.K = g.K;
+    c.rows = r.count * g.nm;
+    c.last = g.last;
+    c.grp = w / g.Ks;
+    c.ks = w % g.Ks;
+    c.base = tiled_region(P, c.kind, c.layer, g, r);
+}
+
+// Tile t + warps from tile t: (grp, ks) of t = grp * Ks + ks.
+__device__ __forceinline__ void tile_step(uint32_t &grp, uint32_t &ks, uint32_t Ks, uint32_t warps)
+{
+    ks += warps;
+    while (ks >= Ks)
+    {
+        ks -= Ks;
+        ++grp;
+    }
 }
 
 __device__ __forceinline__ void cursor_settle(const PersistParams &P, Cursor &c, uint32_t w)
 {
     // Skip phases where this warp has no chunk.
-    while (!c.done && c.k >= kind_chunks(P, c.kind, w))
+    while (!c.done && c.k >= c.nk)
     {
         c.k = 0;
         if (c.kind == PK_LOGITS)
@@ -307,15 +346,9 @@ __device__ __forceinline__ void cursor_settle(const PersistParams &P, Cursor &c,
         }
         else
             ++c.kind;
+        if (!c.done)
+            cursor_enter(P, c, w);
     }
-}
-
-// This CTA's region of a phase matrix in the decode copy: its rows' bytes of the row-major matrix.
-__device__ __forceinline__ const __half *tiled_region(const PersistParams &P, uint32_t kind, uint32_t layer,
-                                                      const TileGeom &g, const UnitRange &r)
-{
-    const __half *base = kind == PK_LOGITS ? P.tiled_logits : P.tiled[layer * 4 + kind];
-    return base + (uint64_t)r.u0 * g.nm * g.K;
 }
 
 // Issues the single bulk copy of the cursor's tile into `dst` (lane 0).
@@ -325,12 +358,9 @@ __device__ __forceinline__ void cursor_issue(const PersistParams &P, const Curso
     const uint32_t lane = threadIdx.x & 31;
     if (lane != 0)
         return;
-    const TileGeom &g = P.tg[c.kind];
-    const UnitRange r = cta_units(g.units);
-    const uint32_t t = w + P.warps * c.k, grp = t / g.Ks, ks = t % g.Ks;
-    const uint32_t r0 = grp * kTileRows, nvalid = min(kTileRows, r.count * g.nm - r0);
-    const uint32_t width = ks + 1 == g.Ks ? g.last : kSegHalves;
-    const __half *src = tiled_region(P, c.kind, c.layer, g, r) + (uint64_t)r0 * g.K + (uint64_t)ks * nvalid * kSegHalves;
+    const uint32_t r0 = c.grp * kTileRows, nvalid = min(kTileRows, c.rows - r0);
+    const uint32_t width = c.ks + 1 == c.Ks ? c.last : kSegHalves;
+    const __half *src = c.base + (uint64_t)r0 * c.K + (uint64_t)c.ks * nvalid * kSegHalves;
     const uint32_t bytes = nvalid * width * 2;
     mbar_arrive_expect_tx(bar, bytes);
     fence_proxy_async(); // this warp's earlier reads of the stage precede the async refill
@@ -358,6 +388,7 @@ __device__ __forceinline__ void pipe_advance(const PersistParams &P, WarpPipe &w
                  wp.policy);
     ++wp.issued;
     ++wp.cur.k;
+    tile_step(wp.cur.grp, wp.cur.ks, wp.cur.Ks, P.warps);
     cursor_settle(P, wp.cur, warp);
 }
 
@@ -467,7 +498,8 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
     const bool wt = P.wtrace && blockIdx.x == 0 && lane == 0;
     unsigned long long t_wait = 0, t_cons = 0, t_comp = 0;
     bool ok = true;
-    for (uint32_t k = 0; k < nk; ++k)
+    uint32_t grp = warp / g.Ks, ks = warp % g.Ks; // tile t = warp + warps * k = grp * Ks + ks
+    for (uint32_t k = 0; k < nk; ++k, tile_step(grp, ks, g.Ks, P.warps))
     {
         const uint32_t gi = wp.consumed, s = gi % P.spw;
         const long long c0 = wt ? clock64() : 0;
@@ -479,30 +511,53 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
         }
         const long long c1 = wt ? clock64() : 0;
         t_wait += (unsigned long long)(c1 - c0);
-        const uint32_t t = warp + P.warps * k, grp = t / g.Ks, ks = t % g.Ks;
         const uint32_t width = ks + 1 == g.Ks ? g.last : kSegHalves;
         const unsigned char *st = wp.stage + (size_t)s * kTileBytes;
         // ldmatrix rows: lanes 0-15 -> tile rows 0-15 at chunk 2j, lanes 16-31 -> rows 0-15 at chunk 2j + 1
         const uint32_t tr = lane & 15, half = lane >> 4, nchunks = width >> 3;
         const uint32_t row_addr = smem_u32(st + tr * width * 2);
-        const uint32_t *xk = reinterpret_cast<const uint32_t *>(xs + ks * kSegHalves + 2 * (lane & 3));
         // two accumulator chains (even / odd k-steps) halve the dependent MMA latency
         float c[4] = {0.f, 0.f, 0.f, 0.f}, d[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t kk = 0;
-#pragma unroll 2
-        for (; kk + 32 <= width; kk += 32)
+        if (width == kSegHalves)
         {
-            uint32_t a0, a1, a2, a3, e0, e1, e2, e3;
-            ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + half, tr, nchunks), a0, a1, a2, a3);
-            ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + 2 + half, tr, nchunks), e0, e1, e2, e3);
-            mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
-            mma_16816(d, e0, e1, e2, e3, xk[kk / 2 + 8], xk[kk / 2 + 12]);
+            // Full tile: every 16 B chunk c of row r sits at c ^ (r & 7). For chunk 4i + h (h < 4) that
+            // is 4 (i ^ (r >> 2 & 1)) + (h ^ (r & 3)), so each row's ldmatrix address is one of two
+            // per-lane bases (i even / odd) plus 64 i bytes. The input vector (the B operand, equal in
+            // all 8 columns) comes from one ldmatrix.x4 whose 8 row addresses per matrix coincide:
+            // matrix m holds xs[kk + 8m .. kk + 8m + 7], so lane l receives the pair at 2 (l & 3).
+            const uint32_t lo = tr & 3, b64 = 64 * ((tr >> 2) & 1);
+            const uint32_t a_base = row_addr + 16 * (half ^ lo), e_base = row_addr + 16 * ((2 + half) ^ lo);
+            const uint32_t a_ev = a_base + b64, a_od = a_base - b64, e_ev = e_base + b64, e_od = e_base - b64;
+            const uint32_t xb = smem_u32(xs + ks * kSegHalves) + 16 * (lane >> 3);
+#pragma unroll
+            for (uint32_t i = 0; i < kSegHalves / 32; ++i)
+            {
+                uint32_t a0, a1, a2, a3, e0, e1, e2, e3, x0, x1, x2, x3;
+                ldsm_x4(((i & 1) ? a_od : a_ev) + 64 * i, a0, a1, a2, a3);
+                ldsm_x4(((i & 1) ? e_od : e_ev) + 64 * i, e0, e1, e2, e3);
+                ldsm_x4(xb + 64 * i, x0, x1, x2, x3);
+                mma_16816(c, a0, a1, a2, a3, x0, x1);
+                mma_16816(d, e0, e1, e2, e3, x2, x3);
+            }
         }
-        if (kk < width)
+        else
         {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + half, tr, nchunks), a0, a1, a2, a3);
-            mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
+            const uint32_t *xk = reinterpret_cast<const uint32_t *>(xs + ks * kSegHalves + 2 * (lane & 3));
+            uint32_t kk = 0;
+            for (; kk + 32 <= width; kk += 32)
+            {
+                uint32_t a0, a1, a2, a3, e0, e1, e2, e3;
+                ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + half, tr, nchunks), a0, a1, a2, a3);
+                ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + 2 + half, tr, nchunks), e0, e1, e2, e3);
+                mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
+                mma_16816(d, e0, e1, e2, e3, xk[kk / 2 + 8], xk[kk / 2 + 12]);
+            }
+            if (kk < width)
+            {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(row_addr + 16 * tile_chunk((kk >> 3) + half, tr, nchunks), a0, a1, a2, a3);
+                mma_16816(c, a0, a1, a2, a3, xk[kk / 2], xk[kk / 2 + 4]);
+            }
         }
         if ((lane & 3) == 0)
         {
@@ -574,26 +629,32 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
     float *acc = sc + ((chunk + 31) & ~31u); // [G][hd] per-group partial outputs
     __shared__ uint32_t flag_s;
     const uint32_t target = ns * (aepoch + 1);
+    // tracing: CTA 0's thread 0 stamps the sub-steps of each item in shared memory (no live registers)
+    __shared__ long long att_ts[kAttTraceSlots];
+    auto amark = [&](uint32_t k) {
+        if (P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
+            att_ts[k] = clock64();
+    };
     for (uint32_t it = blockIdx.x; it < dd.H * ns; it += gridDim.x)
     {
+        amark(0);
         const uint32_t h = it / ns, split = it % ns;
         const uint32_t j0 = split * chunk, j1 = min(Lk, j0 + chunk);
         const uint32_t nkeys = j1 > j0 ? j1 - j0 : 0, rounds = (nkeys + G - 1) / G;
         for (uint32_t d = tid; d < hd; d += nt)
             qs[d] = __half2float(__ldcg(P.q + h * hd + d));
         __syncthreads();
-        const __half *kb = lw.kcache + (uint64_t)h * dd.ctx * hd;
+        amark(1);
+        // lane piece pc of key row j: krow[j * pieces], of value row j: vrow[j * pieces]
+        const uint4 *krow = reinterpret_cast<const uint4 *>(lw.kcache + (uint64_t)h * dd.ctx * hd) + pc;
+        const uint4 *vrow = reinterpret_cast<const uint4 *>(lw.vcache + (uint64_t)h * dd.ctx * hd) + pc;
+        auto load_row = [&](const uint4 *rows, uint32_t j) {
+            return (lane_on && j < j1) ? __ldcg(rows + (uint64_t)j * pieces) : make_uint4(0, 0, 0, 0);
+        };
         float mx = -FLT_MAX;
-        // one round of key rows loads ahead of the round being reduced
-        uint4 nxt = (lane_on && j0 + gi < j1) ? __ldcg(reinterpret_cast<const uint4 *>(kb + (uint64_t)(j0 + gi) * hd) + pc)
-                                              : make_uint4(0, 0, 0, 0);
-        for (uint32_t rr = 0; rr < rounds; ++rr)
-        {
-            const uint32_t j = j0 + gi + G * rr;
+        // scores of key j (every lane calls it: the lpk lanes of a key sum with shuffles)
+        auto score_key = [&](const uint4 &raw, uint32_t j) {
             const bool valid = lane_on && j < j1;
-            const uint4 raw = nxt;
-            if (rr + 1 < rounds && lane_on && j + G < j1)
-                nxt = __ldcg(reinterpret_cast<const uint4 *>(kb + (uint64_t)(j + G) * hd) + pc);
             float a = 0.f;
             if (valid)
             {
@@ -618,6 +679,31 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                 }
                 mx = fmaxf(mx, s);
             }
+        };
+        // The key rows of the first kAttWindow rounds load at once; later rounds one round ahead.
+        uint4 win[kAttWindow];
+#pragma unroll
+        for (uint32_t r = 0; r < kAttWindow; ++r)
+            win[r] = load_row(krow, j0 + gi + G * r);
+        uint4 nxt = load_row(krow, j0 + gi + G * kAttWindow);
+#pragma unroll
+        for (uint32_t r = 0; r < kAttWindow; ++r)
+            if (r < rounds)
+                score_key(win[r], j0 + gi + G * r);
+        for (uint32_t rr = kAttWindow; rr < rounds; ++rr)
+        {
+            const uint4 raw = nxt;
+            if (rr + 1 < rounds)
+                nxt = load_row(krow, j0 + gi + G * (rr + 1));
+            score_key(raw, j0 + gi + G * rr);
+        }
+        amark(2);
+        // the value rows of the window load while the statistics are reduced and the siblings wait
+        if (Lk != hd)
+        {
+#pragma unroll
+            for (uint32_t r = 0; r < kAttWindow; ++r)
+                win[r] = load_row(vrow, j0 + gi + G * r);
         }
         // this split's max and sum of exp (the reference's reductions over the whole row, in parts)
         mx = warp_max(mx);
@@ -632,6 +718,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
             l += expf(sc[j] - m);
         __syncthreads();
         l = block_sum(l, red);
+        amark(3);
         if (tid == 0)
         {
             bool ok = true;
@@ -661,6 +748,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
         __syncthreads();
         if (!flag_s)
             return false;
+        amark(4);
         // the head's max and sum over its splits (ns <= 32: one lane per split), broadcast in smem
         if (tid < 32)
         {
@@ -674,6 +762,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
             }
         }
         __syncthreads();
+        amark(5);
         const float M = red[0], L = red[1];
         const __half *vb = lw.vcache + (uint64_t)h * dd.ctx * hd;
         float *op = P.opart + ((uint64_t)h * ns + split) * hd;
@@ -696,14 +785,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
         else
         {
             float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            uint4 vn = (lane_on && j0 + gi < j1) ? __ldcg(reinterpret_cast<const uint4 *>(vb + (uint64_t)(j0 + gi) * hd) + pc)
-                                                 : make_uint4(0, 0, 0, 0);
-            for (uint32_t rr = 0; rr < rounds; ++rr)
-            {
-                const uint32_t j = j0 + gi + G * rr;
-                const uint4 raw = vn;
-                if (rr + 1 < rounds && lane_on && j + G < j1)
-                    vn = __ldcg(reinterpret_cast<const uint4 *>(vb + (uint64_t)(j + G) * hd) + pc);
+            auto accumulate = [&](const uint4 &raw, uint32_t j) {
                 if (lane_on && j < j1)
                 {
                     const float pj = round_f16(expf(sc[j - j0] - M) / L);
@@ -716,6 +798,18 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                         a[2 * e + 1] = fmaf(pj, f.y, a[2 * e + 1]);
                     }
                 }
+            };
+            uint4 vn = load_row(vrow, j0 + gi + G * kAttWindow);
+#pragma unroll
+            for (uint32_t r = 0; r < kAttWindow; ++r)
+                if (r < rounds)
+                    accumulate(win[r], j0 + gi + G * r);
+            for (uint32_t rr = kAttWindow; rr < rounds; ++rr)
+            {
+                const uint4 raw = vn;
+                if (rr + 1 < rounds)
+                    vn = load_row(vrow, j0 + gi + G * (rr + 1));
+                accumulate(raw, j0 + gi + G * rr);
             }
             // the key groups of a warp (32 / lpk of them) are summed with shuffles, then the warps'
             // sums in smem, in warp order
@@ -738,6 +832,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
             }
         }
         __syncthreads();
+        amark(6);
         if (tid == 0)
         {
             uint32_t prev;
@@ -755,6 +850,13 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                 P.attn[h * hd + d] = __float2half_rn(o);
             }
         __syncthreads();
+        amark(7);
+        if (P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
+        {
+            for (uint32_t k = 0; k + 1 < kAttTraceSlots; ++k)
+                atomicAdd(P.wtrace + kAttTraceBase + k, (unsigned long long)(att_ts[k + 1] - att_ts[k]));
+            atomicAdd(P.wtrace + kAttTraceBase + kAttTraceSlots - 1, 1ull);
+        }
     }
     return true;
 }
@@ -813,7 +915,7 @@ __device__ __forceinline__ void stage_copy_h(const __half *__restrict__ x, uint3
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(PersistParams P)
+__global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(PersistParams P)
 {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
@@ -831,7 +933,11 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
     wp.stage = stages + (size_t)warp * P.spw * kTileBytes;
     wp.consumed = 0;
     wp.issued = 0;
-    wp.cur = Cursor{0, 0, PK_QKV, 0, P.n_steps == 0};
+    wp.cur = Cursor{};
+    wp.cur.kind = PK_QKV;
+    wp.cur.done = P.n_steps == 0;
+    if (!wp.cur.done)
+        cursor_enter(P, wp.cur, warp);
     bool ok = true;
     SyncState tr{1, 0}; // thread 0: trace entry 0 is the start
     if (threadIdx.x == 0)
@@ -854,6 +960,7 @@ __global__ void __launch_bounds__(kStreamMaxWarps * 32, 1) k_decode_persistent(P
         cursor_issue(P, wp.cur, warp, wp.stage + (size_t)wp.issued * kTileBytes, &wp.bar[wp.issued], wp.policy);
         ++wp.issued;
         ++wp.cur.k;
+        tile_step(wp.cur.grp, wp.cur.ks, wp.cur.Ks, P.warps);
         cursor_settle(P, wp.cur, warp);
     }
 
