@@ -140,6 +140,11 @@ extern uint32_t vkllm_b200_engine_read_trace(struct vkllm_context *context, stru
  * layout (other entries undefined). Returns the count copied, 0 when tracing is off. */
 extern uint32_t vkllm_b200_engine_read_trace_last(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                                   uint64_t *out, uint32_t cap);
+/* Tracing: %globaltimer (ns) of every CTA's arrival at each of the first 1023 grid barriers of the
+ * last persistent launch, out[barrier * grid + cta] with grid = the SM count; row 1023 holds each
+ * CTA's %smid. Returns the count copied, 0 when tracing is off. */
+extern uint32_t vkllm_b200_engine_read_cta_trace(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                 uint64_t *out, uint32_t cap);
 /* Tracing: CTA 0's per-warp weight-pipeline accounting, in SM cycles, summed over every persistent
  * launch since the engine was built: out[(warp * 5 + kind) * 4 + {0: mbarrier wait, 1: consume
  * (compute + refill issue), 2: chunks, 3: compute}], kind 0..4 = QKV, Wo, up/gate, down, logits.

@@ -58,9 +58,11 @@ constexpr uint32_t kTileBytes = kTileRows * kSegHalves * 2; // one stage (a full
 // At most 24 warps per CTA, so that the launch bound leaves each thread 80 registers (65536 / 768);
 // shared memory limits the 7B and 13B shapes to 23 and 22 warps of one 8 KB stage each anyway.
 constexpr int kPersistMaxWarps = 24;
+constexpr uint32_t kPersistMaxGrid = 256; // CTAs (one per SM)
 constexpr uint32_t kAttWindow = 4; // attention key rounds whose K (then V) rows are loaded at once
 // Trace slots after the per-warp pipeline accounting: CTA 0's attention sub-steps (SM cycles).
 constexpr uint32_t kAttTraceBase = kStreamMaxWarps * PK_COUNT * 4, kAttTraceSlots = 8;
+constexpr uint32_t kCtaTraceBarriers = 1024, kCtaTraceMaxCtas = 256;
 
 // Physical 16-byte chunk of logical chunk c in row r of a tile whose rows hold nchunks chunks:
 // swizzled within aligned groups of 8 (the tail of a row that is not a whole group stays in place).
@@ -107,10 +109,13 @@ struct PersistParams
     const __half *const *tiled; // decode copy of the weights: [layer * 4 + kind] (QKV, Wo, up/gate, down)
     const __half *tiled_logits; // decode copy of the output matrix
     const float *rope_den;      // [hd / 2] RoPE denominators base^(2w / hd)
+    const uint32_t *utab;       // [kind][grid + 1]: CTA b owns units [utab[b], utab[b + 1]) of each phase
     uint64_t *trace;        // optional: CTA 0 records %globaltimer at every barrier arrival/release
     uint32_t trace_cap;     // entries available in `trace`
     unsigned long long *wtrace; // optional: CTA 0 per (warp, kind): wait, consume, chunks, compute part
     uint64_t *trace_last;       // optional: per trace entry, %globaltimer when the last CTA arrived
+    uint64_t *trace_cta;        // optional: [barrier][CTA] %globaltimer of each CTA's arrival (first
+                                // kCtaTraceBarriers grid barriers of a launch)
     uint32_t l2_bytes;          // per CTA: next-phase weights prefetched into L2 at each barrier
     uint32_t l2_hint;           // 1: stage loads mark their lines evict-first in L2
     // Tensor parallelism over peer memory (tp_size 1: off). Each rank owns H / N heads, F / N FFN
@@ -151,6 +156,8 @@ __device__ __forceinline__ bool grid_sync(const PersistParams &P, SyncState &tr)
             P.trace[tr.n] = global_ns();
         ++tr.n;
         bool ok = true;
+        if (P.trace_cta && tr.epoch < kCtaTraceBarriers - 1)
+            P.trace_cta[(uint64_t)tr.epoch * gridDim.x + blockIdx.x] = global_ns();
         const uint32_t target = (++tr.epoch) * gridDim.x;
         uint32_t prev;
         asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.bar_count) : "memory");
@@ -214,10 +221,12 @@ struct UnitRange
     uint32_t u0, count;
 };
 
-__device__ __forceinline__ UnitRange cta_units(uint32_t units)
+// This CTA's units of each phase, loaded from P.utab when the launch starts.
+__shared__ UnitRange s_units[PK_COUNT];
+
+__device__ __forceinline__ UnitRange cta_units(uint32_t kind)
 {
-    const uint32_t base = units / gridDim.x, rem = units % gridDim.x;
-    return UnitRange{blockIdx.x * base + min(blockIdx.x, rem), base + (blockIdx.x < rem ? 1u : 0u)};
+    return s_units[kind];
 }
 
 // Tensor-parallel allreduce of this CTA's output rows of the Wo (site 0) or down (site 1) phase:
@@ -258,7 +267,7 @@ __device__ __forceinline__ bool tp_allreduce_rows(const PersistParams &P, uint32
     __syncthreads();
     if (!ok_s)
         return false;
-    const UnitRange r = cta_units(P.tg[site == 0 ? PK_WO : PK_DOWN].units);
+    const UnitRange r = cta_units(site == 0 ? PK_WO : PK_DOWN);
     const float *rx = P.tp_x[P.tp_rank] + (uint64_t)site * P.tp_size * P.dd.D;
     for (uint32_t i = threadIdx.x; i < r.count; i += blockDim.x)
     {
@@ -301,7 +310,7 @@ __device__ __forceinline__ const __half *tiled_region(const PersistParams &P, ui
 __device__ __forceinline__ void cursor_enter(const PersistParams &P, Cursor &c, uint32_t w)
 {
     const TileGeom &g = P.tg[c.kind];
-    const UnitRange r = cta_units(g.units);
+    const UnitRange r = cta_units(c.kind);
     const uint32_t T = cta_tiles(g, r.count);
     c.nk = T > w ? (T - w + P.warps - 1) / P.warps : 0;
     c.Ks = g.Ks;
@@ -401,7 +410,7 @@ __device__ __forceinline__ void prefetch_slice(const PersistParams &P, uint32_t 
     if (P.l2_bytes == 0)
         return;
     const TileGeom &g = P.tg[kind];
-    const UnitRange r = cta_units(g.units);
+    const UnitRange r = cta_units(kind);
     const uint64_t region = (uint64_t)r.count * g.nm * g.K * 2, staged = (uint64_t)P.warps * P.spw * kTileBytes;
     if (staged >= region)
         return;
@@ -490,7 +499,7 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom &g = P.tg[kind];
-    const UnitRange r = cta_units(g.units);
+    const UnitRange r = cta_units(kind);
     const uint32_t groups = (r.count * NM + kTileRows - 1) / kTileRows, pitch = groups * kTileRows;
     const uint32_t T = groups * g.Ks;
     const uint32_t nk = T > warp ? (T - warp + P.warps - 1) / P.warps : 0;
@@ -652,6 +661,13 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
             return (lane_on && j < j1) ? __ldcg(rows + (uint64_t)j * pieces) : make_uint4(0, 0, 0, 0);
         };
         float mx = -FLT_MAX;
+        // this lane's 8 query values stay in registers for all its keys
+        float qr[8];
+        {
+            const float4 a = lane_on ? *reinterpret_cast<const float4 *>(qs + 8 * pc) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 b = lane_on ? *reinterpret_cast<const float4 *>(qs + 8 * pc + 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            qr[0] = a.x, qr[1] = a.y, qr[2] = a.z, qr[3] = a.w, qr[4] = b.x, qr[5] = b.y, qr[6] = b.z, qr[7] = b.w;
+        }
         // scores of key j (every lane calls it: the lpk lanes of a key sum with shuffles)
         auto score_key = [&](const uint4 &raw, uint32_t j) {
             const bool valid = lane_on && j < j1;
@@ -663,8 +679,8 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                 for (int e = 0; e < 4; ++e)
                 {
                     const float2 f = __half22float2(hh[e]);
-                    a = fmaf(qs[8 * pc + 2 * e], f.x, a);
-                    a = fmaf(qs[8 * pc + 2 * e + 1], f.y, a);
+                    a = fmaf(qr[2 * e], f.x, a);
+                    a = fmaf(qr[2 * e + 1], f.y, a);
                 }
             }
             for (uint32_t o = lpk / 2; o > 0; o >>= 1)
@@ -784,11 +800,15 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
         }
         else
         {
+            // the softmax node's output p_j = fp16(exp(s_j - M) / L), once per key, in place of s_j
+            for (uint32_t i = tid; i < nkeys; i += nt)
+                sc[i] = round_f16(expf(sc[i] - M) / L);
+            __syncthreads();
             float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             auto accumulate = [&](const uint4 &raw, uint32_t j) {
                 if (lane_on && j < j1)
                 {
-                    const float pj = round_f16(expf(sc[j - j0] - M) / L);
+                    const float pj = sc[j - j0];
                     const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
@@ -823,12 +843,18 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                 for (int e = 0; e < 8; ++e)
                     acc[(tid >> 5) * hd + 8 * pc + e] = a[e];
             __syncthreads();
-            for (uint32_t d = tid; d < hd; d += nt)
+            // the warps' rows summed by 4 threads per output (warps q, q + 4, ...), then 2 shuffles
+            for (uint32_t t = tid; t < ((4 * hd + 31) & ~31u); t += nt)
             {
+                const uint32_t d = t >> 2, qq = t & 3;
                 float o = 0.f;
-                for (uint32_t w = 0; w < nwarp; ++w)
-                    o += acc[w * hd + d];
-                op[d] = o;
+                if (d < hd)
+                    for (uint32_t w = qq; w < nwarp; w += 4)
+                        o += acc[w * hd + d];
+                o += __shfl_xor_sync(0xffffffffu, o, 1);
+                o += __shfl_xor_sync(0xffffffffu, o, 2);
+                if (qq == 0 && d < hd)
+                    op[d] = o;
             }
         }
         __syncthreads();
@@ -933,6 +959,13 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
     wp.stage = stages + (size_t)warp * P.spw * kTileBytes;
     wp.consumed = 0;
     wp.issued = 0;
+    // this CTA's units of every phase (the cursor needs them first)
+    if (threadIdx.x < PK_COUNT)
+    {
+        const uint32_t *t = P.utab + threadIdx.x * (gridDim.x + 1) + blockIdx.x;
+        s_units[threadIdx.x] = UnitRange{__ldg(t), __ldg(t + 1) - __ldg(t)};
+    }
+    __syncthreads();
     wp.cur = Cursor{};
     wp.cur.kind = PK_QKV;
     wp.cur.done = P.n_steps == 0;
@@ -940,6 +973,12 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
         cursor_enter(P, wp.cur, warp);
     bool ok = true;
     SyncState tr{1, 0}; // thread 0: trace entry 0 is the start
+    if (P.trace_cta && threadIdx.x == 0) // the last row of the arrival trace: each CTA's SM
+    {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        P.trace_cta[(uint64_t)(kCtaTraceBarriers - 1) * gridDim.x + blockIdx.x] = smid;
+    }
     if (threadIdx.x == 0)
         xfail_s = 0;
     if (P.trace && blockIdx.x == 0 && threadIdx.x == 0 && P.trace_cap > 0)
@@ -979,7 +1018,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
         const uint32_t tok = tok0 < P.Vg ? tok0 : P.unk; // src/shaders/vkllm_embedding.comp:57-60
         // The residual rows this CTA owns (the Wo / down output rows) start as the embedding.
         {
-            const UnitRange r = cta_units(P.tg[PK_WO].units);
+            const UnitRange r = cta_units(PK_WO);
             for (uint32_t i = threadIdx.x; i < r.count; i += blockDim.x)
                 P.x[r.u0 + i] = P.embed[(uint64_t)tok * dd.D + r.u0 + i];
         }
@@ -1054,7 +1093,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
         // Per-CTA argmax partials over its logits rows, per class i mod 32: the first (smallest
         // index) strict maximum (src/shaders/vkllm_arg_max.comp:54-69).
         {
-            const UnitRange r = cta_units(P.tg[PK_LOGITS].units);
+            const UnitRange r = cta_units(PK_LOGITS);
             if (warp == 0)
             {
                 // class of a row = its vocabulary index (v0 + local row) mod 32

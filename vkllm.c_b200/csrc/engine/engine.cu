@@ -53,6 +53,10 @@ struct Engine
     __half *tiled = nullptr;                    // decode copy of the weights (persistent kernel's tile layout)
     void *d_tiled_ptrs = nullptr;               // [layer * 4 + phase] pointers into `tiled`
     float *rope_den = nullptr;                  // RoPE denominators of the persistent kernel
+    // persistent kernel's row partition: [kind][grid + 1] prefix offsets of each CTA's units
+    std::vector<uint32_t> htab;
+    uint32_t *utab = nullptr;
+    uint32_t unit_cap[PK_COUNT] = {}; // most units a CTA may hold in a phase (sizes the partials)
 };
 
 // Peer-memory exchange of a tensor-parallel rank: one device buffer, exported with CUDA IPC, holding
@@ -175,13 +179,20 @@ template <class Op> void allow_smem(const StreamGeom &g)
 // of s0, then s1, then s2; mode 1: rows alternate s0, s1, i.e. up/gate pairs) belongs to the CTA
 // owning unit R / nm; within that CTA's rows, 16-row groups, then K segments, are contiguous tiles
 // whose rows hold the segment's chunks swizzled by tile_chunk.
+// Copies one matrix into the persistent kernel's tile layout. Source row R (mode 1: rows of s0 and s1
+// interleaved; else s0, then s1, then s2) belongs to unit R / nm; CTA b owns units [tab[b], tab[b + 1])
+// and its rows are contiguous in the copy, as tiles of 16 rows x 256 columns in (row group, segment)
+// order, each tile contiguous with its 16-byte chunks swizzled by row (tile_chunk).
 __global__ void k_relayout(__half *__restrict__ dst, const __half *s0, const __half *s1, const __half *s2,
                            uint32_t rows0, uint32_t rows1, int mode, uint32_t K, uint32_t total_rows, uint32_t nm,
-                           uint32_t units, uint32_t grid)
+                           const uint32_t *__restrict__ tab, uint32_t grid)
 {
+    __shared__ uint32_t st[kPersistMaxGrid + 1];
+    for (uint32_t i = threadIdx.x; i <= grid; i += blockDim.x)
+        st[i] = tab[i];
+    __syncthreads();
     const uint32_t nch = K / 8;
     const uint64_t n = (uint64_t)total_rows * nch;
-    const uint32_t base = units / grid, rem = units % grid;
     const uint32_t Ks = (K + kSegHalves - 1) / kSegHalves, last = K - kSegHalves * (Ks - 1);
     for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < n; t += (uint64_t)gridDim.x * blockDim.x)
     {
@@ -196,8 +207,16 @@ __global__ void k_relayout(__half *__restrict__ dst, const __half *s0, const __h
         else
             src = s2 + (uint64_t)(R - rows0 - rows1) * K;
         const uint32_t u = R / nm;
-        const uint32_t b = u < rem * (base + 1) ? u / (base + 1) : rem + (u - rem * (base + 1)) / base;
-        const uint32_t u0 = b * base + min(b, rem), cnt = base + (b < rem ? 1u : 0u);
+        uint32_t lo = 0, hi = grid; // st[lo] <= u < st[hi]: the owner is the CTA whose range holds u
+        while (hi - lo > 1)
+        {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (st[mid] <= u)
+                lo = mid;
+            else
+                hi = mid;
+        }
+        const uint32_t b = lo, u0 = st[b], cnt = st[b + 1] - st[b];
         const uint32_t rl = R - u0 * nm, rows_b = cnt * nm;
         const uint32_t g = rl / kTileRows, r = rl % kTileRows, nv = min(kTileRows, rows_b - g * kTileRows);
         const uint32_t ks = c / (kSegHalves / 8), cc = c % (kSegHalves / 8);
@@ -212,6 +231,48 @@ __global__ void k_rope_den(float *den, uint32_t half_hd, uint32_t hd, float base
 {
     for (uint32_t w = threadIdx.x; w < half_hd; w += blockDim.x)
         den[w] = powf(base, (float)(2 * w) / (float)hd);
+}
+
+// Uploads the row partition (e->htab) and rewrites the decode copy of the weights for it; the
+// per-matrix start pointers do not depend on the partition. Enqueued on `st`.
+cudaError_t relayout_weights(Engine *e, cudaStream_t st, std::vector<const __half *> *ptrs)
+{
+    const DecodeDims &dd = e->dd;
+    const uint32_t HD = dd.H * dd.hd, L = (uint32_t)e->layers.size(), grid = (uint32_t)e->ctx->device->sm_count;
+    cudaError_t err = cudaMemcpyAsync(e->utab, e->htab.data(), sizeof(uint32_t) * e->htab.size(),
+                                      cudaMemcpyHostToDevice, st);
+    if (err != cudaSuccess)
+        return err;
+    const uint32_t *tq = e->utab + PK_QKV * (grid + 1), *two = e->utab + PK_WO * (grid + 1),
+                   *tu = e->utab + PK_UPGATE * (grid + 1), *td = e->utab + PK_DOWN * (grid + 1),
+                   *tl = e->utab + PK_LOGITS * (grid + 1);
+    const unsigned rb = grid * 8;
+    __half *cur = e->tiled;
+    if (ptrs)
+        ptrs->assign(4 * L, nullptr);
+    for (uint32_t l = 0; l < L; ++l)
+    {
+        const LayerW &w = e->layers[l];
+        if (ptrs)
+            (*ptrs)[4 * l + PK_QKV] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wq, w.wk, w.wv, HD, HD, 0, dd.D, 3 * HD, 2, tq, grid);
+        cur += (size_t)3 * HD * dd.D;
+        if (ptrs)
+            (*ptrs)[4 * l + PK_WO] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wo, nullptr, nullptr, dd.D, 0, 0, HD, dd.D, 1, two, grid);
+        cur += (size_t)dd.D * HD;
+        if (ptrs)
+            (*ptrs)[4 * l + PK_UPGATE] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wu, w.wg, nullptr, 0, 0, 1, dd.D, 2 * dd.F, 2, tu, grid);
+        cur += (size_t)2 * dd.F * dd.D;
+        if (ptrs)
+            (*ptrs)[4 * l + PK_DOWN] = cur;
+        k_relayout<<<rb, 256, 0, st>>>(cur, w.wd, nullptr, nullptr, dd.D, 0, 0, dd.F, dd.D, 1, td, grid);
+        cur += (size_t)dd.D * dd.F;
+    }
+    k_relayout<<<rb, 256, 0, st>>>(cur, e->wout, nullptr, nullptr, dd.V, 0, 0, dd.D, dd.V, 1, tl, grid);
+    e->pp.tiled_logits = cur;
+    return cudaGetLastError();
 }
 
 void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_t spw, uint32_t l2_kb)
@@ -251,8 +312,11 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     P.err = &e->state->error;
     P.att_split = att_split;
     P.l2_bytes = l2_kb * 1024;
+    // weight-tile loads mark their L2 lines evict-first (they are read once per step), so the K/V rows
+    // and the barrier prefetches stay resident: 7B 2.844 -> 2.813 ms/token. "0" turns it off.
     const char *hint = getenv("VKLLM_B200_PERSIST_L2_HINT");
-    P.l2_hint = hint ? (uint32_t)atoi(hint) : 0u;
+    P.l2_hint = hint ? (uint32_t)atoi(hint) : 1u;
+
     // Weight tiles of 16 rows x 256 columns; every K must be a multiple of 16 (MMA k-step).
     if (dd.D % 16 != 0 || HD % 16 != 0 || dd.F % 16 != 0)
         return;
@@ -271,6 +335,18 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     P.tg[PK_DOWN] = tile_geom(dd.D, 1, dd.F);
     P.tg[PK_LOGITS] = tile_geom(dd.V, 1, dd.D);
     const uint32_t grid = (uint32_t)ctx->device->sm_count;
+    if (grid > kPersistMaxGrid)
+        return;
+    // Row partition: CTA b owns units [tab[b], tab[b + 1]) of each phase, equal shares to start with
+    // (balance_persistent may move units between CTAs later, up to unit_cap per CTA).
+    e->htab.assign((size_t)PK_COUNT * (grid + 1), 0);
+    for (int k = 0; k < PK_COUNT; ++k)
+    {
+        const uint32_t units = P.tg[k].units, base = units / grid, rem = units % grid;
+        for (uint32_t b = 0; b <= grid; ++b)
+            e->htab[(size_t)k * (grid + 1) + b] = b * base + (b < rem ? b : rem);
+        e->unit_cap[k] = (units + grid - 1) / grid + (units / grid) / 4 + 1; // +25 %
+    }
     uint32_t maxk = dd.D > HD ? dd.D : HD;
     if (dd.F > maxk)
         maxk = dd.F;
@@ -278,7 +354,7 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     for (int k = 0; k < PK_COUNT; ++k)
     {
         const TileGeom &g = P.tg[k];
-        const uint32_t rows = (g.units + grid - 1) / grid * g.nm;
+        const uint32_t rows = e->unit_cap[k] * g.nm;
         const size_t need = (size_t)(rows + kTileRows - 1) / kTileRows * kTileRows * g.Ks;
         part_floats = need > part_floats ? need : part_floats;
     }
@@ -335,6 +411,12 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
             (void)cudaGetLastError();
             P.trace_last = nullptr;
         }
+        if (grid <= kCtaTraceMaxCtas &&
+            cudaMalloc(&P.trace_cta, sizeof(uint64_t) * kCtaTraceBarriers * grid) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            P.trace_cta = nullptr;
+        }
         const size_t wbytes = sizeof(unsigned long long) * (kStreamMaxWarps * PK_COUNT * 4 + kAttTraceSlots);
         if (cudaMalloc(&P.wtrace, wbytes) != cudaSuccess || cudaMemset(P.wtrace, 0, wbytes) != cudaSuccess)
         {
@@ -371,29 +453,16 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
         e->tiled = nullptr;
         return;
     }
-    std::vector<const __half *> ptrs(4 * L);
     cudaStream_t st = ctx->runtime->stream;
-    const unsigned rb = (unsigned)ctx->device->sm_count * 8;
-    __half *cur = e->tiled;
-    for (uint32_t l = 0; l < L; ++l)
+    if (cudaMalloc(&e->utab, sizeof(uint32_t) * e->htab.size()) != cudaSuccess)
     {
-        const LayerW &w = e->layers[l];
-        ptrs[4 * l + PK_QKV] = cur;
-        k_relayout<<<rb, 256, 0, st>>>(cur, w.wq, w.wk, w.wv, HD, HD, 0, dd.D, 3 * HD, 2, 3 * HD / 2, grid);
-        cur += (size_t)3 * HD * dd.D;
-        ptrs[4 * l + PK_WO] = cur;
-        k_relayout<<<rb, 256, 0, st>>>(cur, w.wo, nullptr, nullptr, dd.D, 0, 0, HD, dd.D, 1, dd.D, grid);
-        cur += (size_t)dd.D * HD;
-        ptrs[4 * l + PK_UPGATE] = cur;
-        k_relayout<<<rb, 256, 0, st>>>(cur, w.wu, w.wg, nullptr, 0, 0, 1, dd.D, 2 * dd.F, 2, dd.F, grid);
-        cur += (size_t)2 * dd.F * dd.D;
-        ptrs[4 * l + PK_DOWN] = cur;
-        k_relayout<<<rb, 256, 0, st>>>(cur, w.wd, nullptr, nullptr, dd.D, 0, 0, dd.F, dd.D, 1, dd.D, grid);
-        cur += (size_t)dd.D * dd.F;
+        (void)cudaGetLastError();
+        return;
     }
-    k_relayout<<<rb, 256, 0, st>>>(cur, e->wout, nullptr, nullptr, dd.V, 0, 0, dd.D, dd.V, 1, dd.V, grid);
-    P.tiled_logits = cur;
-    if (cudaMemcpyAsync(e->d_tiled_ptrs, ptrs.data(), sizeof(__half *) * 4 * L, cudaMemcpyHostToDevice, st) !=
+    P.utab = e->utab;
+    std::vector<const __half *> ptrs;
+    if (relayout_weights(e, st, &ptrs) != cudaSuccess ||
+        cudaMemcpyAsync(e->d_tiled_ptrs, ptrs.data(), sizeof(__half *) * 4 * L, cudaMemcpyHostToDevice, st) !=
             cudaSuccess ||
         cudaStreamSynchronize(st) != cudaSuccess)
     {
@@ -453,6 +522,187 @@ vkllm_err_t run_persistent(Engine *e, uint32_t n, cudaStream_t s)
         n -= k;
     }
     return VKLLM_ERR_OK;
+}
+
+// Splits `units` over CTAs in proportion to `w` (largest remainders), each CTA in [1, cap].
+std::vector<uint32_t> apportion(uint32_t units, const std::vector<double> &w, uint32_t cap)
+{
+    const size_t n = w.size();
+    std::vector<uint32_t> c(n, 1);
+    if (units < n)
+        return c; // more CTAs than units: the caller keeps its split (sum check)
+    std::vector<double> want(n);
+    double tw = 0.0;
+    for (double x : w)
+        tw += x;
+    for (size_t i = 0; i < n; ++i)
+        want[i] = (double)units * w[i] / tw;
+    uint32_t left = units - (uint32_t)n;
+    // hand out units one at a time to the CTA furthest below its share (n and units are small)
+    while (left > 0)
+    {
+        size_t best = n;
+        double gap = -1e30;
+        for (size_t i = 0; i < n; ++i)
+            if (c[i] < cap && want[i] - c[i] > gap)
+            {
+                gap = want[i] - c[i];
+                best = i;
+            }
+        if (best == n)
+            break;
+        ++c[best];
+        --left;
+    }
+    return c;
+}
+
+// Per-SM speed differs systematically (the same SMs finish their share of a phase several us late in
+// every step), so the persistent kernel's row partition is calibrated once per engine: `rounds`
+// one-step launches at the last cache position (whose KV row any real decode rewrites before it is
+// read), each CTA's time per phase taken from its grid-barrier arrival times, and each phase's units
+// re-split in proportion to the measured rate units / time (damped). Any partition gives the same
+// results: a row's reduction does not depend on the CTA that computes it. The step state is restored.
+void balance_persistent(Engine *e, uint32_t rounds)
+{
+    const DecodeDims &dd = e->dd;
+    const uint32_t grid = (uint32_t)e->ctx->device->sm_count, L = (uint32_t)e->layers.size();
+    const uint32_t nb = 5 * L + 1; // grid barriers of one step
+    if (!e->persistent || e->tp || rounds == 0 || nb >= kCtaTraceBarriers || dd.ctx < 2)
+        return;
+    cudaStream_t st = e->ctx->runtime->stream;
+    const bool own_trace = e->pp.trace_cta == nullptr;
+    if (own_trace && cudaMalloc(&e->pp.trace_cta, sizeof(uint64_t) * kCtaTraceBarriers * grid) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        e->pp.trace_cta = nullptr;
+        return;
+    }
+    StepState saved{};
+    std::vector<uint64_t> a((size_t)nb * grid);
+    bool ok = cudaStreamSynchronize(st) == cudaSuccess &&
+              cudaMemcpy(&saved, e->state, sizeof(saved), cudaMemcpyDeviceToHost) == cudaSuccess;
+    // the K and V rows at the last position of every layer and head are kept aside and put back
+    const size_t row = (size_t)dd.hd * sizeof(__half), pitch = (size_t)dd.ctx * row;
+    __half *kept = nullptr;
+    ok = ok && cudaMalloc(&kept, row * dd.H * 2 * L) == cudaSuccess;
+    auto keep_rows = [&](bool save) {
+        bool good = true;
+        for (uint32_t l = 0; l < L && good; ++l)
+            for (int kv = 0; kv < 2 && good; ++kv)
+            {
+                char *cache = (char *)(kv ? e->layers[l].vcache : e->layers[l].kcache) + (size_t)(dd.ctx - 1) * row;
+                char *side = (char *)kept + (size_t)(2 * l + kv) * dd.H * row;
+                good = save ? cudaMemcpy2DAsync(side, row, cache, pitch, row, dd.H, cudaMemcpyDeviceToDevice, st) ==
+                                  cudaSuccess
+                            : cudaMemcpy2DAsync(cache, pitch, side, row, row, dd.H, cudaMemcpyDeviceToDevice, st) ==
+                                  cudaSuccess;
+            }
+        return good;
+    };
+    const bool kept_ok = ok && keep_rows(true);
+    ok = kept_ok;
+    for (uint32_t it = 0; ok && it < rounds; ++it)
+    {
+        k_set_state<<<1, 1, 0, st>>>(e->state, nullptr, 1, dd.ctx - 1);
+        StepState after{};
+        ok = run_persistent(e, 1, st) == VKLLM_ERR_OK && cudaStreamSynchronize(st) == cudaSuccess &&
+             cudaMemcpy(&after, e->state, sizeof(after), cudaMemcpyDeviceToHost) == cudaSuccess &&
+             after.error == 0 &&
+             cudaMemcpy(a.data(), e->pp.trace_cta, sizeof(uint64_t) * a.size(), cudaMemcpyDeviceToHost) == cudaSuccess;
+        if (!ok)
+            break;
+        auto rel = [&](uint32_t b) { // release of barrier b ~ its last arrival
+            uint64_t m = 0;
+            for (uint32_t c = 0; c < grid; ++c)
+                m = a[(size_t)b * grid + c] > m ? a[(size_t)b * grid + c] : m;
+            return m;
+        };
+        for (int k = 0; k < PK_COUNT; ++k)
+        {
+            // the barrier that ends phase k of layer l; QKV of layer 0 has no barrier before it
+            std::vector<double> t(grid, 0.0);
+            uint32_t n = 0;
+            for (uint32_t l = 0; l < (k == PK_LOGITS ? 1u : L); ++l)
+            {
+                const uint32_t b = k == PK_LOGITS ? 5 * L : 5 * l + (k == PK_QKV ? 0 : k + 1);
+                if (b == 0)
+                    continue;
+                const uint64_t r0 = rel(b - 1);
+                for (uint32_t c = 0; c < grid; ++c)
+                {
+                    const uint64_t x = a[(size_t)b * grid + c];
+                    t[c] += x > r0 ? (double)(x - r0) : 0.0;
+                }
+                ++n;
+            }
+            if (n == 0)
+                continue;
+            uint32_t *tab = e->htab.data() + (size_t)k * (grid + 1);
+            std::vector<double> w(grid);
+            bool sane = true;
+            for (uint32_t c = 0; c < grid; ++c)
+            {
+                const double cnt = (double)(tab[c + 1] - tab[c]);
+                sane = sane && t[c] > 0.0;
+                w[c] = sane ? cnt / t[c] : 0.0;
+            }
+            if (!sane)
+                continue;
+            {
+                double lo = t[0], hi = t[0], mean = 0.0;
+                for (uint32_t c = 0; c < grid; ++c)
+                {
+                    lo = t[c] < lo ? t[c] : lo;
+                    hi = t[c] > hi ? t[c] : hi;
+                    mean += t[c] / grid;
+                }
+                log_info("persistent decode balance round %u, phase %d: per-CTA time %.2f us mean, %.2f us spread",
+                         it, k, mean / n / 1e3, (hi - lo) / n / 1e3);
+            }
+            // damped: halfway from the current split to the rate-proportional one
+            double tw = 0.0;
+            for (double x : w)
+                tw += x;
+            const uint32_t units = tab[grid];
+            for (uint32_t c = 0; c < grid; ++c)
+                w[c] = 0.5 * (double)(tab[c + 1] - tab[c]) + 0.5 * (double)units * w[c] / tw;
+            const std::vector<uint32_t> cnt = apportion(units, w, e->unit_cap[k]);
+            uint32_t sum = 0;
+            for (uint32_t c = 0; c < grid; ++c)
+                sum += cnt[c];
+            if (sum != units)
+                continue;
+            for (uint32_t c = 0; c < grid; ++c)
+                tab[c + 1] = tab[c] + cnt[c];
+        }
+        ok = relayout_weights(e, st, nullptr) == cudaSuccess && cudaStreamSynchronize(st) == cudaSuccess;
+    }
+    if (!ok)
+    {
+        (void)cudaGetLastError();
+        log_info("persistent decode: row balancing skipped, equal shares kept");
+        for (int k = 0; k < PK_COUNT; ++k)
+        {
+            const uint32_t units = e->pp.tg[k].units, base = units / grid, rem = units % grid;
+            for (uint32_t b = 0; b <= grid; ++b)
+                e->htab[(size_t)k * (grid + 1) + b] = b * base + (b < rem ? b : rem);
+        }
+        if (relayout_weights(e, st, nullptr) != cudaSuccess)
+            (void)cudaGetLastError();
+    }
+    saved.error = 0;
+    if (kept_ok && !keep_rows(false))
+        (void)cudaGetLastError();
+    cudaMemcpyAsync(e->state, &saved, sizeof(saved), cudaMemcpyHostToDevice, st);
+    cudaStreamSynchronize(st);
+    if (kept)
+        cudaFree(kept);
+    if (own_trace)
+    {
+        cudaFree(e->pp.trace_cta);
+        e->pp.trace_cta = nullptr;
+    }
 }
 
 vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine **out)
@@ -665,6 +915,12 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
         delete e;
         return err;
     }
+    // VKLLM_B200_PERSIST_BALANCE: calibration rounds of the row partition (default 0, equal shares;
+    // 7B on one B200: 0 -> 2.857, 3 -> 2.869, 6 -> 2.864 ms/token, although the per-CTA spread of
+    // the up/gate phase shrank from 5.5 to 3.9 us: the phases stream at the HBM rate and the CTAs that
+    // finish first keep HBM busy with the next phase's tiles)
+    const char *bal = getenv("VKLLM_B200_PERSIST_BALANCE");
+    balance_persistent(e, bal ? (uint32_t)atoi(bal) : 0u);
     *out = e;
     return VKLLM_ERR_OK;
 }
@@ -713,6 +969,10 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
         cudaFree(e->pp.wtrace);
     if (e->pp.trace_last)
         cudaFree(e->pp.trace_last);
+    if (e->pp.trace_cta)
+        cudaFree(e->pp.trace_cta);
+    if (e->utab)
+        cudaFree(e->utab);
     delete e;
     model->b200.engine = nullptr;
 }
@@ -1192,6 +1452,22 @@ extern "C" uint32_t vkllm_b200_engine_read_trace_last(struct vkllm_context *cont
     cudaStreamSynchronize(context->runtime->stream);
     uint32_t n = cap < e->pp.trace_cap ? cap : e->pp.trace_cap;
     if (cudaMemcpy(out, e->pp.trace_last, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    return n;
+}
+
+extern "C" uint32_t vkllm_b200_engine_read_cta_trace(struct vkllm_context *context,
+                                                     struct vkllm_models_llama2 *model, uint64_t *out, uint32_t cap)
+{
+    if (!context || !model || !model->b200.engine || !out)
+        return 0;
+    Engine *e = (Engine *)model->b200.engine;
+    if (!e->pp.trace_cta)
+        return 0;
+    cudaStreamSynchronize(context->runtime->stream);
+    const uint32_t total = kCtaTraceBarriers * (uint32_t)e->ctx->device->sm_count;
+    const uint32_t n = cap < total ? cap : total;
+    if (cudaMemcpy(out, e->pp.trace_cta, sizeof(uint64_t) * n, cudaMemcpyDeviceToHost) != cudaSuccess)
         return 0;
     return n;
 }

@@ -168,6 +168,7 @@ _SIGS = {
     "vkllm_b200_engine_read_trace": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
     "vkllm_b200_engine_read_warp_trace": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
     "vkllm_b200_engine_read_trace_last": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
+    "vkllm_b200_engine_read_cta_trace": (C.c_uint32, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32]),
     "vkllm_b200_gemm_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
                                       C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_int, C.c_void_p]),
     "vkllm_b200_gemm_f16_error": (C.c_uint32, []),
