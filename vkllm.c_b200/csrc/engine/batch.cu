@@ -32,6 +32,9 @@ struct BatchLayer
 {
     const __half *wq, *wk, *wv, *wo, *wg, *wu, *wd;
     const float *attn_norm, *ffn_norm;
+    // the batch's concatenated copies: [Wq; Wk; Wv] as [3 HD, D] and [Wup; Wgate] as [2 F, D], so that
+    // each is one GEMM with M = sequences (fewer, larger GEMMs fill the SMs without splitting K)
+    const __half *wqkv, *wug;
 };
 } // namespace vkb
 
@@ -46,8 +49,9 @@ struct vkllm_b200_batch
     const float *out_norm = nullptr;
     void *ws = nullptr;
     __half *kv = nullptr; // [L][2][B][H][cap][hd]
-    __half *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *t0 = nullptr,
-           *up = nullptr, *gate = nullptr, *logits = nullptr;
+    __half *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *t0 = nullptr, *ug = nullptr,
+           *m = nullptr, *logits = nullptr; // qkv [B][3 HD], ug [B][2 F] (up, then SiLU(gate)), m [B][F]
+    __half *wcat = nullptr;                  // the concatenated weight copies of every layer
     uint32_t *tok = nullptr, *pos = nullptr, *ring = nullptr, *err = nullptr;
     uint32_t ring_steps = 0, last_steps = 0;
     std::vector<uint32_t> host_pos; // positions as the host knows them (load + steps)
@@ -94,60 +98,80 @@ __global__ void k_b_embed(const __half *__restrict__ table, uint32_t V, uint32_t
         dst[i] = src[i];
 }
 
-// RMSNORM node per row: fp16((x * g) * rsqrt(mean(x^2) + eps)).
+// RMSNORM node per row: fp16((x * g) * rsqrt(mean(x^2) + eps)); 8 halves per load and store
+// (D % 8 == 0).
 __global__ void k_b_rmsnorm(const __half *__restrict__ x, const float *__restrict__ g, uint32_t D, float eps,
                             __half *__restrict__ y)
 {
     __shared__ float red[32];
-    const __half *xr = x + (uint64_t)blockIdx.x * D;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + (uint64_t)blockIdx.x * D);
+    const uint32_t n8 = D / 8;
     float s = 0.f;
-    for (uint32_t i = threadIdx.x; i < D; i += blockDim.x)
+    for (uint32_t i = threadIdx.x; i < n8; i += blockDim.x)
     {
-        const float f = __half2float(xr[i]);
-        s = fmaf(f, f, s);
+        const uint4 v = xr[i];
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 f = __half22float2(h[e]);
+            s = fmaf(f.x, f.x, s);
+            s = fmaf(f.y, f.y, s);
+        }
     }
     const float alpha = rsqrtf(bsum(s, red) / (float)D + eps);
-    __half *yr = y + (uint64_t)blockIdx.x * D;
-    for (uint32_t i = threadIdx.x; i < D; i += blockDim.x)
-        yr[i] = __float2half_rn((__half2float(xr[i]) * g[i]) * alpha);
+    uint4 *yr = reinterpret_cast<uint4 *>(y + (uint64_t)blockIdx.x * D);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    for (uint32_t i = threadIdx.x; i < n8; i += blockDim.x)
+    {
+        const uint4 v = xr[i];
+        const float4 ga = g4[2 * i], gb = g4[2 * i + 1];
+        const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 f = __half22float2(h[e]);
+            oh[e] = __floats2half2_rn((f.x * gg[2 * e]) * alpha, (f.y * gg[2 * e + 1]) * alpha);
+        }
+        yr[i] = o;
+    }
 }
 
 // ROPE of q and k at each sequence's position (theta = pos / base^(2w / hd)), then the k and v rows
 // written at that position of the sequence's caches (the UPDATE_ROWS nodes). q is rotated in place.
+// Block (head, sequence), one thread per rotation pair w of the head.
 __global__ void k_b_rope_kv(__half *__restrict__ q, const __half *__restrict__ k, const __half *__restrict__ v,
-                            const uint32_t *__restrict__ pos, uint32_t H, uint32_t hd, uint32_t cap, float base,
-                            __half *__restrict__ kc, __half *__restrict__ vc, uint32_t B)
+                            uint32_t stride, const uint32_t *__restrict__ pos, uint32_t H, uint32_t hd, uint32_t cap,
+                            float base, __half *__restrict__ kc, __half *__restrict__ vc, uint32_t B)
 {
-    const uint32_t b = blockIdx.x, HD = H * hd, p = pos[b];
+    const uint32_t h = blockIdx.x, b = blockIdx.y, p = pos[b];
     if (p >= cap)
         return; // flagged by k_b_check_pos; no write outside the sequence's rows
-    __half *qr = q + (uint64_t)b * HD;
-    const __half *kr = k + (uint64_t)b * HD, *vr = v + (uint64_t)b * HD;
-    for (uint32_t i = threadIdx.x; i < HD / 2; i += blockDim.x)
+    const uint64_t src = (uint64_t)b * stride + (uint64_t)h * hd, row = (((uint64_t)b * H + h) * cap + p) * hd;
+    for (uint32_t w = threadIdx.x; w < hd / 2; w += blockDim.x)
     {
-        const uint32_t h = (2 * i) / hd, d = (2 * i) % hd, w = d / 2;
         const float theta = (float)p / powf(base, (float)(2 * w) / (float)hd);
-        const float c = cosf(theta), s = sinf(theta);
-        const float q0 = __half2float(qr[2 * i]), q1 = __half2float(qr[2 * i + 1]);
-        qr[2 * i] = __float2half_rn(c * q0 - s * q1);
-        qr[2 * i + 1] = __float2half_rn(s * q0 + c * q1);
-        const float k0 = __half2float(kr[2 * i]), k1 = __half2float(kr[2 * i + 1]);
-        const uint64_t row = (((uint64_t)b * H + h) * cap + p) * hd + d;
-        kc[row] = __float2half_rn(c * k0 - s * k1);
-        kc[row + 1] = __float2half_rn(s * k0 + c * k1);
-        vc[row] = vr[2 * i];
-        vc[row + 1] = vr[2 * i + 1];
+        const float c = cosf(theta), sn = sinf(theta);
+        __half2 *qp = reinterpret_cast<__half2 *>(q + src) + w;
+        const float2 qf = __half22float2(*qp), kf = __half22float2(reinterpret_cast<const __half2 *>(k + src)[w]);
+        *qp = __floats2half2_rn(c * qf.x - sn * qf.y, sn * qf.x + c * qf.y);
+        reinterpret_cast<__half2 *>(kc + row)[w] = __floats2half2_rn(c * kf.x - sn * kf.y, sn * kf.x + c * kf.y);
+        reinterpret_cast<__half2 *>(vc + row)[w] = reinterpret_cast<const __half2 *>(v + src)[w];
     }
 }
 
 // Attention of one (head, sequence): scores s_j = fp16(scale * q.k_j) over the sequence's Lk = pos + 1
 // keys, softmax p_j = fp16(exp(s_j - max) / sum) (max over all entries, vkllm_softmax.comp), output
 // fp16(sum_j p_j v_j). For Lk == hd the reference reads V as [hd, Lk] (src/core/vkllm_op_matmul.c:14-30):
-// o[w] = sum_k p_k V[w][k].
-__global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ q, const __half *__restrict__ kc,
-                                                     const __half *__restrict__ vc, const uint32_t *__restrict__ pos,
-                                                     uint32_t H, uint32_t hd, uint32_t cap, float scale,
-                                                     __half *__restrict__ out)
+// o[w] = sum_k p_k V[w][k]. Keys are read `lpk` lanes per key row (8 fp16 per lane, 16-byte loads);
+// the CTA's kBT / lpk key groups each sum their keys, then the groups are summed in order.
+__global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ q, uint32_t q_stride,
+                                                     const __half *__restrict__ kc, const __half *__restrict__ vc,
+                                                     const uint32_t *__restrict__ pos, uint32_t H, uint32_t hd,
+                                                     uint32_t cap, float scale, __half *__restrict__ out)
 {
     extern __shared__ float sm[];
     float *qs = sm;           // [hd]
@@ -159,22 +183,47 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
     const uint32_t Lk = pos[b] + 1;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x)
-        qs[d] = __half2float(q[(uint64_t)b * HD + h * hd + d]);
+        qs[d] = __half2float(q[(uint64_t)b * q_stride + h * hd + d]);
     __syncthreads();
     const __half *kb = kc + ((uint64_t)b * H + h) * cap * hd;
     const __half *vb = vc + ((uint64_t)b * H + h) * cap * hd;
+    const uint32_t pieces = hd / 8;
+    uint32_t lpk = 1;
+    while (lpk < pieces)
+        lpk <<= 1;
+    const uint32_t G = blockDim.x / lpk, gi = threadIdx.x / lpk, pc = threadIdx.x % lpk;
+    const bool lane_on = pc < pieces;
+    float qr[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        qr[e] = lane_on ? qs[8 * pc + e] : 0.f;
     float mx = -FLT_MAX;
-    for (uint32_t j = warp; j < Lk; j += nw)
+    for (uint32_t j0 = 0; j0 < Lk; j0 += G)
     {
-        const __half *kr = kb + (uint64_t)j * hd;
+        const uint32_t j = j0 + gi;
+        const bool valid = lane_on && j < Lk;
         float a = 0.f;
-        for (uint32_t d = lane; d < hd; d += 32)
-            a = fmaf(qs[d], __half2float(kr[d]), a);
-        a = warp_sum(a);
-        const float s = round_f16(a * scale);
-        if (lane == 0)
-            sc[j] = s;
-        mx = fmaxf(mx, s);
+        if (valid)
+        {
+            const uint4 raw = reinterpret_cast<const uint4 *>(kb + (uint64_t)j * hd)[pc];
+            const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+            {
+                const float2 f = __half22float2(hh[e]);
+                a = fmaf(qr[2 * e], f.x, a);
+                a = fmaf(qr[2 * e + 1], f.y, a);
+            }
+        }
+        for (uint32_t o = lpk / 2; o > 0; o >>= 1)
+            a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (j < Lk)
+        {
+            const float s = round_f16(a * scale);
+            if (pc == 0)
+                sc[j] = s;
+            mx = fmaxf(mx, s);
+        }
     }
     mx = warp_max(mx);
     if (lane == 0)
@@ -203,24 +252,57 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
         }
         return;
     }
-    // thread (d, part): dims d, keys j = part, part + parts, ...; partial sums combined in smem
-    const uint32_t parts = blockDim.x / hd > 0 ? blockDim.x / hd : 1;
-    float *acc = sc + ((Lk + 31) & ~31u); // [parts][hd]
-    for (uint32_t t = threadIdx.x; t < parts * hd; t += blockDim.x)
-    {
-        const uint32_t d = t % hd, part = t / hd;
-        float a = 0.f;
-        for (uint32_t j = part; j < Lk; j += parts)
-            a = fmaf(sc[j], __half2float(vb[(uint64_t)j * hd + d]), a);
-        acc[part * hd + d] = a;
-    }
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (lane_on)
+        for (uint32_t j = gi; j < Lk; j += G)
+        {
+            const uint4 raw = reinterpret_cast<const uint4 *>(vb + (uint64_t)j * hd)[pc];
+            const float pj = sc[j];
+            const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+            {
+                const float2 f = __half22float2(hh[e]);
+                a[2 * e] = fmaf(pj, f.x, a[2 * e]);
+                a[2 * e + 1] = fmaf(pj, f.y, a[2 * e + 1]);
+            }
+        }
+    float *acc = sc + ((Lk + 31) & ~31u); // [G][hd]
+    if (lane_on)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            acc[gi * hd + 8 * pc + e] = a[e];
     __syncthreads();
     for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x)
     {
-        float a = 0.f;
-        for (uint32_t part = 0; part < parts; ++part)
-            a += acc[part * hd + d];
-        o[d] = __float2half_rn(a);
+        float t = 0.f;
+        for (uint32_t g2 = 0; g2 < G; ++g2)
+            t += acc[g2 * hd + d];
+        o[d] = __float2half_rn(t);
+    }
+}
+
+// The gate BIN mul from the concatenated up/gate GEMM output: m[b][f] = fp16(ug[b][f] * ug[b][F + f])
+// (the gate half already SiLU'd by the GEMM epilogue), 8 halves per thread (F % 8 == 0).
+__global__ void k_b_gate(__half *__restrict__ m, const __half *__restrict__ ug, uint32_t F, uint32_t B)
+{
+    const uint32_t f8 = F / 8;
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < (uint64_t)B * f8;
+         t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t b = (uint32_t)(t / f8), c = (uint32_t)(t % f8);
+        const uint4 u = reinterpret_cast<const uint4 *>(ug + (uint64_t)b * 2 * F)[c];
+        const uint4 gt = reinterpret_cast<const uint4 *>(ug + (uint64_t)b * 2 * F + F)[c];
+        const __half2 *uh = reinterpret_cast<const __half2 *>(&u), *gh = reinterpret_cast<const __half2 *>(&gt);
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 a = __half22float2(uh[e]), g = __half22float2(gh[e]);
+            oh[e] = __floats2half2_rn(a.x * g.x, a.y * g.y);
+        }
+        reinterpret_cast<uint4 *>(m + (uint64_t)b * F)[c] = o;
     }
 }
 
@@ -299,9 +381,11 @@ __global__ void k_b_check_pos(const uint32_t *pos, uint32_t cap, uint32_t B, uin
             atomicOr(err, 1u);
 }
 
-bool gemm(const __half *A, const __half *W, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s)
+bool gemm(const __half *A, const __half *W, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s,
+          uint32_t act_from = 0)
 {
     GemmArgs g{};
+    g.act_from = act_from;
     g.A = A;
     g.B = W;
     g.C = C;
@@ -324,26 +408,30 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
     const uint32_t B = bt->B, D = dd.D, HD = bt->HD, F = dd.F, H = dd.H, hd = dd.hd;
     k_b_check_pos<<<1, 64, 0, s>>>(bt->pos, bt->cap, B, bt->err);
     k_b_embed<<<B, kBT, 0, s>>>(bt->embed, dd.V, D, bt->unk, bt->tok, bt->x);
-    const size_t att_smem = (256 + ((bt->cap + 31) & ~31u) + (size_t)(kBT / hd > 0 ? kBT / hd : 1) * hd) * 4;
+    uint32_t lpk = 1;
+    while (lpk < hd / 8)
+        lpk <<= 1;
+    const size_t att_smem = (256 + ((bt->cap + 31) & ~31u) + (size_t)(kBT / lpk) * hd) * 4;
     for (uint32_t l = 0; l < bt->L; ++l)
     {
         const BatchLayer &w = bt->layers[l];
         __half *kc = bt->kv + ((uint64_t)l * 2 + 0) * B * H * bt->cap * hd;
         __half *vc = bt->kv + ((uint64_t)l * 2 + 1) * B * H * bt->cap * hd;
         k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
-        if (!gemm(bt->xn, w.wq, bt->q, B, HD, D, 0, s) || !gemm(bt->xn, w.wk, bt->k, B, HD, D, 0, s) ||
-            !gemm(bt->xn, w.wv, bt->v, B, HD, D, 0, s))
+        if (!gemm(bt->xn, w.wqkv, bt->qkv, B, 3 * HD, D, 0, s))
             return VKLLM_ERR_VULKAN;
-        k_b_rope_kv<<<B, kBT, 0, s>>>(bt->q, bt->k, bt->v, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
-        k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->q, kc, vc, bt->pos, H, hd, bt->cap, dd.scale, bt->attn);
+        k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD,
+                                                                     bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
+        k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
+                                                         bt->attn);
         if (!gemm(bt->attn, w.wo, bt->t0, B, D, HD, 0, s))
             return VKLLM_ERR_VULKAN;
         k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
         k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.ffn_norm, D, dd.eps, bt->xn);
-        if (!gemm(bt->xn, w.wu, bt->up, B, F, D, 0, s) || !gemm(bt->xn, w.wg, bt->gate, B, F, D, 1, s))
+        if (!gemm(bt->xn, w.wug, bt->ug, B, 2 * F, D, 1, s, F)) // SiLU on the gate half only
             return VKLLM_ERR_VULKAN;
-        k_b_bin8<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->up, bt->up, bt->gate, (uint64_t)B * F / 8, 1);
-        if (!gemm(bt->up, w.wd, bt->t0, B, D, F, 0, s))
+        k_b_gate<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->ug, F, B);
+        if (!gemm(bt->m, w.wd, bt->t0, B, D, F, 0, s))
             return VKLLM_ERR_VULKAN;
         k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
     }
@@ -385,7 +473,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->L = model->meta.block_count;
     bt->unk = model->meta.padding_token_id;
     bt->host_pos.assign(n_seqs, 0);
-    if (dd.D % 8 || dd.F % 8 || bt->HD % 8 || dd.hd > 256 || dd.hd % 2 || bt->cap > 8192 - 256)
+    if (dd.D % 8 || dd.F % 8 || bt->HD % 8 || dd.hd > 256 || dd.hd % 8 || bt->cap > 8192 - 256)
     {
         delete bt;
         return VKLLM_ERR_ARGS;
@@ -412,8 +500,8 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->ring_steps = 1024;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t kv_bytes = al((size_t)bt->L * 2 * B * dd.H * bt->cap * dd.hd * 2);
-    const size_t act = al((size_t)B * D * 2) * 3 + al((size_t)B * HD * 2) * 4 + al((size_t)B * F * 2) * 2 +
-                       al((size_t)B * dd.V * 2);
+    const size_t act = al((size_t)B * D * 2) * 3 + al((size_t)B * 3 * HD * 2) + al((size_t)B * HD * 2) +
+                       al((size_t)B * 2 * F * 2) + al((size_t)B * F * 2) + al((size_t)B * dd.V * 2);
     const size_t small = al((size_t)B * 4) * 2 + al((size_t)bt->ring_steps * B * 4) + al(16);
     if (cudaMalloc(&bt->ws, kv_bytes + act + small) != cudaSuccess)
     {
@@ -431,24 +519,46 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->x = (__half *)take((size_t)B * D * 2);
     bt->xn = (__half *)take((size_t)B * D * 2);
     bt->t0 = (__half *)take((size_t)B * D * 2);
-    bt->q = (__half *)take((size_t)B * HD * 2);
-    bt->k = (__half *)take((size_t)B * HD * 2);
-    bt->v = (__half *)take((size_t)B * HD * 2);
+    bt->qkv = (__half *)take((size_t)B * 3 * HD * 2);
     bt->attn = (__half *)take((size_t)B * HD * 2);
-    bt->up = (__half *)take((size_t)B * F * 2);
-    bt->gate = (__half *)take((size_t)B * F * 2);
+    bt->ug = (__half *)take((size_t)B * 2 * F * 2);
+    bt->m = (__half *)take((size_t)B * F * 2);
     bt->logits = (__half *)take((size_t)B * dd.V * 2);
     bt->tok = (uint32_t *)take((size_t)B * 4);
     bt->pos = (uint32_t *)take((size_t)B * 4);
     bt->ring = (uint32_t *)take((size_t)bt->ring_steps * B * 4);
     bt->err = (uint32_t *)take(16); // [0] error bits, [1] step counter
     cudaStream_t s = ctx->runtime->stream;
-    if (cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
+    // concatenated weight copies, per layer [Wq; Wk; Wv] then [Wup; Wgate]
+    const size_t per_layer = ((size_t)3 * HD + (size_t)2 * F) * D;
+    if (cudaMalloc(&bt->wcat, per_layer * bt->L * sizeof(__half)) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        cudaFree(bt->ws);
+        delete bt;
+        return VKLLM_ERR_ALLOC;
+    }
+    bool copied = true;
+    for (uint32_t l = 0; l < bt->L && copied; ++l)
+    {
+        BatchLayer &w = bt->layers[l];
+        __half *qkv = bt->wcat + per_layer * l, *ug = qkv + (size_t)3 * HD * D;
+        const size_t mat = (size_t)HD * D * sizeof(__half), fm = (size_t)F * D * sizeof(__half);
+        copied = cudaMemcpyAsync(qkv, w.wq, mat, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+                 cudaMemcpyAsync(qkv + (size_t)HD * D, w.wk, mat, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+                 cudaMemcpyAsync(qkv + (size_t)2 * HD * D, w.wv, mat, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+                 cudaMemcpyAsync(ug, w.wu, fm, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
+                 cudaMemcpyAsync(ug + (size_t)F * D, w.wg, fm, cudaMemcpyDeviceToDevice, s) == cudaSuccess;
+        w.wqkv = qkv;
+        w.wug = ug;
+    }
+    if (!copied || cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess)
     {
         (void)cudaGetLastError();
         cudaFree(bt->ws);
+        cudaFree(bt->wcat);
         delete bt;
         return VKLLM_ERR_VULKAN;
     }
@@ -567,5 +677,7 @@ extern "C" void vkllm_b200_batch_free(struct vkllm_context *ctx, struct vkllm_b2
         cudaDeviceSynchronize();
         cudaFree(bt->ws);
     }
+    if (bt->wcat)
+        cudaFree(bt->wcat);
     delete bt;
 }

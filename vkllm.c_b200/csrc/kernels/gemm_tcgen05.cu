@@ -17,7 +17,9 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "kernels.h"
 
@@ -110,6 +112,7 @@ struct TcParams
     uint64_t c_sb, c_sc;
     float scale;
     int act;
+    uint32_t act_from; // act applies to output columns >= act_from
     __half *C;
     uint32_t *err;
     // Split-K: `splits` CTAs share a tile, each over kb_per k-blocks, writing fp32 partials to
@@ -144,7 +147,7 @@ __device__ __forceinline__ void store_row32(__half *crow, uint32_t nb, const uin
     for (int j = 0; j < 32; ++j)
     {
         float v = __uint_as_float(r[j]) * p.scale;
-        if (p.act)
+        if (p.act && nb + j >= p.act_from)
             v = v / (1.0f + expf(-v)); // SiLU as the reference evaluates it
         h[j] = __float2half_rn(v);
     }
@@ -330,30 +333,51 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
 // unsplit kernel). One thread per 4 columns.
 __global__ void k_splitk_reduce(const float *__restrict__ ws, TcParams p, uint32_t batch)
 {
-    const uint32_t n4 = (p.N + 3) / 4;
-    const uint64_t total = (uint64_t)batch * p.M * n4;
+    // 8 consecutive columns per thread: two 16-byte loads per split, one 16-byte fp16 store when the
+    // rows of C allow it (the sum runs in split order either way, so both paths give the same bits)
+    const uint32_t n8 = (p.N + 7) / 8;
+    const uint64_t total = (uint64_t)batch * p.M * n8;
     const uint64_t plane = (uint64_t)batch * p.M * p.N;
+    const bool vec = (p.N % 8) == 0 && (p.ldc % 8) == 0 && (p.c_sb % 8) == 0 && (p.c_sc % 8) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.C) & 15) == 0;
     for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x)
     {
-        const uint32_t c4 = (uint32_t)(t % n4);
-        const uint64_t rz = t / n4;
+        const uint32_t c8 = (uint32_t)(t % n8);
+        const uint64_t rz = t / n8;
         const uint32_t row = (uint32_t)(rz % p.M), z = (uint32_t)(rz / p.M);
         const uint32_t zb = z / p.batch_c, zc = z % p.batch_c;
         __half *crow = p.C + zb * p.c_sb + zc * p.c_sc + (uint64_t)row * p.ldc;
-        const uint64_t off = ((uint64_t)z * p.M + row) * p.N;
-        for (uint32_t j = 0; j < 4; ++j)
+        const uint64_t off = ((uint64_t)z * p.M + row) * p.N + 8ull * c8;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (vec)
         {
-            const uint32_t n = 4 * c4 + j;
-            if (n >= p.N)
-                break;
-            float v = 0.f;
             for (uint32_t sidx = 0; sidx < p.splits; ++sidx)
-                v += ws[sidx * plane + off + n];
-            v *= p.scale;
-            if (p.act)
-                v = v / (1.0f + expf(-v));
-            crow[n] = __float2half_rn(v);
+            {
+                const float4 a = __ldcs(reinterpret_cast<const float4 *>(ws + sidx * plane + off));
+                const float4 b = __ldcs(reinterpret_cast<const float4 *>(ws + sidx * plane + off) + 1);
+                v[0] += a.x, v[1] += a.y, v[2] += a.z, v[3] += a.w, v[4] += b.x, v[5] += b.y, v[6] += b.z, v[7] += b.w;
+            }
         }
+        else
+        {
+            for (uint32_t sidx = 0; sidx < p.splits; ++sidx)
+                for (uint32_t j = 0; j < 8 && 8 * c8 + j < p.N; ++j)
+                    v[j] += ws[sidx * plane + off + j];
+        }
+        __half h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+        {
+            float x = v[j] * p.scale;
+            if (p.act && 8 * c8 + j >= p.act_from)
+                x = x / (1.0f + expf(-x));
+            h[j] = __float2half_rn(x);
+        }
+        if (vec)
+            *reinterpret_cast<uint4 *>(crow + 8 * c8) = *reinterpret_cast<const uint4 *>(h);
+        else
+            for (uint32_t j = 0; j < 8 && 8 * c8 + j < p.N; ++j)
+                crow[8 * c8 + j] = h[j];
     }
 }
 
@@ -491,6 +515,7 @@ template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s, uint
     p.c_sc = g.c_sc;
     p.scale = g.scale;
     p.act = g.act;
+    p.act_from = g.act_from;
     p.C = (__half *)g.C;
     p.err = error_word(dev);
     if (!p.err)
@@ -514,8 +539,8 @@ template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s, uint
     k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
     if (p.splits > 1)
     {
-        const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 3) / 4);
-        const unsigned blocks = (unsigned)((work + 255) / 256 < 148u * 8u ? (work + 255) / 256 : 148u * 8u);
+        const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 7) / 8);
+        const unsigned blocks = (unsigned)((work + 255) / 256 < 148u * 16u ? (work + 255) / 256 : 148u * 16u);
         k_splitk_reduce<<<blocks, 256, 0, s>>>(p.ws, p, g.batch);
     }
     return cudaGetLastError() == cudaSuccess;
@@ -570,46 +595,163 @@ bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool tran
     return true;
 }
 
+namespace
+{
+// A launch configuration: tile (0: 128 x 128, 1: 128 x 256, 2: 256 x 256) and K splits.
+struct TcChoice
+{
+    uint8_t tile = 0, splits = 1;
+};
+
+bool launch_choice(const GemmArgs &g, cudaStream_t s, TcChoice c)
+{
+    switch (c.tile)
+    {
+    case 2:
+        return launch_tc<256, 256>(g, s, c.splits);
+    case 1:
+        return launch_tc<128, 256>(g, s, c.splits);
+    default:
+        return launch_tc<128, 128>(g, s, c.splits);
+    }
+}
+
+// Cost-model choice: the tile minimising waves x time per tile; small M (GEMM-shaped decode) splits K
+// so that every SM streams.
+TcChoice model_choice(const GemmArgs &g, int sms)
+{
+    auto tiles = [&](uint32_t bm, uint32_t bn) {
+        return (uint64_t)((g.N + bn - 1) / bn) * ((g.M + bm - 1) / bm) * g.batch;
+    };
+    auto cost = [&](uint32_t bm, uint32_t bn, double per_tile) {
+        return (double)((tiles(bm, bn) + sms - 1) / sms) * per_tile;
+    };
+    TcChoice c;
+    const uint64_t t128 = tiles(128, 128);
+    if (g.M <= 128 && t128 * 2 <= (uint64_t)sms)
+    {
+        const uint64_t sp = (uint64_t)sms / t128;
+        c.splits = (uint8_t)(sp > 8 ? 8 : sp);
+        return c;
+    }
+    // Per K step, a 128 x 128 tile takes ~0.85 and a 256 x 256 tile ~1.64 of the time of a 128 x 256
+    // tile (L2-to-SM operand bandwidth, measured on B200).
+    const double c128 = cost(128, 128, 0.85), c256 = cost(128, 256, 1.0), c2x = g.M > 128 ? cost(256, 256, 1.64) : 1e30;
+    c.tile = (c2x < c256 && c2x < c128) ? 2 : (c256 < c128 ? 1 : 0);
+    return c;
+}
+
+struct TuneKey
+{
+    int dev;
+    uint32_t M, N, K, batch;
+    bool operator<(const TuneKey &o) const
+    {
+        return std::tie(dev, M, N, K, batch) < std::tie(o.dev, o.M, o.N, o.K, o.batch);
+    }
+};
+
+// Times each candidate (tile x splits) twice after one warm-up launch and returns the fastest; the
+// model's choice is kept unless another is more than 3 % faster. Every candidate computes the same
+// C (to fp32 summation order), so the trials are harmless; the caller then launches the winner.
+TcChoice tune(const GemmArgs &g, cudaStream_t s, int sms, TcChoice model)
+{
+    cudaEvent_t e0, e1;
+    if (cudaEventCreate(&e0) != cudaSuccess)
+        return model;
+    if (cudaEventCreate(&e1) != cudaSuccess)
+    {
+        cudaEventDestroy(e0);
+        return model;
+    }
+    auto time_of = [&](TcChoice c) {
+        if (!launch_choice(g, s, c))
+            return 1e30f;
+        float best = 1e30f;
+        for (int r = 0; r < 2; ++r)
+        {
+            float ms = 0.f;
+            if (cudaEventRecord(e0, s) != cudaSuccess || !launch_choice(g, s, c) ||
+                cudaEventRecord(e1, s) != cudaSuccess || cudaEventSynchronize(e1) != cudaSuccess ||
+                cudaEventElapsedTime(&ms, e0, e1) != cudaSuccess)
+                return 1e30f;
+            best = ms < best ? ms : best;
+        }
+        return best;
+    };
+    const uint32_t kb_all = (g.K + kBK - 1) / kBK;
+    float t_model = time_of(model), t_best = t_model;
+    TcChoice best = model;
+    const uint32_t bms[3] = {128, 128, 256}, bns[3] = {128, 256, 256};
+    for (uint8_t t = 0; t < 3; ++t)
+    {
+        if (t == 2 && g.M <= 128)
+            continue;
+        const uint64_t n_tiles = (uint64_t)((g.N + bns[t] - 1) / bns[t]) * ((g.M + bms[t] - 1) / bms[t]) * g.batch;
+        for (uint8_t sp : {1, 2, 3, 4, 6, 8})
+        {
+            if (sp > kb_all || (sp > 1 && n_tiles * sp > 2ull * (uint64_t)sms) || (t == model.tile && sp == model.splits))
+                continue;
+            const float tm = time_of(TcChoice{t, sp});
+            if (tm < t_best)
+            {
+                t_best = tm;
+                best = TcChoice{t, sp};
+            }
+        }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    (void)cudaGetLastError();
+    return t_best < 0.97f * t_model ? best : model;
+}
+} // namespace
+
 bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
 {
     if (g.batch == 0 || g.batch_c == 0)
         return false;
-    // The largest tile that still gives every SM a tile: 256 x 256, then 128 x 256, then 128 x 128.
-    auto tiles = [&](uint32_t bm, uint32_t bn) {
-        return (uint64_t)((g.N + bn - 1) / bn) * ((g.M + bm - 1) / bm) * g.batch;
-    };
-    const char *force = getenv("VKLLM_B200_GEMM_TILE");
+    const char *force = getenv("VKLLM_B200_GEMM_TILE"), *force_splits = getenv("VKLLM_B200_GEMM_SPLITS");
     if (force)
     {
+        const uint32_t sp = force_splits ? (uint32_t)atoi(force_splits) : 1u;
         if (!strcmp(force, "256x256"))
-            return launch_tc<256, 256>(g, s);
+            return launch_tc<256, 256>(g, s, sp);
         if (!strcmp(force, "128x256"))
-            return launch_tc<128, 256>(g, s);
+            return launch_tc<128, 256>(g, s, sp);
         if (!strcmp(force, "128x128"))
-            return launch_tc<128, 128>(g, s);
+            return launch_tc<128, 128>(g, s, sp);
     }
-    // Pick the tile minimising waves x time per tile. Per K step, a 128 x 128 tile takes ~0.85 and a
-    // 256 x 256 tile ~1.64 of the time of a 128 x 256 tile (L2-to-SM operand bandwidth, measured on
-    // B200), so larger tiles win unless they leave SMs idle in the last wave.
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    auto cost = [&](uint32_t bm, uint32_t bn, double per_tile) {
-        return (double)((tiles(bm, bn) + sms - 1) / sms) * per_tile;
-    };
-    // Small M (GEMM-shaped decode): few tiles, weights-bound; split K so that every SM streams.
-    const uint64_t t128 = tiles(128, 128);
-    if (g.M <= 128 && t128 * 2 <= (uint64_t)sms)
+    const TcChoice model = model_choice(g, sms);
+    // Shapes worth more than ~1 GFLOP are tuned once per process (VKLLM_B200_GEMM_TUNE=0: model only);
+    // never inside stream capture, where the model's choice (or an earlier tuning result) is used.
+    static std::map<TuneKey, TcChoice> cache;
+    static std::mutex mu;
+    const TuneKey key{dev, g.M, g.N, g.K, g.batch};
     {
-        const uint32_t splits = (uint32_t)((uint64_t)sms / t128) > 8 ? 8 : (uint32_t)((uint64_t)sms / t128);
-        return launch_tc<128, 128>(g, s, splits);
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end())
+            return launch_choice(g, s, it->second);
     }
-    const double c128 = cost(128, 128, 0.85), c256 = cost(128, 256, 1.0), c2x = g.M > 128 ? cost(256, 256, 1.64) : 1e30;
-    if (c2x < c256 && c2x < c128)
-        return launch_tc<256, 256>(g, s);
-    if (c256 < c128)
-        return launch_tc<128, 256>(g, s);
-    return launch_tc<128, 128>(g, s);
+    const char *tune_env = getenv("VKLLM_B200_GEMM_TUNE");
+    const bool tune_on = !(tune_env && atoi(tune_env) == 0);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (!tune_on || 2.0 * g.M * g.N * (double)g.K * g.batch < 1e9 || cudaStreamIsCapturing(s, &cap) != cudaSuccess ||
+        cap != cudaStreamCaptureStatusNone)
+    {
+        (void)cudaGetLastError();
+        return launch_choice(g, s, model);
+    }
+    const TcChoice best = tune(g, s, sms, model);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        cache[key] = best;
+    }
+    return launch_choice(g, s, best);
 }
 
 uint32_t gemm_tcgen05_error(int dev)

@@ -24,6 +24,7 @@ struct GemmArgs
     uint64_t c_sb, c_sc;
     float scale;
     int act;
+    uint32_t act_from = 0; // act applies to output columns >= act_from (0: all)
 };
 
 // Fills `g` from 4-D descriptors when the tensor-core path applies (B read as [N, K] with unit
