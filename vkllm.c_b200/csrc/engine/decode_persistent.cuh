@@ -47,6 +47,7 @@ constexpr uint32_t kErrBarrierTimeout = 0x200;
 constexpr uint32_t kErrPeerTimeout = 0x400;
 constexpr uint32_t kTpMax = 8;     // ranks
 constexpr uint32_t kTpCtas = 256;  // flag slots per site (>= CTAs of the grid)
+constexpr uint32_t kTpRows = 64;   // Wo / down output rows a CTA may own under tensor parallelism
 constexpr uint32_t kErrPosition = 0x1;
 
 #ifndef VKB_PERSIST_SEG
@@ -122,7 +123,7 @@ struct PersistParams
     // rows and V / N vocabulary rows (from v0); the Wo and down outputs are partial sums that every
     // rank writes, per output row, into every peer's receive area, then raises a flag per CTA.
     uint32_t tp_size, tp_rank, v0, Vg;
-    float *tp_x[kTpMax];          // rank q's receive area [2 sites][N ranks][D] fp32
+    float *tp_x[kTpMax];          // rank q's receive area [2 sites][N ranks][kTpCtas][kTpRows] fp32
     uint32_t *tp_flag[kTpMax];    // rank q's flags [3 sites][kTpCtas][N ranks]
     float *tp_amv[kTpMax];        // rank q's argmax class slots [N ranks][32]
     uint32_t *tp_ami[kTpMax];
@@ -229,14 +230,30 @@ __device__ __forceinline__ UnitRange cta_units(uint32_t kind)
     return s_units[kind];
 }
 
+// This CTA's fp32 partials of its Wo / down output rows under tensor parallelism (the epilogue
+// stages them here; tp_allreduce_rows pushes them to the peers as one block).
+__shared__ __align__(16) float s_tp_stage[kTpRows];
+
 // Tensor-parallel allreduce of this CTA's output rows of the Wo (site 0) or down (site 1) phase:
-// the epilogue wrote each row's partial into every rank's receive area; here thread 0 publishes a
-// flag to the same CTA index of every rank and waits (bounded) for theirs; then each row is summed
-// over the ranks in rank order (fp32), rounded to fp16 (the projection node) and added to the
-// residual: x = fp16(x + fp16(sum)). Returns false on a timed-out wait or a reported error.
+// the CTA's staged row partials go to the same CTA slot of every rank's receive area as one
+// contiguous block of 16-byte stores (NVLink carries full-width writes instead of 4-byte ones); then
+// thread 0 publishes a flag to the same CTA index of every rank and waits (bounded) for theirs; then
+// each row is summed over the ranks in rank order (fp32), rounded to fp16 (the projection node) and
+// added to the residual: x = fp16(x + fp16(sum)). Returns false on a timed-out wait or a reported
+// error.
 __device__ __forceinline__ bool tp_allreduce_rows(const PersistParams &P, uint32_t site, uint32_t epoch)
 {
     __shared__ uint32_t ok_s;
+    __syncthreads();
+    {
+        const uint32_t n4 = (cta_units(site == 0 ? PK_WO : PK_DOWN).count + 3) / 4;
+        const uint64_t blk = (((uint64_t)site * P.tp_size + P.tp_rank) * kTpCtas + blockIdx.x) * kTpRows;
+        for (uint32_t t = threadIdx.x; t < n4 * P.tp_size; t += blockDim.x)
+        {
+            const uint32_t q = t / n4, i = t % n4;
+            reinterpret_cast<float4 *>(P.tp_x[q] + blk)[i] = reinterpret_cast<const float4 *>(s_tp_stage)[i];
+        }
+    }
     __syncthreads();
     if (threadIdx.x == 0)
     {
@@ -268,13 +285,13 @@ __device__ __forceinline__ bool tp_allreduce_rows(const PersistParams &P, uint32
     if (!ok_s)
         return false;
     const UnitRange r = cta_units(site == 0 ? PK_WO : PK_DOWN);
-    const float *rx = P.tp_x[P.tp_rank] + (uint64_t)site * P.tp_size * P.dd.D;
+    const float *rx = P.tp_x[P.tp_rank] + ((uint64_t)site * P.tp_size * kTpCtas + blockIdx.x) * kTpRows;
     for (uint32_t i = threadIdx.x; i < r.count; i += blockDim.x)
     {
         const uint32_t u = r.u0 + i;
         float t = 0.f;
         for (uint32_t q = 0; q < P.tp_size; ++q)
-            t += __ldcg(rx + (uint64_t)q * P.dd.D + u);
+            t += __ldcg(rx + (uint64_t)q * kTpCtas * kTpRows + i);
         P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(t));
     }
     return true;
@@ -453,13 +470,8 @@ __device__ __forceinline__ void persist_epilogue(const PersistParams &P, uint32_
     }
     case PK_WO:
     case PK_DOWN:
-        if (P.tp_size > 1)
-        {
-            // partial over this rank's K slice -> every rank's receive area (site 0 = Wo, 1 = down)
-            const uint32_t site = kind == PK_WO ? 0u : 1u;
-            for (uint32_t q = 0; q < P.tp_size; ++q)
-                P.tp_x[q][((uint64_t)site * P.tp_size + P.tp_rank) * dd.D + u] = s[0];
-        }
+        if (P.tp_size > 1) // partial over this rank's K slice, staged for tp_allreduce_rows
+            s_tp_stage[u - cta_units(kind).u0] = s[0];
         else
             P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(s[0]));
         break;

@@ -82,7 +82,8 @@ inline TpLayout tp_layout(uint32_t world, uint32_t D)
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
     TpLayout t;
     t.x = 0;
-    t.flag = t.x + al((size_t)2 * world * D * 4);
+    (void)D;
+    t.flag = t.x + al((size_t)2 * world * kTpCtas * kTpRows * 4);
     t.amv = t.flag + al((size_t)3 * kTpCtas * kTpMax * 4);
     t.ami = t.amv + al((size_t)kTpMax * 32 * 4);
     t.total = t.ami + al((size_t)kTpMax * 32 * 4);
@@ -861,7 +862,8 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
         // Tensor-parallel shards decode only on the persistent kernel, whose Wo / down epilogues
         // exchange the partial sums over peer memory.
         TpComm *c = (TpComm *)model->b200.tp_comm;
-        if (!e->persistent || !c || !c->connected || (uint32_t)sms > kTpCtas)
+        if (!e->persistent || !c || !c->connected || (uint32_t)sms > kTpCtas ||
+            e->htab[PK_WO * ((size_t)sms + 1) + 1] > kTpRows || (dd.D + sms - 1) / sms > kTpRows)
         {
             log_error("tensor-parallel decode needs the persistent kernel and vkllm_b200_tp_connect first");
             if (e->d_layers)
