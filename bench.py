@@ -265,6 +265,130 @@ def batched_decode_leg(vk, model, args, world, rank, stream):
             "path": "tcgen05 GEMMs (M = sequences per rank; [Wq;Wk;Wv] and [Wup;Wgate] concatenated; tile and split-K tuned per shape) + per-sequence RoPE/KV/attention kernels, CUDA graph per step"}
 
 
+def ops_microbench(vk, local, seed):
+    """the operator microbenchmarks, each op run through the reference's op API
+    (tensor_new -> upload -> op init -> run on a commands object -> submit/wait), timed by the
+    per-launch CUDA events of the op executor (VKLLM_NODE_TIMING=1 on a context of its own). L2 is
+    flushed (a 256 MB write on the same stream, queued just before the op) before every timed run;
+    the median of 5 runs is reported. Bytes are the
+    algorithmic bytes of the call (inputs read once, outputs written once); MATMUL at M = 512 is
+    reported in TF/s against the tensor-core peak, everything else in GB/s against the HBM peak."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    os.environ["VKLLM_NODE_TIMING"] = "1"
+    try:
+        ctx = vk.Context(local)
+    finally:
+        os.environ.pop("VKLLM_NODE_TIMING", None)
+    hbm, _ = measured_peaks()
+    tc = tc_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=torch.device("cuda", local))
+    cstream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    rng = np.random.default_rng(seed + 11)
+    lib = vk.lib()
+    out = {}
+    live = []
+
+    def tensor(name, arr, dt):
+        t = vk.tensor_new(ctx, name, arr.shape, dt)
+        vk.put(ctx, t, arr)
+        live.append(t)
+        return t
+
+    def node(name, shape, dt, op, srcs, params):
+        t = vk.tensor_new(ctx, name, shape, dt, op=op, srcs=srcs, params=params)
+        live.append(t)
+        return t
+
+    def timed(n, op):
+        init_fn, run_fn = f"vkllm_op_{op}_init", f"vkllm_op_{op}_run"
+        vk.run_op(ctx, n, init_fn, run_fn)  # init + a first run (GEMM tuning happens here)
+        cmd = vk.Commands(ctx)
+        ts = []
+        try:
+            for _ in range(5):
+                # the flush runs on the op's own (the context's) stream with no host wait, so the GPU
+                # is still busy with it while the op's events and kernels are enqueued: the event pair
+                # then brackets the op's kernels only, not the host's launch latency
+                with torch.cuda.stream(cstream):
+                    flush.zero_()
+                cmd.begin()
+                vk.check(getattr(lib, run_fn)(ctx.ptr, cmd.ptr, n), run_fn)
+                cmd.end()
+                cmd.submit_wait()
+                ns = C.c_uint64()
+                vk.check(lib.vkllm_pipeline_query_exec_time(ctx.ptr, n.contents.pipeline, C.byref(ns)), "exec_time")
+                ts.append(ns.value / 1e3)
+        finally:
+            cmd.close()
+        return float(np.median(ts))
+
+    def report(key, us, nbytes, flops=None):
+        r = {"us": round(us, 2), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
+             "hbm_frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4)}
+        if flops is not None:
+            r["tflops"] = round(flops / (us * 1e-6) / 1e12, 1)
+            r["tc_frac"] = round(flops / (us * 1e-6) / 1e12 / tc, 4)
+        out[key] = r
+
+    try:
+        for M in (1, 8, 64, 512):
+            for N, K in ((4096, 4096), (11008, 4096), (4096, 11008)):
+                a = rng.uniform(-1, 1, (1, 1, M, K)).astype(np.float16)
+                b = rng.uniform(-1, 1, (1, 1, N, K)).astype(np.float16)
+                A, B = tensor("A", a, vk.F16), tensor("B", b, vk.F16)
+                n = node("C", (1, 1, M, N), vk.F16, vk.OP_MATMUL, [A, B], bytes(C.c_float(1.0)) + bytes(C.c_int32(0)))
+                report(f"matmul_M{M}_N{N}_K{K}", timed(n, "matmul"), 2 * (N * K + M * K + M * N),
+                       2.0 * M * N * K if M == 512 else None)
+                for t in (n, A, B):
+                    vk.tensor_free(ctx, t)
+                    live.remove(t)
+        x = rng.uniform(-1, 1, (1, 1, 512, 4096)).astype(np.float16)
+        g = rng.uniform(0.5, 1.5, (1, 1, 1, 4096)).astype(np.float32)
+        X, G = tensor("x", x, vk.F16), tensor("g", g, vk.F32)
+        n = node("y", x.shape, vk.F16, vk.OP_RMSNORM, [X, G], bytes(C.c_float(2.0)) + bytes(C.c_float(1e-5)))
+        report("rmsnorm_512x4096", timed(n, "rmsnorm"), 2 * x.nbytes + g.nbytes)
+        q = rng.uniform(-1, 1, (1, 32, 512, 128)).astype(np.float16)
+        Q = tensor("q", q, vk.F16)
+        rope = bytes(C.c_uint32(0)) + bytes(C.c_float(10000.0)) + bytes(C.c_bool(False)) + bytes(3)
+        n = node("rq", q.shape, vk.F16, vk.OP_ROPE, [Q], rope)
+        report("rope_1x32x512x128", timed(n, "rope"), 2 * q.nbytes)
+        sc = rng.uniform(-4, 4, (1, 32, 1, 4096)).astype(np.float16)
+        S = tensor("s", sc, vk.F16)
+        n = node("p", sc.shape, vk.F16, vk.OP_SOFTMAX, [S], bytes(C.c_int32(1)) + bytes(C.c_uint32(4095)))
+        report("softmax_32x1x4096", timed(n, "softmax"), 2 * sc.nbytes)
+        src = rng.uniform(-1, 1, (1, 32, 1, 128)).astype(np.float16)
+        Sr = tensor("src", src, vk.F16)
+        n = node("cache", (1, 32, 4096, 128), vk.F16, vk.OP_UPDATE_ROWS, [Sr], bytes(C.c_uint32(100)))
+        report("update_rows_1_into_32x4096x128", timed(n, "update_rows"), 2 * src.nbytes)
+        table = rng.uniform(-1, 1, (1, 1, 32000, 4096)).astype(np.float16)
+        ids = rng.integers(0, 32000, size=(1, 1, 1, 512), dtype=np.uint32)
+        T, I = tensor("E", table, vk.F16), tensor("ids", ids, vk.U32)
+        n = node("emb", (1, 1, 512, 4096), vk.F16, vk.OP_EMBEDDING, [I, T], bytes(C.c_uint32(0)))
+        report("embedding_512_of_32000x4096", timed(n, "embedding"), 2 * 512 * 4096 * 2 + ids.nbytes)
+        lg = rng.uniform(-8, 8, (1, 1, 1, 32000)).astype(np.float32)
+        Lg = tensor("l", lg, vk.F32)
+        n = node("am", (1, 1, 1, 1), vk.U32, vk.OP_ARG_MAX, [Lg], None)
+        report("arg_max_32000_f32", timed(n, "arg_max"), lg.nbytes + 4)
+    finally:
+        for t in live:
+            vk.tensor_free(ctx, t)
+        del flush
+        ctx.close()
+    return out
+
+
+def tc_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 CFG_13B = dict(block_count=40, context_length=4096, embedding_length=5120, head_count=40, ffn_length=13824,
                vocab_size=32000, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
 
@@ -503,6 +627,12 @@ def run_ours(args, world, rank, local):
         except Exception as e:  # the baseline must not void the GPU measurement
             result["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     model.free()
+    # ---- operator microbenchmarks, rank 0 of a 1-GPU run ----------------------
+    if args.ops and world == 1 and result is not None:
+        try:
+            result["ops"] = ops_microbench(vk, local, SEED)
+        except Exception as e:  # a failing microbenchmark must not void the decode measurement
+            result["ops"] = {"error": str(e)[:200]}
     # ---- 13B tensor parallel ---------------------------------------------------
     if args.tp_steps > 0:
         tp = tp13b_leg(vk, ctx, args, world, rank, stream)
@@ -588,6 +718,7 @@ def main():
     # Profiling case only (ncu): fewer layers, no prefill / e2e / per-kernel extras, no JSON result line.
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--ops", type=int, default=1, help="operator microbenchmark leg (0: skip)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_setup() if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),

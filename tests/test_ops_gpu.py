@@ -262,6 +262,31 @@ def test_arg_max_exact(vk, ctx, orc, shape, dts):
         vk.tensor_free(ctx, t)
 
 
+@pytest.mark.parametrize("dts", ["f32", "f16"])
+def test_arg_max_long_rows_tie_rule(vk, ctx, orc, dts):
+    """Rows of >= 1024 entries take the block-per-row kernel: the same lane/tree tie rule (maxima in
+    several classes, repeated maxima inside one class far apart, all-equal rows) and the shader's
+    NaN behaviour (a class whose first element is NaN keeps it; later NaNs never win)."""
+    W = 32000
+    npdt = np.float16 if dts == "f16" else np.float32
+    x = rand((1, 1, 6, W), npdt, -4, 4)
+    x[0, 0, 0, [5, 37, 100, 31999]] = 7.0      # classes 5, 5, 4, 31: the reference's tree decides
+    x[0, 0, 1, [40 + 32 * 900, 8]] = 7.0        # class 8 twice, far apart: its first strict max wins
+    x[0, 0, 2, :] = 1.0                         # all equal
+    x[0, 0, 3, 3] = np.nan                      # class 3 starts with NaN and keeps it
+    x[0, 0, 3, [3 + 32 * 10, 70]] = 7.0
+    x[0, 0, 4, [900, 17 + 32 * 500]] = np.nan   # later NaNs never win
+    x[0, 0, 4, 12345] = 7.0
+    X = mk(vk, ctx, "x", x, vk.F16 if dts == "f16" else vk.F32)
+    node = op_node(vk, ctx, "am", (1, 1, 6, 1), vk.U32, vk.OP_ARG_MAX, [X], None)
+    vk.run_op(ctx, node, "vkllm_op_arg_max_init", "vkllm_op_arg_max_run")
+    got = vk.fetch(ctx, node).reshape(-1)
+    ref = orc.arg_max(x).reshape(-1)
+    assert np.array_equal(got, ref), (got, ref)
+    for t in (node, X):
+        vk.tensor_free(ctx, t)
+
+
 def test_arg_max_tie_rule(vk, ctx, orc):
     """Equal maxima: the winner follows the reference's lane/tree rule, not the lowest index."""
     W = 1000

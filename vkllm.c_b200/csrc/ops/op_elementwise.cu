@@ -85,6 +85,56 @@ __global__ void k_rmsnorm(const __half *x, Desc4 dx, const float *g, __half *y, 
     }
 }
 
+// Contiguous rows (W % 8 == 0, 16-byte aligned): the same node with 16-byte loads and stores, the
+// row held in registers between the two passes (W <= 8 * blockDim.x).
+__global__ void k_rmsnorm_vec(const __half *x, Desc4 dx, const float *g, __half *y, Desc4 dy, float eps)
+{
+    __shared__ float red[32];
+    const uint32_t row = blockIdx.x;
+    const uint32_t h = row % dx.shape[2], c = (row / dx.shape[2]) % dx.shape[1], b = row / (dx.shape[2] * dx.shape[1]);
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + d4_offset(dx, b, c, h, 0));
+    uint4 *yr = reinterpret_cast<uint4 *>(y + d4_offset(dy, b, c, h, 0));
+    const uint32_t W = dx.shape[3], n8 = W / 8;
+    const uint4 v = threadIdx.x < n8 ? xr[threadIdx.x] : make_uint4(0, 0, 0, 0);
+    const __half2 *vh = reinterpret_cast<const __half2 *>(&v);
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+    {
+        const float2 f = __half22float2(vh[e]);
+        s = fmaf(f.x, f.x, s);
+        s = fmaf(f.y, f.y, s);
+    }
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32)
+    {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0)
+            red[0] = t;
+    }
+    __syncthreads();
+    const float alpha = rsqrtf(red[0] / (float)W + eps);
+    if (threadIdx.x < n8)
+    {
+        const float4 ga = reinterpret_cast<const float4 *>(g)[2 * threadIdx.x];
+        const float4 gb = reinterpret_cast<const float4 *>(g)[2 * threadIdx.x + 1];
+        const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 f = __half22float2(vh[e]);
+            oh[e] = __floats2half2_rn((f.x * gg[2 * e]) * alpha, (f.y * gg[2 * e + 1]) * alpha);
+        }
+        yr[threadIdx.x] = o;
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // ROPE (src/shaders/vkllm_rope.comp:39-79): one thread per rotated pair.
 template <typename T>
@@ -123,6 +173,23 @@ __global__ void k_rope(const T *in, Desc4 di, T *out, Desc4 dout, uint32_t offse
     }
 }
 
+// fp16, normal-style pairs, unit innermost strides: the same rotation with one half2 load and store
+// per pair of the input and output, 32-bit index arithmetic (n < 2^32).
+__global__ void k_rope_h2(const __half *in, Desc4 di, __half *out, Desc4 dout, uint32_t offset, float base)
+{
+    const uint32_t half_w = di.shape[3] / 2, H = di.shape[2], Cc = di.shape[1];
+    const uint32_t n = di.shape[0] * Cc * H * half_w;
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x)
+    {
+        const uint32_t w = t % half_w, r = t / half_w, h = r % H, r2 = r / H, c = r2 % Cc, b = r2 / Cc;
+        const float theta = (float)(offset + h) / powf(base, (float)(2 * w) / (float)di.shape[3]);
+        const float cs = cosf(theta), sn = sinf(theta);
+        const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(in + d4_offset(di, b, c, h, 2 * w)));
+        *reinterpret_cast<__half2 *>(out + d4_offset(dout, b, c, h, 2 * w)) =
+            __floats2half2_rn(cs * v.x - sn * v.y, sn * v.x + cs * v.y);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // SOFTMAX (src/shaders/vkllm_softmax.comp:42-96): one warp per row; max over ALL entries, sum over
 // unmasked ones, masked outputs 0. Input addressed with the output layout, as in the reference.
@@ -157,6 +224,46 @@ template <typename T> __global__ void k_softmax(const T *in, T *out, Desc4 d, in
             out[o] = from_f32<T>(0.f);
         else
             out[o] = from_f32<T>(expf(to_f32(in[o]) - m) / s);
+    }
+}
+
+// Long rows (W >= 1024, e.g. decode scores over a long cache): one block per row, same node.
+template <typename T> __global__ void k_softmax_block(const T *in, T *out, Desc4 d, int seq_mask, uint32_t offsets)
+{
+    __shared__ float red[32];
+    const uint32_t row = blockIdx.x;
+    const uint32_t h = row % d.shape[2], c = (row / d.shape[2]) % d.shape[1], b = row / (d.shape[2] * d.shape[1]);
+    const uint64_t base = d4_offset(d, b, c, h, 0);
+    const uint32_t W = d.shape[3], nw = blockDim.x >> 5, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float m = to_f32(in[base]);
+    for (uint32_t i = threadIdx.x; i < W; i += blockDim.x)
+        m = fmaxf(m, to_f32(in[base + (uint64_t)i * d.stride[3]]));
+    m = warp_max(m);
+    if (lane == 0)
+        red[warp] = m;
+    __syncthreads();
+    m = red[0];
+    for (uint32_t w = 1; w < nw; ++w)
+        m = fmaxf(m, red[w]);
+    __syncthreads();
+    float s = 0.f;
+    for (uint32_t i = threadIdx.x; i < W; i += blockDim.x)
+        if (!(seq_mask > 0 && i > h + offsets))
+            s += expf(to_f32(in[base + (uint64_t)i * d.stride[3]]) - m);
+    s = warp_sum(s);
+    if (lane == 0)
+        red[warp] = s;
+    __syncthreads();
+    float tot = 0.f;
+    for (uint32_t w = 0; w < nw; ++w)
+        tot += red[w];
+    for (uint32_t i = threadIdx.x; i < W; i += blockDim.x)
+    {
+        const uint64_t o = base + (uint64_t)i * d.stride[3];
+        if (seq_mask > 0 && i > h + offsets)
+            out[o] = from_f32<T>(0.f);
+        else
+            out[o] = from_f32<T>(expf(to_f32(in[o]) - m) / tot);
     }
 }
 
@@ -313,6 +420,73 @@ template <typename T> __global__ void k_arg_max(const T *in, Desc4 di, uint32_t 
         out[d4_offset(dout, b, c, h, 0)] = mi;
 }
 
+// Long rows: one block per row with the same result. Lane l of the reference scans class l (i = l,
+// l + 32, ...) from its first element and replaces on a strict maximum, so the class result is (its
+// first element, index l) when that element is NaN (nothing compares greater), else the largest
+// non-NaN value at its smallest index. The warps split each class's elements, the per-class results
+// are combined in shared memory, then the reference's 16/8/4/2/1 tree runs unchanged.
+template <typename T> __global__ void k_arg_max_block(const T *in, Desc4 di, uint32_t *out, Desc4 dout)
+{
+    __shared__ float cv[32][32];
+    __shared__ uint32_t ci[32][32];
+    const uint32_t row = blockIdx.x;
+    const uint32_t h = row % di.shape[2], c = (row / di.shape[2]) % di.shape[1], b = row / (di.shape[2] * di.shape[1]);
+    const uint64_t base = d4_offset(di, b, c, h, 0);
+    const uint32_t W = di.shape[3], nw = blockDim.x >> 5, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float v = -FLT_MAX;
+    uint32_t idx = 0xffffffffu;
+    for (uint32_t i = lane + 32 * warp; i < W; i += 32 * nw)
+    {
+        const float x = to_f32(in[base + (uint64_t)i * di.stride[3]]);
+        if (x == x && (idx == 0xffffffffu || x > v)) // NaN never wins a strict comparison
+        {
+            v = x;
+            idx = i;
+        }
+    }
+    cv[warp][lane] = v;
+    ci[warp][lane] = idx;
+    __syncthreads();
+    if (warp != 0)
+        return;
+    float mv = -FLT_MAX;
+    uint32_t mi = 0xffffffffu;
+    for (uint32_t w = 0; w < nw; ++w) // the warps interleave a class's elements: ties go to the smaller index
+        if (ci[w][lane] != 0xffffffffu &&
+            (mi == 0xffffffffu || cv[w][lane] > mv || (cv[w][lane] == mv && ci[w][lane] < mi)))
+        {
+            mv = cv[w][lane];
+            mi = ci[w][lane];
+        }
+    if (lane < W)
+    {
+        const float first = to_f32(in[base + (uint64_t)lane * di.stride[3]]);
+        if (first != first || mi == 0xffffffffu)
+        {
+            mv = first;
+            mi = lane;
+        }
+    }
+    else
+    {
+        mv = -FLT_MAX; // no element in this class: the reference's initial lane state
+        mi = lane;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float ov = __shfl_down_sync(0xffffffffu, mv, o);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, mi, o);
+        if ((int)lane < o && ov > mv)
+        {
+            mv = ov;
+            mi = oi;
+        }
+    }
+    if (lane == 0)
+        out[d4_offset(dout, b, c, h, 0)] = mi;
+}
+
 } // namespace
 
 // =================================================================================================
@@ -345,8 +519,17 @@ extern "C" vkllm_err_t vkllm_op_rmsnorm_run(vkllm_context *context, vkllm_comman
     cudaStream_t s = stream_of(context, commands);
     uint32_t rows = in0->shapes[0] * in0->shapes[1] * in0->shapes[2];
     timing_begin(context, tensor->pipeline, s);
-    k_rmsnorm<<<rows, 512, 0, s>>>((const __half *)x, desc_of(in0), (const float *)g, (__half *)y, desc_of(tensor),
-                                    p->eps);
+    const Desc4 dx = desc_of(in0), dy = desc_of(tensor);
+    const uint32_t W = in0->shapes[3];
+    const bool vec = dx.stride[3] == 1 && dy.stride[3] == 1 && W % 8 == 0 && W / 8 <= 1024 && dx.stride[2] % 8 == 0 &&
+                     dy.stride[2] % 8 == 0 && dx.stride[1] % 8 == 0 && dy.stride[1] % 8 == 0 && dx.stride[0] % 8 == 0 &&
+                     dy.stride[0] % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0 &&
+                     ((uintptr_t)g & 15) == 0;
+    if (vec)
+        k_rmsnorm_vec<<<rows, (W / 8 + 31) / 32 * 32, 0, s>>>((const __half *)x, dx, (const float *)g, (__half *)y, dy,
+                                                               p->eps);
+    else
+        k_rmsnorm<<<rows, 512, 0, s>>>((const __half *)x, dx, (const float *)g, (__half *)y, dy, p->eps);
     timing_end(context, tensor->pipeline, s);
     return launch_status("k_rmsnorm");
 }
@@ -396,9 +579,16 @@ extern "C" vkllm_err_t vkllm_op_rope_run(vkllm_context *context, vkllm_commands 
         return VKLLM_ERR_OK;
     unsigned grid = grid_1d(n, 256);
     timing_begin(context, tensor->pipeline, s);
-    if (in0->dtype == vkllm_dtype_float16)
-        k_rope<__half><<<grid, 256, 0, s>>>((const __half *)x, desc_of(in0), (__half *)y, desc_of(tensor), p->offset,
-                                             p->base, p->neox_style ? 1 : 0);
+    const Desc4 di = desc_of(in0), dout = desc_of(tensor);
+    const bool h2 = in0->dtype == vkllm_dtype_float16 && !p->neox_style && di.stride[3] == 1 && dout.stride[3] == 1 &&
+                    in0->shapes[3] % 2 == 0 && di.stride[2] % 2 == 0 && di.stride[1] % 2 == 0 &&
+                    di.stride[0] % 2 == 0 && dout.stride[2] % 2 == 0 && dout.stride[1] % 2 == 0 &&
+                    dout.stride[0] % 2 == 0 && ((uintptr_t)x & 3) == 0 && ((uintptr_t)y & 3) == 0 && n < (1ull << 32);
+    if (h2)
+        k_rope_h2<<<grid, 256, 0, s>>>((const __half *)x, di, (__half *)y, dout, p->offset, p->base);
+    else if (in0->dtype == vkllm_dtype_float16)
+        k_rope<__half><<<grid, 256, 0, s>>>((const __half *)x, di, (__half *)y, dout, p->offset, p->base,
+                                             p->neox_style ? 1 : 0);
     else
         k_rope<float><<<grid, 256, 0, s>>>((const float *)x, desc_of(in0), (float *)y, desc_of(tensor), p->offset,
                                             p->base, p->neox_style ? 1 : 0);
@@ -452,7 +642,14 @@ extern "C" vkllm_err_t vkllm_op_softmax_run(vkllm_context *context, vkllm_comman
     uint64_t rows = (uint64_t)tensor->shapes[0] * tensor->shapes[1] * tensor->shapes[2];
     unsigned grid = grid_1d(rows * 32, 256);
     timing_begin(context, tensor->pipeline, s);
-    if (in0->dtype == vkllm_dtype_float16)
+    const bool block = tensor->shapes[3] >= 1024 && rows <= 0x7fffffffu;
+    if (block && in0->dtype == vkllm_dtype_float16)
+        k_softmax_block<__half><<<(unsigned)rows, 256, 0, s>>>((const __half *)x, (__half *)y, desc_of(tensor),
+                                                                p->seq_mask, p->offsets);
+    else if (block)
+        k_softmax_block<float><<<(unsigned)rows, 256, 0, s>>>((const float *)x, (float *)y, desc_of(tensor), p->seq_mask,
+                                                               p->offsets);
+    else if (in0->dtype == vkllm_dtype_float16)
         k_softmax<__half><<<grid, 256, 0, s>>>((const __half *)x, (__half *)y, desc_of(tensor), p->seq_mask,
                                                 p->offsets);
     else
@@ -753,7 +950,15 @@ extern "C" vkllm_err_t vkllm_op_arg_max_run(vkllm_context *context, vkllm_comman
     uint64_t rows = (uint64_t)in0->shapes[0] * in0->shapes[1] * in0->shapes[2];
     unsigned grid = grid_1d(rows * 32, 128);
     timing_begin(context, tensor->pipeline, s);
-    if (in0->dtype == vkllm_dtype_float16)
+    const unsigned bt = in0->shapes[3] >= 8192 ? 1024u : 256u;
+    const bool block = in0->shapes[3] >= 1024 && rows <= 0x7fffffffu;
+    if (block && in0->dtype == vkllm_dtype_float16)
+        k_arg_max_block<__half><<<(unsigned)rows, bt, 0, s>>>((const __half *)x, desc_of(in0), (uint32_t *)y,
+                                                              desc_of(tensor));
+    else if (block)
+        k_arg_max_block<float><<<(unsigned)rows, bt, 0, s>>>((const float *)x, desc_of(in0), (uint32_t *)y,
+                                                             desc_of(tensor));
+    else if (in0->dtype == vkllm_dtype_float16)
         k_arg_max<__half><<<grid, 128, 0, s>>>((const __half *)x, desc_of(in0), (uint32_t *)y, desc_of(tensor));
     else
         k_arg_max<float><<<grid, 128, 0, s>>>((const float *)x, desc_of(in0), (uint32_t *)y, desc_of(tensor));

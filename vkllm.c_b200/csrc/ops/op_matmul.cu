@@ -68,8 +68,22 @@ __global__ void k_gemv(const T *a, Desc4 da, const T *w, Desc4 dw, T *out, Desc4
             // 16-byte chunks of 8 halves; K % 8 == 0 and 16-byte aligned rows are checked on the host.
             const uint4 *ap = reinterpret_cast<const uint4 *>(a + a_off);
             const uint4 *wp = reinterpret_cast<const uint4 *>(w + w_off);
-            uint32_t nchunk = K / 8;
-            for (uint32_t i = lane; i < nchunk; i += 32)
+            uint32_t nchunk = K / 8, i = lane;
+            // eight 16-byte weight loads in flight per lane, summed in the same chunk order
+            for (; i + 32 * 7 < nchunk; i += 32 * 8)
+            {
+                uint4 wv[8], av[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                {
+                    wv[u] = ldg_stream(wp + i + 32 * u);
+                    av[u] = ap[i + 32 * u];
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    acc = dot8_f16(av[u], wv[u], acc);
+            }
+            for (; i < nchunk; i += 32)
                 acc = dot8_f16(ap[i], ldg_stream(wp + i), acc);
         }
         else
