@@ -3,6 +3,7 @@
 // blocks are the reference's, so the op-by-op executor computes the reference's rounding points.
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 
 #include "../runtime/internal.h"
 #include "vkllm_kvcache.h"
@@ -13,6 +14,15 @@
 
 namespace
 {
+
+// buf = a + b, truncated to the buffer (node names are built per token, so no printf formatting).
+void join(char *buf, size_t cap, const char *a, const char *b)
+{
+    size_t la = strnlen(a, cap - 1), lb = strnlen(b, cap - 1 - la);
+    memcpy(buf, a, la);
+    memcpy(buf + la, b, lb);
+    buf[la + lb] = 0;
+}
 
 // Creates a node and appends it to the graph; frees it again if the append fails.
 vkllm_err_t add(vkllm_context *ctx, vkllm_graph *g, const char *name, const uint32_t *shapes, vkllm_dtype_t dt,
@@ -64,39 +74,39 @@ extern "C" vkllm_err_t vkllm_llama2_build_ffn_layer(struct vkllm_context *contex
     vkllm_tensor *norm, *up, *gate, *mul, *down, *out;
     vkllm_tensor *norm_srcs[] = {input, params.norm_weight};
     vkllm_op_rmsnorm_params np = {params.norm_power, params.norm_eps};
-    snprintf(buf, sizeof(buf), "%s.norm", name);
+    join(buf, sizeof(buf), name, ".norm");
     _CHECK(add(context, graph, buf, input->shapes, input->dtype, VKLLM_OP_RMSNORM, norm_srcs, 2, &np, sizeof(np),
                false, &norm));
 
     uint32_t up_shape[4] = {B, C, S, F};
     vkllm_tensor *up_srcs[] = {norm, params.WU};
     vkllm_op_matmul_params up_p = {1.0f, 0};
-    snprintf(buf, sizeof(buf), "%s.up", name);
+    join(buf, sizeof(buf), name, ".up");
     _CHECK(add(context, graph, buf, up_shape, norm->dtype, VKLLM_OP_MATMUL, up_srcs, 2, &up_p, sizeof(up_p), false,
                &up));
 
     vkllm_tensor *gate_srcs[] = {norm, params.WG};
     vkllm_op_matmul_params gate_p = {1.0f, 1};
-    snprintf(buf, sizeof(buf), "%s.gate", name);
+    join(buf, sizeof(buf), name, ".gate");
     _CHECK(add(context, graph, buf, up_shape, norm->dtype, VKLLM_OP_MATMUL, gate_srcs, 2, &gate_p, sizeof(gate_p),
                false, &gate));
 
     vkllm_tensor *mul_srcs[] = {up, gate};
     int32_t mul_op = 2;
-    snprintf(buf, sizeof(buf), "%s.mul", name);
+    join(buf, sizeof(buf), name, ".mul");
     _CHECK(add(context, graph, buf, up_shape, gate->dtype, VKLLM_OP_BIN, mul_srcs, 2, &mul_op, sizeof(mul_op), false,
                &mul));
 
     uint32_t down_shape[4] = {B, C, S, params.WD->shapes[2]};
     vkllm_tensor *down_srcs[] = {mul, params.WD};
     vkllm_op_matmul_params down_p = {1.0f, 0};
-    snprintf(buf, sizeof(buf), "%s.down", name);
+    join(buf, sizeof(buf), name, ".down");
     _CHECK(add(context, graph, buf, down_shape, mul->dtype, VKLLM_OP_MATMUL, down_srcs, 2, &down_p, sizeof(down_p),
                false, &down));
 
     vkllm_tensor *add_srcs[] = {input, down};
     int32_t add_op = 0;
-    snprintf(buf, sizeof(buf), "%s.add", name);
+    join(buf, sizeof(buf), name, ".add");
     _CHECK(add(context, graph, buf, input->shapes, input->dtype, VKLLM_OP_BIN, add_srcs, 2, &add_op, sizeof(add_op),
                false, &out));
     return VKLLM_ERR_OK;
@@ -132,20 +142,20 @@ extern "C" vkllm_err_t vkllm_llama2_build_self_attn_layer(struct vkllm_context *
     vkllm_tensor *norm, *Q, *K, *V;
     vkllm_tensor *norm_srcs[] = {input, params.norm_weight};
     vkllm_op_rmsnorm_params np = {params.norm_power, params.norm_eps};
-    snprintf(buf, sizeof(buf), "%s.norm", name);
+    join(buf, sizeof(buf), name, ".norm");
     _CHECK(add(context, graph, buf, input->shapes, input->dtype, VKLLM_OP_RMSNORM, norm_srcs, 2, &np, sizeof(np),
                false, &norm));
 
     uint32_t qkv_shape[4] = {B, 1, S, HD};
     vkllm_op_matmul_params mp = {1.0f, 0};
     vkllm_tensor *q_srcs[] = {norm, params.WQ};
-    snprintf(buf, sizeof(buf), "%s.Q", name);
+    join(buf, sizeof(buf), name, ".Q");
     _CHECK(add(context, graph, buf, qkv_shape, norm->dtype, VKLLM_OP_MATMUL, q_srcs, 2, &mp, sizeof(mp), false, &Q));
     vkllm_tensor *k_srcs[] = {norm, params.WK};
-    snprintf(buf, sizeof(buf), "%s.K", name);
+    join(buf, sizeof(buf), name, ".K");
     _CHECK(add(context, graph, buf, qkv_shape, norm->dtype, VKLLM_OP_MATMUL, k_srcs, 2, &mp, sizeof(mp), false, &K));
     vkllm_tensor *v_srcs[] = {norm, params.WV};
-    snprintf(buf, sizeof(buf), "%s.V", name);
+    join(buf, sizeof(buf), name, ".V");
     _CHECK(add(context, graph, buf, qkv_shape, norm->dtype, VKLLM_OP_MATMUL, v_srcs, 2, &mp, sizeof(mp), false, &V));
 
     // [B,1,S,H*hd] -> [B,S,H,hd] -> permute(0,2,1,3) -> [B,H,S,hd] views.
@@ -157,10 +167,10 @@ extern "C" vkllm_err_t vkllm_llama2_build_self_attn_layer(struct vkllm_context *
     _CHECK(view(context, graph, V, heads_shape, perm, &Vr));
 
     vkllm_tensor *RQ, *RK;
-    snprintf(buf, sizeof(buf), "%s.RQ", name);
+    join(buf, sizeof(buf), name, ".RQ");
     _CHECK(add(context, graph, buf, Qr->shapes, Qr->dtype, VKLLM_OP_ROPE, &Qr, 1, &rope_p, sizeof(rope_p), false,
                &RQ));
-    snprintf(buf, sizeof(buf), "%s.RK", name);
+    join(buf, sizeof(buf), name, ".RK");
     _CHECK(add(context, graph, buf, Kr->shapes, Kr->dtype, VKLLM_OP_ROPE, &Kr, 1, &rope_p, sizeof(rope_p), false,
                &RK));
 
@@ -176,12 +186,12 @@ extern "C" vkllm_err_t vkllm_llama2_build_self_attn_layer(struct vkllm_context *
     vkllm_tensor *scores, *probs, *attn;
     vkllm_tensor *s_srcs[] = {RQ, RK};
     vkllm_op_matmul_params sp = {1.0f / sqrtf((float)hd), 0};
-    snprintf(buf, sizeof(buf), "%s.scores", name);
+    join(buf, sizeof(buf), name, ".scores");
     _CHECK(add(context, graph, buf, scores_shape, input->dtype, VKLLM_OP_MATMUL, s_srcs, 2, &sp, sizeof(sp), false,
                &scores));
 
     vkllm_op_softmax_params smp = {1, params.offsets};
-    snprintf(buf, sizeof(buf), "%s.attn_weights", name);
+    join(buf, sizeof(buf), name, ".attn_weights");
     _CHECK(add(context, graph, buf, scores_shape, input->dtype, VKLLM_OP_SOFTMAX, &scores, 1, &smp, sizeof(smp),
                false, &probs));
 
@@ -195,7 +205,7 @@ extern "C" vkllm_err_t vkllm_llama2_build_self_attn_layer(struct vkllm_context *
     // [B,H,S,hd] -> permute -> [B,S,H,hd] -> COPY (materialise) -> reshape [B,1,S,H*hd].
     vkllm_tensor *attn_ref, *concat, *concat_ref;
     _CHECK(view(context, graph, attn, nullptr, perm, &attn_ref));
-    snprintf(buf, sizeof(buf), "%s.concated_heads", name);
+    join(buf, sizeof(buf), name, ".concated_heads");
     _CHECK(add(context, graph, buf, attn_ref->shapes, attn_ref->dtype, VKLLM_OP_COPY, &attn_ref, 1, NULL, 0, false,
                &concat));
     uint32_t concat_shape[4] = {B, 1, S, HD};
@@ -204,12 +214,12 @@ extern "C" vkllm_err_t vkllm_llama2_build_self_attn_layer(struct vkllm_context *
     uint32_t final_shape[4] = {B, 1, S, hidden};
     vkllm_tensor *f_srcs[] = {concat_ref, params.WO};
     vkllm_tensor *final_out, *final_add;
-    snprintf(buf, sizeof(buf), "%s.final_output", name);
+    join(buf, sizeof(buf), name, ".final_output");
     _CHECK(add(context, graph, buf, final_shape, concat->dtype, VKLLM_OP_MATMUL, f_srcs, 2, &op1, sizeof(op1), false,
                &final_out));
     vkllm_tensor *a_srcs[] = {input, final_out};
     int32_t add_op = 0;
-    snprintf(buf, sizeof(buf), "%s.final_output_add", name);
+    join(buf, sizeof(buf), name, ".final_output_add");
     _CHECK(add(context, graph, buf, final_out->shapes, final_out->dtype, VKLLM_OP_BIN, a_srcs, 2, &add_op,
                sizeof(add_op), false, &final_add));
     return VKLLM_ERR_OK;

@@ -81,6 +81,8 @@ extern "C" void vkllm_context_free(struct vkllm_context *p)
                 cudaEventDestroy((cudaEvent_t)kv.second->ev_end);
             free(kv.second);
         }
+        for (void *b : rt->tensor_pool)
+            free(b);
         delete rt->dev_alloc;
         delete rt->host_alloc;
         if (rt->dev_error_word)

@@ -84,6 +84,7 @@ struct vkllm_b200_runtime
     int exec_mode = VKLLM_EXEC_FUSED;
     bool node_timing = false;
     int* dev_error_word = nullptr; // device-side error flag written by kernels with bounded waits
+    std::vector<void *> tensor_pool; // freed tensor structs of the pooled size (tensor.cpp)
 };
 
 namespace vkb

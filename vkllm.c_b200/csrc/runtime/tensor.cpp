@@ -29,9 +29,48 @@ vkllm_err_t calc_strides(const uint32_t *shapes, vkllm_dtype_t dtype, uint32_t *
     return VKLLM_ERR_OK;
 }
 
-void set_name(vkllm_tensor *t, const char *fmt, const char *a, const char *b)
+// name = a + b, a cut so that the whole fits (what "%.{127 - |b|}s%s" prints), without printf: views
+// are created per token by the graph builders.
+void set_name(vkllm_tensor *t, const char *a, const char *b)
 {
-    snprintf((char *)t->name, sizeof(t->name), fmt, a, b);
+    char *n = (char *)t->name;
+    const size_t lb = strnlen(b, sizeof(t->name) - 1), la = strnlen(a, sizeof(t->name) - 1 - lb);
+    memcpy(n, a, la);
+    memcpy(n + la, b, lb);
+    n[la + lb] = 0;
+}
+
+// Tensor structs come from a per-context free list when their params block fits kPoolParams bytes:
+// the graph builders create and free ~20 nodes per layer every token. A 16-byte header before the
+// struct records whether the block has the pooled size.
+constexpr size_t kPoolParams = 64, kTensorHdr = 16;
+
+vkllm_tensor *tensor_alloc(vkllm_context *ctx, size_t params_bytes)
+{
+    const bool pooled = ctx && ctx->runtime && params_bytes <= kPoolParams;
+    const size_t bytes = kTensorHdr + sizeof(vkllm_tensor) + (pooled ? kPoolParams : params_bytes);
+    unsigned char *b = nullptr;
+    if (pooled && !ctx->runtime->tensor_pool.empty())
+    {
+        b = (unsigned char *)ctx->runtime->tensor_pool.back();
+        ctx->runtime->tensor_pool.pop_back();
+        memset(b, 0, bytes);
+    }
+    else
+        b = (unsigned char *)calloc(1, bytes);
+    if (!b)
+        return nullptr;
+    b[0] = pooled ? 1 : 0;
+    return (vkllm_tensor *)(b + kTensorHdr);
+}
+
+void tensor_release(vkllm_context *ctx, vkllm_tensor *t)
+{
+    unsigned char *b = (unsigned char *)t - kTensorHdr;
+    if (b[0] && ctx && ctx->runtime && ctx->runtime->tensor_pool.size() < 4096)
+        ctx->runtime->tensor_pool.push_back(b);
+    else
+        free(b);
 }
 
 } // namespace
@@ -102,16 +141,20 @@ extern "C" vkllm_err_t vkllm_tensor_new(struct vkllm_context *context, const cha
     _CHECK_ARGS(n_srcs <= VKLLM_MAX_SRCS);
     _CHECK_ARGS(n_srcs == 0 || srcs);
 
-    vkllm_tensor *t = (vkllm_tensor *)calloc(1, sizeof(vkllm_tensor) + params_bytes);
+    vkllm_tensor *t = tensor_alloc(context, params_bytes);
     if (!t)
         return VKLLM_ERR_ALLOC;
-    snprintf((char *)t->name, sizeof(t->name), "%s", name ? name : "");
+    if (name)
+    {
+        const size_t ln = strnlen(name, sizeof(t->name) - 1);
+        memcpy((char *)t->name, name, ln); // calloc'd: the terminator is already there
+    }
     t->dtype = dtype;
     memcpy(t->shapes, shapes, sizeof(t->shapes));
     vkllm_err_t err = calc_strides(shapes, dtype, t->strides);
     if (err != VKLLM_ERR_OK)
     {
-        free(t);
+        tensor_release(context, t);
         return err;
     }
     uint64_t total = (uint64_t)shapes[0] * t->strides[0];
@@ -131,7 +174,7 @@ extern "C" vkllm_err_t vkllm_tensor_new(struct vkllm_context *context, const cha
         if (!h)
         {
             log_error("pinned host allocation of %u bytes failed", t->bytes);
-            free(t);
+            tensor_release(context, t);
             return VKLLM_ERR_ALLOC;
         }
         void *d = nullptr;
@@ -139,7 +182,7 @@ extern "C" vkllm_err_t vkllm_tensor_new(struct vkllm_context *context, const cha
         {
             (void)cudaGetLastError();
             context->runtime->host_alloc->release(h);
-            free(t);
+            tensor_release(context, t);
             return VKLLM_ERR_VULKAN;
         }
         t->data.host = h;
@@ -163,7 +206,7 @@ extern "C" void vkllm_tensor_free(struct vkllm_context *context, struct vkllm_te
         else if (tensor->data.dev)
             context->runtime->dev_alloc->release(tensor->data.dev);
     }
-    free(tensor);
+    tensor_release(context, tensor);
     if (context)
         context->stats.tensor_free_counts += 1;
 }
@@ -240,10 +283,10 @@ extern "C" vkllm_err_t vkllm_tensor_copy_ref(struct vkllm_context *context, stru
                                              struct vkllm_tensor **p)
 {
     _CHECK_ARGS(context && tensor && p);
-    vkllm_tensor *t = (vkllm_tensor *)calloc(1, sizeof(vkllm_tensor));
+    vkllm_tensor *t = tensor_alloc(context, 0);
     if (!t)
         return VKLLM_ERR_ALLOC;
-    set_name(t, "%.123s%s", tensor->name, "_ref");
+    set_name(t, tensor->name, "_ref");
     t->dtype = tensor->dtype;
     memcpy(t->shapes, tensor->shapes, sizeof(t->shapes));
     memcpy(t->strides, tensor->strides, sizeof(t->strides));
@@ -270,7 +313,7 @@ extern "C" vkllm_err_t vkllm_tensor_slice0(struct vkllm_context *context, struct
         _CHECK_ARGS(extents[i] > 0 && extents[i] <= tensor->shapes[i]);
     _CHECK(vkllm_tensor_copy_ref(context, tensor, slice));
     vkllm_tensor *t = *slice;
-    set_name(t, "%.120s%s", tensor->name, "_slice0");
+    set_name(t, tensor->name, "_slice0");
     memcpy(t->shapes, extents, sizeof(t->shapes));
     return VKLLM_ERR_OK;
 }
