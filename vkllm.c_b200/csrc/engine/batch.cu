@@ -333,20 +333,52 @@ __global__ void k_b_argmax(const __half *__restrict__ logits, uint32_t V, uint32
                            uint32_t *__restrict__ pos, uint32_t *__restrict__ ring, uint32_t ring_steps,
                            uint32_t *__restrict__ step_ctr, uint32_t B)
 {
-    const uint32_t b = blockIdx.x, lane = threadIdx.x;
+    // The reference's rule (src/shaders/vkllm_arg_max.comp:40-97): lane l scans class l (i = l, l + 32,
+    // ...) from its first element and replaces on a strict maximum; then 16/8/4/2/1 keeps the left
+    // value unless the right one is strictly greater. The block's warps split each class: a class's
+    // result is (its first element, index l) when that element is NaN, else its largest non-NaN value
+    // at its smallest index.
+    __shared__ float cv[32][32];
+    __shared__ uint32_t ci[32][32];
+    const uint32_t b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const __half *row = logits + (uint64_t)b * V;
     float v = -FLT_MAX;
-    uint32_t idx = lane;
-    if (lane < V)
-        v = __half2float(row[lane]);
-    for (uint32_t i = lane + 32; i < V; i += 32)
+    uint32_t idx = 0xffffffffu;
+    for (uint32_t i = lane + 32 * warp; i < V; i += 32 * nw)
     {
         const float c = __half2float(row[i]);
-        if (c > v)
+        if (c == c && (idx == 0xffffffffu || c > v))
         {
             v = c;
             idx = i;
         }
+    }
+    cv[warp][lane] = v;
+    ci[warp][lane] = idx;
+    __syncthreads();
+    if (warp != 0)
+        return;
+    v = -FLT_MAX;
+    idx = 0xffffffffu;
+    for (uint32_t w = 0; w < nw; ++w) // interleaved indices: ties go to the smaller one
+        if (ci[w][lane] != 0xffffffffu && (idx == 0xffffffffu || cv[w][lane] > v || (cv[w][lane] == v && ci[w][lane] < idx)))
+        {
+            v = cv[w][lane];
+            idx = ci[w][lane];
+        }
+    if (lane < V)
+    {
+        const float first = __half2float(row[lane]);
+        if (first != first || idx == 0xffffffffu)
+        {
+            v = first;
+            idx = lane;
+        }
+    }
+    else
+    {
+        v = -FLT_MAX;
+        idx = lane;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
@@ -438,7 +470,7 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
     k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, bt->out_norm, D, dd.eps, bt->xn);
     if (!gemm(bt->xn, bt->wout, bt->logits, B, dd.V, D, 0, s))
         return VKLLM_ERR_VULKAN;
-    k_b_argmax<<<B, 32, 0, s>>>(bt->logits, dd.V, bt->tok, bt->pos, bt->ring, bt->ring_steps, bt->err + 1, B);
+    k_b_argmax<<<B, 1024, 0, s>>>(bt->logits, dd.V, bt->tok, bt->pos, bt->ring, bt->ring_steps, bt->err + 1, B);
     k_b_step_done<<<1, 1, 0, s>>>(bt->err + 1);
     return cudaGetLastError() == cudaSuccess ? VKLLM_ERR_OK : VKLLM_ERR_VULKAN;
 }

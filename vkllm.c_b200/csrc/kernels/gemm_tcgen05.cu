@@ -15,6 +15,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -728,11 +729,29 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
     const TcChoice model = model_choice(g, sms);
     // Shapes worth more than ~1 GFLOP are tuned once per process (VKLLM_B200_GEMM_TUNE=0: model only);
     // never inside stream capture, where the model's choice (or an earlier tuning result) is used.
+    // VKLLM_B200_GEMM_TUNE_FILE: choices are read from this file at the first call and appended to
+    // it when tuned, so later processes (or a profiler run, whose timings would mislead the tuner)
+    // reuse them. One line per shape: "M N K batch tile splits".
     static std::map<TuneKey, TcChoice> cache;
     static std::mutex mu;
+    static bool file_loaded = false;
+    const char *tune_file = getenv("VKLLM_B200_GEMM_TUNE_FILE");
     const TuneKey key{dev, g.M, g.N, g.K, g.batch};
     {
         std::lock_guard<std::mutex> lk(mu);
+        if (tune_file && !file_loaded)
+        {
+            file_loaded = true;
+            if (FILE *f = fopen(tune_file, "r"))
+            {
+                unsigned m, n, k, b, t, sp;
+                while (fscanf(f, "%u %u %u %u %u %u", &m, &n, &k, &b, &t, &sp) == 6)
+                    if (t <= 2 && sp >= 1 && sp <= 8)
+                        for (int d = 0; d < 64; ++d) // the file carries no device: it applies to each
+                            cache[TuneKey{d, m, n, k, b}] = TcChoice{(uint8_t)t, (uint8_t)sp};
+                fclose(f);
+            }
+        }
         auto it = cache.find(key);
         if (it != cache.end())
             return launch_choice(g, s, it->second);
@@ -750,6 +769,12 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
     {
         std::lock_guard<std::mutex> lk(mu);
         cache[key] = best;
+        if (tune_file)
+            if (FILE *f = fopen(tune_file, "a"))
+            {
+                fprintf(f, "%u %u %u %u %u %u\n", g.M, g.N, g.K, g.batch, (unsigned)best.tile, (unsigned)best.splits);
+                fclose(f);
+            }
     }
     return launch_choice(g, s, best);
 }
