@@ -198,31 +198,42 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
     for (int e = 0; e < 8; ++e)
         qr[e] = lane_on ? qs[8 * pc + e] : 0.f;
     float mx = -FLT_MAX;
-    for (uint32_t j0 = 0; j0 < Lk; j0 += G)
+    // four rounds of key rows in flight per lane, then their dot products in order
+    for (uint32_t j0 = 0; j0 < Lk; j0 += 4 * G)
     {
-        const uint32_t j = j0 + gi;
-        const bool valid = lane_on && j < Lk;
-        float a = 0.f;
-        if (valid)
-        {
-            const uint4 raw = reinterpret_cast<const uint4 *>(kb + (uint64_t)j * hd)[pc];
-            const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+        uint4 raw[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-            {
-                const float2 f = __half22float2(hh[e]);
-                a = fmaf(qr[2 * e], f.x, a);
-                a = fmaf(qr[2 * e + 1], f.y, a);
-            }
-        }
-        for (uint32_t o = lpk / 2; o > 0; o >>= 1)
-            a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (j < Lk)
+        for (int u = 0; u < 4; ++u)
         {
-            const float s = round_f16(a * scale);
-            if (pc == 0)
-                sc[j] = s;
-            mx = fmaxf(mx, s);
+            const uint32_t j = j0 + u * G + gi;
+            raw[u] = (lane_on && j < Lk) ? reinterpret_cast<const uint4 *>(kb + (uint64_t)j * hd)[pc]
+                                         : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+        {
+            const uint32_t j = j0 + u * G + gi;
+            float a = 0.f;
+            if (lane_on && j < Lk)
+            {
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                {
+                    const float2 f = __half22float2(hh[e]);
+                    a = fmaf(qr[2 * e], f.x, a);
+                    a = fmaf(qr[2 * e + 1], f.y, a);
+                }
+            }
+            for (uint32_t o = lpk / 2; o > 0; o >>= 1)
+                a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (j < Lk)
+            {
+                const float s = round_f16(a * scale);
+                if (pc == 0)
+                    sc[j] = s;
+                mx = fmaxf(mx, s);
+            }
         }
     }
     mx = warp_max(mx);
@@ -254,17 +265,30 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
     }
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (lane_on)
-        for (uint32_t j = gi; j < Lk; j += G)
+        for (uint32_t j0 = gi; j0 < Lk; j0 += 4 * G) // four value rows in flight, summed in key order
         {
-            const uint4 raw = reinterpret_cast<const uint4 *>(vb + (uint64_t)j * hd)[pc];
-            const float pj = sc[j];
-            const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+            uint4 raw[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
+            for (int u = 0; u < 4; ++u)
             {
-                const float2 f = __half22float2(hh[e]);
-                a[2 * e] = fmaf(pj, f.x, a[2 * e]);
-                a[2 * e + 1] = fmaf(pj, f.y, a[2 * e + 1]);
+                const uint32_t j = j0 + u * G;
+                raw[u] = j < Lk ? reinterpret_cast<const uint4 *>(vb + (uint64_t)j * hd)[pc] : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+            {
+                const uint32_t j = j0 + u * G;
+                if (j >= Lk)
+                    break;
+                const float pj = sc[j];
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&raw[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                {
+                    const float2 f = __half22float2(hh[e]);
+                    a[2 * e] = fmaf(pj, f.x, a[2 * e]);
+                    a[2 * e + 1] = fmaf(pj, f.y, a[2 * e + 1]);
+                }
             }
         }
     float *acc = sc + ((Lk + 31) & ~31u); // [G][hd]
