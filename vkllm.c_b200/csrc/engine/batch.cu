@@ -52,6 +52,7 @@ struct vkllm_b200_batch
     __half *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *t0 = nullptr, *ug = nullptr,
            *m = nullptr, *logits = nullptr; // qkv [B][3 HD], ug [B][2 F] (up, then SiLU(gate)), m [B][F]
     __half *wcat = nullptr;                  // the concatenated weight copies of every layer
+    float *part = nullptr;                   // [4][B][D] fp32 split-K partials of the Wo / down GEMMs
     uint32_t *tok = nullptr, *pos = nullptr, *ring = nullptr, *err = nullptr;
     uint32_t ring_steps = 0, last_steps = 0;
     std::vector<uint32_t> host_pos; // positions as the host knows them (load + steps)
@@ -65,6 +66,7 @@ namespace
 {
 
 constexpr int kBT = 256;
+constexpr uint32_t kProjSplits = 4; // K splits of the Wo / down GEMMs (M = sequences)
 
 __device__ __forceinline__ float bsum(float v, float *red)
 {
@@ -330,6 +332,63 @@ __global__ void k_b_gate(__half *__restrict__ m, const __half *__restrict__ ug, 
     }
 }
 
+// Three graph nodes in one pass over each sequence's row: the projection's output from its split-K
+// partials, t = fp16(sum of the partials in split order) (the GEMM node, scale 1); the residual BIN
+// add x = fp16(x + t); and the next RMSNORM node xn = fp16((x * g) * rsqrt(mean(x^2) + eps)) over the
+// new fp16 row. Block per sequence with kBT threads, 8 halves per chunk in k_b_rmsnorm's thread
+// mapping (so the norm reduces in the same order).
+__global__ void k_b_proj_residual_norm(const float *__restrict__ part, uint32_t splits, __half *__restrict__ x,
+                                       const float *__restrict__ g, uint32_t D, float eps, __half *__restrict__ xn,
+                                       uint32_t B)
+{
+    __shared__ float red[32];
+    const uint32_t b = blockIdx.x, n8 = D / 8;
+    const uint64_t plane = (uint64_t)B * D;
+    uint4 *xr = reinterpret_cast<uint4 *>(x + (uint64_t)b * D);
+    float s = 0.f;
+    for (uint32_t i = threadIdx.x; i < n8; i += blockDim.x)
+    {
+        float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (uint32_t sp = 0; sp < splits; ++sp)
+        {
+            const float4 *src = reinterpret_cast<const float4 *>(part + sp * plane + (uint64_t)b * D + 8ull * i);
+            const float4 a = __ldcg(src), c = __ldcg(src + 1);
+            t[0] += a.x, t[1] += a.y, t[2] += a.z, t[3] += a.w, t[4] += c.x, t[5] += c.y, t[6] += c.z, t[7] += c.w;
+        }
+        const uint4 xv = xr[i];
+        const __half *xh = reinterpret_cast<const __half *>(&xv);
+        uint4 o;
+        __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+        {
+            oh[e] = __float2half_rn(__half2float(xh[e]) + round_f16(t[e]));
+            const float f = __half2float(oh[e]);
+            s = fmaf(f, f, s);
+        }
+        xr[i] = o;
+    }
+    const float alpha = rsqrtf(bsum(s, red) / (float)D + eps);
+    uint4 *yr = reinterpret_cast<uint4 *>(xn + (uint64_t)b * D);
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    for (uint32_t i = threadIdx.x; i < n8; i += blockDim.x)
+    {
+        const uint4 v = xr[i]; // this thread's own chunk, written above
+        const float4 ga = g4[2 * i], gb = g4[2 * i + 1];
+        const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 f = __half22float2(h[e]);
+            oh[e] = __floats2half2_rn((f.x * gg[2 * e]) * alpha, (f.y * gg[2 * e + 1]) * alpha);
+        }
+        yr[i] = o;
+    }
+}
+
 // x = fp16(x + t) (the residual BIN add) or m = fp16(a * b) (the gate BIN mul), 8 halves per thread.
 __global__ void k_b_bin8(__half *__restrict__ out, const __half *__restrict__ a, const __half *__restrict__ b,
                          uint64_t n8, int mul)
@@ -458,6 +517,48 @@ bool gemm(const __half *A, const __half *W, __half *C, uint32_t M, uint32_t N, u
     return gemm_tcgen05_launch(g, s);
 }
 
+// C = A . W^T as fp32 split-K partials in `part` (no reduction); false when the GEMM cannot split.
+bool gemm_partials(const __half *A, const __half *W, float *part, uint32_t M, uint32_t N, uint32_t K, uint32_t splits,
+                   uint32_t *used, cudaStream_t s)
+{
+    GemmArgs g{};
+    g.A = A;
+    g.B = W;
+    g.C = nullptr;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.lda = K;
+    g.ldb = K;
+    g.ldc = N;
+    g.batch = 1;
+    g.batch_c = 1;
+    g.scale = 1.0f;
+    g.act = 0;
+    return gemm_tcgen05_partials(g, s, splits, part, used);
+}
+
+// The Wo / down projection with its residual add and the following RMSNORM (gains g) in one pass
+// over the rows when the GEMM can split K 4 ways into bt->part, else the three nodes separately.
+vkllm_err_t proj_residual_norm(vkllm_b200_batch *bt, const __half *in, const __half *w, uint32_t K, const float *g,
+                               cudaStream_t s)
+{
+    const BatchDims &dd = bt->dd;
+    const uint32_t B = bt->B, D = dd.D;
+    uint32_t used = 0;
+    if (gemm_partials(in, w, bt->part, B, D, K, kProjSplits, &used, s))
+    {
+        k_b_proj_residual_norm<<<B, kBT, 0, s>>>(bt->part, used, bt->x, g, D, dd.eps, bt->xn, B);
+        return VKLLM_ERR_OK;
+    }
+    (void)cudaGetLastError();
+    if (!gemm(in, w, bt->t0, B, D, K, 0, s))
+        return VKLLM_ERR_VULKAN;
+    k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
+    k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, g, D, dd.eps, bt->xn);
+    return VKLLM_ERR_OK;
+}
+
 vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
 {
     const BatchDims &dd = bt->dd;
@@ -473,25 +574,21 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
         const BatchLayer &w = bt->layers[l];
         __half *kc = bt->kv + ((uint64_t)l * 2 + 0) * B * H * bt->cap * hd;
         __half *vc = bt->kv + ((uint64_t)l * 2 + 1) * B * H * bt->cap * hd;
-        k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
+        if (l == 0) // later layers get xn from the previous layer's down projection pass
+            k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
         if (!gemm(bt->xn, w.wqkv, bt->qkv, B, 3 * HD, D, 0, s))
             return VKLLM_ERR_VULKAN;
         k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD,
                                                                      bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
         k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
                                                          bt->attn);
-        if (!gemm(bt->attn, w.wo, bt->t0, B, D, HD, 0, s))
-            return VKLLM_ERR_VULKAN;
-        k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
-        k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.ffn_norm, D, dd.eps, bt->xn);
+        _CHECK(proj_residual_norm(bt, bt->attn, w.wo, HD, w.ffn_norm, s));
         if (!gemm(bt->xn, w.wug, bt->ug, B, 2 * F, D, 1, s, F)) // SiLU on the gate half only
             return VKLLM_ERR_VULKAN;
         k_b_gate<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->ug, F, B);
-        if (!gemm(bt->m, w.wd, bt->t0, B, D, F, 0, s))
-            return VKLLM_ERR_VULKAN;
-        k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
+        // the down projection's pass also norms for the next layer (or the output norm after the last)
+        _CHECK(proj_residual_norm(bt, bt->m, w.wd, F, l + 1 < bt->L ? bt->layers[l + 1].attn_norm : bt->out_norm, s));
     }
-    k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, bt->out_norm, D, dd.eps, bt->xn);
     if (!gemm(bt->xn, bt->wout, bt->logits, B, dd.V, D, 0, s))
         return VKLLM_ERR_VULKAN;
     k_b_argmax<<<B, 1024, 0, s>>>(bt->logits, dd.V, bt->tok, bt->pos, bt->ring, bt->ring_steps, bt->err + 1, B);
@@ -557,7 +654,8 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t kv_bytes = al((size_t)bt->L * 2 * B * dd.H * bt->cap * dd.hd * 2);
     const size_t act = al((size_t)B * D * 2) * 3 + al((size_t)B * 3 * HD * 2) + al((size_t)B * HD * 2) +
-                       al((size_t)B * 2 * F * 2) + al((size_t)B * F * 2) + al((size_t)B * dd.V * 2);
+                       al((size_t)B * 2 * F * 2) + al((size_t)B * F * 2) + al((size_t)B * dd.V * 2) +
+                       al((size_t)4 * B * D * 4);
     const size_t small = al((size_t)B * 4) * 2 + al((size_t)bt->ring_steps * B * 4) + al(16);
     if (cudaMalloc(&bt->ws, kv_bytes + act + small) != cudaSuccess)
     {
@@ -580,6 +678,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->ug = (__half *)take((size_t)B * 2 * F * 2);
     bt->m = (__half *)take((size_t)B * F * 2);
     bt->logits = (__half *)take((size_t)B * dd.V * 2);
+    bt->part = (float *)take((size_t)4 * B * D * 4);
     bt->tok = (uint32_t *)take((size_t)B * 4);
     bt->pos = (uint32_t *)take((size_t)B * 4);
     bt->ring = (uint32_t *)take((size_t)bt->ring_steps * B * 4);

@@ -474,7 +474,11 @@ uint32_t *error_word(int dev)
     return words[dev];
 }
 
-template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1)
+// ws_ext / splits_out: when given, the split-K partials go to the caller's buffer ([splits][batch][M]
+// [N] fp32, splits > 1) and no reduction is launched; *splits_out receives the split count used.
+template <int BM, int BN>
+bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws_ext = nullptr,
+               uint32_t *splits_out = nullptr)
 {
     using Cfg = TileCfg<BM, BN>;
     int dev = 0, cc = 0, optin = 0;
@@ -527,7 +531,14 @@ template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s, uint
     p.kb_per = (kb_all + splits - 1) / splits;
     p.splits = splits > 1 ? (kb_all + p.kb_per - 1) / p.kb_per : 1; // every split gets >= 1 k-block
     p.ws = nullptr;
-    if (p.splits > 1)
+    if (ws_ext)
+    {
+        if (p.splits < 2)
+            return false;
+        p.ws = ws_ext;
+        *splits_out = p.splits;
+    }
+    else if (p.splits > 1)
     {
         p.ws = splitk_workspace(dev, (size_t)p.splits * g.batch * g.M * g.N * sizeof(float), s);
         if (!p.ws)
@@ -538,7 +549,7 @@ template <int BM, int BN> bool launch_tc(const GemmArgs &g, cudaStream_t s, uint
     }
     dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch * p.splits);
     k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
-    if (p.splits > 1)
+    if (p.splits > 1 && !ws_ext)
     {
         const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 7) / 8);
         const unsigned blocks = (unsigned)((work + 255) / 256 < 148u * 16u ? (work + 255) / 256 : 148u * 16u);
@@ -777,6 +788,13 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
             }
     }
     return launch_choice(g, s, best);
+}
+
+bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, float *ws, uint32_t *splits_used)
+{
+    if (g.batch == 0 || g.batch_c == 0 || !ws || !splits_used || splits < 2)
+        return false;
+    return launch_tc<128, 128>(g, s, splits, ws, splits_used);
 }
 
 uint32_t gemm_tcgen05_error(int dev)
