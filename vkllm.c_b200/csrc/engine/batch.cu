@@ -32,9 +32,11 @@ struct BatchLayer
 {
     const __half *wq, *wk, *wv, *wo, *wg, *wu, *wd;
     const float *attn_norm, *ffn_norm;
-    // the batch's concatenated copies: [Wq; Wk; Wv] as [3 HD, D] and [Wup; Wgate] as [2 F, D], so that
-    // each is one GEMM with M = sequences (fewer, larger GEMMs fill the SMs without splitting K)
-    const __half *wqkv, *wug;
+    // The GEMM operands, the batch's own copies: [Wq; Wk; Wv] as [3 HD, D] and [Wup; Wgate] as
+    // [2 F, D], so that each is one GEMM with M = sequences (fewer, larger GEMMs fill the SMs without
+    // splitting K). With the tiled layout (the default) these and wo_g / wd_g are gemm_tile_b copies,
+    // whose B loads stream contiguous 16 KB tiles; otherwise wo_g / wd_g are the model's matrices.
+    const __half *wqkv, *wug, *wo_g, *wd_g;
 };
 } // namespace vkb
 
@@ -45,13 +47,14 @@ struct vkllm_b200_batch
     uint32_t B = 0, cap = 0, L = 0, HD = 0, unk = 0;
     vkb::BatchDims dd{};
     std::vector<vkb::BatchLayer> layers;
-    const __half *embed = nullptr, *wout = nullptr;
+    const __half *embed = nullptr, *wout = nullptr, *wout_g = nullptr; // wout_g: the logits GEMM operand
+    uint32_t tiled = 1;                                                  // GEMM operands in tile order
     const float *out_norm = nullptr;
     void *ws = nullptr;
     __half *kv = nullptr; // [L][2][B][H][cap][hd]
     __half *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *t0 = nullptr, *ug = nullptr,
            *m = nullptr, *logits = nullptr; // qkv [B][3 HD], ug [B][2 F] (up, then SiLU(gate)), m [B][F]
-    __half *wcat = nullptr;                  // the concatenated weight copies of every layer
+    __half *wcat = nullptr;                  // the GEMM operand copies of every layer (and wout_g when tiled)
     float *part = nullptr;                   // [4][B][D] fp32 split-K partials of the Wo / down GEMMs
     uint32_t *tok = nullptr, *pos = nullptr, *ring = nullptr, *err = nullptr;
     uint32_t ring_steps = 0, last_steps = 0;
@@ -496,11 +499,12 @@ __global__ void k_b_check_pos(const uint32_t *pos, uint32_t cap, uint32_t B, uin
             atomicOr(err, 1u);
 }
 
-bool gemm(const __half *A, const __half *W, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s,
-          uint32_t act_from = 0)
+bool gemm(const __half *A, const __half *W, uint32_t tiled, __half *C, uint32_t M, uint32_t N, uint32_t K, int act,
+          cudaStream_t s, uint32_t act_from = 0)
 {
     GemmArgs g{};
     g.act_from = act_from;
+    g.b_tiled = tiled;
     g.A = A;
     g.B = W;
     g.C = C;
@@ -518,10 +522,11 @@ bool gemm(const __half *A, const __half *W, __half *C, uint32_t M, uint32_t N, u
 }
 
 // C = A . W^T as fp32 split-K partials in `part` (no reduction); false when the GEMM cannot split.
-bool gemm_partials(const __half *A, const __half *W, float *part, uint32_t M, uint32_t N, uint32_t K, uint32_t splits,
-                   uint32_t *used, cudaStream_t s)
+bool gemm_partials(const __half *A, const __half *W, uint32_t tiled, float *part, uint32_t M, uint32_t N, uint32_t K,
+                   uint32_t splits, uint32_t *used, cudaStream_t s)
 {
     GemmArgs g{};
+    g.b_tiled = tiled;
     g.A = A;
     g.B = W;
     g.C = nullptr;
@@ -546,13 +551,13 @@ vkllm_err_t proj_residual_norm(vkllm_b200_batch *bt, const __half *in, const __h
     const BatchDims &dd = bt->dd;
     const uint32_t B = bt->B, D = dd.D;
     uint32_t used = 0;
-    if (gemm_partials(in, w, bt->part, B, D, K, kProjSplits, &used, s))
+    if (gemm_partials(in, w, bt->tiled, bt->part, B, D, K, kProjSplits, &used, s))
     {
         k_b_proj_residual_norm<<<B, kBT, 0, s>>>(bt->part, used, bt->x, g, D, dd.eps, bt->xn, B);
         return VKLLM_ERR_OK;
     }
     (void)cudaGetLastError();
-    if (!gemm(in, w, bt->t0, B, D, K, 0, s))
+    if (!gemm(in, w, bt->tiled, bt->t0, B, D, K, 0, s))
         return VKLLM_ERR_VULKAN;
     k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
     k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, g, D, dd.eps, bt->xn);
@@ -576,20 +581,21 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
         __half *vc = bt->kv + ((uint64_t)l * 2 + 1) * B * H * bt->cap * hd;
         if (l == 0) // later layers get xn from the previous layer's down projection pass
             k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
-        if (!gemm(bt->xn, w.wqkv, bt->qkv, B, 3 * HD, D, 0, s))
+        if (!gemm(bt->xn, w.wqkv, bt->tiled, bt->qkv, B, 3 * HD, D, 0, s))
             return VKLLM_ERR_VULKAN;
         k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD,
                                                                      bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
         k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
                                                          bt->attn);
-        _CHECK(proj_residual_norm(bt, bt->attn, w.wo, HD, w.ffn_norm, s));
-        if (!gemm(bt->xn, w.wug, bt->ug, B, 2 * F, D, 1, s, F)) // SiLU on the gate half only
+        _CHECK(proj_residual_norm(bt, bt->attn, w.wo_g, HD, w.ffn_norm, s));
+        if (!gemm(bt->xn, w.wug, bt->tiled, bt->ug, B, 2 * F, D, 1, s, F)) // SiLU on the gate half only
             return VKLLM_ERR_VULKAN;
         k_b_gate<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->ug, F, B);
         // the down projection's pass also norms for the next layer (or the output norm after the last)
-        _CHECK(proj_residual_norm(bt, bt->m, w.wd, F, l + 1 < bt->L ? bt->layers[l + 1].attn_norm : bt->out_norm, s));
+        _CHECK(
+            proj_residual_norm(bt, bt->m, w.wd_g, F, l + 1 < bt->L ? bt->layers[l + 1].attn_norm : bt->out_norm, s));
     }
-    if (!gemm(bt->xn, bt->wout, bt->logits, B, dd.V, D, 0, s))
+    if (!gemm(bt->xn, bt->wout_g, bt->tiled, bt->logits, B, dd.V, D, 0, s))
         return VKLLM_ERR_VULKAN;
     k_b_argmax<<<B, 1024, 0, s>>>(bt->logits, dd.V, bt->tok, bt->pos, bt->ring, bt->ring_steps, bt->err + 1, B);
     k_b_step_done<<<1, 1, 0, s>>>(bt->err + 1);
@@ -684,9 +690,14 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->ring = (uint32_t *)take((size_t)bt->ring_steps * B * 4);
     bt->err = (uint32_t *)take(16); // [0] error bits, [1] step counter
     cudaStream_t s = ctx->runtime->stream;
-    // concatenated weight copies, per layer [Wq; Wk; Wv] then [Wup; Wgate]
-    const size_t per_layer = ((size_t)3 * HD + (size_t)2 * F) * D;
-    if (cudaMalloc(&bt->wcat, per_layer * bt->L * sizeof(__half)) != cudaSuccess)
+    // GEMM operand copies, per layer [Wq; Wk; Wv] then [Wup; Wgate] (then Wo and Wdown when tiled)
+    const char *tiled_env = getenv("VKLLM_B200_BATCH_TILED");
+    bt->tiled = tiled_env && atoi(tiled_env) == 0 ? 0u : 1u;
+    const size_t t_qkv = gemm_tiled_b_elems(3 * HD, D), t_ug = gemm_tiled_b_elems(2 * F, D),
+                 t_wo = gemm_tiled_b_elems(D, HD), t_wd = gemm_tiled_b_elems(D, F);
+    const size_t per_layer = bt->tiled ? t_qkv + t_ug + t_wo + t_wd : ((size_t)3 * HD + (size_t)2 * F) * D;
+    const size_t extra = bt->tiled ? gemm_tiled_b_elems(dd.V, D) : 0;
+    if (cudaMalloc(&bt->wcat, (per_layer * bt->L + extra) * sizeof(__half)) != cudaSuccess)
     {
         (void)cudaGetLastError();
         cudaFree(bt->ws);
@@ -697,7 +708,20 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     for (uint32_t l = 0; l < bt->L && copied; ++l)
     {
         BatchLayer &w = bt->layers[l];
-        __half *qkv = bt->wcat + per_layer * l, *ug = qkv + (size_t)3 * HD * D;
+        __half *qkv = bt->wcat + per_layer * l;
+        if (bt->tiled)
+        {
+            __half *ug = qkv + t_qkv, *wo = ug + t_ug, *wd = wo + t_wo;
+            copied = gemm_tile_b(TileSrcs{{w.wq, w.wk, w.wv}, {HD, HD, HD}, 3}, D, qkv, s) &&
+                     gemm_tile_b(TileSrcs{{w.wu, w.wg}, {F, F}, 2}, D, ug, s) &&
+                     gemm_tile_b(TileSrcs{{w.wo}, {D}, 1}, HD, wo, s) && gemm_tile_b(TileSrcs{{w.wd}, {D}, 1}, F, wd, s);
+            w.wqkv = qkv;
+            w.wug = ug;
+            w.wo_g = wo;
+            w.wd_g = wd;
+            continue;
+        }
+        __half *ug = qkv + (size_t)3 * HD * D;
         const size_t mat = (size_t)HD * D * sizeof(__half), fm = (size_t)F * D * sizeof(__half);
         copied = cudaMemcpyAsync(qkv, w.wq, mat, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
                  cudaMemcpyAsync(qkv + (size_t)HD * D, w.wk, mat, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
@@ -706,7 +730,17 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
                  cudaMemcpyAsync(ug + (size_t)F * D, w.wg, fm, cudaMemcpyDeviceToDevice, s) == cudaSuccess;
         w.wqkv = qkv;
         w.wug = ug;
+        w.wo_g = w.wo;
+        w.wd_g = w.wd;
     }
+    if (bt->tiled)
+    {
+        __half *wo = bt->wcat + per_layer * bt->L;
+        copied = copied && gemm_tile_b(TileSrcs{{bt->wout}, {dd.V}, 1}, D, wo, s);
+        bt->wout_g = wo;
+    }
+    else
+        bt->wout_g = bt->wout;
     if (!copied || cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess)

@@ -30,6 +30,7 @@ namespace
 {
 
 constexpr uint32_t kBK = 64;
+constexpr uint32_t kTileRows = 128; // rows of one B tile in the tiled operand layout
 constexpr uint64_t kTcWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t su32(const void *p)
@@ -114,6 +115,7 @@ struct TcParams
     float scale;
     int act;
     uint32_t act_from; // act applies to output columns >= act_from
+    uint32_t b_tiled;  // B in 128-row x 64-column tiles (gemm_tile_b); its map is (64, 128, k-block, n-tile)
     __half *C;
     uint32_t *err;
     // Split-K: `splits` CTAs share a tile, each over kb_per k-blocks, writing fp32 partials to
@@ -227,7 +229,10 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
                          "r"(Cfg::kStageBytes)
                          : "memory");
             tma_load_4d(sa, &tmA, (int32_t)((kb_lo + kb) * kBK), (int32_t)m0, ca, ba, &full[s]); // BM rows
-            tma_load_4d(sb, &tmB, (int32_t)((kb_lo + kb) * kBK), (int32_t)n0, cb, bb, &full[s]);
+            if (p.b_tiled) // BN / 128 consecutive tiles of the k-block: the same smem image as BN rows
+                tma_load_4d(sb, &tmB, 0, 0, (int32_t)(kb_lo + kb), (int32_t)(n0 / kTileRows), &full[s]);
+            else
+                tma_load_4d(sb, &tmB, (int32_t)((kb_lo + kb) * kBK), (int32_t)n0, cb, bb, &full[s]);
             ++issued;
         }
         if (!ok)
@@ -456,6 +461,24 @@ bool encode_operand(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// B in tile order (gemm_tile_b): dims (64, 128, k-blocks, n-tiles), every box (64, 128, 1,
+// box_rows / 128) a contiguous run of box_rows * 128 bytes.
+bool encode_tiled_b(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t N, uint32_t box_rows)
+{
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || box_rows % kTileRows)
+        return false;
+    const uint64_t kbs = (K + kBK - 1) / kBK, nts = (N + kTileRows - 1) / kTileRows;
+    const uint64_t tile_b = (uint64_t)kTileRows * kBK * 2;
+    cuuint64_t dims[4] = {kBK, kTileRows, kbs, nts};
+    cuuint64_t strides[3] = {kBK * 2, tile_b, tile_b * kbs};
+    cuuint32_t box[4] = {kBK, kTileRows, 1, box_rows / kTileRows};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 uint32_t *error_word(int dev)
 {
     static uint32_t *words[64] = {};
@@ -504,7 +527,13 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
     // broadcast dimensions (stride 0) are described with extent 1 and indexed 0 by the kernel
     if (!encode_operand(&ma, g.A, g.K, g.M, g.lda, g.a_sc ? g.batch_c : 1, g.a_sc, g.a_sb ? batch_b : 1, g.a_sb, BM))
         return false;
-    if (!encode_operand(&mb, g.B, g.K, g.N, g.ldb, g.b_sc ? g.batch_c : 1, g.b_sc, g.b_sb ? batch_b : 1, g.b_sb, BN))
+    if (g.b_tiled)
+    {
+        if (g.batch != 1 || !encode_tiled_b(&mb, g.B, g.K, g.N, BN))
+            return false;
+    }
+    else if (!encode_operand(&mb, g.B, g.K, g.N, g.ldb, g.b_sc ? g.batch_c : 1, g.b_sc, g.b_sb ? batch_b : 1, g.b_sb,
+                             BN))
         return false;
     TcParams p{};
     p.M = g.M;
@@ -521,6 +550,7 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
     p.scale = g.scale;
     p.act = g.act;
     p.act_from = g.act_from;
+    p.b_tiled = g.b_tiled ? 1u : 0u;
     p.C = (__half *)g.C;
     p.err = error_word(dev);
     if (!p.err)
@@ -656,10 +686,10 @@ TcChoice model_choice(const GemmArgs &g, int sms)
 struct TuneKey
 {
     int dev;
-    uint32_t M, N, K, batch;
+    uint32_t M, N, K, batch, tiled;
     bool operator<(const TuneKey &o) const
     {
-        return std::tie(dev, M, N, K, batch) < std::tie(o.dev, o.M, o.N, o.K, o.batch);
+        return std::tie(dev, M, N, K, batch, tiled) < std::tie(o.dev, o.M, o.N, o.K, o.batch, o.tiled);
     }
 };
 
@@ -742,12 +772,12 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
     // never inside stream capture, where the model's choice (or an earlier tuning result) is used.
     // VKLLM_B200_GEMM_TUNE_FILE: choices are read from this file at the first call and appended to
     // it when tuned, so later processes (or a profiler run, whose timings would mislead the tuner)
-    // reuse them. One line per shape: "M N K batch tile splits".
+    // reuse them. One line per shape: "M N K batch b_tiled tile splits".
     static std::map<TuneKey, TcChoice> cache;
     static std::mutex mu;
     static bool file_loaded = false;
     const char *tune_file = getenv("VKLLM_B200_GEMM_TUNE_FILE");
-    const TuneKey key{dev, g.M, g.N, g.K, g.batch};
+    const TuneKey key{dev, g.M, g.N, g.K, g.batch, g.b_tiled ? 1u : 0u};
     {
         std::lock_guard<std::mutex> lk(mu);
         if (tune_file && !file_loaded)
@@ -755,11 +785,11 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
             file_loaded = true;
             if (FILE *f = fopen(tune_file, "r"))
             {
-                unsigned m, n, k, b, t, sp;
-                while (fscanf(f, "%u %u %u %u %u %u", &m, &n, &k, &b, &t, &sp) == 6)
-                    if (t <= 2 && sp >= 1 && sp <= 8)
+                unsigned m, n, k, b, bt, t, sp;
+                while (fscanf(f, "%u %u %u %u %u %u %u", &m, &n, &k, &b, &bt, &t, &sp) == 7)
+                    if (bt <= 1 && t <= 2 && sp >= 1 && sp <= 8)
                         for (int d = 0; d < 64; ++d) // the file carries no device: it applies to each
-                            cache[TuneKey{d, m, n, k, b}] = TcChoice{(uint8_t)t, (uint8_t)sp};
+                            cache[TuneKey{d, m, n, k, b, bt}] = TcChoice{(uint8_t)t, (uint8_t)sp};
                 fclose(f);
             }
         }
@@ -783,7 +813,8 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
         if (tune_file)
             if (FILE *f = fopen(tune_file, "a"))
             {
-                fprintf(f, "%u %u %u %u %u %u\n", g.M, g.N, g.K, g.batch, (unsigned)best.tile, (unsigned)best.splits);
+                fprintf(f, "%u %u %u %u %u %u %u\n", g.M, g.N, g.K, g.batch, g.b_tiled ? 1u : 0u, (unsigned)best.tile,
+                        (unsigned)best.splits);
                 fclose(f);
             }
     }
@@ -795,6 +826,67 @@ bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, f
     if (g.batch == 0 || g.batch_c == 0 || !ws || !splits_used || splits < 2)
         return false;
     return launch_tc<128, 128>(g, s, splits, ws, splits_used);
+}
+
+namespace
+{
+// One 16-byte chunk (8 fp16) of the tiled copy per thread; rows past the sources and columns past K
+// are zero.
+__global__ void k_tile_b(TileSrcs src, uint32_t K, uint32_t kbs, __half *__restrict__ dst, uint64_t chunks, bool vec)
+{
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < chunks; i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t c8 = (uint32_t)(i & 7), r = (uint32_t)((i >> 3) % kTileRows);
+        const uint64_t tk = (i >> 3) / kTileRows;
+        const uint32_t kb = (uint32_t)(tk % kbs), nt = (uint32_t)(tk / kbs);
+        uint32_t n = nt * kTileRows + r;
+        const uint32_t k = kb * kBK + 8 * c8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        uint32_t si = 0;
+        while (si < src.n && n >= src.rows[si])
+            n -= src.rows[si++];
+        if (si < src.n && k < K)
+        {
+            const __half *row = src.ptr[si] + (uint64_t)n * K;
+            if (vec)
+                v = *reinterpret_cast<const uint4 *>(row + k);
+            else
+            {
+                __half *h = reinterpret_cast<__half *>(&v);
+                for (uint32_t e = 0; e < 8 && k + e < K; ++e)
+                    h[e] = row[k + e];
+            }
+        }
+        reinterpret_cast<uint4 *>(dst)[i] = v;
+    }
+}
+} // namespace
+
+uint64_t gemm_tiled_b_elems(uint32_t N, uint32_t K)
+{
+    return (uint64_t)((N + kTileRows - 1) / kTileRows) * kTileRows * ((K + kBK - 1) / kBK) * kBK;
+}
+
+bool gemm_tile_b(const TileSrcs &src, uint32_t K, __half *dst, cudaStream_t s)
+{
+    uint64_t n = 0;
+    bool vec = (K % 8) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+    if (src.n == 0 || src.n > TileSrcs::kMax || K == 0)
+        return false;
+    for (uint32_t i = 0; i < src.n; ++i)
+    {
+        if (!src.ptr[i])
+            return false;
+        n += src.rows[i];
+        vec = vec && (reinterpret_cast<uintptr_t>(src.ptr[i]) & 15) == 0;
+    }
+    if (n == 0 || n > 0xffffffffull)
+        return false;
+    const uint64_t chunks = gemm_tiled_b_elems((uint32_t)n, K) / 8;
+    const uint64_t blocks = (chunks + 255) / 256;
+    k_tile_b<<<(unsigned)(blocks < 148u * 32u ? blocks : 148u * 32u), 256, 0, s>>>(src, K, (K + kBK - 1) / kBK, dst,
+                                                                                chunks, vec);
+    return cudaGetLastError() == cudaSuccess;
 }
 
 uint32_t gemm_tcgen05_error(int dev)

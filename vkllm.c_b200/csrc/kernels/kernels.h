@@ -25,7 +25,26 @@ struct GemmArgs
     float scale;
     int act;
     uint32_t act_from = 0; // act applies to output columns >= act_from (0: all)
+    uint32_t b_tiled = 0;  // B is a gemm_tile_b copy (batch 1 only; ldb and the B strides are unused)
 };
+
+// Row sources of one tiled B operand: rows [0, rows[0]) come from ptr[0], the next rows[1] from
+// ptr[1], ... (each source row-major [rows][K]).
+struct TileSrcs
+{
+    static constexpr uint32_t kMax = 4;
+    const __half *ptr[kMax];
+    uint32_t rows[kMax];
+    uint32_t n;
+};
+
+// Elements of the tiled copy of an [N, K] B operand: [ceil(N/128)][ceil(K/64)][128][64] fp16, each
+// 128 x 64 tile (one k-block of 128 rows) contiguous, so that the GEMM's B loads read whole 16 KB
+// runs of HBM instead of 128-byte pieces of 128 rows. Padding rows and columns are zero.
+uint64_t gemm_tiled_b_elems(uint32_t N, uint32_t K);
+
+// Writes the tiled copy of the row-concatenation of `src` (K columns each) to `dst`.
+bool gemm_tile_b(const TileSrcs &src, uint32_t K, __half *dst, cudaStream_t s);
 
 // Fills `g` from 4-D descriptors when the tensor-core path applies (B read as [N, K] with unit
 // inner stride, all row strides multiples of 8 elements, 16-byte aligned bases). Returns false
