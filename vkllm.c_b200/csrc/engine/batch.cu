@@ -71,6 +71,13 @@ namespace
 constexpr int kBT = 256;
 constexpr uint32_t kProjSplits = 4; // K splits of the Wo / down GEMMs (M = sequences)
 
+// Lets the next kernel in the stream, when it was launched as this one's programmatic dependent (the
+// batch's GEMMs), start its CTAs now; it still waits for this grid's completion before reading.
+__device__ __forceinline__ void pdl_trigger()
+{
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
 __device__ __forceinline__ float bsum(float v, float *red)
 {
     v = warp_sum(v);
@@ -108,6 +115,7 @@ __global__ void k_b_embed(const __half *__restrict__ table, uint32_t V, uint32_t
 __global__ void k_b_rmsnorm(const __half *__restrict__ x, const float *__restrict__ g, uint32_t D, float eps,
                             __half *__restrict__ y)
 {
+    pdl_trigger();
     __shared__ float red[32];
     const uint4 *xr = reinterpret_cast<const uint4 *>(x + (uint64_t)blockIdx.x * D);
     const uint32_t n8 = D / 8;
@@ -178,6 +186,7 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
                                                      const uint32_t *__restrict__ pos, uint32_t H, uint32_t hd,
                                                      uint32_t cap, float scale, __half *__restrict__ out)
 {
+    pdl_trigger();
     extern __shared__ float sm[];
     float *qs = sm;           // [hd]
     float *sc = sm + 256;     // [Lk]
@@ -315,6 +324,7 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
 // (the gate half already SiLU'd by the GEMM epilogue), 8 halves per thread (F % 8 == 0).
 __global__ void k_b_gate(__half *__restrict__ m, const __half *__restrict__ ug, uint32_t F, uint32_t B)
 {
+    pdl_trigger();
     const uint32_t f8 = F / 8;
     for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < (uint64_t)B * f8;
          t += (uint64_t)gridDim.x * blockDim.x)
@@ -344,6 +354,7 @@ __global__ void k_b_proj_residual_norm(const float *__restrict__ part, uint32_t 
                                        const float *__restrict__ g, uint32_t D, float eps, __half *__restrict__ xn,
                                        uint32_t B)
 {
+    pdl_trigger();
     __shared__ float red[32];
     const uint32_t b = blockIdx.x, n8 = D / 8;
     const uint64_t plane = (uint64_t)B * D;
@@ -505,6 +516,7 @@ bool gemm(const __half *A, const __half *W, uint32_t tiled, __half *C, uint32_t 
     GemmArgs g{};
     g.act_from = act_from;
     g.b_tiled = tiled;
+    g.pdl = 1;
     g.A = A;
     g.B = W;
     g.C = C;
@@ -527,6 +539,7 @@ bool gemm_partials(const __half *A, const __half *W, uint32_t tiled, float *part
 {
     GemmArgs g{};
     g.b_tiled = tiled;
+    g.pdl = 1;
     g.A = A;
     g.B = W;
     g.C = nullptr;

@@ -181,6 +181,9 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     __shared__ uint32_t fail_s;
 
+    // a kernel launched as this one's programmatic dependent may start its CTAs now (its own wait
+    // still orders it after this grid's completion)
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, z = blockIdx.z / p.splits, split = blockIdx.z % p.splits;
     const uint32_t zb = z / p.batch_c, zc = z % p.batch_c;
@@ -214,9 +217,31 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         // Producer.
         const int32_t ca = p.a_cc ? 0 : (int32_t)zc, ba = p.a_bc ? 0 : (int32_t)zb;
         const int32_t cb = p.b_cc ? 0 : (int32_t)zc, bb = p.b_bc ? 0 : (int32_t)zb;
-        uint32_t issued = 0;
+        auto load_b = [&](uint32_t kb, uint32_t sb, uint64_t *bar) {
+            if (p.b_tiled) // BN / 128 consecutive tiles of the k-block: the same smem image as BN rows
+                tma_load_4d(sb, &tmB, 0, 0, (int32_t)(kb_lo + kb), (int32_t)(n0 / kTileRows), bar);
+            else
+                tma_load_4d(sb, &tmB, (int32_t)((kb_lo + kb) * kBK), (int32_t)n0, cb, bb, bar);
+        };
+        // The first stages' B tiles (weights, never written by the kernels this one may overlap) load
+        // before the wait for the previous kernel in the stream (a no-op unless launched as its
+        // programmatic dependent); A, its output, loads after it.
+        const uint32_t pre = kb_n < Cfg::kStages ? kb_n : Cfg::kStages;
+        for (uint32_t kb = 0; kb < pre; ++kb)
+        {
+            const uint32_t sa = base + kb * Cfg::kStageBytes;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(&full[kb])),
+                         "r"(Cfg::kStageBytes)
+                         : "memory");
+            load_b(kb, sa + Cfg::kABytes, &full[kb]);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (uint32_t kb = 0; kb < pre; ++kb)
+            tma_load_4d(base + kb * Cfg::kStageBytes, &tmA, (int32_t)((kb_lo + kb) * kBK), (int32_t)m0, ca, ba,
+                        &full[kb]);
+        uint32_t issued = pre;
         bool ok = true;
-        for (uint32_t kb = 0; kb < kb_n; ++kb)
+        for (uint32_t kb = pre; kb < kb_n; ++kb)
         {
             const uint32_t s = kb % Cfg::kStages, n = kb / Cfg::kStages;
             if (n > 0 && !wait_bounded(&empty[s], (n - 1) & 1u, kTcWaitNs))
@@ -229,10 +254,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
                          "r"(Cfg::kStageBytes)
                          : "memory");
             tma_load_4d(sa, &tmA, (int32_t)((kb_lo + kb) * kBK), (int32_t)m0, ca, ba, &full[s]); // BM rows
-            if (p.b_tiled) // BN / 128 consecutive tiles of the k-block: the same smem image as BN rows
-                tma_load_4d(sb, &tmB, 0, 0, (int32_t)(kb_lo + kb), (int32_t)(n0 / kTileRows), &full[s]);
-            else
-                tma_load_4d(sb, &tmB, (int32_t)((kb_lo + kb) * kBK), (int32_t)n0, cb, bb, &full[s]);
+            load_b(kb, sb, &full[s]);
             ++issued;
         }
         if (!ok)
@@ -578,7 +600,25 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
         }
     }
     dim3 grid((g.N + BN - 1) / BN, (g.M + BM - 1) / BM, g.batch * p.splits);
-    k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
+    if (g.pdl)
+    {
+        // programmatic dependent of the previous kernel in the stream: CTAs start (and prefetch B)
+        // while it finishes; griddepcontrol.wait in the producer orders everything else after it
+        cudaLaunchConfig_t lc{};
+        lc.gridDim = grid;
+        lc.blockDim = dim3(192);
+        lc.dynamicSmemBytes = Cfg::kSmem;
+        lc.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        if (cudaLaunchKernelEx(&lc, k_gemm_tc<BM, BN>, ma, mb, p) != cudaSuccess)
+            return false;
+    }
+    else
+        k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
     if (p.splits > 1 && !ws_ext)
     {
         const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 7) / 8);
@@ -696,8 +736,11 @@ struct TuneKey
 // Times each candidate (tile x splits) twice after one warm-up launch and returns the fastest; the
 // model's choice is kept unless another is more than 3 % faster. Every candidate computes the same
 // C (to fp32 summation order), so the trials are harmless; the caller then launches the winner.
-TcChoice tune(const GemmArgs &g, cudaStream_t s, int sms, TcChoice model)
+TcChoice tune(const GemmArgs &g_in, cudaStream_t s, int sms, TcChoice model)
 {
+    GemmArgs g = g_in;
+    g.pdl = 0; // trials run one after another, without overlapping the previous one
+
     cudaEvent_t e0, e1;
     if (cudaEventCreate(&e0) != cudaSuccess)
         return model;

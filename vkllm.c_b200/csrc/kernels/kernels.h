@@ -26,6 +26,11 @@ struct GemmArgs
     int act;
     uint32_t act_from = 0; // act applies to output columns >= act_from (0: all)
     uint32_t b_tiled = 0;  // B is a gemm_tile_b copy (batch 1 only; ldb and the B strides are unused)
+    // Launch as a programmatic dependent of the previous kernel in the stream: the CTAs start while
+    // it runs and load the first stages of B before waiting for its completion, so B must not be
+    // written by that kernel (weights). Everything else (A, C, the split-K workspace) is touched
+    // only after the wait.
+    uint32_t pdl = 0;
 };
 
 // Row sources of one tiled B operand: rows [0, rows[0]) come from ptr[0], the next rows[1] from
