@@ -12,6 +12,8 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
+#include <initializer_list>
 #include <vector>
 
 #include "../kernels/kernels.h"
@@ -55,7 +57,7 @@ struct vkllm_b200_batch
     __half *x = nullptr, *xn = nullptr, *qkv = nullptr, *attn = nullptr, *t0 = nullptr, *ug = nullptr,
            *m = nullptr, *logits = nullptr; // qkv [B][3 HD], ug [B][2 F] (up, then SiLU(gate)), m [B][F]
     __half *wcat = nullptr;                  // the GEMM operand copies of every layer (and wout_g when tiled)
-    float *part = nullptr;                   // [4][B][D] fp32 split-K partials of the Wo / down GEMMs
+    float *part = nullptr; // fp32 split-K partials of the GEMMs ([splits][B][N], summed by their consumers)
     uint32_t *tok = nullptr, *pos = nullptr, *ring = nullptr, *err = nullptr;
     uint32_t ring_steps = 0, last_steps = 0;
     std::vector<uint32_t> host_pos; // positions as the host knows them (load + steps)
@@ -70,6 +72,8 @@ namespace
 
 constexpr int kBT = 256;
 constexpr uint32_t kProjSplits = 4; // K splits of the Wo / down GEMMs (M = sequences)
+constexpr uint32_t kQkvSplits = 2;  // K splits of the QKV GEMM (128 x 256 tiles)
+constexpr uint32_t kUgSplits = 3;   // K splits of the up/gate GEMM (128 x 256 tiles)
 
 // Lets the next kernel in the stream, when it was launched as this one's programmatic dependent (the
 // batch's GEMMs), start its CTAs now; it still waits for this grid's completion before reading.
@@ -173,6 +177,38 @@ __global__ void k_b_rope_kv(__half *__restrict__ q, const __half *__restrict__ k
         *qp = __floats2half2_rn(c * qf.x - sn * qf.y, sn * qf.x + c * qf.y);
         reinterpret_cast<__half2 *>(kc + row)[w] = __floats2half2_rn(c * kf.x - sn * kf.y, sn * kf.x + c * kf.y);
         reinterpret_cast<__half2 *>(vc + row)[w] = reinterpret_cast<const __half2 *>(v + src)[w];
+    }
+}
+
+// k_b_rope_kv reading the QKV GEMM's fp32 split-K partials ([splits][B][3 HD]) instead of its
+// output: q, k, v = fp16(sum of the splits in split order), the rounding of the GEMM's own reduction,
+// then the same rotation. The rotated q goes to q (row stride 3 HD) for the attention kernel.
+__global__ void k_b_rope_kv_part(const float *__restrict__ part, uint32_t splits, __half *__restrict__ q, uint32_t HD,
+                                 const uint32_t *__restrict__ pos, uint32_t H, uint32_t hd, uint32_t cap, float base,
+                                 __half *__restrict__ kc, __half *__restrict__ vc, uint32_t B)
+{
+    const uint32_t h = blockIdx.x, b = blockIdx.y, p = pos[b];
+    if (p >= cap)
+        return; // flagged by k_b_check_pos; no write outside the sequence's rows
+    const uint64_t plane = (uint64_t)B * 3 * HD;
+    const uint64_t src = (uint64_t)b * 3 * HD + (uint64_t)h * hd, row = (((uint64_t)b * H + h) * cap + p) * hd;
+    for (uint32_t w = threadIdx.x; w < hd / 2; w += blockDim.x)
+    {
+        float2 qs = make_float2(0.f, 0.f), ks = qs, vs = qs;
+        for (uint32_t sp = 0; sp < splits; ++sp)
+        {
+            const float *pp = part + sp * plane + src + 2 * w;
+            const float2 a = __ldcs(reinterpret_cast<const float2 *>(pp));
+            const float2 c = __ldcs(reinterpret_cast<const float2 *>(pp + HD));
+            const float2 d = __ldcs(reinterpret_cast<const float2 *>(pp + 2 * HD));
+            qs.x += a.x, qs.y += a.y, ks.x += c.x, ks.y += c.y, vs.x += d.x, vs.y += d.y;
+        }
+        const float theta = (float)p / powf(base, (float)(2 * w) / (float)hd);
+        const float c = cosf(theta), sn = sinf(theta);
+        const float2 qf = make_float2(round_f16(qs.x), round_f16(qs.y)), kf = make_float2(round_f16(ks.x), round_f16(ks.y));
+        reinterpret_cast<__half2 *>(q + src)[w] = __floats2half2_rn(c * qf.x - sn * qf.y, sn * qf.x + c * qf.y);
+        reinterpret_cast<__half2 *>(kc + row)[w] = __floats2half2_rn(c * kf.x - sn * kf.y, sn * kf.x + c * kf.y);
+        reinterpret_cast<__half2 *>(vc + row)[w] = __floats2half2_rn(vs.x, vs.y);
     }
 }
 
@@ -322,6 +358,39 @@ __global__ void __launch_bounds__(kBT) k_b_attention(const __half *__restrict__ 
 
 // The gate BIN mul from the concatenated up/gate GEMM output: m[b][f] = fp16(ug[b][f] * ug[b][F + f])
 // (the gate half already SiLU'd by the GEMM epilogue), 8 halves per thread (F % 8 == 0).
+// k_b_gate reading the up/gate GEMM's fp32 split-K partials ([splits][B][2 F]): up = fp16(sum),
+// gate = fp16(SiLU(sum)) as the GEMM's reduction rounds them, m = fp16(up * gate).
+__global__ void k_b_gate_part(__half *__restrict__ m, const float *__restrict__ part, uint32_t splits, uint32_t F,
+                              uint32_t B)
+{
+    pdl_trigger();
+    const uint32_t f8 = F / 8;
+    const uint64_t plane = (uint64_t)B * 2 * F;
+    for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < (uint64_t)B * f8;
+         t += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t b = (uint32_t)(t / f8), c = (uint32_t)(t % f8);
+        float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (uint32_t sp = 0; sp < splits; ++sp)
+        {
+            const float4 *pu = reinterpret_cast<const float4 *>(part + sp * plane + (uint64_t)b * 2 * F + 8ull * c);
+            const float4 *pg = reinterpret_cast<const float4 *>(part + sp * plane + (uint64_t)b * 2 * F + F + 8ull * c);
+            const float4 a0 = __ldcs(pu), a1 = __ldcs(pu + 1), g0 = __ldcs(pg), g1 = __ldcs(pg + 1);
+            u[0] += a0.x, u[1] += a0.y, u[2] += a0.z, u[3] += a0.w, u[4] += a1.x, u[5] += a1.y, u[6] += a1.z, u[7] += a1.w;
+            g[0] += g0.x, g[1] += g0.y, g[2] += g0.z, g[3] += g0.w, g[4] += g1.x, g[5] += g1.y, g[6] += g1.z, g[7] += g1.w;
+        }
+        uint4 o;
+        __half *oh = reinterpret_cast<__half *>(&o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+        {
+            const float gs = g[e] / (1.0f + expf(-g[e])); // SiLU as the GEMM epilogue evaluates it
+            oh[e] = __float2half_rn(round_f16(u[e]) * round_f16(gs));
+        }
+        reinterpret_cast<uint4 *>(m + (uint64_t)b * F)[c] = o;
+    }
+}
+
 __global__ void k_b_gate(__half *__restrict__ m, const __half *__restrict__ ug, uint32_t F, uint32_t B)
 {
     pdl_trigger();
@@ -535,7 +604,7 @@ bool gemm(const __half *A, const __half *W, uint32_t tiled, __half *C, uint32_t 
 
 // C = A . W^T as fp32 split-K partials in `part` (no reduction); false when the GEMM cannot split.
 bool gemm_partials(const __half *A, const __half *W, uint32_t tiled, float *part, uint32_t M, uint32_t N, uint32_t K,
-                   uint32_t splits, uint32_t *used, cudaStream_t s)
+                   uint32_t splits, uint32_t *used, cudaStream_t s, uint32_t tile = 0)
 {
     GemmArgs g{};
     g.b_tiled = tiled;
@@ -553,7 +622,7 @@ bool gemm_partials(const __half *A, const __half *W, uint32_t tiled, float *part
     g.batch_c = 1;
     g.scale = 1.0f;
     g.act = 0;
-    return gemm_tcgen05_partials(g, s, splits, part, used);
+    return gemm_tcgen05_partials(g, s, splits, part, used, tile);
 }
 
 // The Wo / down projection with its residual add and the following RMSNORM (gains g) in one pass
@@ -594,16 +663,33 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
         __half *vc = bt->kv + ((uint64_t)l * 2 + 1) * B * H * bt->cap * hd;
         if (l == 0) // later layers get xn from the previous layer's down projection pass
             k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
-        if (!gemm(bt->xn, w.wqkv, bt->tiled, bt->qkv, B, 3 * HD, D, 0, s))
-            return VKLLM_ERR_VULKAN;
-        k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD,
-                                                                     bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
+        // QKV as split-K partials summed by the RoPE / KV-row kernel (else the GEMM's own reduction)
+        uint32_t used = 0;
+        if (gemm_partials(bt->xn, w.wqkv, bt->tiled, bt->part, B, 3 * HD, D, kQkvSplits, &used, s, 1))
+            k_b_rope_kv_part<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->part, used, bt->qkv, HD, bt->pos, H, hd,
+                                                                              bt->cap, dd.rope_base, kc, vc, B);
+        else
+        {
+            (void)cudaGetLastError();
+            if (!gemm(bt->xn, w.wqkv, bt->tiled, bt->qkv, B, 3 * HD, D, 0, s))
+                return VKLLM_ERR_VULKAN;
+            k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(
+                bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
+        }
         k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
                                                          bt->attn);
         _CHECK(proj_residual_norm(bt, bt->attn, w.wo_g, HD, w.ffn_norm, s));
-        if (!gemm(bt->xn, w.wug, bt->tiled, bt->ug, B, 2 * F, D, 1, s, F)) // SiLU on the gate half only
-            return VKLLM_ERR_VULKAN;
-        k_b_gate<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->ug, F, B);
+        // up/gate as split-K partials summed by the gate kernel (else the GEMM's own reduction, with
+        // SiLU on the gate half only)
+        if (gemm_partials(bt->xn, w.wug, bt->tiled, bt->part, B, 2 * F, D, kUgSplits, &used, s, 1))
+            k_b_gate_part<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->part, used, F, B);
+        else
+        {
+            (void)cudaGetLastError();
+            if (!gemm(bt->xn, w.wug, bt->tiled, bt->ug, B, 2 * F, D, 1, s, F))
+                return VKLLM_ERR_VULKAN;
+            k_b_gate<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->ug, F, B);
+        }
         // the down projection's pass also norms for the next layer (or the output norm after the last)
         _CHECK(
             proj_residual_norm(bt, bt->m, w.wd_g, F, l + 1 < bt->L ? bt->layers[l + 1].attn_norm : bt->out_norm, s));
@@ -672,9 +758,11 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->ring_steps = 1024;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t kv_bytes = al((size_t)bt->L * 2 * B * dd.H * bt->cap * dd.hd * 2);
+    const size_t part_elems = (size_t)B * std::max({(size_t)kProjSplits * D, (size_t)kQkvSplits * 3 * HD,
+                                                    (size_t)kUgSplits * 2 * F});
     const size_t act = al((size_t)B * D * 2) * 3 + al((size_t)B * 3 * HD * 2) + al((size_t)B * HD * 2) +
                        al((size_t)B * 2 * F * 2) + al((size_t)B * F * 2) + al((size_t)B * dd.V * 2) +
-                       al((size_t)4 * B * D * 4);
+                       al(part_elems * 4);
     const size_t small = al((size_t)B * 4) * 2 + al((size_t)bt->ring_steps * B * 4) + al(16);
     if (cudaMalloc(&bt->ws, kv_bytes + act + small) != cudaSuccess)
     {
@@ -697,7 +785,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->ug = (__half *)take((size_t)B * 2 * F * 2);
     bt->m = (__half *)take((size_t)B * F * 2);
     bt->logits = (__half *)take((size_t)B * dd.V * 2);
-    bt->part = (float *)take((size_t)4 * B * D * 4);
+    bt->part = (float *)take(part_elems * 4);
     bt->tok = (uint32_t *)take((size_t)B * 4);
     bt->pos = (uint32_t *)take((size_t)B * 4);
     bt->ring = (uint32_t *)take((size_t)bt->ring_steps * B * 4);

@@ -864,11 +864,13 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
     return launch_choice(g, s, best);
 }
 
-bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, float *ws, uint32_t *splits_used)
+bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, float *ws, uint32_t *splits_used,
+                           uint32_t tile)
 {
     if (g.batch == 0 || g.batch_c == 0 || !ws || !splits_used || splits < 2)
         return false;
-    return launch_tc<128, 128>(g, s, splits, ws, splits_used);
+    return tile == 1 ? launch_tc<128, 256>(g, s, splits, ws, splits_used)
+                     : launch_tc<128, 128>(g, s, splits, ws, splits_used);
 }
 
 namespace

@@ -60,11 +60,12 @@ bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool tran
 // Enqueues the tcgen05 GEMM; returns false when it cannot run on this device / shape.
 bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s);
 
-// The tcgen05 GEMM (128 x 128 tiles) with K split `splits` ways, writing its fp32 partial sums
-// [splits][batch][M][N] to `ws` instead of C (no reduction is launched; the caller sums the partials
-// in split order, then applies scale / act / fp16 as the plain GEMM would). *splits_used receives
-// the split count (<= splits: every split gets at least one 64-deep k-block).
-bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, float *ws, uint32_t *splits_used);
+// The tcgen05 GEMM (tile 0: 128 x 128, 1: 128 x 256) with K split `splits` ways, writing its fp32
+// partial sums [splits][batch][M][N] to `ws` instead of C (no reduction is launched; the caller sums
+// the partials in split order, then applies scale / act / fp16 as the plain GEMM would).
+// *splits_used receives the split count (<= splits: every split gets at least one 64-deep k-block).
+bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, float *ws, uint32_t *splits_used,
+                           uint32_t tile = 0);
 
 // Sticky error word of the tcgen05 GEMM on device `dev` (bit 0: a bounded wait expired).
 uint32_t gemm_tcgen05_error(int dev);
