@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "../kernels/kernels.h"
+#include "gemv_stream.cuh"
 #include "../runtime/internal.h"
 #include "vkllm_b200.h"
 #include "vkllm_kvcache.h"
@@ -51,6 +52,7 @@ struct vkllm_b200_batch
     std::vector<vkb::BatchLayer> layers;
     const __half *embed = nullptr, *wout = nullptr, *wout_g = nullptr; // wout_g: the logits GEMM operand
     uint32_t tiled = 1;                                                  // GEMM operands in tile order
+    uint32_t att_staged = 256; // threads of k_b_attention_staged (0: k_b_attention)
     const float *out_norm = nullptr;
     void *ws = nullptr;
     __half *kv = nullptr; // [L][2][B][H][cap][hd]
@@ -209,6 +211,203 @@ __global__ void k_b_rope_kv_part(const float *__restrict__ part, uint32_t splits
         reinterpret_cast<__half2 *>(q + src)[w] = __floats2half2_rn(c * qf.x - sn * qf.y, sn * qf.x + c * qf.y);
         reinterpret_cast<__half2 *>(kc + row)[w] = __floats2half2_rn(c * kf.x - sn * kf.y, sn * kf.x + c * kf.y);
         reinterpret_cast<__half2 *>(vc + row)[w] = __floats2half2_rn(vs.x, vs.y);
+    }
+}
+
+constexpr uint32_t kAttChunk = 64;   // key rows per staged chunk (staged attention)
+constexpr uint32_t kAttStages = 3;   // chunk buffers in flight per CTA
+constexpr uint32_t kAttThreads = 512; // most threads of the staged attention kernel
+constexpr uint32_t kErrAttTimeout = 2u; // batch error bit: a staged-attention copy wait expired
+
+// Dynamic shared memory of k_b_attention_staged for head size hd and cap KV rows.
+__host__ __device__ constexpr size_t att_staged_smem(uint32_t hd, uint32_t cap, uint32_t threads)
+{
+    return (size_t)kAttStages * kAttChunk * hd * 2 + 8 * kAttStages +
+           4 * ((size_t)((hd + 3) & ~3u) + ((cap + 3) & ~3u) + (size_t)(threads / 32) * hd);
+}
+
+// Attention of one (head, sequence) as k_b_attention computes it, with the sequence's key rows and
+// then its value rows streamed through shared memory: 64-row chunks (Lk x hd fp16 rows are
+// contiguous in the batch's cache) are fetched by cp.async.bulk into a ring of kAttStages buffers,
+// so the copies of later chunks (the first value chunks included) are in flight while the scores,
+// the softmax statistics and the probabilities of earlier ones are computed. Scores: `lpk` lanes
+// per key row (8 fp16 each) and a shuffle sum; probabilities: the same rounding points as
+// k_b_attention. Each mbarrier wait is bounded; on expiry the CTA sets kErrAttTimeout in *err,
+// waits (bounded) for its copies in flight and returns.
+__global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half *__restrict__ q, uint32_t q_stride,
+                                                                  const __half *__restrict__ kc,
+                                                                  const __half *__restrict__ vc,
+                                                                  const uint32_t *__restrict__ pos, uint32_t H,
+                                                                  uint32_t hd, uint32_t cap, float scale,
+                                                                  __half *__restrict__ out, uint32_t *err)
+{
+    pdl_trigger();
+    extern __shared__ __align__(128) unsigned char att_sm[];
+    const uint32_t chunk_elems = kAttChunk * hd;
+    __half *ring = reinterpret_cast<__half *>(att_sm);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(att_sm + (size_t)kAttStages * chunk_elems * 2);
+    float *qs = reinterpret_cast<float *>(bars + kAttStages);
+    float *sc = qs + ((hd + 3) & ~3u);
+    float *acc = sc + ((cap + 3) & ~3u); // [warps][hd]
+    __shared__ float red[32];
+    const uint32_t h = blockIdx.x, b = blockIdx.y, HD = H * hd, tid = threadIdx.x;
+    if (pos[b] >= cap)
+        return; // flagged by k_b_check_pos
+    const uint32_t Lk = pos[b] + 1, nk = (Lk + kAttChunk - 1) / kAttChunk, total = 2 * nk;
+    const uint32_t warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const __half *kb = kc + ((uint64_t)b * H + h) * cap * hd;
+    const __half *vb = vc + ((uint64_t)b * H + h) * cap * hd;
+    // chunk c < nk: key rows [64 c, ...); c >= nk: value rows [64 (c - nk), ...); buffer c % stages
+    auto issue = [&](uint32_t c) {
+        const uint32_t r0 = (c < nk ? c : c - nk) * kAttChunk, rows = min(kAttChunk, Lk - r0);
+        const uint32_t st = c % kAttStages;
+        mbar_arrive_expect_tx(&bars[st], rows * hd * 2);
+        bulk_g2s(ring + (size_t)st * chunk_elems, (c < nk ? kb : vb) + (uint64_t)r0 * hd, rows * hd * 2, &bars[st]);
+    };
+    if (tid == 0)
+    {
+        for (uint32_t st = 0; st < kAttStages; ++st)
+            mbar_init(&bars[st], 1);
+        fence_barrier_init();
+    }
+    for (uint32_t d = tid; d < hd; d += blockDim.x)
+        qs[d] = __half2float(q[(uint64_t)b * q_stride + h * hd + d]);
+    __syncthreads();
+    if (tid == 0)
+        for (uint32_t c = 0; c < kAttStages && c < total; ++c)
+            issue(c);
+    const uint32_t pieces = hd / 8;
+    uint32_t lpk = 1;
+    while (lpk < pieces)
+        lpk <<= 1;
+    const uint32_t G = blockDim.x / lpk, gi = tid / lpk, pc = tid % lpk;
+    const bool lane_on = pc < pieces;
+    float qr[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        qr[e] = lane_on ? qs[8 * pc + e] : 0.f;
+    float mx = -FLT_MAX;
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const bool quirk = Lk == hd; // V read as [hd, Lk] (src/core/vkllm_op_matmul.c:14-30)
+    __half *o = out + (uint64_t)b * HD + h * hd;
+    for (uint32_t c = 0; c < total; ++c)
+    {
+        const uint32_t st = c % kAttStages;
+        const bool timed_out = !mbar_wait_bounded(&bars[st], (c / kAttStages) & 1u, kWaitLimitNs);
+        if (__syncthreads_or(timed_out))
+        {
+            if (tid == 0)
+            {
+                atomicOr(err, kErrAttTimeout);
+                // the copies issued and not yet consumed must land before the CTA exits
+                for (uint32_t k = c; k < total && k < c + kAttStages; ++k)
+                    (void)mbar_wait_bounded(&bars[k % kAttStages], (k / kAttStages) & 1u, kWaitLimitNs / 4);
+            }
+            return;
+        }
+        const __half *buf = ring + (size_t)st * chunk_elems;
+        const uint32_t r0 = (c < nk ? c : c - nk) * kAttChunk, rows = min(kAttChunk, Lk - r0);
+        if (c < nk)
+        {
+            // scores of this chunk's keys: group gi takes rows gi, gi + G, ...
+            for (uint32_t rb = 0; rb < rows; rb += G)
+            {
+                const uint32_t r = rb + gi;
+                const bool valid = lane_on && r < rows;
+                float d = 0.f;
+                if (valid)
+                {
+                    const uint4 raw = *reinterpret_cast<const uint4 *>(buf + (size_t)r * hd + 8 * pc);
+                    const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                    {
+                        const float2 f = __half22float2(hh[e]);
+                        d = fmaf(qr[2 * e], f.x, d);
+                        d = fmaf(qr[2 * e + 1], f.y, d);
+                    }
+                }
+                for (uint32_t sh = lpk / 2; sh > 0; sh >>= 1)
+                    d += __shfl_xor_sync(0xffffffffu, d, sh);
+                if (r < rows)
+                {
+                    const float sv = round_f16(d * scale);
+                    if (pc == 0)
+                        sc[r0 + r] = sv;
+                    mx = fmaxf(mx, sv);
+                }
+            }
+            if (c + 1 == nk)
+            {
+                // softmax over the whole row: max, sum of exp, p_j = fp16(exp(s_j - max) / sum)
+                mx = warp_max(mx);
+                if (lane == 0)
+                    red[warp] = mx;
+                __syncthreads();
+                float m = -FLT_MAX;
+                for (uint32_t w = 0; w < nw; ++w)
+                    m = fmaxf(m, red[w]);
+                __syncthreads();
+                float l = 0.f;
+                for (uint32_t j = tid; j < Lk; j += blockDim.x)
+                    l += expf(sc[j] - m);
+                l = bsum(l, red);
+                for (uint32_t j = tid; j < Lk; j += blockDim.x)
+                    sc[j] = round_f16(expf(sc[j] - m) / l);
+            }
+        }
+        else if (quirk)
+        {
+            // o[w] = sum_k p_k V[w][k] for the value rows w of this chunk
+            for (uint32_t r = tid; r < rows; r += blockDim.x)
+            {
+                float v = 0.f;
+                for (uint32_t k = 0; k < Lk; ++k)
+                    v = fmaf(sc[k], __half2float(buf[(size_t)r * hd + k]), v);
+                o[r0 + r] = __float2half_rn(v);
+            }
+        }
+        else if (lane_on)
+        {
+            for (uint32_t r = gi; r < rows; r += G)
+            {
+                const float pj = sc[r0 + r];
+                const uint4 raw = *reinterpret_cast<const uint4 *>(buf + (size_t)r * hd + 8 * pc);
+                const __half2 *hh = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                {
+                    const float2 f = __half22float2(hh[e]);
+                    a[2 * e] = fmaf(pj, f.x, a[2 * e]);
+                    a[2 * e + 1] = fmaf(pj, f.y, a[2 * e + 1]);
+                }
+            }
+        }
+        __syncthreads(); // buffer st is free (and, after the last key chunk, the probabilities are set)
+        if (tid == 0 && c + kAttStages < total)
+        {
+            fence_proxy_async();
+            issue(c + kAttStages);
+        }
+    }
+    if (quirk)
+        return;
+    // the key groups of a warp are summed with shuffles, then the warps' sums in warp order
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        for (uint32_t sh = lpk; sh < 32; sh <<= 1)
+            a[e] += __shfl_xor_sync(0xffffffffu, a[e], sh);
+    if (lane < lpk && lane_on)
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            acc[warp * hd + 8 * pc + e] = a[e];
+    __syncthreads();
+    for (uint32_t d = tid; d < hd; d += blockDim.x)
+    {
+        float v = 0.f;
+        for (uint32_t w = 0; w < nw; ++w)
+            v += acc[w * hd + d];
+        o[d] = __float2half_rn(v);
     }
 }
 
@@ -676,8 +875,12 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
             k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(
                 bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
         }
-        k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
-                                                         bt->attn);
+        if (bt->att_staged)
+            k_b_attention_staged<<<dim3(H, B), bt->att_staged, att_staged_smem(hd, bt->cap, bt->att_staged), s>>>(
+                bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale, bt->attn, bt->err);
+        else
+            k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
+                                                             bt->attn);
         _CHECK(proj_residual_norm(bt, bt->attn, w.wo_g, HD, w.ffn_norm, s));
         // up/gate as split-K partials summed by the gate kernel (else the GEMM's own reduction, with
         // SiLU on the gate half only)
@@ -792,6 +995,11 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->err = (uint32_t *)take(16); // [0] error bits, [1] step counter
     cudaStream_t s = ctx->runtime->stream;
     // GEMM operand copies, per layer [Wq; Wk; Wv] then [Wup; Wgate] (then Wo and Wdown when tiled)
+    const char *att_env = getenv("VKLLM_B200_BATCH_ATT_STAGED");
+    bt->att_staged = att_env ? (uint32_t)atoi(att_env) : 256u;
+    if (!(bt->att_staged == 128 || bt->att_staged == 256 || bt->att_staged == 512) || dd.hd % 8 || dd.hd > 128 ||
+        att_staged_smem(dd.hd, bt->cap, bt->att_staged) > 200 * 1024)
+        bt->att_staged = 0;
     const char *tiled_env = getenv("VKLLM_B200_BATCH_TILED");
     bt->tiled = tiled_env && atoi(tiled_env) == 0 ? 0u : 1u;
     const size_t t_qkv = gemm_tiled_b_elems(3 * HD, D), t_ug = gemm_tiled_b_elems(2 * F, D),
@@ -844,6 +1052,8 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         bt->wout_g = bt->wout;
     if (!copied || cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
+        (bt->att_staged && cudaFuncSetAttribute(k_b_attention_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                (int)att_staged_smem(dd.hd, bt->cap, bt->att_staged)) != cudaSuccess) ||
         cudaStreamSynchronize(s) != cudaSuccess)
     {
         (void)cudaGetLastError();
@@ -931,7 +1141,9 @@ extern "C" vkllm_err_t vkllm_b200_batch_decode_steps(struct vkllm_context *ctx, 
     VKB_CUDA(cudaStreamSynchronize(s));
     if (e[0] != 0 || gemm_tcgen05_error(ctx->device->ordinal) != 0)
     {
-        log_error("batched decode: %s", e[0] ? "a sequence reached its KV capacity" : "tensor-core GEMM wait expired");
+        log_error("batched decode: %s", (e[0] & 1u)                ? "a sequence reached its KV capacity"
+                                        : (e[0] & kErrAttTimeout) ? "an attention copy wait expired"
+                                                                  : "tensor-core GEMM wait expired");
         return VKLLM_ERR_ARGS;
     }
     return VKLLM_ERR_OK;
