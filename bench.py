@@ -262,7 +262,9 @@ def batched_decode_leg(vk, model, args, world, rank, stream):
     return {"sequences": n_local * world, "per_rank": n_local, "steps": K, "prompt": P, "kv_rows": cap,
             "tok_s": round(n_local * world * K / (ms / 1000.0), 1), "ms_per_step": round(ms / K, 4),
             "hbm_frac_per_rank": round(step_bytes / (ms / K * 1e-3) / 1e9 / peak, 4),
-            "path": "tcgen05 GEMMs (M = sequences per rank; [Wq;Wk;Wv] and [Wup;Wgate] concatenated; tile and split-K tuned per shape) + per-sequence RoPE/KV/attention kernels, CUDA graph per step"}
+            "path": "tcgen05 GEMMs (M = sequences per rank) on tile-order weight copies ([Wq;Wk;Wv], [Wup;Wgate], Wo, "
+                    "Wdown, output), launched as programmatic dependents; split-K partials summed by the consumer "
+                    "kernels (RoPE/KV rows, gate, residual + RMSNORM); bulk-copy staged attention; CUDA graph per step"}
 
 
 def ops_microbench(vk, local, seed):
