@@ -10,13 +10,24 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-PROMPTS = [(11, 8), (12, 12), (13, 5), (14, 1)]
+# (seed, prompt length); the last sequence passes Lk == hd (48 on the tiny model), where the
+# reference reads V transposed
+PROMPTS = [(11, 8), (12, 12), (13, 5), (14, 1), (15, 40)]
 N_STEPS = 20
 
+# the batch's kernel choices (read when the batch is created): the default (bulk-copy staged
+# attention, tile-order GEMM operands), the register-loading attention kernel, the staged kernel
+# with 128 threads, and row-major GEMM operands
+VARIANTS = {"default": {}, "att_registers": {"VKLLM_B200_BATCH_ATT_STAGED": "0"},
+            "att_staged_128": {"VKLLM_B200_BATCH_ATT_STAGED": "128"}, "rowmajor_b": {"VKLLM_B200_BATCH_TILED": "0"}}
 
-def test_batched_decode_matches_each_sequence_alone(vk, ctx, tiny_gguf, orc):
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
+def test_batched_decode_matches_each_sequence_alone(vk, ctx, tiny_gguf, orc, variant, monkeypatch):
     import gen_gguf
 
+    for k, v in VARIANTS[variant].items():
+        monkeypatch.setenv(k, v)
     path, weights = tiny_gguf
     cfg = dict(gen_gguf.TINY)
     prompts = [gen_gguf.prompt(seed, n) for seed, n in PROMPTS]

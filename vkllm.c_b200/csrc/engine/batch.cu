@@ -73,7 +73,7 @@ namespace
 {
 
 constexpr int kBT = 256;
-constexpr uint32_t kProjSplits = 4; // K splits of the Wo / down GEMMs (M = sequences)
+constexpr uint32_t kProjSplits = 4; // K splits of the Wo / down GEMMs (M = sequences); <= kMaxPartSplits
 constexpr uint32_t kQkvSplits = 2;  // K splits of the QKV GEMM (128 x 256 tiles)
 constexpr uint32_t kUgSplits = 3;   // K splits of the up/gate GEMM (128 x 256 tiles)
 
@@ -82,6 +82,35 @@ constexpr uint32_t kUgSplits = 3;   // K splits of the up/gate GEMM (128 x 256 t
 __device__ __forceinline__ void pdl_trigger()
 {
     asm volatile("griddepcontrol.launch_dependents;");
+}
+
+constexpr uint32_t kMaxPartSplits = 4; // most split-K partials a consumer kernel sums
+static_assert(kProjSplits <= kMaxPartSplits && kQkvSplits <= kMaxPartSplits && kUgSplits <= kMaxPartSplits,
+              "the partial-summing kernels read at most kMaxPartSplits splits");
+
+// t[e] = sum over the splits (in split order, from 0) of the 8 fp32 partials at src + s * plane.
+// Every split's loads are issued before the first add, so the reads overlap (the partials were just
+// written and sit in L2).
+__device__ __forceinline__ void sum_splits8(const float *src, uint64_t plane, uint32_t splits, float (&t)[8])
+{
+    float4 a[kMaxPartSplits], c[kMaxPartSplits];
+#pragma unroll
+    for (uint32_t sp = 0; sp < kMaxPartSplits; ++sp)
+        if (sp < splits)
+        {
+            a[sp] = __ldcs(reinterpret_cast<const float4 *>(src + sp * plane));
+            c[sp] = __ldcs(reinterpret_cast<const float4 *>(src + sp * plane) + 1);
+        }
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        t[e] = 0.f;
+#pragma unroll
+    for (uint32_t sp = 0; sp < kMaxPartSplits; ++sp)
+        if (sp < splits)
+        {
+            t[0] += a[sp].x, t[1] += a[sp].y, t[2] += a[sp].z, t[3] += a[sp].w;
+            t[4] += c[sp].x, t[5] += c[sp].y, t[6] += c[sp].z, t[7] += c[sp].w;
+        }
 }
 
 __device__ __forceinline__ float bsum(float v, float *red)
@@ -196,15 +225,22 @@ __global__ void k_b_rope_kv_part(const float *__restrict__ part, uint32_t splits
     const uint64_t src = (uint64_t)b * 3 * HD + (uint64_t)h * hd, row = (((uint64_t)b * H + h) * cap + p) * hd;
     for (uint32_t w = threadIdx.x; w < hd / 2; w += blockDim.x)
     {
+        // every split's loads first, then the sums in split order
+        float2 pa[kMaxPartSplits], pk[kMaxPartSplits], pv[kMaxPartSplits];
+#pragma unroll
+        for (uint32_t sp = 0; sp < kMaxPartSplits; ++sp)
+            if (sp < splits)
+            {
+                const float *pp = part + sp * plane + src + 2 * w;
+                pa[sp] = __ldcs(reinterpret_cast<const float2 *>(pp));
+                pk[sp] = __ldcs(reinterpret_cast<const float2 *>(pp + HD));
+                pv[sp] = __ldcs(reinterpret_cast<const float2 *>(pp + 2 * HD));
+            }
         float2 qs = make_float2(0.f, 0.f), ks = qs, vs = qs;
-        for (uint32_t sp = 0; sp < splits; ++sp)
-        {
-            const float *pp = part + sp * plane + src + 2 * w;
-            const float2 a = __ldcs(reinterpret_cast<const float2 *>(pp));
-            const float2 c = __ldcs(reinterpret_cast<const float2 *>(pp + HD));
-            const float2 d = __ldcs(reinterpret_cast<const float2 *>(pp + 2 * HD));
-            qs.x += a.x, qs.y += a.y, ks.x += c.x, ks.y += c.y, vs.x += d.x, vs.y += d.y;
-        }
+#pragma unroll
+        for (uint32_t sp = 0; sp < kMaxPartSplits; ++sp)
+            if (sp < splits)
+                qs.x += pa[sp].x, qs.y += pa[sp].y, ks.x += pk[sp].x, ks.y += pk[sp].y, vs.x += pv[sp].x, vs.y += pv[sp].y;
         const float theta = (float)p / powf(base, (float)(2 * w) / (float)hd);
         const float c = cosf(theta), sn = sinf(theta);
         const float2 qf = make_float2(round_f16(qs.x), round_f16(qs.y)), kf = make_float2(round_f16(ks.x), round_f16(ks.y));
@@ -569,15 +605,9 @@ __global__ void k_b_gate_part(__half *__restrict__ m, const float *__restrict__ 
          t += (uint64_t)gridDim.x * blockDim.x)
     {
         const uint32_t b = (uint32_t)(t / f8), c = (uint32_t)(t % f8);
-        float u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (uint32_t sp = 0; sp < splits; ++sp)
-        {
-            const float4 *pu = reinterpret_cast<const float4 *>(part + sp * plane + (uint64_t)b * 2 * F + 8ull * c);
-            const float4 *pg = reinterpret_cast<const float4 *>(part + sp * plane + (uint64_t)b * 2 * F + F + 8ull * c);
-            const float4 a0 = __ldcs(pu), a1 = __ldcs(pu + 1), g0 = __ldcs(pg), g1 = __ldcs(pg + 1);
-            u[0] += a0.x, u[1] += a0.y, u[2] += a0.z, u[3] += a0.w, u[4] += a1.x, u[5] += a1.y, u[6] += a1.z, u[7] += a1.w;
-            g[0] += g0.x, g[1] += g0.y, g[2] += g0.z, g[3] += g0.w, g[4] += g1.x, g[5] += g1.y, g[6] += g1.z, g[7] += g1.w;
-        }
+        float u[8], g[8];
+        sum_splits8(part + (uint64_t)b * 2 * F + 8ull * c, plane, splits, u);
+        sum_splits8(part + (uint64_t)b * 2 * F + F + 8ull * c, plane, splits, g);
         uint4 o;
         __half *oh = reinterpret_cast<__half *>(&o);
 #pragma unroll
@@ -630,13 +660,8 @@ __global__ void k_b_proj_residual_norm(const float *__restrict__ part, uint32_t 
     float s = 0.f;
     for (uint32_t i = threadIdx.x; i < n8; i += blockDim.x)
     {
-        float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (uint32_t sp = 0; sp < splits; ++sp)
-        {
-            const float4 *src = reinterpret_cast<const float4 *>(part + sp * plane + (uint64_t)b * D + 8ull * i);
-            const float4 a = __ldcg(src), c = __ldcg(src + 1);
-            t[0] += a.x, t[1] += a.y, t[2] += a.z, t[3] += a.w, t[4] += c.x, t[5] += c.y, t[6] += c.z, t[7] += c.w;
-        }
+        float t[8];
+        sum_splits8(part + (uint64_t)b * D + 8ull * i, plane, splits, t);
         const uint4 xv = xr[i];
         const __half *xh = reinterpret_cast<const __half *>(&xv);
         uint4 o;
@@ -834,7 +859,9 @@ vkllm_err_t proj_residual_norm(vkllm_b200_batch *bt, const __half *in, const __h
     uint32_t used = 0;
     if (gemm_partials(in, w, bt->tiled, bt->part, B, D, K, kProjSplits, &used, s))
     {
-        k_b_proj_residual_norm<<<B, kBT, 0, s>>>(bt->part, used, bt->x, g, D, dd.eps, bt->xn, B);
+        // a thread per 8 columns (up to 1024), so each thread's partial loads are issued at once
+        const uint32_t threads = std::min(1024u, std::max(64u, (D / 8 + 31) & ~31u));
+        k_b_proj_residual_norm<<<B, threads, 0, s>>>(bt->part, used, bt->x, g, D, dd.eps, bt->xn, B);
         return VKLLM_ERR_OK;
     }
     (void)cudaGetLastError();
