@@ -53,6 +53,7 @@ struct vkllm_b200_batch
     const __half *embed = nullptr, *wout = nullptr, *wout_g = nullptr; // wout_g: the logits GEMM operand
     uint32_t tiled = 1;                                                  // GEMM operands in tile order
     uint32_t att_staged = 256; // threads of k_b_attention_staged (0: k_b_attention)
+    uint32_t att_chunk = 64, att_ring = 3; // its rows per chunk and chunk buffers
     const float *out_norm = nullptr;
     void *ws = nullptr;
     __half *kv = nullptr; // [L][2][B][H][cap][hd]
@@ -250,15 +251,17 @@ __global__ void k_b_rope_kv_part(const float *__restrict__ part, uint32_t splits
     }
 }
 
-constexpr uint32_t kAttChunk = 64;   // key rows per staged chunk (staged attention)
-constexpr uint32_t kAttStages = 3;   // chunk buffers in flight per CTA
+constexpr uint32_t kAttChunk = 64;    // key rows per staged chunk (staged attention), default
+constexpr uint32_t kAttStages = 3;    // chunk buffers in flight per CTA, default
+constexpr uint32_t kAttMaxStages = 8; // most chunk buffers
 constexpr uint32_t kAttThreads = 512; // most threads of the staged attention kernel
 constexpr uint32_t kErrAttTimeout = 2u; // batch error bit: a staged-attention copy wait expired
 
 // Dynamic shared memory of k_b_attention_staged for head size hd and cap KV rows.
-__host__ __device__ constexpr size_t att_staged_smem(uint32_t hd, uint32_t cap, uint32_t threads)
+__host__ __device__ constexpr size_t att_staged_smem(uint32_t hd, uint32_t cap, uint32_t threads, uint32_t chunk,
+                                                     uint32_t stages)
 {
-    return (size_t)kAttStages * kAttChunk * hd * 2 + 8 * kAttStages +
+    return (size_t)stages * chunk * hd * 2 + 8 * stages +
            4 * ((size_t)((hd + 3) & ~3u) + ((cap + 3) & ~3u) + (size_t)(threads / 32) * hd);
 }
 
@@ -275,34 +278,35 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
                                                                   const __half *__restrict__ vc,
                                                                   const uint32_t *__restrict__ pos, uint32_t H,
                                                                   uint32_t hd, uint32_t cap, float scale,
-                                                                  __half *__restrict__ out, uint32_t *err)
+                                                                  __half *__restrict__ out, uint32_t *err,
+                                                                  uint32_t chunk, uint32_t stages)
 {
     pdl_trigger();
     extern __shared__ __align__(128) unsigned char att_sm[];
-    const uint32_t chunk_elems = kAttChunk * hd;
+    const uint32_t chunk_elems = chunk * hd; // chunk: rows per chunk (multiple of 8), stages <= kAttMaxStages
     __half *ring = reinterpret_cast<__half *>(att_sm);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(att_sm + (size_t)kAttStages * chunk_elems * 2);
-    float *qs = reinterpret_cast<float *>(bars + kAttStages);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(att_sm + (size_t)stages * chunk_elems * 2);
+    float *qs = reinterpret_cast<float *>(bars + stages);
     float *sc = qs + ((hd + 3) & ~3u);
     float *acc = sc + ((cap + 3) & ~3u); // [warps][hd]
     __shared__ float red[32];
     const uint32_t h = blockIdx.x, b = blockIdx.y, HD = H * hd, tid = threadIdx.x;
     if (pos[b] >= cap)
         return; // flagged by k_b_check_pos
-    const uint32_t Lk = pos[b] + 1, nk = (Lk + kAttChunk - 1) / kAttChunk, total = 2 * nk;
+    const uint32_t Lk = pos[b] + 1, nk = (Lk + chunk - 1) / chunk, total = 2 * nk;
     const uint32_t warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const __half *kb = kc + ((uint64_t)b * H + h) * cap * hd;
     const __half *vb = vc + ((uint64_t)b * H + h) * cap * hd;
     // chunk c < nk: key rows [64 c, ...); c >= nk: value rows [64 (c - nk), ...); buffer c % stages
     auto issue = [&](uint32_t c) {
-        const uint32_t r0 = (c < nk ? c : c - nk) * kAttChunk, rows = min(kAttChunk, Lk - r0);
-        const uint32_t st = c % kAttStages;
+        const uint32_t r0 = (c < nk ? c : c - nk) * chunk, rows = min(chunk, Lk - r0);
+        const uint32_t st = c % stages;
         mbar_arrive_expect_tx(&bars[st], rows * hd * 2);
         bulk_g2s(ring + (size_t)st * chunk_elems, (c < nk ? kb : vb) + (uint64_t)r0 * hd, rows * hd * 2, &bars[st]);
     };
     if (tid == 0)
     {
-        for (uint32_t st = 0; st < kAttStages; ++st)
+        for (uint32_t st = 0; st < stages; ++st)
             mbar_init(&bars[st], 1);
         fence_barrier_init();
     }
@@ -310,7 +314,7 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
         qs[d] = __half2float(q[(uint64_t)b * q_stride + h * hd + d]);
     __syncthreads();
     if (tid == 0)
-        for (uint32_t c = 0; c < kAttStages && c < total; ++c)
+        for (uint32_t c = 0; c < stages && c < total; ++c)
             issue(c);
     const uint32_t pieces = hd / 8;
     uint32_t lpk = 1;
@@ -328,21 +332,21 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
     __half *o = out + (uint64_t)b * HD + h * hd;
     for (uint32_t c = 0; c < total; ++c)
     {
-        const uint32_t st = c % kAttStages;
-        const bool timed_out = !mbar_wait_bounded(&bars[st], (c / kAttStages) & 1u, kWaitLimitNs);
+        const uint32_t st = c % stages;
+        const bool timed_out = !mbar_wait_bounded(&bars[st], (c / stages) & 1u, kWaitLimitNs);
         if (__syncthreads_or(timed_out))
         {
             if (tid == 0)
             {
                 atomicOr(err, kErrAttTimeout);
                 // the copies issued and not yet consumed must land before the CTA exits
-                for (uint32_t k = c; k < total && k < c + kAttStages; ++k)
-                    (void)mbar_wait_bounded(&bars[k % kAttStages], (k / kAttStages) & 1u, kWaitLimitNs / 4);
+                for (uint32_t k = c; k < total && k < c + stages; ++k)
+                    (void)mbar_wait_bounded(&bars[k % stages], (k / stages) & 1u, kWaitLimitNs / 4);
             }
             return;
         }
         const __half *buf = ring + (size_t)st * chunk_elems;
-        const uint32_t r0 = (c < nk ? c : c - nk) * kAttChunk, rows = min(kAttChunk, Lk - r0);
+        const uint32_t r0 = (c < nk ? c : c - nk) * chunk, rows = min(chunk, Lk - r0);
         if (c < nk)
         {
             // scores of this chunk's keys: group gi takes rows gi, gi + G, ...
@@ -420,10 +424,10 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
             }
         }
         __syncthreads(); // buffer st is free (and, after the last key chunk, the probabilities are set)
-        if (tid == 0 && c + kAttStages < total)
+        if (tid == 0 && c + stages < total)
         {
             fence_proxy_async();
-            issue(c + kAttStages);
+            issue(c + stages);
         }
     }
     if (quirk)
@@ -734,6 +738,7 @@ __global__ void k_b_argmax(const __half *__restrict__ logits, uint32_t V, uint32
     const __half *row = logits + (uint64_t)b * V;
     float v = -FLT_MAX;
     uint32_t idx = 0xffffffffu;
+#pragma unroll 8 // eight loads in flight per thread; the comparisons still run in index order
     for (uint32_t i = lane + 32 * warp; i < V; i += 32 * nw)
     {
         const float c = __half2float(row[i]);
@@ -903,8 +908,10 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
                 bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
         }
         if (bt->att_staged)
-            k_b_attention_staged<<<dim3(H, B), bt->att_staged, att_staged_smem(hd, bt->cap, bt->att_staged), s>>>(
-                bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale, bt->attn, bt->err);
+            k_b_attention_staged<<<dim3(H, B), bt->att_staged,
+                                   att_staged_smem(hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring), s>>>(
+                bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale, bt->attn, bt->err, bt->att_chunk,
+                bt->att_ring);
         else
             k_b_attention<<<dim3(H, B), kBT, att_smem, s>>>(bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale,
                                                              bt->attn);
@@ -1024,8 +1031,16 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     // GEMM operand copies, per layer [Wq; Wk; Wv] then [Wup; Wgate] (then Wo and Wdown when tiled)
     const char *att_env = getenv("VKLLM_B200_BATCH_ATT_STAGED");
     bt->att_staged = att_env ? (uint32_t)atoi(att_env) : 256u;
+    const char *chunk_env = getenv("VKLLM_B200_BATCH_ATT_CHUNK"), *ring_env = getenv("VKLLM_B200_BATCH_ATT_RING");
+    bt->att_chunk = chunk_env ? (uint32_t)atoi(chunk_env) : kAttChunk;
+    bt->att_ring = ring_env ? (uint32_t)atoi(ring_env) : kAttStages;
+    if (bt->att_chunk < 8 || bt->att_chunk > 256 || bt->att_chunk % 8 || bt->att_ring < 2 || bt->att_ring > kAttMaxStages)
+    {
+        bt->att_chunk = kAttChunk;
+        bt->att_ring = kAttStages;
+    }
     if (!(bt->att_staged == 128 || bt->att_staged == 256 || bt->att_staged == 512) || dd.hd % 8 || dd.hd > 128 ||
-        att_staged_smem(dd.hd, bt->cap, bt->att_staged) > 200 * 1024)
+        att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_staged = 0;
     const char *tiled_env = getenv("VKLLM_B200_BATCH_TILED");
     bt->tiled = tiled_env && atoi(tiled_env) == 0 ? 0u : 1u;
@@ -1080,7 +1095,8 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     if (!copied || cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
         (bt->att_staged && cudaFuncSetAttribute(k_b_attention_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                (int)att_staged_smem(dd.hd, bt->cap, bt->att_staged)) != cudaSuccess) ||
+                                                (int)att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk,
+                                                                     bt->att_ring)) != cudaSuccess) ||
         cudaStreamSynchronize(s) != cudaSuccess)
     {
         (void)cudaGetLastError();
