@@ -248,16 +248,23 @@ def batched_decode_leg(vk, model, args, world, rank, stream):
         barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if args.profile_batched:  # a profiler started with --profile-from-start off sees the timed steps only
+            torch.cuda.profiler.start()
         e0.record(stream)
         b.decode(K)
         e1.record(stream)
         e1.synchronize()
+        if args.profile_batched:
+            torch.cuda.profiler.stop()
         ms = max_over_ranks(world, e0.elapsed_time(e1))
     finally:
         b.free()
-    D, L = 4096, 32
+    cfg = dict(CFG_7B)
+    if args.layers:  # profiling case with fewer layers
+        cfg["block_count"] = args.layers
+    D, L = cfg["embedding_length"], cfg["block_count"]
     mean_lk = P + 3 + (K + 1) / 2.0
-    step_bytes = weight_bytes(CFG_7B) + n_local * L * 2 * D * 2 * mean_lk
+    step_bytes = weight_bytes(cfg) + n_local * L * 2 * D * 2 * mean_lk
     peak, _ = measured_peaks()
     return {"sequences": n_local * world, "per_rank": n_local, "steps": K, "prompt": P, "kv_rows": cap,
             "tok_s": round(n_local * world * K / (ms / 1000.0), 1), "ms_per_step": round(ms / K, 4),
@@ -271,7 +278,9 @@ def ops_microbench(vk, local, seed):
     """the operator microbenchmarks, each op run through the reference's op API
     (tensor_new -> upload -> op init -> run on a commands object -> submit/wait), timed by the
     per-launch CUDA events of the op executor (VKLLM_NODE_TIMING=1 on a context of its own). L2 is
-    flushed (a 256 MB write on the same stream, queued just before the op) before every timed run;
+    flushed before every timed run: a 256 MB write, then a 256 MB read of another buffer that evicts
+    the written lines (so their write-back is not charged to the op), both on the op's stream and
+    queued just before it;
     the median of 5 runs is reported. Bytes are the
     algorithmic bytes of the call (inputs read once, outputs written once); MATMUL at M = 512 is
     reported in TF/s against the tensor-core peak, everything else in GB/s against the HBM peak."""
@@ -288,6 +297,7 @@ def ops_microbench(vk, local, seed):
     hbm, _ = measured_peaks()
     tc = tc_peak()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=torch.device("cuda", local))
+    flush_rd = torch.ones(64 << 20, dtype=torch.float32, device=torch.device("cuda", local))
     cstream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
     rng = np.random.default_rng(seed + 11)
     lib = vk.lib()
@@ -317,6 +327,7 @@ def ops_microbench(vk, local, seed):
                 # then brackets the op's kernels only, not the host's launch latency
                 with torch.cuda.stream(cstream):
                     flush.zero_()
+                    flush_rd.sum()
                 cmd.begin()
                 vk.check(getattr(lib, run_fn)(ctx.ptr, cmd.ptr, n), run_fn)
                 cmd.end()
@@ -378,7 +389,7 @@ def ops_microbench(vk, local, seed):
     finally:
         for t in live:
             vk.tensor_free(ctx, t)
-        del flush
+        del flush, flush_rd
         ctx.close()
     return out
 
@@ -466,6 +477,13 @@ def run_ours(args, world, rank, local):
     l = vk.lib()
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
     prompt = prompt_tokens(rank)
+    if args.profile_batched:
+        batched = batched_decode_leg(vk, model, args, world, rank, stream)
+        if rank == 0:
+            print(json.dumps({"profile_case": "batched", "layers": cfg["block_count"], **batched}), flush=True)
+        model.free()
+        ctx.close()
+        return None
 
     # Prefill through the drop-in API (timed separately, reported as prefill tok/s): one untimed
     # warm-up prefill (first-use costs: kernel attributes, tensor maps, allocator growth), then the
@@ -720,6 +738,8 @@ def main():
     # Profiling case only (ncu): fewer layers, no prefill / e2e / per-kernel extras, no JSON result line.
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--profile-batched", action="store_true",
+                    help="profiling case: only the batched decode leg (with --layers), no JSON result line")
     ap.add_argument("--ops", type=int, default=1, help="operator microbenchmark leg (0: skip)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

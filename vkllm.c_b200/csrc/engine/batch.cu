@@ -738,14 +738,27 @@ __global__ void k_b_argmax(const __half *__restrict__ logits, uint32_t V, uint32
     const __half *row = logits + (uint64_t)b * V;
     float v = -FLT_MAX;
     uint32_t idx = 0xffffffffu;
-#pragma unroll 8 // eight loads in flight per thread; the comparisons still run in index order
-    for (uint32_t i = lane + 32 * warp; i < V; i += 32 * nw)
+    // this thread's elements i = lane + 32 warp + k * 32 nw, eight loads in flight at a time, compared
+    // in increasing k
+    const uint32_t stride = 32 * nw;
+    for (uint32_t base = lane + 32 * warp; base < V; base += 8 * stride)
     {
-        const float c = __half2float(row[i]);
-        if (c == c && (idx == 0xffffffffu || c > v))
+        float c[8];
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
         {
-            v = c;
-            idx = i;
+            const uint32_t i = base + u * stride;
+            c[u] = i < V ? __half2float(row[i]) : 0.f;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
+        {
+            const uint32_t i = base + u * stride;
+            if (i < V && c[u] == c[u] && (idx == 0xffffffffu || c[u] > v))
+            {
+                v = c[u];
+                idx = i;
+            }
         }
     }
     cv[warp][lane] = v;
