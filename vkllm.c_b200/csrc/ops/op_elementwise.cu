@@ -235,9 +235,27 @@ template <typename T> __global__ void k_softmax_block(const T *in, T *out, Desc4
     const uint32_t h = row % d.shape[2], c = (row / d.shape[2]) % d.shape[1], b = row / (d.shape[2] * d.shape[1]);
     const uint64_t base = d4_offset(d, b, c, h, 0);
     const uint32_t W = d.shape[3], nw = blockDim.x >> 5, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // each pass reads this thread's elements i = tid + k * blockDim eight at a time (all loads of a
+    // group issued before their uses); the sums still run in increasing k
+    const uint32_t nt = blockDim.x;
+    auto load8 = [&](uint32_t i0, float (&xs)[8]) {
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
+        {
+            const uint32_t i = i0 + u * nt;
+            xs[u] = i < W ? to_f32(in[base + (uint64_t)i * d.stride[3]]) : 0.f;
+        }
+    };
     float m = to_f32(in[base]);
-    for (uint32_t i = threadIdx.x; i < W; i += blockDim.x)
-        m = fmaxf(m, to_f32(in[base + (uint64_t)i * d.stride[3]]));
+    for (uint32_t i0 = threadIdx.x; i0 < W; i0 += 8 * nt)
+    {
+        float xs[8];
+        load8(i0, xs);
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
+            if (i0 + u * nt < W)
+                m = fmaxf(m, xs[u]);
+    }
     m = warp_max(m);
     if (lane == 0)
         red[warp] = m;
@@ -247,9 +265,18 @@ template <typename T> __global__ void k_softmax_block(const T *in, T *out, Desc4
         m = fmaxf(m, red[w]);
     __syncthreads();
     float s = 0.f;
-    for (uint32_t i = threadIdx.x; i < W; i += blockDim.x)
-        if (!(seq_mask > 0 && i > h + offsets))
-            s += expf(to_f32(in[base + (uint64_t)i * d.stride[3]]) - m);
+    for (uint32_t i0 = threadIdx.x; i0 < W; i0 += 8 * nt)
+    {
+        float xs[8];
+        load8(i0, xs);
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
+        {
+            const uint32_t i = i0 + u * nt;
+            if (i < W && !(seq_mask > 0 && i > h + offsets))
+                s += expf(xs[u] - m);
+        }
+    }
     s = warp_sum(s);
     if (lane == 0)
         red[warp] = s;
@@ -257,13 +284,22 @@ template <typename T> __global__ void k_softmax_block(const T *in, T *out, Desc4
     float tot = 0.f;
     for (uint32_t w = 0; w < nw; ++w)
         tot += red[w];
-    for (uint32_t i = threadIdx.x; i < W; i += blockDim.x)
+    for (uint32_t i0 = threadIdx.x; i0 < W; i0 += 8 * nt)
     {
-        const uint64_t o = base + (uint64_t)i * d.stride[3];
-        if (seq_mask > 0 && i > h + offsets)
-            out[o] = from_f32<T>(0.f);
-        else
-            out[o] = from_f32<T>(expf(to_f32(in[o]) - m) / tot);
+        float xs[8];
+        load8(i0, xs); // each element is read and then written by the same thread (in may be out)
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
+        {
+            const uint32_t i = i0 + u * nt;
+            if (i >= W)
+                continue;
+            const uint64_t o = base + (uint64_t)i * d.stride[3];
+            if (seq_mask > 0 && i > h + offsets)
+                out[o] = from_f32<T>(0.f);
+            else
+                out[o] = from_f32<T>(expf(xs[u] - m) / tot);
+        }
     }
 }
 
@@ -366,8 +402,19 @@ __global__ void k_embedding(const uint32_t *ids, Desc4 di, const T *table, Desc4
     {
         const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
         uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-        for (uint32_t i = threadIdx.x; i < dim / V; i += blockDim.x)
-            d4[i] = s4[i];
+        const uint32_t n4 = dim / V, nt = blockDim.x;
+        for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += 4 * nt) // four 16-byte loads in flight, then the stores
+        {
+            uint4 t[4];
+#pragma unroll
+            for (uint32_t u = 0; u < 4; ++u)
+                if (i0 + u * nt < n4)
+                    t[u] = s4[i0 + u * nt];
+#pragma unroll
+            for (uint32_t u = 0; u < 4; ++u)
+                if (i0 + u * nt < n4)
+                    d4[i0 + u * nt] = t[u];
+        }
     }
     else
     {
@@ -435,13 +482,27 @@ template <typename T> __global__ void k_arg_max_block(const T *in, Desc4 di, uin
     const uint32_t W = di.shape[3], nw = blockDim.x >> 5, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     float v = -FLT_MAX;
     uint32_t idx = 0xffffffffu;
-    for (uint32_t i = lane + 32 * warp; i < W; i += 32 * nw)
+    // this thread's elements i = lane + 32 warp + k * 32 nw: eight loads in flight at a time, then the
+    // comparisons in increasing k
+    const uint32_t stride = 32 * nw;
+    for (uint32_t i0 = lane + 32 * warp; i0 < W; i0 += 8 * stride)
     {
-        const float x = to_f32(in[base + (uint64_t)i * di.stride[3]]);
-        if (x == x && (idx == 0xffffffffu || x > v)) // NaN never wins a strict comparison
+        float xs[8];
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
         {
-            v = x;
-            idx = i;
+            const uint32_t i = i0 + u * stride;
+            xs[u] = i < W ? to_f32(in[base + (uint64_t)i * di.stride[3]]) : 0.f;
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < 8; ++u)
+        {
+            const uint32_t i = i0 + u * stride;
+            if (i < W && xs[u] == xs[u] && (idx == 0xffffffffu || xs[u] > v)) // NaN never wins a strict comparison
+            {
+                v = xs[u];
+                idx = i;
+            }
         }
     }
     cv[warp][lane] = v;
