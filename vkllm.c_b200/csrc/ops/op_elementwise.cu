@@ -175,18 +175,59 @@ __global__ void k_rope(const T *in, Desc4 di, T *out, Desc4 dout, uint32_t offse
 
 // fp16, normal-style pairs, unit innermost strides: the same rotation with one half2 load and store
 // per pair of the input and output, 32-bit index arithmetic (n < 2^32).
+// The denominators base^(2w / W) are computed once per block into shared memory (the same powf of
+// the same arguments, so theta keeps its bits) when W / 2 <= kRopeTab.
+constexpr uint32_t kRopeTab = 512;
 __global__ void k_rope_h2(const __half *in, Desc4 di, __half *out, Desc4 dout, uint32_t offset, float base)
 {
+    __shared__ float den_s[kRopeTab];
     const uint32_t half_w = di.shape[3] / 2, H = di.shape[2], Cc = di.shape[1];
     const uint32_t n = di.shape[0] * Cc * H * half_w;
+    const bool tab = half_w <= kRopeTab;
+    if (tab)
+    {
+        for (uint32_t w = threadIdx.x; w < half_w; w += blockDim.x)
+            den_s[w] = powf(base, (float)(2 * w) / (float)di.shape[3]);
+        __syncthreads();
+    }
     for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x)
     {
         const uint32_t w = t % half_w, r = t / half_w, h = r % H, r2 = r / H, c = r2 % Cc, b = r2 / Cc;
-        const float theta = (float)(offset + h) / powf(base, (float)(2 * w) / (float)di.shape[3]);
+        const float den = tab ? den_s[w] : powf(base, (float)(2 * w) / (float)di.shape[3]);
+        const float theta = (float)(offset + h) / den;
         const float cs = cosf(theta), sn = sinf(theta);
         const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(in + d4_offset(di, b, c, h, 2 * w)));
         *reinterpret_cast<__half2 *>(out + d4_offset(dout, b, c, h, 2 * w)) =
             __floats2half2_rn(cs * v.x - sn * v.y, sn * v.x + cs * v.y);
+    }
+}
+
+// As k_rope_h2, four pairs (one 16-byte load and store) per thread, so that the index arithmetic is
+// paid once per four rotations: W % 8 == 0, W / 2 <= kRopeTab, 16-byte aligned rows.
+__global__ void k_rope_h8(const __half *in, Desc4 di, __half *out, Desc4 dout, uint32_t offset, float base)
+{
+    __shared__ float den_s[kRopeTab];
+    const uint32_t half_w = di.shape[3] / 2, q8 = di.shape[3] / 8, H = di.shape[2], Cc = di.shape[1];
+    const uint32_t n = di.shape[0] * Cc * H * q8;
+    for (uint32_t w = threadIdx.x; w < half_w; w += blockDim.x)
+        den_s[w] = powf(base, (float)(2 * w) / (float)di.shape[3]);
+    __syncthreads();
+    for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < n; t += gridDim.x * blockDim.x)
+    {
+        const uint32_t qd = t % q8, r = t / q8, h = r % H, r2 = r / H, c = r2 % Cc, b = r2 / Cc;
+        const uint4 v = *reinterpret_cast<const uint4 *>(in + d4_offset(di, b, c, h, 8 * qd));
+        const __half2 *vh = reinterpret_cast<const __half2 *>(&v);
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (uint32_t e = 0; e < 4; ++e)
+        {
+            const float theta = (float)(offset + h) / den_s[4 * qd + e];
+            const float cs = cosf(theta), sn = sinf(theta);
+            const float2 f = __half22float2(vh[e]);
+            oh[e] = __floats2half2_rn(cs * f.x - sn * f.y, sn * f.x + cs * f.y);
+        }
+        *reinterpret_cast<uint4 *>(out + d4_offset(dout, b, c, h, 8 * qd)) = o;
     }
 }
 
@@ -645,7 +686,13 @@ extern "C" vkllm_err_t vkllm_op_rope_run(vkllm_context *context, vkllm_commands 
                     in0->shapes[3] % 2 == 0 && di.stride[2] % 2 == 0 && di.stride[1] % 2 == 0 &&
                     di.stride[0] % 2 == 0 && dout.stride[2] % 2 == 0 && dout.stride[1] % 2 == 0 &&
                     dout.stride[0] % 2 == 0 && ((uintptr_t)x & 3) == 0 && ((uintptr_t)y & 3) == 0 && n < (1ull << 32);
-    if (h2)
+    const bool h8 = h2 && in0->shapes[3] % 8 == 0 && in0->shapes[3] / 2 <= kRopeTab && di.stride[2] % 8 == 0 &&
+                    di.stride[1] % 8 == 0 && di.stride[0] % 8 == 0 && dout.stride[2] % 8 == 0 &&
+                    dout.stride[1] % 8 == 0 && dout.stride[0] % 8 == 0 && ((uintptr_t)x & 15) == 0 &&
+                    ((uintptr_t)y & 15) == 0;
+    if (h8)
+        k_rope_h8<<<grid_1d(n / 4, 256), 256, 0, s>>>((const __half *)x, di, (__half *)y, dout, p->offset, p->base);
+    else if (h2)
         k_rope_h2<<<grid, 256, 0, s>>>((const __half *)x, di, (__half *)y, dout, p->offset, p->base);
     else if (in0->dtype == vkllm_dtype_float16)
         k_rope<__half><<<grid, 256, 0, s>>>((const __half *)x, di, (__half *)y, dout, p->offset, p->base,
