@@ -56,9 +56,25 @@ extern vkllm_err_t vkllm_b200_models_llama2_init_random_tp(struct vkllm_context 
                                                            const struct vkllm_b200_llama2_config *cfg, uint64_t seed,
                                                            uint32_t tp_rank, uint32_t tp_size);
 
+/* Tensor-parallel shard `tp_rank` of `tp_size` (<= 8) of a GGUF model, read at load time: each rank
+ * uploads only its shard of every matrix, with the layout of vkllm_b200_models_llama2_init_random_tp
+ * (rows of Wq, Wk, Wv, Wgate, Wup and output; columns of Wo and Wdown; the embedding and the norm
+ * gains whole). Metadata and the tokenizer vocabulary are read as vkllm_models_llama2_load
+ * (src/models/vkllm_models_llama2.c:67-187) reads them. head_count, vocab_size and the FFN length
+ * must be multiples of tp_size (VKLLM_ERR_ARGS otherwise). tp_size 1 is vkllm_models_llama2_load. */
+extern vkllm_err_t vkllm_b200_models_llama2_load_tp(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                    const char *file, uint32_t tp_rank, uint32_t tp_size);
+
+/* Host only (no device): the shard of tensor `tensor` of a GGUF file that rank tp_rank of tp_size
+ * holds under the layout above, written row-major to dst (dst_bytes at least rows x cols x element
+ * size); shape receives {rows, cols}. dst NULL: shape only. */
+extern vkllm_err_t vkllm_b200_gguf_read_shard(const char *file, const char *tensor, uint32_t tp_rank,
+                                              uint32_t tp_size, void *dst, uint64_t dst_bytes, uint32_t *shape);
+
 /* Tensor parallelism over peer memory (one process per GPU, every rank with its shard from
- * vkllm_b200_models_llama2_init_random_tp). Each rank calls vkllm_b200_tp_init, which allocates its
- * exchange buffer and writes its 64-byte CUDA IPC handle to handle_out; the caller gathers the
+ * vkllm_b200_models_llama2_init_random_tp or vkllm_b200_models_llama2_load_tp). Each rank calls
+ * vkllm_b200_tp_init, which allocates its exchange buffer and writes its 64-byte CUDA IPC handle to
+ * handle_out; the caller gathers the
  * handles of all ranks (rank order, 64 bytes each, e.g. with torch.distributed.all_gather_object)
  * and passes them to vkllm_b200_tp_connect, which maps the peers' buffers. Then the engine entry
  * points decode on every rank in lockstep: the Wo and down projections of each layer exchange

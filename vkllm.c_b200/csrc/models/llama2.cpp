@@ -6,6 +6,7 @@
 #include <cstring>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "../engine/plan.h"
 #include "../runtime/internal.h"
@@ -140,6 +141,81 @@ vkllm_err_t tensor_from_gguf(vkllm_context *ctx, const vkb::GgufTensor &gt, vkll
     return VKLLM_ERR_OK;
 }
 
+// Tensor-parallel split of a llama2 GGUF tensor, by name (the layout init_random_tp writes): 1 = rows
+// (Wq, Wk, Wv, Wgate, Wup, output), 2 = columns (Wo, Wdown), 0 = whole (embedding, norm gains).
+int tp_split_of(const std::string &name)
+{
+    if (name == "output.weight")
+        return 1;
+    const size_t dot = name.rfind(".weight");
+    if (name.compare(0, 4, "blk.") != 0 || dot == std::string::npos)
+        return 0;
+    const size_t leaf = name.find('.', 4);
+    if (leaf == std::string::npos)
+        return 0;
+    const std::string l = name.substr(leaf + 1, dot - leaf - 1);
+    if (l == "attn_q" || l == "attn_k" || l == "attn_v" || l == "ffn_gate" || l == "ffn_up")
+        return 1;
+    if (l == "attn_output" || l == "ffn_down")
+        return 2;
+    return 0;
+}
+
+// The shard of GGUF tensor t held by rank r of n: sp = {row0, rows, col0, cols} (vkllm_b200_tp_shard)
+// of its [rows = ne1][cols = ne0] matrix; 1-D and whole tensors are one row block of all elements.
+// Returns VKLLM_ERR_ARGS for a non-F16/F32 tensor or dimensions the split does not divide.
+vkllm_err_t tp_shard_of(const vkb::GgufTensor &t, uint32_t rank, uint32_t n, uint32_t sp[4], uint32_t *esz)
+{
+    if (t.type != vkb::GGML_F32 && t.type != vkb::GGML_F16)
+        return VKLLM_ERR_ARGS;
+    *esz = t.type == vkb::GGML_F32 ? 4 : 2;
+    const int split = t.n_dims == 2 ? tp_split_of(t.name) : 0;
+    const uint64_t cols = t.dims[0], rows = t.n_dims >= 2 ? t.bytes / (*esz * cols) : 1;
+    if (cols == 0 || rows * cols * *esz != t.bytes || rows > 0xffffffffull || cols > 0xffffffffull)
+        return VKLLM_ERR_ARGS;
+    return vkllm_b200_tp_shard((uint32_t)rows, (uint32_t)cols, split, rank, n, sp);
+}
+
+// Copies shard sp of t (row-major) to dst as a dense [sp[1]][sp[3]] block.
+void copy_tp_shard(const vkb::GgufTensor &t, const uint32_t sp[4], uint32_t esz, uint8_t *dst)
+{
+    const uint64_t cols = t.dims[0], row_b = (uint64_t)sp[3] * esz;
+    if (sp[2] == 0 && sp[3] == cols)
+    {
+        memcpy(dst, t.data + (uint64_t)sp[0] * cols * esz, (uint64_t)sp[1] * row_b);
+        return;
+    }
+    for (uint32_t i = 0; i < sp[1]; ++i)
+        memcpy(dst + i * row_b, t.data + (((uint64_t)sp[0] + i) * cols + sp[2]) * esz, row_b);
+}
+
+// tensor_from_gguf for rank r of n: the tensor holds only its shard ([1, 1, rows, cols] for a 2-D
+// matrix; whole tensors keep their shape), staged on the host and uploaded.
+vkllm_err_t tensor_from_gguf_shard(vkllm_context *ctx, const vkb::GgufTensor &gt, uint32_t rank, uint32_t n,
+                                   vkllm_tensor **out)
+{
+    uint32_t sp[4], esz = 0;
+    if (tp_shard_of(gt, rank, n, sp, &esz) != VKLLM_ERR_OK)
+    {
+        log_error("tensor %s cannot be split %u ways (GGML type %u)", gt.name.c_str(), n, gt.type);
+        return VKLLM_ERR_ARGS;
+    }
+    if (gt.n_dims != 2 || tp_split_of(gt.name) == 0)
+        return tensor_from_gguf(ctx, gt, out);
+    uint32_t shapes[4] = {1, 1, sp[1], sp[3]};
+    _CHECK(vkllm_tensor_new(ctx, gt.name.c_str(), shapes, gt.type == vkb::GGML_F32 ? vkllm_dtype_float32
+                                                                                   : vkllm_dtype_float16,
+                            VKLLM_OP_NONE, NULL, 0, NULL, 0, false, out));
+    void *d = vkb::dev_ptr(ctx, *out);
+    if (!d)
+        return VKLLM_ERR_ALLOC;
+    std::vector<uint8_t> host((size_t)sp[1] * sp[3] * esz);
+    copy_tp_shard(gt, sp, esz, host.data());
+    VKB_CUDA(cudaMemcpyAsync(d, host.data(), host.size(), cudaMemcpyHostToDevice, ctx->runtime->stream));
+    VKB_CUDA(cudaStreamSynchronize(ctx->runtime->stream)); // the staging buffer ends with this call
+    return VKLLM_ERR_OK;
+}
+
 vkllm_err_t create_kvcache(vkllm_context *ctx, vkllm_models_llama2 *m)
 {
     _CHECK_ARGS(m->weights.blocks->used_n > 0 && m->weights.blocks->data[0]->WK && m->weights.blocks->data[0]->WV);
@@ -235,6 +311,127 @@ extern "C" vkllm_err_t vkllm_models_llama2_load(struct vkllm_context *context, s
 fail:
     vkllm_models_llama2_free(context, model);
     return e;
+}
+
+extern "C" vkllm_err_t vkllm_b200_models_llama2_load_tp(struct vkllm_context *context,
+                                                        struct vkllm_models_llama2 *model, const char *file,
+                                                        uint32_t tp_rank, uint32_t tp_size)
+{
+    _CHECK_ARGS(context && model && file && tp_size >= 1 && tp_size <= 8 && tp_rank < tp_size);
+    if (tp_size == 1)
+        return vkllm_models_llama2_load(context, model, file);
+    memset(model, 0, sizeof(*model));
+    vkb::GgufFile gguf;
+    std::string err = gguf.open(file);
+    if (!err.empty())
+    {
+        log_error("failed to open gguf file %s: %s", file, err.c_str());
+        return VKLLM_ERR_ARGS;
+    }
+    set_defaults(model);
+    model->b200.tp_size = tp_size;
+    model->b200.tp_rank = tp_rank;
+    const vkb::GgufKV *tokens = nullptr, *scores = nullptr, *types = nullptr;
+    for (const auto &kv : gguf.kvs())
+    {
+        apply_kv(model, kv);
+        if (kv.key == "tokenizer.ggml.tokens" && kv.type == vkb::GGUF_ARRAY && kv.arr_type == vkb::GGUF_STRING)
+            tokens = &kv;
+        if (kv.key == "tokenizer.ggml.scores" && kv.type == vkb::GGUF_ARRAY && kv.arr_type == vkb::GGUF_F32)
+            scores = &kv;
+        if (kv.key == "tokenizer.ggml.token_type" && kv.type == vkb::GGUF_ARRAY && kv.arr_type == vkb::GGUF_I32)
+            types = &kv;
+    }
+    if (model->meta.head_count % tp_size != 0 || model->meta.vocab_size % tp_size != 0)
+    {
+        log_error("head_count %u and vocab_size %u must be multiples of tp_size %u", model->meta.head_count,
+                  model->meta.vocab_size, tp_size);
+        return VKLLM_ERR_ARGS;
+    }
+    vkllm_err_t e = VKLLM_ERR_OK;
+    if (tokens)
+    {
+        _CHECK(vkllm_array_token_new(&model->meta.tokens, tokens->arr_str.size()));
+        for (size_t i = 0; i < tokens->arr_str.size(); ++i)
+        {
+            vkllm_token t;
+            t.text = strdup(tokens->arr_str[i].c_str());
+            t.score = scores && i < scores->arr_num.size() ? (float)scores->arr_num[i] : 0.0f;
+            t.type = types && i < types->arr_num.size() ? (int32_t)types->arr_num[i] : 0;
+            _CHECK(vkllm_array_token_append(model->meta.tokens, t));
+        }
+    }
+    _CHECK(vkllm_array_block_weights_new(&model->weights.blocks, model->meta.block_count));
+    for (const auto &t : gguf.tensors())
+    {
+        vkllm_tensor **slot = nullptr;
+        if (t.name == "token_embd.weight")
+            slot = &model->weights.tok_embed_weights;
+        else if (t.name == "output_norm.weight")
+            slot = &model->weights.output_norm_weight;
+        else if (t.name == "output.weight")
+            slot = &model->weights.output_weight;
+        else if (t.name.compare(0, 4, "blk.") == 0)
+        {
+            int idx = -1;
+            char leaf[96] = {0};
+            if (sscanf(t.name.c_str(), "blk.%d.%95s", &idx, leaf) == 2 && idx >= 0 && idx < 4096)
+            {
+                e = ensure_blocks(model, (size_t)idx + 1);
+                if (e != VKLLM_ERR_OK)
+                    goto fail;
+                slot = block_slot(model->weights.blocks->data[idx], leaf);
+            }
+        }
+        if (!slot)
+            continue;
+        if (*slot)
+            vkllm_tensor_free(context, *slot);
+        e = tensor_from_gguf_shard(context, t, tp_rank, tp_size, slot);
+        if (e != VKLLM_ERR_OK)
+            goto fail;
+    }
+    if (cudaStreamSynchronize(context->runtime->stream) != cudaSuccess)
+    {
+        e = VKLLM_ERR_VULKAN;
+        goto fail;
+    }
+    e = create_kvcache(context, model);
+    if (e != VKLLM_ERR_OK)
+        goto fail;
+    return VKLLM_ERR_OK;
+fail:
+    vkllm_models_llama2_free(context, model);
+    return e;
+}
+
+extern "C" vkllm_err_t vkllm_b200_gguf_read_shard(const char *file, const char *tensor, uint32_t tp_rank,
+                                                 uint32_t tp_size, void *dst, uint64_t dst_bytes, uint32_t *shape)
+{
+    _CHECK_ARGS(file && tensor && shape && tp_size >= 1 && tp_rank < tp_size);
+    vkb::GgufFile gguf;
+    std::string err = gguf.open(file);
+    if (!err.empty())
+    {
+        log_error("failed to open gguf file %s: %s", file, err.c_str());
+        return VKLLM_ERR_ARGS;
+    }
+    for (const auto &t : gguf.tensors())
+    {
+        if (t.name != tensor)
+            continue;
+        uint32_t sp[4], esz = 0;
+        _CHECK(tp_shard_of(t, tp_rank, tp_size, sp, &esz));
+        shape[0] = sp[1];
+        shape[1] = sp[3];
+        if (!dst)
+            return VKLLM_ERR_OK; // shape query
+        _CHECK_ARGS(dst_bytes >= (uint64_t)sp[1] * sp[3] * esz);
+        copy_tp_shard(t, sp, esz, (uint8_t *)dst);
+        return VKLLM_ERR_OK;
+    }
+    log_error("tensor %s not in %s", tensor, file);
+    return VKLLM_ERR_ARGS;
 }
 
 extern "C" vkllm_err_t vkllm_models_llama2_free(struct vkllm_context *context, struct vkllm_models_llama2 *model)

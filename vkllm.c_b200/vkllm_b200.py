@@ -181,6 +181,10 @@ _SIGS = {
     "vkllm_b200_models_llama2_init_random_tp": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.POINTER(Llama2Config),
                                                           C.c_uint64, C.c_uint32, C.c_uint32]),
     "vkllm_b200_tp_init": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
+    "vkllm_b200_models_llama2_load_tp": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
+                                                   C.c_uint32]),
+    "vkllm_b200_gguf_read_shard": (C.c_int, [C.c_char_p, C.c_char_p, C.c_uint32, C.c_uint32, C.c_void_p,
+                                             C.c_uint64, C.c_void_p]),
     "vkllm_b200_tp_shard": (C.c_int, [C.c_uint32, C.c_uint32, C.c_int, C.c_uint32, C.c_uint32, C.c_void_p]),
     "vkllm_b200_random_f16_host_shard": (None, [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint32, C.c_uint32,
                                                 C.c_uint32, C.c_uint32, C.c_void_p]),
@@ -410,6 +414,13 @@ class Model:
         c = Llama2Config(**cfg)
         check(lib().vkllm_b200_models_llama2_init_random_tp(self.ctx.ptr, C.byref(self.m), C.byref(c), seed, rank,
                                                              world), "llama2_init_random_tp")
+        self.loaded = True
+        return self
+
+    def load_tp(self, path, rank: int, world: int):
+        """Tensor-parallel shard `rank` of `world` of a GGUF model (only the shard is uploaded)."""
+        check(lib().vkllm_b200_models_llama2_load_tp(self.ctx.ptr, C.byref(self.m), path.encode(), rank, world),
+              "llama2_load_tp")
         self.loaded = True
         return self
 
