@@ -46,6 +46,31 @@ struct Cursor
     }
 };
 
+// Bytes of one scalar of a GGUF value type (0 for strings, arrays and unknown types).
+uint64_t scalar_size(uint32_t type)
+{
+    switch (type)
+    {
+    case GGUF_U8:
+    case GGUF_I8:
+    case GGUF_BOOL:
+        return 1;
+    case GGUF_U16:
+    case GGUF_I16:
+        return 2;
+    case GGUF_U32:
+    case GGUF_I32:
+    case GGUF_F32:
+        return 4;
+    case GGUF_U64:
+    case GGUF_I64:
+    case GGUF_F64:
+        return 8;
+    default:
+        return 0;
+    }
+}
+
 bool read_scalar(Cursor &c, uint32_t type, GgufKV &kv)
 {
     switch (type)
@@ -160,7 +185,11 @@ std::string GgufFile::open(const char *path)
         {
             kv.arr_type = c.get<uint32_t>();
             uint64_t n = c.get<uint64_t>();
-            if (!c.ok || n > map_len_)
+            // every element takes at least its scalar size (a string: its 8-byte length) of the
+            // bytes left, which bounds what is reserved below
+            const uint64_t left = (uint64_t)(c.end - c.p);
+            const uint64_t esz = kv.arr_type == GGUF_STRING ? 8 : scalar_size(kv.arr_type);
+            if (!c.ok || (esz > 0 && n > left / esz))
                 return "corrupt array in metadata key " + kv.key;
             if (kv.arr_type == GGUF_STRING)
             {
@@ -187,7 +216,11 @@ std::string GgufFile::open(const char *path)
         else if (!read_scalar(c, kv.type, kv))
             return "corrupt value of metadata key " + kv.key;
         if (kv.key == "general.alignment" && kv.u > 0)
+        {
+            if (kv.u > (1u << 20) || kv.u % 8 != 0) // the format asks for a multiple of 8
+                return "unsupported general.alignment " + std::to_string(kv.u);
             alignment = kv.u;
+        }
         kvs_.push_back(std::move(kv));
     }
     for (uint64_t t = 0; t < n_tensors; ++t)
@@ -203,7 +236,12 @@ std::string GgufFile::open(const char *path)
         ti.offset = c.get<uint64_t>();
         if (!c.ok)
             return "truncated tensor descriptors";
-        uint64_t n = ti.dims[0] * ti.dims[1] * ti.dims[2] * ti.dims[3];
+        uint64_t n = 1;
+        for (uint32_t d = 0; d < 4; ++d)
+            if (ti.dims[d] > 0xffffffffull || __builtin_mul_overflow(n, ti.dims[d], &n))
+                return "corrupt dimensions of tensor " + ti.name;
+        if ((ti.type == GGML_F32 || ti.type == GGML_F16) && n > map_len_) // cannot fit in the file
+            return "tensor " + ti.name + " is larger than the file";
         if (ti.type == GGML_F32)
             ti.bytes = n * 4;
         else if (ti.type == GGML_F16)
@@ -218,7 +256,7 @@ std::string GgufFile::open(const char *path)
     {
         if (ti.bytes == 0)
             continue;
-        if (data_start + ti.offset + ti.bytes > map_len_)
+        if (data_start > map_len_ || ti.offset > map_len_ - data_start || ti.bytes > map_len_ - data_start - ti.offset)
             return "tensor " + ti.name + " extends past the end of the file";
         ti.data = base + data_start + ti.offset;
     }
