@@ -266,8 +266,8 @@ __host__ __device__ constexpr size_t att_staged_smem(uint32_t hd, uint32_t cap, 
 }
 
 // Attention of one (head, sequence) as k_b_attention computes it, with the sequence's key rows and
-// then its value rows streamed through shared memory: 64-row chunks (Lk x hd fp16 rows are
-// contiguous in the batch's cache) are fetched by cp.async.bulk into a ring of kAttStages buffers,
+// then its value rows streamed through shared memory: `chunk`-row chunks (Lk x hd fp16 rows are
+// contiguous in the batch's cache) are fetched by cp.async.bulk into a ring of `stages` buffers,
 // so the copies of later chunks (the first value chunks included) are in flight while the scores,
 // the softmax statistics and the probabilities of earlier ones are computed. Scores: `lpk` lanes
 // per key row (8 fp16 each) and a shuffle sum; probabilities: the same rounding points as
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
     const uint32_t warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const __half *kb = kc + ((uint64_t)b * H + h) * cap * hd;
     const __half *vb = vc + ((uint64_t)b * H + h) * cap * hd;
-    // chunk c < nk: key rows [64 c, ...); c >= nk: value rows [64 (c - nk), ...); buffer c % stages
+    // chunk c < nk: key rows [chunk c, ...); c >= nk: value rows [chunk (c - nk), ...); buffer c % stages
     auto issue = [&](uint32_t c) {
         const uint32_t r0 = (c < nk ? c : c - nk) * chunk, rows = min(chunk, Lk - r0);
         const uint32_t st = c % stages;
