@@ -59,24 +59,32 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """nvidia-smi clock/throttle sampling during the timed region (a read-only query every 20 ms into a
+    temporary file). Entering waits, up to 3 s, for the first sample, so that a timed region of a few
+    tens of milliseconds is still covered."""
 
     def __init__(self, gpu):
+        import tempfile
+
         self.gpu = gpu
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu}.csv")
+        fd, self.path = tempfile.mkstemp(prefix=f"vkllm_clocks_gpu{gpu}_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return self
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and os.path.getsize(self.path) == 0 and self.proc.poll() is None:
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *a):
@@ -87,16 +95,21 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
             self.f.close()
+        self.rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        self.rows.append(parts)
+            os.unlink(self.path)
+        except OSError:
+            pass
 
     def summary(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+        rows = self.rows
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]

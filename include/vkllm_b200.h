@@ -227,12 +227,21 @@ extern vkllm_err_t vkllm_b200_engine_bench_kernel(struct vkllm_context *context,
  *   kcache  fp16 [heads, cache_rows, head_dim], vcache likewise; keys/values 0 .. n_keys-1 are used
  *   out     fp16 [heads, head_dim]
  *   scale   score scale (1/sqrt(head_dim) for LLaMA-2); stream is a cudaStream_t (NULL = legacy)
+ * kcache and vcache must be 8-byte aligned (rows are read 4 halves at a time), q and out 2-byte
+ * aligned; other pointers return VKLLM_ERR_ARGS without launching anything.
+ * When n_keys == head_dim the result is the reference graph's, not textbook attention: its MATMUL
+ * decides "B is transposed" from shapes alone (src/core/vkllm_op_matmul.c:14-30), so at that one key
+ * count the probs.V node computes out[w] = sum_k p_k * V[w][k]. This entry point reproduces that.
  * All scratch lives in one static device array of about 1.1 MiB that every GPU loading the library
  * holds until exit. Limits: heads <= 64, head_dim <= 256 and a multiple of 4,
  * heads * cache_rows <= 262144; larger sizes return VKLLM_ERR_ARGS. The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress, with that device current) and should
- * come before any stream capture. Every call shares the array: calls that overlap on the GPU (two
- * streams, or two host threads) race on it and must be serialised by the caller. */
+ * come before any stream capture; the device that is current at each call must be the one that owns
+ * `stream` and the buffers. The looked-up address is kept for the life of the process, so calls
+ * after a cudaDeviceReset of that device are not supported. The kernels contain no waits: a fault
+ * shows up as a CUDA error at the caller's next synchronisation of `stream`. Every call shares the
+ * array: calls that overlap on the GPU (two streams, or two host threads) race on it and must be
+ * serialised by the caller. */
 extern vkllm_err_t vkllm_b200_attention_decode_noalloc(const void *q, const void *kcache, const void *vcache,
                                                        uint32_t heads, uint32_t head_dim, uint32_t cache_rows,
                                                        uint32_t n_keys, float scale, void *out, void *stream);

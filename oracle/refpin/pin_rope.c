@@ -1,0 +1,16 @@
+/* TEST INFRASTRUCTURE (oracle pin). Compiles the reference's own tests/vkllm_test_op_rope.c from
+ * where it lies (the include path points at the reference checkout) and exports its CPU reference
+ * function, rope_op_host (tests/vkllm_test_op_rope.c:17-94), so that golden vectors come from the reference's code. The file's GPU test
+ * bodies are compiled but unreachable and dropped at link time; nothing of this library reaches
+ * the product. */
+#define main refpin_unused_main_rope
+#include "tests/vkllm_test_op_rope.c"
+#undef main
+#define REFPIN_EXPORT __attribute__((visibility("default")))
+
+REFPIN_EXPORT void refpin_rope(const void *x, void *y, const uint32_t shapes[4], const uint32_t strides[4],
+                                const uint32_t out_shapes[4], const uint32_t out_strides[4], uint32_t offset, float base,
+                                int dtype)
+{
+    rope_op_host(x, y, shapes, strides, out_shapes, out_strides, offset, base, (vkllm_dtype_t)dtype);
+}

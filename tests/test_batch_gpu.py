@@ -2,9 +2,10 @@
 model): every sequence of the batch must decode exactly what it decodes alone. Each sequence is
 prefilled through the drop-in graph API, moved into its batch slot, then all decode together on the
 tensor-core GEMM path (M = number of sequences). Reference: the CPU oracle run on each sequence
-separately (prefill + the same number of greedy steps). Bar: fp16 logits within max-abs 2e-2 /
-mean-abs 2e-3 at every step whose inputs agree, and identical token ids except where the reference's
-own fp16 logits tie (top choice within 2 fp16 ulps of ours), since summation order differs."""
+separately (prefill + the same number of greedy steps). Bar: identical
+greedy token ids for the first 32 steps of every sequence, and fp16 logits within max-abs 2e-2 /
+mean-abs 2e-3 at every step. A token mismatch fails with the reference's logits of both tokens and
+its top two, so a tie broken the other way by a different fp32 summation order is visible as such."""
 import numpy as np
 import pytest
 
@@ -13,7 +14,7 @@ pytestmark = pytest.mark.gpu
 # (seed, prompt length); the last sequence passes Lk == hd (48 on the tiny model), where the
 # reference reads V transposed
 PROMPTS = [(11, 8), (12, 12), (13, 5), (14, 1), (15, 40)]
-N_STEPS = 20
+N_STEPS = 32
 
 # the batch's kernel choices (read when the batch is created): the default (bulk-copy staged
 # attention, tile-order GEMM operands), the register-loading attention kernel, the staged kernel
@@ -34,7 +35,7 @@ def test_batched_decode_matches_each_sequence_alone(vk, ctx, tiny_gguf, orc, var
     model = vk.Model(ctx).load(path)
     batch = None
     try:
-        batch = vk.Batch(model, len(prompts), 64)
+        batch = vk.Batch(model, len(prompts), 96)
         firsts = [batch.add_prompt(i, p) for i, p in enumerate(prompts)]
         toks, logits = [], []
         for _ in range(N_STEPS):  # step by step to compare every step's logits
@@ -45,7 +46,6 @@ def test_batched_decode_matches_each_sequence_alone(vk, ctx, tiny_gguf, orc, var
         if batch is not None:
             batch.free()
         model.free()
-    exact = 0
     for i, p in enumerate(prompts):
         m = orc.Llama2(cfg, weights)
         ref_toks, ref_logits = m.generate(p, N_STEPS + 1)
@@ -53,21 +53,14 @@ def test_batched_decode_matches_each_sequence_alone(vk, ctx, tiny_gguf, orc, var
         assert firsts[i] == ref_toks[0]
         ours = [int(t) for t in toks[:, i]]
         ref = ref_toks[1:N_STEPS + 1]
-        fd = next((s for s in range(N_STEPS) if ours[s] != ref[s]), N_STEPS)
-        for s in range(min(fd + 1, N_STEPS)):  # inputs agree up to and including step fd
+        for s in range(N_STEPS):
             r = np.asarray(ref_logits[s + 1], dtype=np.float32)
             d = np.abs(logits[s][i].astype(np.float32) - r)
             assert d.max() <= 2e-2 and d.mean() <= 2e-3, (i, s, d.max(), d.mean())
-        if fd < N_STEPS:
-            # A divergence is only acceptable at a tie of the reference's own fp16 logits: the token we
-            # chose scores within 2 fp16 ulps of the reference's choice there (fp32 summation order
-            # differs between the two, so such ties can break either way).
-            r = np.asarray(ref_logits[fd + 1], dtype=np.float32)
-            top = float(r[ref[fd]])
-            ulp = 2.0 ** (np.floor(np.log2(max(abs(top), 2.0 ** -14))) - 10)
-            assert top - float(r[ours[fd]]) <= 2 * ulp, (i, fd, top, float(r[ours[fd]]))
-        exact += fd == N_STEPS
-    assert exact >= 1
+            if ours[s] != ref[s]:
+                raise AssertionError(f"sequence {i} step {s}: token {ours[s]} vs reference {ref[s]}; reference "
+                                     f"logits {r[ref[s]]} (its choice) / {r[ours[s]]} (ours), its top two "
+                                     f"{np.sort(r)[-2:]}; our logits {logits[s][i][ref[s]]} / {logits[s][i][ours[s]]}")
 
 
 def test_batch_rejects_a_sequence_past_its_capacity(vk, ctx, tiny_gguf):

@@ -4,8 +4,11 @@ driven by the reference token loop (tests/vkllm_test_infer_gguf.c:181-272) throu
 the CPU oracle's restatement of the reference graph on the same weights and prompt.
 
 Bar: greedy token ids identical for the first 32 steps; fp16 logits within
-max-abs 2e-2 and mean-abs 2e-3 at every step whose inputs agree. Both execution paths are checked:
-node by node (STRICT, the reference's own DAG) and the fused CUDA-Graph decode engine (FUSED)."""
+max-abs 2e-2 and mean-abs 2e-3 at every step whose inputs agree. Every execution path is checked:
+node by node (STRICT, the reference's own DAG), the persistent decode kernel (FUSED, the default),
+the CUDA-graph decode path that runs when cooperative launch is unavailable (VKLLM_B200_DECODE=graph),
+and the persistent kernel with its row partition calibrated at engine creation
+(VKLLM_B200_PERSIST_BALANCE=2)."""
 import numpy as np
 import pytest
 
@@ -27,8 +30,16 @@ def reference_run(tiny_gguf, orc):
     return prompt, toks, logits
 
 
-@pytest.mark.parametrize("mode", ["strict", "fused"])
-def test_tiny_token_loop_parity(vk, ctx, tiny_gguf, reference_run, mode):
+MODES = {"strict": {}, "fused": {}, "fused_graph": {"VKLLM_B200_DECODE": "graph"},
+         "fused_balanced": {"VKLLM_B200_PERSIST_BALANCE": "2"}}
+
+
+@pytest.mark.parametrize("mode", list(MODES))
+def test_tiny_token_loop_parity(vk, ctx, tiny_gguf, reference_run, mode, monkeypatch):
+    import ctypes as C
+
+    for k, v in MODES[mode].items():  # read when the model's decode engine is created
+        monkeypatch.setenv(k, v)
     path, _ = tiny_gguf
     prompt, ref_toks, ref_logits = reference_run
     ctx.set_exec_mode(vk.EXEC_STRICT if mode == "strict" else vk.EXEC_FUSED)
@@ -37,6 +48,9 @@ def test_tiny_token_loop_parity(vk, ctx, tiny_gguf, reference_run, mode):
         assert model.meta.embedding_length == 288 and model.meta.block_count == 6
         logits = []
         toks = model.generate(prompt, N_STEPS, logits)
+        if mode != "strict":
+            persistent = vk.lib().vkllm_b200_engine_is_persistent(ctx.ptr, C.byref(model.m))
+            assert bool(persistent) == (mode != "fused_graph"), (mode, persistent)
     finally:
         model.free()
         ctx.set_exec_mode(vk.EXEC_FUSED)

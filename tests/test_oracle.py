@@ -1,6 +1,7 @@
 """Pins the oracle (oracle/, the CPU restatement of the reference's shaders) to the reference's own
 test-side CPU references: tests/golden/ref_ops.npz holds seeded inputs and the outputs of those
-functions (restated by tests/golden/make_golden.py). CPU only.
+functions, compiled from the reference's test files and called by tests/golden/make_golden.py
+(oracle/refpin/Makefile builds them). CPU only.
 
 Bars: bit-exact for gather / row copies / argmax; for floating point, the reference tests' own
 mean-squared-error thresholds (matmul 1e-2, rope 1e-2 for fp16; tests/vkllm_test_op_matmul.c:382,
@@ -76,9 +77,63 @@ def test_update_rows_is_exact(orc, g):
 
 
 def test_embedding_is_exact_with_unk(orc, g):
+    """The reference test's function maps out-of-range ids to row 0 (the shader's unk parameter,
+    which the model sets to padding_token_id, defaults to 0)."""
     ids = g["emb_ids"]
-    out = orc.embedding(ids, g["emb_table"], (1, 1, ids.shape[3], g["emb_table"].shape[3]), 2)
+    out = orc.embedding(ids, g["emb_table"], (1, 1, ids.shape[3], g["emb_table"].shape[3]), 0)
     assert out.tobytes() == g["emb_out"].tobytes()
+
+
+def test_copy_of_permuted_view_is_exact(orc, g):
+    x = g["copy_x"].transpose(0, 2, 1, 3)
+    assert orc.copy(x).tobytes() == g["copy_out"].tobytes()
+
+
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+@pytest.mark.parametrize("dt", ["float16", "float32"])
+def test_bin_matches_reference_test_formula(orc, g, op, dt):
+    key = f"bin_{op}_{dt}"
+    a, b, ref = g[f"{key}_a"], g[f"{key}_b"], g[f"{key}_out"]
+    got = orc.bin_op(a, b, op, ref.dtype)
+    if dt == "float32":
+        np.testing.assert_array_equal(got, ref)
+    else:
+        close(got, ref, 1e-4)
+
+
+def test_header_fp16_helper_is_the_reference_helper(tmp_path, g):
+    """include/vkllm_common.h's vkllm_fp32_to_fp16 (which reference-style callers use to fill
+    tensors) gives the reference helper's bits on every value, NaN, infinities and denormals
+    included."""
+    import ctypes as C
+    import subprocess
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = tmp_path / "h.c"
+    src.write_text('#include "vkllm_common.h"\n'
+                   "unsigned short conv(float v) { return vkllm_fp32_to_fp16(v).bits; }\n"
+                   "float back(unsigned short b) { vkllm_fp16_pack p = {b}; return vkllm_fp16_to_fp32(p); }\n")
+    so = tmp_path / "h.so"
+    subprocess.run(["gcc", "-O2", "-shared", "-fPIC", "-I", os.path.join(root, "include"), str(src), "-o", str(so)],
+                   check=True)
+    lib = C.CDLL(str(so))
+    lib.conv.restype, lib.conv.argtypes = C.c_ushort, [C.c_float]
+    got = np.array([lib.conv(float(v)) for v in g["f16_vals"]], dtype=np.uint16)
+    np.testing.assert_array_equal(got, g["f16_bits"])
+
+
+def test_fixture_is_reproduced_by_the_reference_functions():
+    """Where the reference's test functions were compiled here (oracle/_ref/librefpin.so), every
+    stored array is regenerated from them and compared byte for byte."""
+    import make_golden
+
+    if not os.path.exists(make_golden.REFPIN):
+        pytest.skip("oracle/_ref/librefpin.so not built (needs the reference checkout)")
+    fresh = make_golden.generate(make_golden.refpin())
+    stored = np.load(GOLD)
+    assert sorted(fresh) == sorted(stored.files)
+    for k in fresh:
+        assert fresh[k].tobytes() == stored[k].tobytes(), k
 
 
 def test_planted_error_is_caught(orc, g):

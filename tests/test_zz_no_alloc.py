@@ -1,12 +1,13 @@
 """The allocation-free decode attention entry point (vkllm_b200_attention_decode_noalloc), for callers
 that cannot allocate device memory (during stream capture, under a fixed memory budget, on
-real-time paths). It is checked against the existing entry points that compute the same thing: the
-reference's three attention nodes run through vkllm_op_matmul (scores, scale 1/sqrt(hd)),
-vkllm_op_softmax (causal mask at offset n_keys-1) and vkllm_op_matmul (probs . V) on the same
-inputs, with the op tests' fp16 tolerance, on two calls in a row (the second with a different key
-count, so stale scratch from the first call would show). This file sorts last so that a run that
-stops at the first failure has already run every other test; it also passes alone in a fresh
-process."""
+real-time paths). It is checked against two things that compute the same result: the CPU oracle's
+restatement of the reference's three attention nodes (scores MATMUL with scale 1/sqrt(hd), SOFTMAX
+with the causal mask at offset n_keys-1, probs.V MATMUL, each rounded to fp16), and the existing
+entry points that run those nodes on the GPU (vkllm_op_matmul, vkllm_op_softmax). Two calls run in
+a row (the second with a different key count, so stale scratch from the first call would show).
+The kernels behind it contain no waits, so a fault would surface as a CUDA error when the stream is
+synchronised by the read-back. This file sorts last so that a run that stops at the first failure
+has already run every other test; it also passes alone in a fresh process."""
 import ctypes as C
 
 import numpy as np
@@ -23,6 +24,16 @@ def close(gpu, ref, rel=2e-3):
     scale = max(np.abs(r).max(), 1e-6)
     bad = np.abs(g - r) > rel * np.abs(r) + rel * scale
     assert not bad.any(), f"{bad.sum()} of {bad.size} mismatches; max abs diff {np.abs(g - r).max()}"
+
+
+def attention_via_oracle(orc, q, kc, vc, H, hd, n_keys):
+    """The reference graph's attention nodes on the CPU (quirk Q1 included: at n_keys == hd the
+    probs.V node reads V transposed, by the same shape predicate)."""
+    ks = np.ascontiguousarray(kc[:, :, :n_keys, :])
+    vs = np.ascontiguousarray(vc[:, :, :n_keys, :])
+    scores = orc.matmul(q, ks, (1, H, 1, n_keys), 1.0 / np.sqrt(hd), 0)
+    probs = orc.softmax(scores, 1, n_keys - 1)
+    return orc.matmul(probs, vs, (1, H, 1, hd), 1.0, 0).reshape(H, hd)
 
 
 def attention_via_ops(vk, ctx, Qt, Kt, Vt, H, hd, n_keys):
@@ -50,7 +61,7 @@ def attention_via_ops(vk, ctx, Qt, Kt, Vt, H, hd, n_keys):
 
 @pytest.mark.parametrize("H,hd,rows,keys", [(6, 48, 256, (100, 37)), (32, 128, 1024, (777, 513)),
                                             (6, 48, 256, (48, 201))])
-def test_noalloc_attention_matches_op_path(vk, ctx, H, hd, rows, keys):
+def test_noalloc_attention_matches_oracle_and_op_path(vk, ctx, orc, H, hd, rows, keys):
     lib = vk.lib()
     q = RNG.uniform(-1, 1, size=(1, H, 1, hd)).astype(np.float16)
     kc = RNG.uniform(-1, 1, size=(1, H, rows, hd)).astype(np.float16)
@@ -70,6 +81,7 @@ def test_noalloc_attention_matches_op_path(vk, ctx, H, hd, rows, keys):
             assert err == vk.OK
             got = vk.fetch(ctx, Ot).reshape(H, hd)  # same stream: ordered after the attention kernels
             close(got, ref)
+            close(got, attention_via_oracle(orc, q, kc, vc, H, hd, n_keys))
     finally:
         for t in (Qt, Kt, Vt, Ot):
             vk.tensor_free(ctx, t)
@@ -82,3 +94,14 @@ def test_noalloc_attention_rejects_sizes_beyond_the_scratch(vk, ctx):
     assert lib.vkllm_b200_attention_decode_noalloc(dummy, dummy, dummy, 64, 128, 8192, 1, 1.0, dummy, None) == vk.ARGS
     assert lib.vkllm_b200_attention_decode_noalloc(dummy, dummy, dummy, 8, 258, 64, 1, 1.0, dummy, None) == vk.ARGS
     assert lib.vkllm_b200_attention_decode_noalloc(dummy, dummy, dummy, 8, 128, 64, 65, 1.0, dummy, None) == vk.ARGS
+
+
+def test_noalloc_attention_rejects_misaligned_caches(vk, ctx):
+    """Cache rows are read 8 bytes at a time: a cache pointer off an 8-byte boundary (a sub-view of
+    a larger fp16 buffer, say) is refused before any launch instead of faulting on the GPU."""
+    lib = vk.lib()
+    ok, odd2, odd1 = C.c_void_p(256), C.c_void_p(258), C.c_void_p(257)  # never dereferenced
+    assert lib.vkllm_b200_attention_decode_noalloc(ok, odd2, ok, 8, 128, 64, 4, 1.0, ok, None) == vk.ARGS
+    assert lib.vkllm_b200_attention_decode_noalloc(ok, ok, odd2, 8, 128, 64, 4, 1.0, ok, None) == vk.ARGS
+    assert lib.vkllm_b200_attention_decode_noalloc(odd1, ok, ok, 8, 128, 64, 4, 1.0, ok, None) == vk.ARGS
+    assert lib.vkllm_b200_attention_decode_noalloc(ok, ok, ok, 8, 128, 64, 4, 1.0, odd1, None) == vk.ARGS

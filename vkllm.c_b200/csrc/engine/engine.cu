@@ -1372,6 +1372,9 @@ extern "C" vkllm_err_t vkllm_b200_attention_decode_noalloc(const void *q, const 
     _CHECK_ARGS(q && kcache && vcache && out);
     _CHECK_ARGS(heads > 0 && head_dim > 0 && cache_rows > 0);
     _CHECK_ARGS(n_keys >= 1 && n_keys <= cache_rows);
+    // Cache rows are read as 8-byte words (k_dec_attn_scores, k_dec_attn_pv); q and out per half.
+    _CHECK_ARGS((((uintptr_t)kcache | (uintptr_t)vcache) & 7u) == 0);
+    _CHECK_ARGS((((uintptr_t)q | (uintptr_t)out) & 1u) == 0);
     if (heads > kNoAllocMaxHeads || head_dim > kNoAllocMaxHeadDim || head_dim % 4 != 0 ||
         (uint64_t)heads * cache_rows > kNoAllocMaxScoreRows)
     {

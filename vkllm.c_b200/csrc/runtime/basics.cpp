@@ -244,7 +244,7 @@ extern "C" vkllm_err_t vkllm_hashmap_remove(struct vkllm_hashmap *map, const cha
         return VKLLM_ERR_ARGS;
     long s = find_slot(map, key);
     if (s < 0)
-        return VKLLM_ERR_ARGS;
+        return VKLLM_ERR_OK; // removing an absent key is not an error (src/core/vkllm_hashmap.c:197-215)
     free_key(&map->entries[s]);
     map->entries[s].key = (char *)kTombstone;
     map->entries[s].occupied = false;
