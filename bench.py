@@ -179,24 +179,37 @@ def download_weights(vk, ctx, model, cfg):
     return w
 
 
-def cpu_decode_sample(weights, cfg, n_steps=3, threads=0):
-    """Times n single-token decode steps of the oracle (reference algorithm on the CPU) at positions
-    0..n-1. Returns (tok/s, threads used)."""
+def cpu_decode_sample(weights, cfg, n_steps=3, threads=0, prompt=None):
+    """Times n single-token decode steps of the oracle (reference algorithm on the CPU). With a
+    prompt, the steps run at positions len(prompt) .. len(prompt)+n-1 after an untimed prefill of
+    it (the GPU arm's configuration); without one, at positions 1..n. Returns (tok/s, threads used,
+    prefill seconds or None, the greedy tokens: the prefill's prediction then one per step)."""
     import oracle
 
     used = oracle.threads(threads or os.cpu_count() or 1)
+    start = len(prompt) if prompt is not None else 1
+    ctx = start + n_steps + 8
     ocfg = dict(D=cfg["embedding_length"], H=cfg["head_count"], F=cfg["ffn_length"], V=cfg["vocab_size"],
-                L=cfg["block_count"], ctx=64, eps=cfg["rms_eps"], rope_base=cfg["rope_freq_base"])
-    m = oracle.Llama2(ocfg, weights, ctx=64)
-    tok = 1
-    m.step([tok], 0)  # warm-up (page-in)
+                L=cfg["block_count"], ctx=ctx, eps=cfg["rms_eps"], rope_base=cfg["rope_freq_base"])
+    m = oracle.Llama2(ocfg, weights, ctx=ctx)
+    prefill_s = None
+    if prompt is not None:
+        t0 = time.perf_counter()
+        _, out = m.step(list(prompt), 0)
+        prefill_s = time.perf_counter() - t0
+        tok = int(out[-1])
+    else:
+        tok = 1
+        m.step([tok], 0)  # warm-up (page-in)
+    toks = [tok]
     t0 = time.perf_counter()
     for i in range(n_steps):
-        _, out = m.step([tok], i + 1)
+        _, out = m.step([tok], start + i)
         tok = int(out[-1])
+        toks.append(tok)
     dt = time.perf_counter() - t0
     m.close()
-    return n_steps / dt, used
+    return n_steps / dt, used, prefill_s, toks
 
 
 def prefill_gemm_roofline(vk, l, model, cfg, stream):
@@ -651,11 +664,17 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             w = download_weights(vk, ctx, model, cfg)
-            tps, thr = cpu_decode_sample(w, cfg, n_steps=args.cpu_steps)
+            tps, thr, cpu_prefill_s, ref_toks = cpu_decode_sample(w, cfg, n_steps=args.cpu_steps, prompt=prompt)
             result["cpu_baseline"] = {"value": round(tps, 4), "unit": "tokens/s", "cores": thr, "kind": "port",
                                       "sample": f"{args.cpu_steps} single-token decode steps of the same 7B weights at "
-                                                f"positions 1..{args.cpu_steps} (oracle/ C++ restatement of the reference "
-                                                f"shaders, OpenMP)"}
+                                                f"positions {PROMPT_LEN}..{PROMPT_LEN + args.cpu_steps - 1}, after an untimed "
+                                                f"prefill of the same {PROMPT_LEN}-token prompt ({cpu_prefill_s:.1f} s) "
+                                                f"(oracle/ C++ restatement of the reference shaders, OpenMP)"}
+            # The same run is the parity check of the benchmarked configuration: the oracle's prefill
+            # prediction and greedy tokens against the GPU's (API prefill, then the device loop).
+            gpu_toks = [first] + [int(t) for t in toks[:args.cpu_steps]]
+            result["parity"] = {"config": "llama2-7b, this run's weights and prompt", "tokens_gpu": gpu_toks,
+                                "tokens_oracle": ref_toks, "match": gpu_toks == ref_toks}
             del w
         except Exception as e:  # the baseline must not void the GPU measurement
             result["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
@@ -713,7 +732,8 @@ def run_reference(args, world, rank, local):
     mat("output.weight", V, D)
     gen_s = time.perf_counter() - t_gen
     steps = max(1, min(args.steps, 4))
-    tps, thr = cpu_decode_sample(w, cfg, n_steps=steps)
+    prompt = prompt_tokens(0)
+    tps, thr, prefill_s, _ = cpu_decode_sample(w, cfg, n_steps=steps, prompt=prompt)
     return {
         "impl": "reference",
         "metric": "LLaMA2-7B fp16 decode tok/s (batch 1)",
@@ -730,8 +750,9 @@ def run_reference(args, world, rank, local):
         "data": "synthetic (same generator bits as the GPU arm)",
         "config": {"workload": "llama2-7b fp16 batch-1 greedy decode (BASELINE configs[2])", "model": "llama2-7b-arch"},
         "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": thr, "kind": "port",
-                         "sample": f"{steps} single-token decode steps at positions 1..{steps}; weights regenerated "
-                                   f"on the CPU in {gen_s:.1f} s (not timed)"},
+                         "sample": f"{steps} single-token decode steps at positions {PROMPT_LEN}..{PROMPT_LEN + steps - 1} "
+                                   f"after an untimed prefill of the GPU arm's {PROMPT_LEN}-token prompt "
+                                   f"({prefill_s:.1f} s); weights regenerated on the CPU in {gen_s:.1f} s (not timed)"},
         "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "vkllm.c itself needs Vulkan, absent on this box; this is its algorithm restated in C++ (oracle/)",
     }

@@ -46,6 +46,7 @@ def lib():
         V = C.POINTER(_View)
         sig = {
             "oracle_threads": (C.c_int, [C.c_int]),
+            "oracle_set_arith": (C.c_int, [C.c_int]),
             "oracle_op_matmul": (C.c_int, [V, V, V, C.c_float, C.c_int]),
             "oracle_op_rmsnorm": (C.c_int, [V, C.c_void_p, V, C.c_float]),
             "oracle_op_rope": (C.c_int, [V, V, C.c_uint32, C.c_float, C.c_int]),
@@ -72,6 +73,13 @@ def lib():
 
 def threads(n=0):
     return lib().oracle_threads(n)
+
+
+def set_arith(mode):
+    """"fp32" (default): the f16f32 shader variants, the parity target. "fp16": the variants a device
+    with shaderFloat16 selects (fp16 GEMV accumulation, fp16 dot pairs in the GEMM, fp16 softmax and
+    RoPE). Returns the previous mode."""
+    return "fp16" if lib().oracle_set_arith(1 if mode == "fp16" else 0) else "fp32"
 
 
 def _view(arr):

@@ -9,10 +9,20 @@
 // baseline may load this library; the product never does.
 //
 // Parity pins: the reference ships no golden vectors. The per-op formulas are pinned to the CPU
-// references inside the reference's own tests (tests/vkllm_test_op_*.c), re-run here on their
-// shapes by tests/test_oracle.py; the reference itself cannot be built or run here (Vulkan, VMA,
-// gguf-tools, libcheck and Bazel are absent), so end-to-end token parity is pinned to this
-// restatement only.
+// references inside the reference's own tests (tests/vkllm_test_op_*.c), compiled from its checkout
+// by oracle/refpin/Makefile; tests/golden/ref_ops.npz holds their outputs and tests/test_oracle.py
+// checks this restatement against them. The reference's GPU path cannot run here (Vulkan, VMA,
+// gguf-tools and Bazel are absent), so end-to-end token parity is pinned to this restatement.
+//
+// Two arithmetic modes (oracle_set_arith): 0 = the f16f32 variants above (the default, and the parity
+// target); 1 = the variants a device with shaderFloat16 selects (src/core/vkllm_gpu_device.c:232,
+// src/core/vkllm_op_matmul.c:92-102, vkllm_op_softmax.c:22-33, vkllm_op_rope.c:20-30): the GEMV
+// accumulates in fp16 (vkllm_mat_mul_vec.comp f16f16), the GEMM forms each dot(f16vec2) in fp16
+// (vkllm_matmul_t*.comp f16f16f16), and softmax and RoPE compute in fp16 (LOAD_DTYPE float16_t).
+// Each fp16 operation is modelled as the fp32 operation rounded to fp16 (exact for products and
+// sums of two fp16 values up to a rare double rounding); the GPU's own fp16 exp/sin/cos/pow are
+// modelled as the fp32 libm result rounded to fp16. BIN and ARG_MAX give the same results in both
+// modes on fp16 data, RMSNORM is fp32 in both.
 //
 // fp16 <-> fp32 conversions use round-to-nearest-even (GPU conversion semantics). Transcendentals
 // (expf, powf, sinf, cosf, 1/sqrtf) come from the host libm in fp32.
@@ -104,6 +114,8 @@ inline float round16(float f)
 {
     return h2f(f2h(f));
 }
+
+int g_arith16 = 0; // 1: the shaderFloat16 variants (oracle_set_arith)
 
 // ------------------------------------------------------------------------------------------------
 // Strided views: dtype 1 = f32, 2 = f16, 4 = u32 (vkllm_dtype_t values); element strides.
@@ -216,13 +228,27 @@ void gemv(const View &a, const View &w, const View &out, float scale, int act)
                     if (i + q < K)
                         d += a.get(ao + (uint64_t)(i + q) * a.stride[3]) * w.get(wo + (uint64_t)(i + q) * w.stride[3]);
                 }
-                acc = d + acc;
+                // f16f16: acc = ACC_DTYPE(dot(vec4, vec4)) + acc, both in fp16
+                acc = g_arith16 ? round16(round16(d) + acc) : d + acc;
             }
             lanes[l] = acc;
         }
-        float v = subgroup_add(lanes) * scale;
-        if (act == 1)
-            v = silu(v);
+        float v;
+        if (g_arith16)
+        {
+            for (int o = 16; o > 0; o >>= 1) // subgroupAdd in fp16
+                for (int l = 0; l < o; ++l)
+                    lanes[l] = round16(lanes[l] + lanes[l + o]);
+            v = round16(lanes[0] * round16(scale));
+            if (act == 1)
+                v = round16(v / round16(1.0f + round16(expf(-v))));
+        }
+        else
+        {
+            v = subgroup_add(lanes) * scale;
+            if (act == 1)
+                v = silu(v);
+        }
         out.set(out.off(b, c, h, col), v);
     }
 }
@@ -230,40 +256,80 @@ void gemv(const View &a, const View &w, const View &out, float scale, int act)
 // GEMM (src/shaders/vkllm_matmul_t1.comp:90-251 for B [N,K], vkllm_matmul_t0.comp:92-245 for B [K,N]):
 // fp32 sum over K in order of pairwise fp32 dot(vec2) terms; * scale; SiLU; store. Broadcast: a
 // size-1 batch/channel axis is reused (src/core/vkllm_op_matmul.c:65-91).
+//
+// Every output element is acc_{k+2} = acc_k + (a_k b_k + a_{k+1} b_{k+1}) over k = 0, 2, 4, ..., with
+// an odd K padded by a zero pair. The loops below compute 8-32 columns of a row at once (a panel of
+// B converted to fp32 and laid out k-major per block of columns), which the compiler vectorises
+// across columns; each column still sees exactly that sequence of operations.
+constexpr uint32_t kGemmNB = 32; // columns per panel
+constexpr uint32_t kGemmMB = 4;  // rows per register block
+
 void gemm(const View &a, const View &bm, const View &out, bool trans_b, float scale, int act)
 {
-    uint32_t M = out.shape[2], N = out.shape[3], K = a.shape[3];
-    uint64_t total = (uint64_t)out.shape[0] * out.shape[1] * M;
-#pragma omp parallel for schedule(dynamic, 4)
-    for (int64_t idx = 0; idx < (int64_t)total; ++idx)
+    const uint32_t M = out.shape[2], N = out.shape[3], K = a.shape[3], Kp = K + (K & 1u);
+    const uint32_t nb = (N + kGemmNB - 1) / kGemmNB, batches = out.shape[0] * out.shape[1];
+    // A rows in fp32, zero-padded to Kp, for every batch.
+    std::vector<float> af((size_t)batches * M * Kp, 0.f);
+#pragma omp parallel for schedule(static)
+    for (int64_t idx = 0; idx < (int64_t)batches * M; ++idx)
     {
-        uint32_t m = (uint32_t)(idx % M);
-        uint64_t z = (uint64_t)idx / M;
-        uint32_t c = (uint32_t)(z % out.shape[1]), b = (uint32_t)(z / out.shape[1]);
+        uint32_t m = (uint32_t)(idx % M), z = (uint32_t)(idx / M);
+        uint32_t c = z % out.shape[1], b = z / out.shape[1];
         uint64_t ao = (uint64_t)(a.shape[0] == 1 ? 0 : b) * a.stride[0] + (uint64_t)(a.shape[1] == 1 ? 0 : c) * a.stride[1] +
                       (uint64_t)m * a.stride[2];
-        uint64_t bo = (uint64_t)(bm.shape[0] == 1 ? 0 : b) * bm.stride[0] +
-                      (uint64_t)(bm.shape[1] == 1 ? 0 : c) * bm.stride[1];
-        std::vector<float> arow(K + 1, 0.f);
+        float *dst = &af[(size_t)idx * Kp];
         for (uint32_t k = 0; k < K; ++k)
-            arow[k] = a.get(ao + (uint64_t)k * a.stride[3]);
-        for (uint32_t n = 0; n < N; ++n)
+            dst[k] = a.get(ao + (uint64_t)k * a.stride[3]);
+    }
+#pragma omp parallel
+    {
+        std::vector<float> panel((size_t)Kp * kGemmNB);
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t t = 0; t < (int64_t)batches * nb; ++t)
         {
-            float acc = 0.f;
-            for (uint32_t k = 0; k < K; k += 2)
+            const uint32_t z = (uint32_t)(t / nb), n0 = (uint32_t)(t % nb) * kGemmNB;
+            const uint32_t c = z % out.shape[1], b = z / out.shape[1];
+            const uint32_t nn = std::min(kGemmNB, N - n0);
+            const uint64_t bo = (uint64_t)(bm.shape[0] == 1 ? 0 : b) * bm.stride[0] +
+                                (uint64_t)(bm.shape[1] == 1 ? 0 : c) * bm.stride[1];
+            for (uint32_t k = 0; k < Kp; ++k)
+                for (uint32_t j = 0; j < kGemmNB; ++j)
+                {
+                    float v = 0.f;
+                    if (k < K && j < nn)
+                        v = trans_b ? bm.get(bo + (uint64_t)(n0 + j) * bm.stride[2] + (uint64_t)k * bm.stride[3])
+                                    : bm.get(bo + (uint64_t)k * bm.stride[2] + (uint64_t)(n0 + j) * bm.stride[3]);
+                    panel[(size_t)k * kGemmNB + j] = v;
+                }
+            const float *A = &af[(size_t)z * M * Kp];
+            for (uint32_t m0 = 0; m0 < M; m0 += kGemmMB)
             {
-                float b0 = trans_b ? bm.get(bo + (uint64_t)n * bm.stride[2] + (uint64_t)k * bm.stride[3])
-                                   : bm.get(bo + (uint64_t)k * bm.stride[2] + (uint64_t)n * bm.stride[3]);
-                float b1 = 0.f;
-                if (k + 1 < K)
-                    b1 = trans_b ? bm.get(bo + (uint64_t)n * bm.stride[2] + (uint64_t)(k + 1) * bm.stride[3])
-                                 : bm.get(bo + (uint64_t)(k + 1) * bm.stride[2] + (uint64_t)n * bm.stride[3]);
-                acc += arow[k] * b0 + arow[k + 1] * b1;
+                const uint32_t mm = std::min(kGemmMB, M - m0);
+                float acc[kGemmMB][kGemmNB] = {};
+                for (uint32_t k = 0; k < Kp; k += 2)
+                {
+                    const float *b0 = &panel[(size_t)k * kGemmNB], *b1 = b0 + kGemmNB;
+                    for (uint32_t r = 0; r < kGemmMB; ++r)
+                    {
+                        const float a0 = r < mm ? A[(size_t)(m0 + r) * Kp + k] : 0.f;
+                        const float a1 = r < mm ? A[(size_t)(m0 + r) * Kp + k + 1] : 0.f;
+                        if (g_arith16) // f16f16f16: float(dot(f16vec2, f16vec2)), the dot in fp16
+                            for (uint32_t j = 0; j < kGemmNB; ++j)
+                                acc[r][j] += round16(round16(a0 * b0[j]) + round16(a1 * b1[j]));
+                        else
+                            for (uint32_t j = 0; j < kGemmNB; ++j)
+                                acc[r][j] += a0 * b0[j] + a1 * b1[j];
+                    }
+                }
+                for (uint32_t r = 0; r < mm; ++r)
+                    for (uint32_t j = 0; j < nn; ++j)
+                    {
+                        float v = acc[r][j] * scale;
+                        if (act == 1)
+                            v = silu(v);
+                        out.set(out.off(b, c, m0 + r, n0 + j), v);
+                    }
             }
-            float v = acc * scale;
-            if (act == 1)
-                v = silu(v);
-            out.set(out.off(b, c, m, n), v);
         }
     }
 }
@@ -332,9 +398,18 @@ void rope(const View &in, const View &out, uint32_t offset, float base, int neox
                         o0 = out.off(b, c, h, 2 * w);
                         o1 = o0 + out.stride[3];
                     }
+                    float v0 = in.get(i0), v1 = in.get(i1);
+                    if (g_arith16) // LOAD_DTYPE float16_t: every value and operation in fp16
+                    {
+                        float e = round16(round16((float)(2 * w)) / round16((float)in.shape[3]));
+                        float f = round16(round16((float)(offset + h)) / round16(powf(round16(base), e)));
+                        float cs = round16(cosf(f)), sn = round16(sinf(f));
+                        out.set(o0, round16(cs * v0) - round16(sn * v1));
+                        out.set(o1, round16(sn * v0) + round16(cs * v1));
+                        continue;
+                    }
                     float f = (float)(offset + h) / powf(base, (float)(2 * w) / (float)in.shape[3]);
                     float cs = cosf(f), sn = sinf(f);
-                    float v0 = in.get(i0), v1 = in.get(i1);
                     out.set(o0, cs * v0 - sn * v1);
                     out.set(o1, sn * v0 + cs * v1);
                 }
@@ -360,6 +435,8 @@ void softmax(const View &in_as_out, const View &out, int seq_mask, uint32_t offs
                     lm[l] = m;
                 }
                 float gm = subgroup_max(lm);
+                // f16f16 (LOAD_DTYPE float16_t): differences, exponentials, sums and quotients in fp16
+                auto ex = [&](float x) { return g_arith16 ? round16(expf(round16(x - gm))) : expf(x - gm); };
                 for (uint32_t l = 0; l < 32; ++l)
                 {
                     float s = 0.f;
@@ -367,18 +444,28 @@ void softmax(const View &in_as_out, const View &out, int seq_mask, uint32_t offs
                     {
                         if (seq_mask > 0 && i > h + offsets)
                             continue;
-                        s += expf(in_as_out.get(base + (uint64_t)i * out.stride[3]) - gm);
+                        s = g_arith16 ? round16(s + ex(in_as_out.get(base + (uint64_t)i * out.stride[3])))
+                                      : s + ex(in_as_out.get(base + (uint64_t)i * out.stride[3]));
                     }
                     ls[l] = s;
                 }
-                float gs = subgroup_add(ls);
+                float gs;
+                if (g_arith16)
+                {
+                    for (int o = 16; o > 0; o >>= 1)
+                        for (int l = 0; l < o; ++l)
+                            ls[l] = round16(ls[l] + ls[l + o]);
+                    gs = ls[0];
+                }
+                else
+                    gs = subgroup_add(ls);
                 for (uint32_t i = 0; i < W; ++i)
                 {
                     uint64_t o = base + (uint64_t)i * out.stride[3];
                     if (seq_mask > 0 && i > h + offsets)
                         out.set(o, 0.f);
                     else
-                        out.set(o, expf(in_as_out.get(o) - gm) / gs);
+                        out.set(o, ex(in_as_out.get(o)) / gs);
                 }
             }
 }
@@ -466,6 +553,14 @@ struct oracle_view
 static View from(const oracle_view *v)
 {
     return mkview(v->dtype, v->shape, v->stride, v->data);
+}
+
+// 0: f16f32 arithmetic (fp32 math, the default); 1: the shaderFloat16 variants. Returns the previous mode.
+int oracle_set_arith(int mode)
+{
+    int old = g_arith16;
+    g_arith16 = mode ? 1 : 0;
+    return old;
 }
 
 int oracle_threads(int n)
