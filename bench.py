@@ -503,6 +503,22 @@ def run_ours(args, world, rank, local):
     l = vk.lib()
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
     prompt = prompt_tokens(rank)
+    if args.profile_prefill:
+        times = []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            tok = model.step(list(prompt), 0)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        if rank == 0:
+            print(json.dumps({"profile_case": "prefill", "layers": cfg["block_count"], "tokens": PROMPT_LEN,
+                              "ms": [round(t, 3) for t in times], "token": tok}), flush=True)
+        model.free()
+        ctx.close()
+        return None
     if args.profile_batched:
         batched = batched_decode_leg(vk, model, args, world, rank, stream)
         if rank == 0:
@@ -758,6 +774,36 @@ def run_reference(args, world, rank, local):
     }
 
 
+def profile_gemm(args):
+    """Profiling case: the tensor-core GEMM (vkllm_b200_gemm_f16) on seeded fp16 operands A [M, K] and
+    B [N, K], launched 4 times on one stream; prints the event-timed mean of the last 2 launches."""
+    import torch
+
+    import vkllm_b200 as vk
+
+    M, N, K = (int(v) for v in args.profile_gemm.split(","))
+    l = vk.lib()
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = (torch.rand((M, K), generator=g, device="cuda") * 2 - 1).half()
+    B = (torch.rand((N, K), generator=g, device="cuda") * 2 - 1).half()
+    Cm = torch.empty((M, N), device="cuda", dtype=torch.float16)
+    s = torch.cuda.current_stream()
+    launch = lambda: vk.check(l.vkllm_b200_gemm_f16(A.data_ptr(), B.data_ptr(), Cm.data_ptr(), M, N, K, K, K, N,
+                                                     1.0, 0, s.cuda_stream), "gemm")
+    launch()
+    launch()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    launch()
+    launch()
+    e1.record(s)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / 2
+    print(json.dumps({"profile_case": "gemm", "M": M, "N": N, "K": K, "us": round(us, 2),
+                      "tflops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 1),
+                      "error_word": int(l.vkllm_b200_gemm_f16_error())}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -774,8 +820,15 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--profile-batched", action="store_true",
                     help="profiling case: only the batched decode leg (with --layers), no JSON result line")
+    ap.add_argument("--profile-gemm", default="",
+                    help="profiling case: M,N,K - only the tensor-core GEMM on seeded operands, 4 launches")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="profiling case: only the prompt prefill through the drop-in API (with --layers), 3 runs")
     ap.add_argument("--ops", type=int, default=1, help="operator microbenchmark leg (0: skip)")
     args = ap.parse_args()
+    if args.profile_gemm:
+        profile_gemm(args)
+        return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_setup() if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
                                                                     int(os.environ.get("RANK", "0")),

@@ -2,12 +2,15 @@
 model): every sequence of the batch must decode exactly what it decodes alone. Each sequence is
 prefilled through the drop-in graph API, moved into its batch slot, then all decode together on the
 tensor-core GEMM path (M = number of sequences). Reference: the CPU oracle run on each sequence
-separately (prefill + the same number of greedy steps). Bar: identical
-greedy token ids for the first 32 steps of every sequence, and fp16 logits within max-abs 2e-2 /
-mean-abs 2e-3 at every step. A token mismatch fails with the reference's logits of both tokens and
-its top two, so a tie broken the other way by a different fp32 summation order is visible as such."""
+separately (prefill + the same number of greedy steps). Bar: fp16 logits
+within max-abs 2e-2 / mean-abs 2e-3 at every compared step, and identical greedy token ids for 32
+steps of every sequence, except at a reference tie at fp16 resolution (its top two logits within one
+fp16 ulp), which tests/parity.py reports as a warning with both tokens' logits; the comparison of
+that sequence stops there, since later inputs differ."""
 import numpy as np
 import pytest
+
+from parity import compare_greedy
 
 pytestmark = pytest.mark.gpu
 
@@ -53,14 +56,8 @@ def test_batched_decode_matches_each_sequence_alone(vk, ctx, tiny_gguf, orc, var
         assert firsts[i] == ref_toks[0]
         ours = [int(t) for t in toks[:, i]]
         ref = ref_toks[1:N_STEPS + 1]
-        for s in range(N_STEPS):
-            r = np.asarray(ref_logits[s + 1], dtype=np.float32)
-            d = np.abs(logits[s][i].astype(np.float32) - r)
-            assert d.max() <= 2e-2 and d.mean() <= 2e-3, (i, s, d.max(), d.mean())
-            if ours[s] != ref[s]:
-                raise AssertionError(f"sequence {i} step {s}: token {ours[s]} vs reference {ref[s]}; reference "
-                                     f"logits {r[ref[s]]} (its choice) / {r[ours[s]]} (ours), its top two "
-                                     f"{np.sort(r)[-2:]}; our logits {logits[s][i][ref[s]]} / {logits[s][i][ours[s]]}")
+        compare_greedy(ours, [logits[st][i] for st in range(N_STEPS)], ref, ref_logits[1:N_STEPS + 1], 2e-2, 2e-3,
+                       f"{variant} sequence {i}")
 
 
 def test_batch_rejects_a_sequence_past_its_capacity(vk, ctx, tiny_gguf):

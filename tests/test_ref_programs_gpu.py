@@ -15,7 +15,18 @@ tests/vkllm_test_infer_gguf.c is the reference's token loop: load a GGUF, tokeni
 then per token tensor_new / graph_new / build_graph / init / upload / run / post_run / read the
 mapped argmax / graph_free, printing the generated pieces. It runs here on the tiny synthetic GGUF
 (whose vocabulary pieces are "<tN>", so the printed text gives the token ids back), and its tokens
-must equal the CPU oracle's greedy tokens from the same prompt ids for the first 32 steps."""
+must equal the CPU oracle's greedy tokens from the same prompt ids for the first 32 steps.
+
+Three outcomes are the reference's own, not this library's, and the checks below name them exactly:
+  * vkllm_test_op_arg_max compares the GPU with a first-maximum CPU function, while the reference's
+    shader breaks ties by its lane/tree rule (src/shaders/vkllm_arg_max.comp:54-90), which this
+    library keeps. With fp16 inputs in [-1000, 1000] equal maxima occur; a mismatch is accepted
+    only where the two indices hold the same value.
+  * vkllm_test_tensor_reshape's table has three "valid" cases whose element counts differ
+    (entries 4, 8 and 13: [4,8,64,64] -> [1,1,1024,256] twice, [8,16,128,64] -> [2,64,256,64]); the
+    program's own count check fails there before any library call.
+  * vkllm_test_infer_gguf returns its last vkllm_err_t, and VKLLM_ERR_OK is 1
+    (src/core/vkllm_errors.inc:6), so a successful run exits with status 1."""
 import os
 import re
 import subprocess
@@ -40,12 +51,45 @@ def program(name):
     return path
 
 
+RESHAPE_TABLE_BUGS = {4, 8, 13}  # entries of the reshape program's table with unequal element counts
+
+
+def failed_cases(out):
+    """(test name, loop index) of every "...:<name>:<i>: Failed" line of the check runner."""
+    return {(m.group(1), int(m.group(2))) for m in re.finditer(r":(\w+):(\d+): Failed", out)}
+
+
+def argmax_mismatches_are_ties(out):
+    """Every mismatch block the arg_max program prints lists the row with "(gpu max)" and "(host max)"
+    marks; True when each block's two marked values are equal."""
+    blocks = out.split("Mismatch at index")[1:]
+    if not blocks:
+        return False
+    for b in blocks:
+        g = re.search(r"\]: (-?[0-9.]+) \(gpu max\)", b)
+        h = re.search(r"\]: (-?[0-9.]+) \(host max\)", b)
+        if not g or not h or float(g.group(1)) != float(h.group(1)):
+            return False
+    return True
+
+
 @pytest.mark.parametrize("name", OP_PROGRAMS)
 def test_reference_op_program_passes(ctx, name):
     r = subprocess.run([program(name)], capture_output=True, text=True, timeout=900)
     out = r.stdout + r.stderr
     summary = [l for l in out.splitlines() if "Checks:" in l]
-    assert r.returncode == 0 and summary and "Failures: 0" in summary[-1], out[-4000:]
+    assert summary, out[-4000:]
+    if "Failures: 0" in summary[-1]:
+        assert r.returncode == 0, out[-4000:]
+        return
+    failed = failed_cases(out)
+    if name == "vkllm_test_op_arg_max":
+        assert argmax_mismatches_are_ties(out), out[-6000:]
+    elif name == "vkllm_test_tensor_reshape":
+        assert failed == {("test_tensor_reshape_valid", i) for i in RESHAPE_TABLE_BUGS}, (failed, out[-4000:])
+        assert out.count("Assertion 'orig_total == new_total' failed") == len(RESHAPE_TABLE_BUGS), out[-4000:]
+    else:
+        raise AssertionError(out[-4000:])
 
 
 def test_reference_token_loop_program(ctx, tiny_gguf, orc):
@@ -55,7 +99,7 @@ def test_reference_token_loop_program(ctx, tiny_gguf, orc):
     n_tokens = 40
     r = subprocess.run([program("vkllm_test_infer_gguf"), path, str(n_tokens)], capture_output=True, text=True,
                        timeout=600)
-    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-4000:])
+    assert r.returncode == 1, (r.returncode, r.stdout[-2000:], r.stderr[-4000:])  # VKLLM_ERR_OK
     m = re.search(r"input ids: ([0-9 ]+)", r.stderr)
     assert m, r.stderr[-2000:]
     prompt = [int(t) for t in m.group(1).split()]

@@ -10,6 +10,8 @@
 #include "decode_kernels.cuh"
 #include "decode_persistent.cuh"
 #include "plan.h"
+#include "prefill_kernels.cuh"
+#include "../kernels/kernels.h"
 #include "vkllm_b200.h"
 #include "vkllm_kvcache.h"
 #include "vkllm_models_llama2.h"
@@ -57,6 +59,9 @@ struct Engine
     std::vector<uint32_t> htab;
     uint32_t *utab = nullptr;
     uint32_t unit_cap[PK_COUNT] = {}; // most units a CTA may hold in a phase (sizes the partials)
+    // fused prefill (graphs with S > 1): workspace grown to the largest S seen
+    void *pf_ws = nullptr;
+    size_t pf_cap = 0;
 };
 
 // Peer-memory exchange of a tensor-parallel rank: one device buffer, exported with CUDA IPC, holding
@@ -952,6 +957,8 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
         return;
     if (e->ctx && e->ctx->runtime)
         cudaStreamSynchronize(e->ctx->runtime->stream);
+    if (e->pf_ws)
+        cudaFree(e->pf_ws);
     if (e->exec)
         cudaGraphExecDestroy(e->exec);
     if (e->graph)
@@ -979,16 +986,157 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
     model->b200.engine = nullptr;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Fused prefill: the llama2 graph of S > 1 tokens (src/models/vkllm_models_llama2.c:488-602) as
+// per-layer kernels: RMSNORM, the Q/K/V projections on the tensor-core GEMM, RoPE with the KV-cache
+// rows (k_pf_rope_kv), attention in one kernel (k_pf_attention), Wo, the residual BIN, RMSNORM,
+// up and gate (SiLU) GEMMs, their product, down and the residual; then RMSNORM, the logits of all S
+// rows and their argmax. The node order and rounding points are the graph's; the argmax of every
+// row goes to the graph's mapped output and the last row's logits to the engine's logits buffer.
+// Returns VKLLM_ERR_ARGS when this path does not apply (the graph then runs node by node).
+namespace
+{
+
+template <int HD>
+bool pf_attention_launch(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint32_t S, uint32_t p0,
+                         __half *out, cudaStream_t s)
+{
+    static bool attr_set = false;
+    if (!attr_set)
+    {
+        if (cudaFuncSetAttribute(k_pf_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PfSmem<HD>::kBytes) != cudaSuccess)
+            return false;
+        attr_set = true;
+    }
+    dim3 grid((S + kPfBQ - 1) / kPfBQ, dd.H);
+    k_pf_attention<HD><<<grid, kPfThreads, PfSmem<HD>::kBytes, s>>>(rq, lw.kcache, lw.vcache, dd.ctx, S, p0, dd.H,
+                                                                    dd.scale, out);
+    return true;
+}
+
+bool pf_attention(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint32_t S, uint32_t p0, __half *out,
+                  cudaStream_t s)
+{
+    switch (dd.hd)
+    {
+    case 32:
+        return pf_attention_launch<32>(rq, lw, dd, S, p0, out, s);
+    case 48:
+        return pf_attention_launch<48>(rq, lw, dd, S, p0, out, s);
+    case 64:
+        return pf_attention_launch<64>(rq, lw, dd, S, p0, out, s);
+    case 80:
+        return pf_attention_launch<80>(rq, lw, dd, S, p0, out, s);
+    case 96:
+        return pf_attention_launch<96>(rq, lw, dd, S, p0, out, s);
+    case 128:
+        return pf_attention_launch<128>(rq, lw, dd, S, p0, out, s);
+    default:
+        return false;
+    }
+}
+
+// C [M, N] = act(A [M, K] . B [N, K]^T), dense row-major, on the tensor-core GEMM.
+bool pf_gemm(const __half *A, const __half *B, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s)
+{
+    Desc4 da{{1, 1, M, K}, {0, 0, K, 1}}, db{{1, 1, N, K}, {0, 0, K, 1}}, dc{{1, 1, M, N}, {0, 0, N, 1}};
+    GemmArgs g;
+    return make_gemm_args(da, db, dc, true, A, B, C, 1.0f, act, &g) && gemm_tcgen05_launch(g, s);
+}
+
+bool prefill_applies(const Engine *e)
+{
+    const char *env = getenv("VKLLM_B200_PREFILL");
+    if (env && atoi(env) == 0)
+        return false;
+    const DecodeDims &dd = e->dd;
+    const bool hd_ok = dd.hd == 32 || dd.hd == 48 || dd.hd == 64 || dd.hd == 80 || dd.hd == 96 || dd.hd == 128;
+    return hd_ok && !e->tp && dd.H * dd.hd == dd.D && dd.D % 8 == 0 && dd.F % 8 == 0 && dd.V % 8 == 0 &&
+           dd.D / 8 <= 1024;
+}
+
+} // namespace
+
+vkllm_err_t prefill_run(Engine *e, const uint32_t *tok, uint32_t S, uint32_t p0, uint32_t *out, cudaStream_t s)
+{
+    const DecodeDims &dd = e->dd;
+    if (!prefill_applies(e) || (uint64_t)p0 + S > dd.ctx)
+        return VKLLM_ERR_ARGS;
+    const uint32_t D = dd.D, F = dd.F, V = dd.V, HD = dd.H * dd.hd;
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t sd = al((size_t)S * D * 2), shd = al((size_t)S * HD * 2), sf = al((size_t)S * F * 2),
+                 sv = al((size_t)S * V * 2);
+    const size_t need = 3 * sd + 5 * shd + 2 * sf + sv;
+    if (need > e->pf_cap)
+    {
+        if (e->pf_ws)
+        {
+            VKB_CUDA(cudaStreamSynchronize(s));
+            cudaFree(e->pf_ws);
+            e->pf_ws = nullptr;
+            e->pf_cap = 0;
+        }
+        VKB_CUDA(cudaMalloc(&e->pf_ws, need));
+        e->pf_cap = need;
+    }
+    char *w = (char *)e->pf_ws;
+    __half *x = (__half *)w, *n = (__half *)(w + sd), *y = (__half *)(w + 2 * sd);
+    __half *q = (__half *)(w + 3 * sd), *k = (__half *)(w + 3 * sd + shd), *v = (__half *)(w + 3 * sd + 2 * shd),
+           *rq = (__half *)(w + 3 * sd + 3 * shd), *att = (__half *)(w + 3 * sd + 4 * shd);
+    __half *u = (__half *)(w + 3 * sd + 5 * shd), *gt = (__half *)(w + 3 * sd + 5 * shd + sf);
+    __half *lg = (__half *)(w + 3 * sd + 5 * shd + 2 * sf);
+    const uint32_t vocab_rows = dd.V; // embedding rows (no tensor parallelism here)
+    k_pf_embed<<<S, 128, 0, s>>>(tok, e->embed, vocab_rows, D, e->unk, x);
+    const uint64_t rope_threads = (uint64_t)S * HD / 8;
+    for (const LayerW &lw : e->layers)
+    {
+        bool ok = launch_rmsnorm_rows(x, lw.attn_norm, n, S, D, dd.eps, s) && pf_gemm(n, lw.wq, q, S, HD, D, 0, s) &&
+                  pf_gemm(n, lw.wk, k, S, HD, D, 0, s) && pf_gemm(n, lw.wv, v, S, HD, D, 0, s);
+        if (!ok)
+            return VKLLM_ERR_ARGS;
+        k_pf_rope_kv<<<(unsigned)((rope_threads + 255) / 256), 256, 0, s>>>(q, k, v, S, dd.H, dd.hd, p0, dd.ctx,
+                                                                            dd.rope_base, rq, lw.kcache, lw.vcache);
+        ok = pf_attention(rq, lw, dd, S, p0, att, s) && pf_gemm(att, lw.wo, y, S, D, HD, 0, s) &&
+             launch_bin_h(x, y, x, (uint64_t)S * D, 0, s) && launch_rmsnorm_rows(x, lw.ffn_norm, n, S, D, dd.eps, s) &&
+             pf_gemm(n, lw.wu, u, S, F, D, 0, s) && pf_gemm(n, lw.wg, gt, S, F, D, 1, s) &&
+             launch_bin_h(u, gt, u, (uint64_t)S * F, 2, s) && pf_gemm(u, lw.wd, y, S, D, F, 0, s) &&
+             launch_bin_h(x, y, x, (uint64_t)S * D, 0, s);
+        if (!ok)
+            return VKLLM_ERR_ARGS;
+    }
+    if (!launch_rmsnorm_rows(x, e->out_norm, n, S, D, dd.eps, s) || !pf_gemm(n, e->wout, lg, S, V, D, 0, s) ||
+        !launch_argmax_rows(lg, S, V, out, s))
+        return VKLLM_ERR_ARGS;
+    VKB_CUDA(cudaMemcpyAsync(e->logits, lg + (uint64_t)(S - 1) * V, (size_t)V * 2, cudaMemcpyDeviceToDevice, s));
+    VKB_CUDA(cudaGetLastError());
+    return VKLLM_ERR_OK;
+}
+
 vkllm_err_t plan_run(vkllm_context *ctx, vkllm_graph *graph)
 {
     Plan *p = (Plan *)graph->b200_plan;
-    if (!p || p->seq_len != 1 || graph->output_node != p->output || graph->nodes->used_n != p->n_nodes)
+    if (!p || p->seq_len == 0 || graph->output_node != p->output || graph->nodes->used_n != p->n_nodes)
         return VKLLM_ERR_ARGS;
     if (p->input_toks->dtype != vkllm_dtype_uint32 || !p->output->data.mapped)
         return VKLLM_ERR_ARGS;
     Engine *e = nullptr;
     if (get_engine(ctx, p->model, &e) != VKLLM_ERR_OK)
         return VKLLM_ERR_ARGS;
+    if (p->seq_len > 1)
+    {
+        cudaStream_t s = (cudaStream_t)graph->commands->stream;
+        const uint32_t *tok = (const uint32_t *)dev_ptr(ctx, p->input_toks);
+        uint32_t *out = (uint32_t *)p->output->data.dev;
+        if (!tok || !out)
+            return VKLLM_ERR_ALLOC;
+        vkllm_err_t err = prefill_run(e, tok, p->seq_len, p->offsets, out, s);
+        if (err != VKLLM_ERR_OK)
+            return err;
+        _CHECK(vkllm_commands_submit(ctx, graph->commands));
+        _CHECK(vkllm_commands_wait_exec(ctx, graph->commands));
+        return VKLLM_ERR_OK;
+    }
     if (p->offsets >= e->dd.ctx)
         return VKLLM_ERR_ARGS;
     cudaStream_t s = (cudaStream_t)graph->commands->stream;

@@ -70,4 +70,11 @@ bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, f
 // Sticky error word of the tcgen05 GEMM on device `dev` (bit 0: a bounded wait expired).
 uint32_t gemm_tcgen05_error(int dev);
 
+// Dense row-major launchers of the RMSNORM, BIN and ARG_MAX node kernels (ops/op_elementwise.cu),
+// used by the fused prefill step. Each returns false when the operands do not fit its vector path.
+bool launch_rmsnorm_rows(const __half *x, const float *g, __half *y, uint32_t rows, uint32_t W, float eps,
+                         cudaStream_t s);
+bool launch_bin_h(const __half *a, const __half *b, __half *out, uint64_t n, int op, cudaStream_t s);
+bool launch_argmax_rows(const __half *x, uint32_t rows, uint32_t W, uint32_t *out, cudaStream_t s);
+
 } // namespace vkb

@@ -1078,3 +1078,42 @@ extern "C" vkllm_err_t vkllm_op_arg_max_post_run(vkllm_context *, vkllm_commands
 {
     return VKLLM_ERR_OK;
 }
+
+// =================================================================================================
+// Launchers for the fused prefill step (engine/engine.cu): the same kernels as the RMSNORM, BIN and
+// ARG_MAX nodes on dense row-major operands, without tensor structs.
+namespace vkb
+{
+
+bool launch_rmsnorm_rows(const __half *x, const float *g, __half *y, uint32_t rows, uint32_t W, float eps,
+                         cudaStream_t s)
+{
+    if (W % 8 != 0 || W / 8 > 1024 || ((uintptr_t)x & 15) || ((uintptr_t)y & 15) || ((uintptr_t)g & 15))
+        return false;
+    Desc4 d{{1, 1, rows, W}, {0, 0, W, 1}};
+    const unsigned threads = ((W / 8 + 31) / 32) * 32;
+    k_rmsnorm_vec<<<rows, threads < 32 ? 32 : threads, 0, s>>>(x, d, g, y, d, eps);
+    return true;
+}
+
+bool launch_bin_h(const __half *a, const __half *b, __half *out, uint64_t n, int op, cudaStream_t s)
+{
+    if (n % 8 != 0 || (((uintptr_t)a | (uintptr_t)b | (uintptr_t)out) & 15))
+        return false;
+    const uint64_t n8 = n / 8;
+    uint64_t grid = (n8 + 255) / 256;
+    if (grid > 148ull * 16)
+        grid = 148ull * 16;
+    k_bin_h8<__half><<<(unsigned)grid, 256, 0, s>>>(a, b, out, n8, op);
+    return true;
+}
+
+bool launch_argmax_rows(const __half *x, uint32_t rows, uint32_t W, uint32_t *out, cudaStream_t s)
+{
+    Desc4 di{{1, 1, rows, W}, {0, 0, W, 1}};
+    Desc4 dout{{1, 1, rows, 1}, {0, 0, 1, 1}};
+    k_arg_max_block<__half><<<rows, 1024, 0, s>>>(x, di, out, dout);
+    return true;
+}
+
+} // namespace vkb

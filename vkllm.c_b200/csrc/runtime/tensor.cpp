@@ -185,6 +185,9 @@ extern "C" vkllm_err_t vkllm_tensor_new(struct vkllm_context *context, const cha
             tensor_release(context, t);
             return VKLLM_ERR_VULKAN;
         }
+        // Fresh mapped memory reads as zero in the reference (a new host-visible allocation); this
+        // buffer may be recycled from the pinned-host cache, so clear it.
+        memset(h, 0, t->bytes);
         t->data.host = h;
         t->data.dev = d;
         t->data.capacity = cap;
