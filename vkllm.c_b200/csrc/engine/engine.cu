@@ -1037,12 +1037,25 @@ bool pf_attention(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint
     }
 }
 
-// C [M, N] = act(A [M, K] . B [N, K]^T), dense row-major, on the tensor-core GEMM.
-bool pf_gemm(const __half *A, const __half *B, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s)
+// C [M, N] = act(A [M, K] . B [N, K]^T), dense row-major, on the tensor-core GEMM. With B1 (and B2),
+// B is the row concatenation [B; B1; B2] of matrices of N / groups rows each, read in place (one
+// launch instead of one per matrix); act applies from column act_from on.
+bool pf_gemm(const __half *A, const __half *B, __half *C, uint32_t M, uint32_t N, uint32_t K, int act, cudaStream_t s,
+             const __half *B1 = nullptr, const __half *B2 = nullptr, uint32_t act_from = 0)
 {
+    const uint32_t groups = B2 ? 3 : (B1 ? 2 : 1);
     Desc4 da{{1, 1, M, K}, {0, 0, K, 1}}, db{{1, 1, N, K}, {0, 0, K, 1}}, dc{{1, 1, M, N}, {0, 0, N, 1}};
     GemmArgs g;
-    return make_gemm_args(da, db, dc, true, A, B, C, 1.0f, act, &g) && gemm_tcgen05_launch(g, s);
+    if (!make_gemm_args(da, db, dc, true, A, B, C, 1.0f, act, &g))
+        return false;
+    if (groups > 1)
+    {
+        g.B1 = B1;
+        g.B2 = B2;
+        g.b_group_n = N / groups;
+    }
+    g.act_from = act_from;
+    return gemm_tcgen05_launch(g, s);
 }
 
 bool prefill_applies(const Engine *e)
@@ -1067,7 +1080,7 @@ vkllm_err_t prefill_run(Engine *e, const uint32_t *tok, uint32_t S, uint32_t p0,
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
     const size_t sd = al((size_t)S * D * 2), shd = al((size_t)S * HD * 2), sf = al((size_t)S * F * 2),
                  sv = al((size_t)S * V * 2);
-    const size_t need = 3 * sd + 5 * shd + 2 * sf + sv;
+    const size_t need = 3 * sd + 5 * shd + 3 * sf + sv;
     if (need > e->pf_cap)
     {
         if (e->pf_ws)
@@ -1082,26 +1095,40 @@ vkllm_err_t prefill_run(Engine *e, const uint32_t *tok, uint32_t S, uint32_t p0,
     }
     char *w = (char *)e->pf_ws;
     __half *x = (__half *)w, *n = (__half *)(w + sd), *y = (__half *)(w + 2 * sd);
-    __half *q = (__half *)(w + 3 * sd), *k = (__half *)(w + 3 * sd + shd), *v = (__half *)(w + 3 * sd + 2 * shd),
-           *rq = (__half *)(w + 3 * sd + 3 * shd), *att = (__half *)(w + 3 * sd + 4 * shd);
-    __half *u = (__half *)(w + 3 * sd + 5 * shd), *gt = (__half *)(w + 3 * sd + 5 * shd + sf);
-    __half *lg = (__half *)(w + 3 * sd + 5 * shd + 2 * sf);
-    const uint32_t vocab_rows = dd.V; // embedding rows (no tensor parallelism here)
-    k_pf_embed<<<S, 128, 0, s>>>(tok, e->embed, vocab_rows, D, e->unk, x);
-    const uint64_t rope_threads = (uint64_t)S * HD / 8;
+    // q, k, v side by side ([S][3 HD]) when one grouped GEMM makes them, else three [S][HD] blocks
+    __half *qkv = (__half *)(w + 3 * sd), *rq = (__half *)(w + 3 * sd + 3 * shd), *att = (__half *)(w + 3 * sd + 4 * shd);
+    // up and gate side by side ([S][2F]) when grouped, else two [S][F] blocks; then m [S][F]
+    __half *ug = (__half *)(w + 3 * sd + 5 * shd), *mm = (__half *)(w + 3 * sd + 5 * shd + 2 * sf);
+    __half *lg = (__half *)(w + 3 * sd + 5 * shd + 3 * sf);
+    // the grouped GEMMs need every tile width (128, 256) to divide a group's rows
+    const bool grouped = HD % 256 == 0 && F % 256 == 0;
+    const uint32_t ldq = grouped ? 3 * HD : HD, ldu = grouped ? 2 * F : F;
+    __half *q = qkv, *k = grouped ? qkv + HD : qkv + (uint64_t)S * HD, *v = grouped ? qkv + 2 * HD : qkv + 2ull * S * HD;
+    __half *up = ug, *gt = grouped ? ug + F : ug + (uint64_t)S * F;
+    k_pf_embed<<<S, 128, 0, s>>>(tok, e->embed, dd.V, D, e->unk, x);
+    const uint64_t rope_threads = (uint64_t)S * HD / 8, gate_threads = (uint64_t)S * F / 8;
     for (const LayerW &lw : e->layers)
     {
-        bool ok = launch_rmsnorm_rows(x, lw.attn_norm, n, S, D, dd.eps, s) && pf_gemm(n, lw.wq, q, S, HD, D, 0, s) &&
-                  pf_gemm(n, lw.wk, k, S, HD, D, 0, s) && pf_gemm(n, lw.wv, v, S, HD, D, 0, s);
+        bool ok = launch_rmsnorm_rows(x, lw.attn_norm, n, S, D, dd.eps, s);
+        if (grouped)
+            ok = ok && pf_gemm(n, lw.wq, qkv, S, 3 * HD, D, 0, s, lw.wk, lw.wv);
+        else
+            ok = ok && pf_gemm(n, lw.wq, q, S, HD, D, 0, s) && pf_gemm(n, lw.wk, k, S, HD, D, 0, s) &&
+                 pf_gemm(n, lw.wv, v, S, HD, D, 0, s);
         if (!ok)
             return VKLLM_ERR_ARGS;
-        k_pf_rope_kv<<<(unsigned)((rope_threads + 255) / 256), 256, 0, s>>>(q, k, v, S, dd.H, dd.hd, p0, dd.ctx,
+        k_pf_rope_kv<<<(unsigned)((rope_threads + 255) / 256), 256, 0, s>>>(q, k, v, ldq, S, dd.H, dd.hd, p0, dd.ctx,
                                                                             dd.rope_base, rq, lw.kcache, lw.vcache);
         ok = pf_attention(rq, lw, dd, S, p0, att, s) && pf_gemm(att, lw.wo, y, S, D, HD, 0, s) &&
-             launch_bin_h(x, y, x, (uint64_t)S * D, 0, s) && launch_rmsnorm_rows(x, lw.ffn_norm, n, S, D, dd.eps, s) &&
-             pf_gemm(n, lw.wu, u, S, F, D, 0, s) && pf_gemm(n, lw.wg, gt, S, F, D, 1, s) &&
-             launch_bin_h(u, gt, u, (uint64_t)S * F, 2, s) && pf_gemm(u, lw.wd, y, S, D, F, 0, s) &&
-             launch_bin_h(x, y, x, (uint64_t)S * D, 0, s);
+             launch_bin_h(x, y, x, (uint64_t)S * D, 0, s) && launch_rmsnorm_rows(x, lw.ffn_norm, n, S, D, dd.eps, s);
+        if (grouped) // [up | silu(gate)]: SiLU from column F on
+            ok = ok && pf_gemm(n, lw.wu, ug, S, 2 * F, D, 1, s, lw.wg, nullptr, F);
+        else
+            ok = ok && pf_gemm(n, lw.wu, up, S, F, D, 0, s) && pf_gemm(n, lw.wg, gt, S, F, D, 1, s);
+        if (!ok)
+            return VKLLM_ERR_ARGS;
+        k_pf_gate_mul<<<(unsigned)((gate_threads + 255) / 256), 256, 0, s>>>(up, gt, ldu, S, F, mm);
+        ok = pf_gemm(mm, lw.wd, y, S, D, F, 0, s) && launch_bin_h(x, y, x, (uint64_t)S * D, 0, s);
         if (!ok)
             return VKLLM_ERR_ARGS;
     }

@@ -33,12 +33,13 @@ __global__ void k_pf_embed(const uint32_t *__restrict__ ids, const __half *__res
         dst[i] = src[i];
 }
 
-// RoPE of Q and K and the KV-cache rows. q, k, v: [S][H * hd] (the projection nodes). Writes
+// RoPE of Q and K and the KV-cache rows. q, k, v: [S][H * hd] rows `ld` elements apart (the
+// projection nodes, side by side when one grouped GEMM produced them). Writes
 // rq [H][S][hd] (the rotated-Q node, contiguous as the reference's ROPE output), the rotated K rows
 // to kcache[h][p0 + s] and the V rows to vcache[h][p0 + s]. Pair w of a row rotates by
 // theta = (p0 + s) / base^(2w / hd) in fp32. One thread per 8 elements (4 pairs).
 __global__ void k_pf_rope_kv(const __half *__restrict__ q, const __half *__restrict__ k, const __half *__restrict__ v,
-                             uint32_t S, uint32_t H, uint32_t hd, uint32_t p0, uint32_t ctx, float base,
+                             uint32_t ld, uint32_t S, uint32_t H, uint32_t hd, uint32_t p0, uint32_t ctx, float base,
                              __half *__restrict__ rq, __half *__restrict__ kcache, __half *__restrict__ vcache)
 {
     const uint32_t per_row = H * hd / 8;
@@ -47,7 +48,7 @@ __global__ void k_pf_rope_kv(const __half *__restrict__ q, const __half *__restr
         return;
     const uint32_t s = (uint32_t)(t / per_row), c8 = (uint32_t)(t % per_row);
     const uint32_t col = 8 * c8, h = col / hd, d = col % hd;
-    const uint64_t src = (uint64_t)s * H * hd + col;
+    const uint64_t src = (uint64_t)s * ld + col;
     const uint4 qv = *reinterpret_cast<const uint4 *>(q + src);
     const uint4 kv = *reinterpret_cast<const uint4 *>(k + src);
     const __half2 *qh = reinterpret_cast<const __half2 *>(&qv);
@@ -70,6 +71,30 @@ __global__ void k_pf_rope_kv(const __half *__restrict__ q, const __half *__restr
     const uint64_t row = ((uint64_t)h * ctx + p0 + s) * hd + d;
     *reinterpret_cast<uint4 *>(kcache + row) = ko;
     *reinterpret_cast<uint4 *>(vcache + row) = *reinterpret_cast<const uint4 *>(v + src);
+}
+
+// m[s][f] = fp16(up[s][f] * gate[s][f]) (the FFN's BIN mul node); up and gate rows `ld` elements
+// apart, m dense [S][F]. 8 elements per thread.
+__global__ void k_pf_gate_mul(const __half *__restrict__ up, const __half *__restrict__ gate, uint32_t ld, uint32_t S,
+                              uint32_t F, __half *__restrict__ m)
+{
+    const uint32_t per_row = F / 8;
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (uint64_t)S * per_row)
+        return;
+    const uint32_t s = (uint32_t)(t / per_row), c = 8 * (uint32_t)(t % per_row);
+    const uint4 a = *reinterpret_cast<const uint4 *>(up + (uint64_t)s * ld + c);
+    const uint4 b = *reinterpret_cast<const uint4 *>(gate + (uint64_t)s * ld + c);
+    const __half2 *ah = reinterpret_cast<const __half2 *>(&a), *bh = reinterpret_cast<const __half2 *>(&b);
+    uint4 o;
+    __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+    {
+        const float2 x = __half22float2(ah[e]), y = __half22float2(bh[e]);
+        oh[e] = __floats2half2_rn(x.x * y.x, x.y * y.y);
+    }
+    *reinterpret_cast<uint4 *>(m + (uint64_t)s * F + c) = o;
 }
 
 __device__ __forceinline__ uint32_t pf_smem(const void *p)

@@ -116,6 +116,7 @@ struct TcParams
     int act;
     uint32_t act_from; // act applies to output columns >= act_from
     uint32_t b_tiled;  // B in 128-row x 64-column tiles (gemm_tile_b); its map is (64, 128, k-block, n-tile)
+    uint32_t b_group_n; // > 0: B rows come from up to three matrices of b_group_n rows each (tmB, tmB1, tmB2)
     __half *C;
     uint32_t *err;
     // Split-K: `splits` CTAs share a tile, each over kb_per k-blocks, writing fp32 partials to
@@ -169,7 +170,9 @@ __device__ __forceinline__ void store_row32(__half *crow, uint32_t nb, const uin
 
 template <int BM, int BN>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
-                                                     const __grid_constant__ CUtensorMap tmB, TcParams p)
+                                                     const __grid_constant__ CUtensorMap tmB,
+                                                     const __grid_constant__ CUtensorMap tmB1,
+                                                     const __grid_constant__ CUtensorMap tmB2, TcParams p)
 {
     using Cfg = TileCfg<BM, BN>;
     extern __shared__ unsigned char smem_raw[];
@@ -217,11 +220,15 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         // Producer.
         const int32_t ca = p.a_cc ? 0 : (int32_t)zc, ba = p.a_bc ? 0 : (int32_t)zb;
         const int32_t cb = p.b_cc ? 0 : (int32_t)zc, bb = p.b_bc ? 0 : (int32_t)zb;
+        // grouped B: the tile's rows n0 .. n0 + BN - 1 lie in one group (b_group_n % BN == 0, host)
+        const uint32_t grp = p.b_group_n ? n0 / p.b_group_n : 0u;
+        const CUtensorMap *mapB = grp == 0 ? &tmB : (grp == 1 ? &tmB1 : &tmB2);
+        const uint32_t nb0 = n0 - grp * p.b_group_n;
         auto load_b = [&](uint32_t kb, uint32_t sb, uint64_t *bar) {
             if (p.b_tiled) // BN / 128 consecutive tiles of the k-block: the same smem image as BN rows
-                tma_load_4d(sb, &tmB, 0, 0, (int32_t)(kb_lo + kb), (int32_t)(n0 / kTileRows), bar);
+                tma_load_4d(sb, mapB, 0, 0, (int32_t)(kb_lo + kb), (int32_t)(nb0 / kTileRows), bar);
             else
-                tma_load_4d(sb, &tmB, (int32_t)((kb_lo + kb) * kBK), (int32_t)n0, cb, bb, bar);
+                tma_load_4d(sb, mapB, (int32_t)((kb_lo + kb) * kBK), (int32_t)nb0, cb, bb, bar);
         };
         // The first stages' B tiles (weights, never written by the kernels this one may overlap) load
         // before the wait for the previous kernel in the stream (a no-op unless launched as its
@@ -557,7 +564,23 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
     else if (!encode_operand(&mb, g.B, g.K, g.N, g.ldb, g.b_sc ? g.batch_c : 1, g.b_sc, g.b_sb ? batch_b : 1, g.b_sb,
                              BN))
         return false;
+    CUtensorMap mb1 = mb, mb2 = mb;
+    uint32_t group_n = 0;
+    if (g.b_group_n)
+    {
+        // grouped B: N = groups * b_group_n rows, group i from B, B1, B2
+        const uint32_t groups = g.N / g.b_group_n;
+        if (g.b_tiled || g.batch != 1 || g.b_group_n % BN || groups * g.b_group_n != g.N || groups < 1 || groups > 3)
+            return false;
+        const void *src[3] = {g.B, g.B1, g.B2};
+        CUtensorMap *dst[3] = {&mb, &mb1, &mb2};
+        for (uint32_t i = 0; i < groups; ++i)
+            if (!src[i] || !encode_operand(dst[i], src[i], g.K, g.b_group_n, g.ldb, 1, 0, 1, 0, BN))
+                return false;
+        group_n = g.b_group_n;
+    }
     TcParams p{};
+    p.b_group_n = group_n;
     p.M = g.M;
     p.N = g.N;
     p.K = g.K;
@@ -614,11 +637,11 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
         at[0].val.programmaticStreamSerializationAllowed = 1;
         lc.attrs = at;
         lc.numAttrs = 1;
-        if (cudaLaunchKernelEx(&lc, k_gemm_tc<BM, BN>, ma, mb, p) != cudaSuccess)
+        if (cudaLaunchKernelEx(&lc, k_gemm_tc<BM, BN>, ma, mb, mb1, mb2, p) != cudaSuccess)
             return false;
     }
     else
-        k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, p);
+        k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, mb1, mb2, p);
     if (p.splits > 1 && !ws_ext)
     {
         const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 7) / 8);
@@ -815,12 +838,14 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
     // never inside stream capture, where the model's choice (or an earlier tuning result) is used.
     // VKLLM_B200_GEMM_TUNE_FILE: choices are read from this file at the first call and appended to
     // it when tuned, so later processes (or a profiler run, whose timings would mislead the tuner)
-    // reuse them. One line per shape: "M N K batch b_tiled tile splits".
+    // reuse them. One line per shape: "M N K batch layout tile splits" (layout: bit 0 tiled B, bit 1
+    // grouped B).
     static std::map<TuneKey, TcChoice> cache;
     static std::mutex mu;
     static bool file_loaded = false;
     const char *tune_file = getenv("VKLLM_B200_GEMM_TUNE_FILE");
-    const TuneKey key{dev, g.M, g.N, g.K, g.batch, g.b_tiled ? 1u : 0u};
+    const uint32_t layout = (g.b_tiled ? 1u : 0u) | (g.b_group_n ? 2u : 0u); // operand layout of B
+    const TuneKey key{dev, g.M, g.N, g.K, g.batch, layout};
     {
         std::lock_guard<std::mutex> lk(mu);
         if (tune_file && !file_loaded)
@@ -830,7 +855,7 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
             {
                 unsigned m, n, k, b, bt, t, sp;
                 while (fscanf(f, "%u %u %u %u %u %u %u", &m, &n, &k, &b, &bt, &t, &sp) == 7)
-                    if (bt <= 1 && t <= 2 && sp >= 1 && sp <= 8)
+                    if (bt <= 3 && t <= 2 && sp >= 1 && sp <= 8)
                         for (int d = 0; d < 64; ++d) // the file carries no device: it applies to each
                             cache[TuneKey{d, m, n, k, b, bt}] = TcChoice{(uint8_t)t, (uint8_t)sp};
                 fclose(f);
@@ -856,7 +881,7 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
         if (tune_file)
             if (FILE *f = fopen(tune_file, "a"))
             {
-                fprintf(f, "%u %u %u %u %u %u %u\n", g.M, g.N, g.K, g.batch, g.b_tiled ? 1u : 0u, (unsigned)best.tile,
+                fprintf(f, "%u %u %u %u %u %u %u\n", g.M, g.N, g.K, g.batch, layout, (unsigned)best.tile,
                         (unsigned)best.splits);
                 fclose(f);
             }

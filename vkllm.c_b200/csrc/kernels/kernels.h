@@ -26,6 +26,11 @@ struct GemmArgs
     int act;
     uint32_t act_from = 0; // act applies to output columns >= act_from (0: all)
     uint32_t b_tiled = 0;  // B is a gemm_tile_b copy (batch 1 only; ldb and the B strides are unused)
+    // Grouped B (batch 1, row-major B): when b_group_n > 0, rows [0, b_group_n) of B come from B, the
+    // next b_group_n from B1, the next from B2 (N = 2 or 3 groups), each [b_group_n, K] with row
+    // stride ldb; every tile size in use must divide b_group_n, else the launch reports false.
+    const void *B1 = nullptr, *B2 = nullptr;
+    uint32_t b_group_n = 0;
     // Launch as a programmatic dependent of the previous kernel in the stream: the CTAs start while
     // it runs and load the first stages of B before waiting for its completion, so B must not be
     // written by that kernel (weights). Everything else (A, C, the split-K workspace) is touched
