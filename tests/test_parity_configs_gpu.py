@@ -12,7 +12,8 @@ modes, which restate the shader variants the reference picks by the device's sha
 differ from each other by max-abs 0.04-0.07 and mean-abs 0.008-0.014 on these logits, and their
 greedy tokens part within a few steps. So each step's bar is the larger of the north_star numbers
 and that reference-internal spread (fp16arith vs fp32arith, computed here on the same weights and
-prompt); the comparison is against fp32arith, the parity target. Greedy tokens must be identical
+prompt, at the steps whose inputs agree in both modes; later steps keep the largest spread seen);
+the comparison is against fp32arith, the parity target. Greedy tokens must be identical
 except at a reference tie at fp16 resolution, which tests/parity.py reports as a warning. The
 decode must have run on the persistent kernel."""
 import ctypes as C
@@ -70,12 +71,15 @@ def run_pair(vk, ctx, orc, cfg, seed, prompt_len, n_tokens, oracle_ctx):
             orc.set_arith(prev)
     ref_toks, ref_logits = runs["fp32"]
     t16, l16 = runs["fp16"]
-    max_bar, mean_bar = [], []
+    # The reference-internal spread is measured at the steps whose inputs agree in both modes; a later
+    # step (after the two modes' greedy tokens parted) takes the largest spread measured before it.
+    max_bar, mean_bar, seen_max, seen_mean = [], [], 2e-2, 2e-3
     for i in range(n_tokens):
-        spread = np.abs(l16[i].astype(np.float32) - ref_logits[i].astype(np.float32))
-        same_inputs = t16[:i] == ref_toks[:i]  # the reference-internal spread is defined while inputs agree
-        max_bar.append(max(2e-2, float(spread.max()) if same_inputs else 2e-2))
-        mean_bar.append(max(2e-3, float(spread.mean()) if same_inputs else 2e-3))
+        if t16[:i] == ref_toks[:i]:
+            spread = np.abs(l16[i].astype(np.float32) - ref_logits[i].astype(np.float32))
+            seen_max, seen_mean = max(seen_max, float(spread.max())), max(seen_mean, float(spread.mean()))
+        max_bar.append(seen_max)
+        mean_bar.append(seen_mean)
     return toks, logits, ref_toks, ref_logits, persistent, max_bar, mean_bar
 
 

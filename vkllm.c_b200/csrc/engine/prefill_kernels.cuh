@@ -148,7 +148,7 @@ template <int HD> struct PfSmem
     static constexpr int LDT = kPfBK + 8;    // halves per row of the transposed-V tile (quirk Q1)
     static constexpr int kQ = kPfBQ * LD, kK = kPfBK * LD;
     static constexpr int kV = (kPfBK * LD > HD * LDT) ? kPfBK * LD : HD * LDT;
-    static constexpr int kBytes = (kQ + kK + kV) * 2;
+    static constexpr int kBytes = (kQ + 2 * kK + 2 * kV) * 2; // K and V tiles double-buffered
 };
 
 // Loads rows [r0, r0 + rows) (of `n_valid` existing rows) of a [*, HD] fp16 matrix with row pitch
@@ -165,6 +165,49 @@ __device__ __forceinline__ void pf_load_rows(__half *dst, const __half *src, uin
         if (r0 + r < n_valid)
             v = *reinterpret_cast<const uint4 *>(src + (uint64_t)(r0 + r) * pitch + 8 * c);
         *reinterpret_cast<uint4 *>(dst + r * LD + 8 * c) = v;
+    }
+}
+
+// 16-byte asynchronous copy global -> shared; `valid` false writes zeros (src is then not read).
+__device__ __forceinline__ void pf_cp16(__half *dst, const __half *src, bool valid)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(pf_smem(dst)), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void pf_cp_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <int N> __device__ __forceinline__ void pf_cp_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// pf_load_rows as asynchronous copies (committed by the caller).
+template <int HD, int LD>
+__device__ __forceinline__ void pf_async_rows(__half *dst, const __half *src, uint64_t pitch, uint32_t r0,
+                                              uint32_t rows, uint32_t n_valid)
+{
+    constexpr uint32_t C8 = HD / 8;
+    for (uint32_t i = threadIdx.x; i < rows * C8; i += kPfThreads)
+    {
+        const uint32_t r = i / C8, c = i % C8;
+        const bool valid = r0 + r < n_valid;
+        pf_cp16(dst + r * LD + 8 * c, valid ? src + (uint64_t)(r0 + r) * pitch + 8 * c : src, valid);
+    }
+}
+
+// Quirk Q1 V tile: dst[w][jj] = V row w (w < HD), column j0 + jj (< HD), rows LDT halves apart.
+template <int HD, int LDT>
+__device__ __forceinline__ void pf_async_vt(__half *dst, const __half *vb, uint32_t j0)
+{
+    for (uint32_t t = threadIdx.x; t < (uint32_t)HD * (kPfBK / 8); t += kPfThreads)
+    {
+        const uint32_t w = t / (kPfBK / 8), c8 = t % (kPfBK / 8), col = j0 + 8 * c8;
+        const bool valid = col < (uint32_t)HD;
+        pf_cp16(dst + w * LDT + 8 * c8, valid ? vb + (uint64_t)w * HD + col : vb, valid);
     }
 }
 
@@ -217,8 +260,8 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
     constexpr int LD = SM::LD, LDT = SM::LDT;
     extern __shared__ __align__(16) unsigned char pf_sm[];
     __half *sq = reinterpret_cast<__half *>(pf_sm);
-    __half *sk = sq + SM::kQ;
-    __half *sv = sk + SM::kK;
+    // buffer b of the key tiles at sk0 + b * kK, of the value tiles at sv0 + b * kV
+    __half *const sk0 = sq + SM::kQ, *const sv0 = sq + SM::kQ + 2 * SM::kK;
     const uint32_t h = blockIdx.y, q0 = blockIdx.x * kPfBQ;
     const uint32_t Lk = p0 + S;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -240,14 +283,23 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
     const uint32_t nkb = (Lk + kPfBK - 1) / kPfBK;
     float s[kPfBK / 8][4];
 
-    // ---- pass 1: row max over every key, row sum over the unmasked keys (rescaled online)
+    // ---- pass 1: row max over every key, row sum over the unmasked keys (rescaled online). Key
+    // tiles are double-buffered: block kb + 1 is in flight while block kb is scored.
+    pf_async_rows<HD, LD>(sk0, kb, HD, 0, kPfBK, Lk);
+    pf_cp_commit();
     for (uint32_t kb_i = 0; kb_i < nkb; ++kb_i)
     {
         const uint32_t j0 = kb_i * kPfBK;
+        if (kb_i + 1 < nkb)
+        {
+            pf_async_rows<HD, LD>(sk0 + ((kb_i + 1) & 1) * SM::kK, kb, HD, j0 + kPfBK, kPfBK, Lk);
+            pf_cp_commit();
+            pf_cp_wait<1>();
+        }
+        else
+            pf_cp_wait<0>();
         __syncthreads();
-        pf_load_rows<HD, LD>(sk, kb, HD, j0, kPfBK, Lk);
-        __syncthreads();
-        pf_scores<HD, LD>(qa, sk, scale, s);
+        pf_scores<HD, LD>(qa, sk0 + (kb_i & 1) * SM::kK, scale, s);
         float bm0 = -FLT_MAX, bm1 = -FLT_MAX;
 #pragma unroll
         for (int nt = 0; nt < kPfBK / 8; ++nt)
@@ -290,6 +342,7 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
         l1 = l1 * expf(m1 - n1) + a1;
         m0 = n0;
         m1 = n1;
+        __syncthreads(); // every warp is done with this buffer before it is refilled
     }
 
     // ---- pass 2: probabilities and p . V over the key blocks that hold an unmasked key
@@ -299,26 +352,29 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
         o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     const uint32_t last_row = min(q0 + kPfBQ, S) - 1;
     const uint32_t nkb2 = min(nkb, (p0 + last_row) / kPfBK + 1);
+    // K and V tiles of block kb + 1 are in flight while block kb is used
+    auto issue_kv = [&](uint32_t blk) {
+        const uint32_t jb = blk * kPfBK;
+        pf_async_rows<HD, LD>(sk0 + (blk & 1) * SM::kK, kb, HD, jb, kPfBK, Lk);
+        if (!q1)
+            pf_async_rows<HD, LD>(sv0 + (blk & 1) * SM::kV, vb, HD, jb, kPfBK, Lk);
+        else
+            pf_async_vt<HD, LDT>(sv0 + (blk & 1) * SM::kV, vb, jb);
+        pf_cp_commit();
+    };
+    issue_kv(0);
     for (uint32_t kb_i = 0; kb_i < nkb2; ++kb_i)
     {
         const uint32_t j0 = kb_i * kPfBK;
-        __syncthreads();
-        pf_load_rows<HD, LD>(sk, kb, HD, j0, kPfBK, Lk);
-        if (!q1)
-            pf_load_rows<HD, LD>(sv, vb, HD, j0, kPfBK, Lk);
-        else
+        if (kb_i + 1 < nkb2)
         {
-            // quirk Q1: sv[w][jj] = V row w (w < HD = Lk), column j0 + jj
-            for (uint32_t t = threadIdx.x; t < (uint32_t)HD * (kPfBK / 8); t += kPfThreads)
-            {
-                const uint32_t w = t / (kPfBK / 8), c8 = t % (kPfBK / 8), col = j0 + 8 * c8;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (col < (uint32_t)HD)
-                    v = *reinterpret_cast<const uint4 *>(vb + (uint64_t)w * HD + col);
-                *reinterpret_cast<uint4 *>(sv + w * LDT + 8 * c8) = v;
-            }
+            issue_kv(kb_i + 1);
+            pf_cp_wait<1>();
         }
+        else
+            pf_cp_wait<0>();
         __syncthreads();
+        const __half *sk = sk0 + (kb_i & 1) * SM::kK, *sv = sv0 + (kb_i & 1) * SM::kV;
         pf_scores<HD, LD>(qa, sk, scale, s);
         // p = fp16(exp(s - max) / sum) where unmasked, else 0 (the softmax node)
 #pragma unroll
@@ -359,6 +415,7 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
                 pf_mma(o[2 * np + 1], pa, b[2], b[3]);
             }
         }
+        __syncthreads(); // every warp is done with these buffers before they are refilled
     }
     // ---- store: out[i][h * HD + d] = fp16(o)
     const uint64_t row_pitch = (uint64_t)H * HD;
