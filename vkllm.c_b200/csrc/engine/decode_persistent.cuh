@@ -117,6 +117,15 @@ struct PersistParams
     uint64_t *trace_last;       // optional: per trace entry, %globaltimer when the last CTA arrived
     uint64_t *trace_cta;        // optional: [barrier][CTA] %globaltimer of each CTA's arrival (first
                                 // kCtaTraceBarriers grid barriers of a launch)
+    // Fine-grained Wo and down phases (fine = 1): instead of a grid barrier after attention and after
+    // up/gate, each producer publishes an epoch flag (head_flag[h] once head h's attention output is
+    // combined, cta_flag[b] once CTA b's up/gate rows are written), and a Wo or down tile waits only
+    // for the producers of its 256 input columns: the heads they span, or dn_seg[2 k] .. dn_seg[2 k + 1],
+    // the first and last CTA whose up/gate units intersect segment k.
+    uint32_t fine;
+    uint32_t *cta_flag;         // [grid], zeroed before each launch (grows within a launch)
+    uint32_t *head_flag;        // [H]: epoch once a head's attention output is combined (fine = 1)
+    const uint32_t *dn_seg;     // [2 * segments of the down phase]
     uint32_t l2_bytes;          // per CTA: next-phase weights prefetched into L2 at each barrier
     uint32_t l2_hint;           // 1: stage loads mark their lines evict-first in L2
     // Tensor parallelism over peer memory (tp_size 1: off). Each rank owns H / N heads, F / N FFN
@@ -502,12 +511,76 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+constexpr uint32_t kFineMaxSegs = 64;
+// Segment states of the fine-grained down phase in this CTA: 0 not staged, 1 being staged, 2 ready.
+__shared__ uint32_t s_seg[kFineMaxSegs];
+
+__device__ __forceinline__ void st_release_gpu_u32(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Makes input segment ks (columns 256 ks .. 256 ks + width) of a gated phase ready in xs: the first
+// warp to need it waits (bounded) until flags[first .. last] all reached `epoch`, then copies the
+// columns from src (L2); other warps that need it meanwhile wait (bounded) for that copy.
+// Warp-uniform; false on a timed-out wait or a reported error.
+__device__ __forceinline__ bool fine_segment(const PersistParams &P, uint32_t ks, uint32_t width, __half *xs,
+                                             const __half *src, const uint32_t *flags, uint32_t first, uint32_t last,
+                                             uint32_t epoch)
+{
+    const uint32_t lane = threadIdx.x & 31;
+    uint32_t st = 0;
+    if (lane == 0)
+        st = atomicCAS(&s_seg[ks], 0u, 1u);
+    st = __shfl_sync(0xffffffffu, st, 0);
+    if (st == 2)
+    {
+        __threadfence_block();
+        return true;
+    }
+    const uint64_t t0 = global_ns();
+    if (st == 1)
+    {
+        // another warp stages it
+        bool ok = true;
+        if (lane == 0)
+            while (*reinterpret_cast<volatile uint32_t *>(&s_seg[ks]) != 2u)
+                if (global_ns() - t0 > kWaitLimitNs || ld_acquire_u32(P.err) != 0)
+                {
+                    ok = false;
+                    break;
+                }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        __threadfence_block();
+        return ok;
+    }
+    // this warp stages it: every lane acquires every producer's flag itself, then loads
+    for (uint32_t b = first; b <= last; ++b)
+        while (ld_acquire_u32(flags + b) < epoch)
+            if (global_ns() - t0 > kWaitLimitNs || ld_acquire_u32(P.err) != 0)
+            {
+                if (lane == 0)
+                    atomicOr(P.err, kErrBarrierTimeout);
+                return false;
+            }
+    const uint32_t n4 = width / 8; // 16-byte chunks, at most 32
+    if (lane < n4)
+        reinterpret_cast<uint4 *>(xs + ks * kSegHalves)[lane] =
+            __ldcg(reinterpret_cast<const uint4 *>(src + ks * kSegHalves) + lane);
+    __syncwarp();
+    __threadfence_block();
+    if (lane == 0)
+        atomicExch(&s_seg[ks], 2u);
+    return true;
+}
+
 // One GEMV phase: consumes this warp's tiles (partials to `part`), then the CTA sums the partials
 // of each of its units in segment order and runs the epilogue. Returns false when a wait timed out
 // in any warp of the CTA.
-template <int NM>
+template <int NM, bool GATED = false>
 __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t kind, uint32_t layer, WarpPipe &wp,
-                                             const __half *xs, float *part, uint32_t pos, SyncState &tr)
+                                             const __half *xs, float *part, uint32_t pos, SyncState &tr,
+                                             uint32_t gate_epoch = 0)
 {
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileGeom &g = P.tg[kind];
@@ -522,6 +595,22 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
     uint32_t grp = warp / g.Ks, ks = warp % g.Ks; // tile t = warp + warps * k = grp * Ks + ks
     for (uint32_t k = 0; k < nk; ++k, tile_step(grp, ks, g.Ks, P.warps))
     {
+        if constexpr (GATED)
+        {
+            const uint32_t width = ks + 1 == g.Ks ? g.last : kSegHalves;
+            bool okg;
+            if (kind == PK_WO) // input: the attention output; producers: the heads the segment spans
+                okg = fine_segment(P, ks, width, const_cast<__half *>(xs), P.attn, P.head_flag, ks * kSegHalves / P.dd.hd,
+                                   (ks * kSegHalves + width - 1) / P.dd.hd, gate_epoch);
+            else // PK_DOWN: input m; producers: the up/gate CTAs of the segment
+                okg = fine_segment(P, ks, width, const_cast<__half *>(xs), P.m, P.cta_flag, __ldg(P.dn_seg + 2 * ks),
+                                   __ldg(P.dn_seg + 2 * ks + 1), gate_epoch);
+            if (!okg)
+            {
+                ok = false;
+                break;
+            }
+        }
         const uint32_t gi = wp.consumed, s = gi % P.spw;
         const long long c0 = wt ? clock64() : 0;
         const bool okw = mbar_wait_bounded(&wp.bar[s], (gi / P.spw) & 1u, kWaitLimitNs);
@@ -888,6 +977,11 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                 P.attn[h * hd + d] = __float2half_rn(o);
             }
         __syncthreads();
+        if (flag_s && tid == 0 && P.fine) // the head's output is complete: the Wo tiles reading it may start
+        {
+            __threadfence();
+            st_release_gpu_u32(P.head_flag + h, aepoch + 1);
+        }
         amark(7);
         if (P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
         {
@@ -1050,14 +1144,31 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 ok = false;
                 break;
             }
-            if (!persist_attention(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
+            if (P.fine)
             {
-                ok = false;
-                break;
+                // Wo tiles wait only for the heads their input columns span
+                if (!persist_attention(P, l, pos, step * P.L + l, scratch, sred))
+                {
+                    ok = false;
+                    break;
+                }
+                if (threadIdx.x < kFineMaxSegs)
+                    s_seg[threadIdx.x] = 0;
+                __syncthreads();
+                trace_mark(P, tr);
+                ok = persist_gemv<1, true>(P, PK_WO, l, wp, xs, part, pos, tr, step * P.L + l + 1);
             }
-            stage_copy_h(P.attn, dd.H * dd.hd, xs);
-            trace_mark(P, tr);
-            ok = persist_gemv<1>(P, PK_WO, l, wp, xs, part, pos, tr);
+            else
+            {
+                if (!persist_attention(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
+                {
+                    ok = false;
+                    break;
+                }
+                stage_copy_h(P.attn, dd.H * dd.hd, xs);
+                trace_mark(P, tr);
+                ok = persist_gemv<1>(P, PK_WO, l, wp, xs, part, pos, tr);
+            }
             if (threadIdx.x == 0)
                 prefetch_slice(P, PK_UPGATE, l);
             if (P.tp_size > 1 && __syncthreads_and(ok))
@@ -1072,14 +1183,37 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
             ok = persist_gemv<2>(P, PK_UPGATE, l, wp, xs, part, pos, tr);
             if (threadIdx.x == 0)
                 prefetch_slice(P, PK_DOWN, l);
-            if (!__syncthreads_and(ok) || !grid_sync(P, tr))
+            if (P.fine)
             {
-                ok = false;
-                break;
+                // publish this CTA's up/gate rows, then stage the down input segment by segment
+                const uint32_t fe = step * P.L + l + 1;
+                if (!__syncthreads_and(ok))
+                {
+                    ok = false;
+                    break;
+                }
+                if (threadIdx.x == 0)
+                {
+                    __threadfence();
+                    st_release_gpu_u32(P.cta_flag + blockIdx.x, fe);
+                }
+                if (threadIdx.x < kFineMaxSegs)
+                    s_seg[threadIdx.x] = 0;
+                __syncthreads();
+                trace_mark(P, tr);
+                ok = persist_gemv<1, true>(P, PK_DOWN, l, wp, xs, part, pos, tr, fe);
             }
-            stage_copy_h(P.m, dd.F, xs);
-            trace_mark(P, tr);
-            ok = persist_gemv<1>(P, PK_DOWN, l, wp, xs, part, pos, tr);
+            else
+            {
+                if (!__syncthreads_and(ok) || !grid_sync(P, tr))
+                {
+                    ok = false;
+                    break;
+                }
+                stage_copy_h(P.m, dd.F, xs);
+                trace_mark(P, tr);
+                ok = persist_gemv<1>(P, PK_DOWN, l, wp, xs, part, pos, tr);
+            }
             if (threadIdx.x == 0)
                 prefetch_slice(P, l + 1 < P.L ? PK_QKV : PK_LOGITS, l + 1 < P.L ? l + 1 : 0);
             if (P.tp_size > 1 && __syncthreads_and(ok))

@@ -1,6 +1,7 @@
 // Fused decode engine: owns the decode workspace of one model, captures one decode step as a CUDA
 // Graph, and runs it for vkllm_graph_run (graphs carrying a plan) and for the device-resident
 // token loop of vkllm_b200.h.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -57,7 +58,8 @@ struct Engine
     float *rope_den = nullptr;                  // RoPE denominators of the persistent kernel
     // persistent kernel's row partition: [kind][grid + 1] prefix offsets of each CTA's units
     std::vector<uint32_t> htab;
-    uint32_t *utab = nullptr;
+    uint32_t *utab = nullptr;                   // htab on the device, then the down-phase segment producers
+    std::vector<uint32_t> seg_host;             // [2 * kFineMaxSegs] first / last producer CTA per segment
     uint32_t unit_cap[PK_COUNT] = {}; // most units a CTA may hold in a phase (sizes the partials)
     // fused prefill (graphs with S > 1): workspace grown to the largest S seen
     void *pf_ws = nullptr;
@@ -249,6 +251,30 @@ cudaError_t relayout_weights(Engine *e, cudaStream_t st, std::vector<const __hal
                                       cudaMemcpyHostToDevice, st);
     if (err != cudaSuccess)
         return err;
+    {
+        // producers of each 256-column input segment of the down phase: the first and last CTA whose
+        // up/gate units (columns of m) intersect it (fine-grained down phase)
+        const uint32_t Ks = e->pp.tg[PK_DOWN].Ks;
+        const uint32_t *tu = e->htab.data() + (size_t)PK_UPGATE * (grid + 1);
+        e->seg_host.assign(2 * kFineMaxSegs, 0);
+        for (uint32_t k = 0; k < Ks && k < kFineMaxSegs; ++k)
+        {
+            const uint32_t c0 = k * kSegHalves, c1 = std::min(dd.F, c0 + kSegHalves);
+            uint32_t first = grid, last = 0;
+            for (uint32_t b = 0; b < grid; ++b)
+                if (tu[b] < c1 && tu[b + 1] > c0)
+                {
+                    first = std::min(first, b);
+                    last = std::max(last, b);
+                }
+            e->seg_host[2 * k] = first < grid ? first : 0;
+            e->seg_host[2 * k + 1] = first < grid ? last : 0;
+        }
+        err = cudaMemcpyAsync(e->utab + e->htab.size(), e->seg_host.data(), sizeof(uint32_t) * e->seg_host.size(),
+                              cudaMemcpyHostToDevice, st);
+        if (err != cudaSuccess)
+            return err;
+    }
     const uint32_t *tq = e->utab + PK_QKV * (grid + 1), *two = e->utab + PK_WO * (grid + 1),
                    *tu = e->utab + PK_UPGATE * (grid + 1), *td = e->utab + PK_DOWN * (grid + 1),
                    *tl = e->utab + PK_LOGITS * (grid + 1);
@@ -314,6 +340,8 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     P.bar_count = e->bar;
     P.head_cnt = e->bar + 1;
     P.head_done = e->bar + 1 + dd.H;
+    P.cta_flag = e->bar + 1 + 2 * dd.H;
+    P.head_flag = e->bar + 1 + 2 * dd.H + kPersistMaxGrid;
     P.attn = e->attn;
     P.err = &e->state->error;
     P.att_split = att_split;
@@ -460,12 +488,17 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
         return;
     }
     cudaStream_t st = ctx->runtime->stream;
-    if (cudaMalloc(&e->utab, sizeof(uint32_t) * e->htab.size()) != cudaSuccess)
+    if (cudaMalloc(&e->utab, sizeof(uint32_t) * (e->htab.size() + 2 * kFineMaxSegs)) != cudaSuccess)
     {
         (void)cudaGetLastError();
         return;
     }
     P.utab = e->utab;
+    P.dn_seg = e->utab + e->htab.size();
+    // Fine-grained Wo and down phases (default on; VKLLM_B200_PERSIST_FINE=0: a grid barrier and a
+    // full staging of the input instead). The phases' segments must fit the per-CTA state table.
+    const char *fine = getenv("VKLLM_B200_PERSIST_FINE");
+    P.fine = (fine && atoi(fine) == 0) || P.tg[PK_DOWN].Ks > kFineMaxSegs || P.tg[PK_WO].Ks > kFineMaxSegs ? 0u : 1u;
     std::vector<const __half *> ptrs;
     if (relayout_weights(e, st, &ptrs) != cudaSuccess ||
         cudaMemcpyAsync(e->d_tiled_ptrs, ptrs.data(), sizeof(__half *) * 4 * L, cudaMemcpyHostToDevice, st) !=
@@ -501,7 +534,7 @@ vkllm_err_t run_persistent(Engine *e, uint32_t n, cudaStream_t s)
     {
         const uint32_t k = n > 64 ? 64 : n;
         // barrier arrivals and per-head attention counters (they only grow during a launch)
-        VKB_CUDA(cudaMemsetAsync(e->bar, 0, 4 * (1 + 2 * (size_t)e->dd.H), s));
+        VKB_CUDA(cudaMemsetAsync(e->bar, 0, 4 * (1 + 3 * (size_t)e->dd.H + kPersistMaxGrid), s));
         PersistParams P = e->pp;
         P.n_steps = k;
         if (e->tp)
@@ -794,7 +827,8 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
            off_cnt = off_opart + al((size_t)dd.H * max_split * dd.hd * 4), off_lcnt = off_cnt + al(dd.H * 4),
            off_ring = off_lcnt + al(4), off_state = off_ring + al((size_t)dd.ctx * 4),
            off_amv = off_state + al(sizeof(StepState)), off_ami = off_amv + al((size_t)sms * 32 * 4),
-           off_bar = off_ami + al((size_t)sms * 32 * 4), total = off_bar + al(4 * (1 + 2 * (size_t)dd.H));
+           off_bar = off_ami + al((size_t)sms * 32 * 4),
+           total = off_bar + al(4 * (1 + 3 * (size_t)dd.H + kPersistMaxGrid)); // + per-CTA and per-head flags
     if (cudaMalloc(&e->ws, total) != cudaSuccess)
     {
         (void)cudaGetLastError();
