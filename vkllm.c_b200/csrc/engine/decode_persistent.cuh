@@ -545,24 +545,41 @@ __device__ __forceinline__ bool fine_segment(const PersistParams &P, uint32_t ks
         bool ok = true;
         if (lane == 0)
             while (*reinterpret_cast<volatile uint32_t *>(&s_seg[ks]) != 2u)
+            {
                 if (global_ns() - t0 > kWaitLimitNs || ld_acquire_u32(P.err) != 0)
                 {
                     ok = false;
                     break;
                 }
+                __nanosleep(32);
+            }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         __threadfence_block();
         return ok;
     }
-    // this warp stages it: every lane acquires every producer's flag itself, then loads
-    for (uint32_t b = first; b <= last; ++b)
-        while (ld_acquire_u32(flags + b) < epoch)
-            if (global_ns() - t0 > kWaitLimitNs || ld_acquire_u32(P.err) != 0)
+    // this warp stages it: lane 0 acquires every producer's flag, polling with a growing sleep so that
+    // waiting warps do not flood the flags' L2 lines; __syncwarp then orders the lanes' loads after it
+    bool okw = true;
+    if (lane == 0)
+    {
+        uint32_t nap = 32;
+        for (uint32_t b = first; b <= last && okw; ++b)
+            while (ld_acquire_u32(flags + b) < epoch)
             {
-                if (lane == 0)
+                if (global_ns() - t0 > kWaitLimitNs || ld_acquire_u32(P.err) != 0)
+                {
                     atomicOr(P.err, kErrBarrierTimeout);
-                return false;
+                    okw = false;
+                    break;
+                }
+                __nanosleep(nap);
+                nap = nap < 512 ? 2 * nap : nap;
             }
+    }
+    okw = __shfl_sync(0xffffffffu, okw, 0);
+    if (!okw)
+        return false;
+    __syncwarp();
     const uint32_t n4 = width / 8; // 16-byte chunks, at most 32
     if (lane < n4)
         reinterpret_cast<uint4 *>(xs + ks * kSegHalves)[lane] =
