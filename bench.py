@@ -495,6 +495,14 @@ def run_ours(args, world, rank, local):
 
     import vkllm_b200 as vk
 
+    if args.profile_tp:
+        ctx = vk.Context(local)
+        stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+        tp = tp13b_leg(vk, ctx, args, world, rank, stream)
+        if rank == 0:
+            print(json.dumps({"profile_case": "tp13b", **tp}), flush=True)
+        ctx.close()
+        return None
     cfg = dict(CFG_7B)
     if args.layers:
         cfg["block_count"] = args.layers
@@ -824,6 +832,8 @@ def main():
                     help="profiling case: M,N,K - only the tensor-core GEMM on seeded operands, 4 launches")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="profiling case: only the prompt prefill through the drop-in API (with --layers), 3 runs")
+    ap.add_argument("--profile-tp", action="store_true",
+                    help="profiling case: only the 13B tensor-parallel decode leg over the ranks")
     ap.add_argument("--ops", type=int, default=1, help="operator microbenchmark leg (0: skip)")
     args = ap.parse_args()
     if args.profile_gemm:

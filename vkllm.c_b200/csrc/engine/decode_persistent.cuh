@@ -221,9 +221,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p)
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v)
+// A flag store after the caller's __threadfence_system(): that one fence orders every earlier store
+// of the thread (and, after __syncthreads, of its CTA) before the flags, so the flags to each peer
+// need no release of their own (a system-scope release per peer costs a fence each).
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t *p, uint32_t v)
 {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 struct UnitRange
@@ -269,7 +272,7 @@ __device__ __forceinline__ bool tp_allreduce_rows(const PersistParams &P, uint32
         __threadfence_system(); // this CTA's partial stores to the peers precede the flags
         const uint32_t slot = (site * kTpCtas + blockIdx.x) * kTpMax + P.tp_rank;
         for (uint32_t q = 0; q < P.tp_size; ++q)
-            st_release_sys_u32(P.tp_flag[q] + slot, epoch);
+            st_relaxed_sys_u32(P.tp_flag[q] + slot, epoch);
         bool ok = true;
         const uint32_t *mine = P.tp_flag[P.tp_rank] + (site * kTpCtas + blockIdx.x) * kTpMax;
         const uint64_t t0 = global_ns();
@@ -1340,7 +1343,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                         {
                             __threadfence_system();
                             for (uint32_t q = 0; q < P.tp_size; ++q)
-                                st_release_sys_u32(P.tp_flag[q] + (2 * kTpCtas) * kTpMax + P.tp_rank, epoch);
+                                st_relaxed_sys_u32(P.tp_flag[q] + (2 * kTpCtas) * kTpMax + P.tp_rank, epoch);
                         }
                     }
                     bool okw = true;
