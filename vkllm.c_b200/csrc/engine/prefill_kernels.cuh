@@ -148,7 +148,11 @@ template <int HD> struct PfSmem
     static constexpr int LDT = kPfBK + 8;    // halves per row of the transposed-V tile (quirk Q1)
     static constexpr int kQ = kPfBQ * LD, kK = kPfBK * LD;
     static constexpr int kV = (kPfBK * LD > HD * LDT) ? kPfBK * LD : HD * LDT;
-    static constexpr int kBytes = (kQ + 2 * kK + 2 * kV) * 2; // K and V tiles double-buffered
+    // [Q tile, later value buffer 1 | key buffer 0 | key buffer 1 | value buffer 0]: the Q tile is read
+    // into registers before the first value tile is issued, so its space serves as value buffer 1
+    // (three CTAs per SM fit at HD = 128)
+    static constexpr int kQV = kQ > kV ? kQ : kV;
+    static constexpr int kBytes = (kQV + 2 * kK + kV) * 2;
 };
 
 // Loads rows [r0, r0 + rows) (of `n_valid` existing rows) of a [*, HD] fp16 matrix with row pitch
@@ -251,7 +255,7 @@ __device__ __forceinline__ void pf_scores(const uint32_t (&qa)[HD / 16][4], cons
 // When Lk == HD the reference's shape-only predicate reads the V slice as [HD, Lk]
 // (src/core/vkllm_op_matmul.c:14-30): the product is then out[i][w] = sum_j p_ij V[w][j].
 template <int HD>
-__global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__restrict__ rq, const __half *__restrict__ kc,
+__global__ void __launch_bounds__(kPfThreads, 3) k_pf_attention(const __half *__restrict__ rq, const __half *__restrict__ kc,
                                                              const __half *__restrict__ vc, uint32_t ctx, uint32_t S,
                                                              uint32_t p0, uint32_t H, float scale,
                                                              __half *__restrict__ out)
@@ -260,8 +264,8 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
     constexpr int LD = SM::LD, LDT = SM::LDT;
     extern __shared__ __align__(16) unsigned char pf_sm[];
     __half *sq = reinterpret_cast<__half *>(pf_sm);
-    // buffer b of the key tiles at sk0 + b * kK, of the value tiles at sv0 + b * kV
-    __half *const sk0 = sq + SM::kQ, *const sv0 = sq + SM::kQ + 2 * SM::kK;
+    // key buffer b at sk0 + b * kK; value buffer 0 at sv0, value buffer 1 where the Q tile was
+    __half *const sk0 = sq + SM::kQV, *const sv0 = sq + SM::kQV + 2 * SM::kK;
     const uint32_t h = blockIdx.y, q0 = blockIdx.x * kPfBQ;
     const uint32_t Lk = p0 + S;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -357,9 +361,9 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
         const uint32_t jb = blk * kPfBK;
         pf_async_rows<HD, LD>(sk0 + (blk & 1) * SM::kK, kb, HD, jb, kPfBK, Lk);
         if (!q1)
-            pf_async_rows<HD, LD>(sv0 + (blk & 1) * SM::kV, vb, HD, jb, kPfBK, Lk);
+            pf_async_rows<HD, LD>(((blk & 1) ? sq : sv0), vb, HD, jb, kPfBK, Lk);
         else
-            pf_async_vt<HD, LDT>(sv0 + (blk & 1) * SM::kV, vb, jb);
+            pf_async_vt<HD, LDT>(((blk & 1) ? sq : sv0), vb, jb);
         pf_cp_commit();
     };
     issue_kv(0);
@@ -374,7 +378,7 @@ __global__ void __launch_bounds__(kPfThreads) k_pf_attention(const __half *__res
         else
             pf_cp_wait<0>();
         __syncthreads();
-        const __half *sk = sk0 + (kb_i & 1) * SM::kK, *sv = sv0 + (kb_i & 1) * SM::kV;
+        const __half *sk = sk0 + (kb_i & 1) * SM::kK, *sv = ((kb_i & 1) ? sq : sv0);
         pf_scores<HD, LD>(qa, sk, scale, s);
         // p = fp16(exp(s - max) / sum) where unmasked, else 0 (the softmax node)
 #pragma unroll
