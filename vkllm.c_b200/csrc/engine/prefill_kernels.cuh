@@ -255,7 +255,7 @@ __device__ __forceinline__ void pf_scores(const uint32_t (&qa)[HD / 16][4], cons
 // When Lk == HD the reference's shape-only predicate reads the V slice as [HD, Lk]
 // (src/core/vkllm_op_matmul.c:14-30): the product is then out[i][w] = sum_j p_ij V[w][j].
 template <int HD>
-__global__ void __launch_bounds__(kPfThreads, 3) k_pf_attention(const __half *__restrict__ rq, const __half *__restrict__ kc,
+__global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(const __half *__restrict__ rq, const __half *__restrict__ kc,
                                                              const __half *__restrict__ vc, uint32_t ctx, uint32_t S,
                                                              uint32_t p0, uint32_t H, float scale,
                                                              __half *__restrict__ out)
