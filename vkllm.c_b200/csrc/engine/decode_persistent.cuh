@@ -128,8 +128,6 @@ struct PersistParams
     const uint32_t *dn_seg;     // [2 * segments of the down phase]
     uint32_t l2_bytes;          // per CTA: next-phase weights prefetched into L2 at each barrier
     uint32_t l2_hint;           // 1: stage loads mark their lines evict-first in L2
-    uint32_t l2_after;          // 1: the L2 prefetch of the next phase is issued once the grid barrier
-                                // released (0: when the CTA arrives at it)
     // Tensor parallelism over peer memory (tp_size 1: off). Each rank owns H / N heads, F / N FFN
     // rows and V / N vocabulary rows (from v0); the Wo and down outputs are partial sums that every
     // rank writes, per output row, into every peer's receive area, then raises a flag per CTA.
@@ -1159,15 +1157,13 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 stage_rmsnorm_h(P.x, lw.attn_norm, dd.D, dd.eps, xs, sred);
             trace_mark(P, tr);
             ok = persist_gemv<2>(P, PK_QKV, l, wp, xs, part, pos, tr);
-            if (threadIdx.x == 0 && !P.l2_after)
+            if (threadIdx.x == 0)
                 prefetch_slice(P, PK_WO, l);
             if (!__syncthreads_and(ok) || !grid_sync(P, tr))
             {
                 ok = false;
                 break;
             }
-            if (threadIdx.x == 0 && P.l2_after)
-                prefetch_slice(P, PK_WO, l);
             if (P.fine)
             {
                 // Wo tiles wait only for the heads their input columns span
@@ -1193,7 +1189,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 trace_mark(P, tr);
                 ok = persist_gemv<1>(P, PK_WO, l, wp, xs, part, pos, tr);
             }
-            if (threadIdx.x == 0 && !P.l2_after)
+            if (threadIdx.x == 0)
                 prefetch_slice(P, PK_UPGATE, l);
             if (P.tp_size > 1 && __syncthreads_and(ok))
                 ok = tp_allreduce_rows(P, 0, P.tp_base[0] + step * P.L + l + 1);
@@ -1202,12 +1198,10 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 ok = false;
                 break;
             }
-            if (threadIdx.x == 0 && P.l2_after)
-                prefetch_slice(P, PK_UPGATE, l);
             stage_rmsnorm_h(P.x, lw.ffn_norm, dd.D, dd.eps, xs, sred);
             trace_mark(P, tr);
             ok = persist_gemv<2>(P, PK_UPGATE, l, wp, xs, part, pos, tr);
-            if (threadIdx.x == 0 && !P.l2_after)
+            if (threadIdx.x == 0)
                 prefetch_slice(P, PK_DOWN, l);
             if (P.fine)
             {
@@ -1236,13 +1230,11 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                     ok = false;
                     break;
                 }
-                if (threadIdx.x == 0 && P.l2_after)
-                    prefetch_slice(P, PK_DOWN, l);
                 stage_copy_h(P.m, dd.F, xs);
                 trace_mark(P, tr);
                 ok = persist_gemv<1>(P, PK_DOWN, l, wp, xs, part, pos, tr);
             }
-            if (threadIdx.x == 0 && !P.l2_after)
+            if (threadIdx.x == 0)
                 prefetch_slice(P, l + 1 < P.L ? PK_QKV : PK_LOGITS, l + 1 < P.L ? l + 1 : 0);
             if (P.tp_size > 1 && __syncthreads_and(ok))
                 ok = tp_allreduce_rows(P, 1, P.tp_base[1] + step * P.L + l + 1);
@@ -1251,8 +1243,6 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 ok = false;
                 break;
             }
-            if (threadIdx.x == 0 && P.l2_after)
-                prefetch_slice(P, l + 1 < P.L ? PK_QKV : PK_LOGITS, l + 1 < P.L ? l + 1 : 0);
         }
         if (!ok)
             break;

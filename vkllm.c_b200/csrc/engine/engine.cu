@@ -350,8 +350,6 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     // and the barrier prefetches stay resident: 7B 2.844 -> 2.813 ms/token. "0" turns it off.
     const char *hint = getenv("VKLLM_B200_PERSIST_L2_HINT");
     P.l2_hint = hint ? (uint32_t)atoi(hint) : 1u;
-    const char *after = getenv("VKLLM_B200_PERSIST_L2_AFTER");
-    P.l2_after = after && atoi(after) != 0 ? 1u : 0u;
 
     // Weight tiles of 16 rows x 256 columns; every K must be a multiple of 16 (MMA k-step).
     if (dd.D % 16 != 0 || HD % 16 != 0 || dd.F % 16 != 0)
