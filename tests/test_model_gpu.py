@@ -8,8 +8,8 @@ max-abs 2e-2 and mean-abs 2e-3 at every step whose inputs agree. Every execution
 node by node (STRICT, the reference's own DAG), the persistent decode kernel (FUSED, the default),
 the CUDA-graph decode path that runs when cooperative launch is unavailable (VKLLM_B200_DECODE=graph),
 the persistent kernel with its row partition calibrated at engine creation
-(VKLLM_B200_PERSIST_BALANCE=2), and the persistent kernel with a grid barrier before the down phase
-instead of per-segment waits (VKLLM_B200_PERSIST_FINE=0)."""
+(VKLLM_B200_PERSIST_BALANCE=2), and the persistent kernel whose Wo and down tiles wait per input
+segment for its producers instead of at grid barriers (VKLLM_B200_PERSIST_FINE=1)."""
 import numpy as np
 import pytest
 
@@ -32,7 +32,7 @@ def reference_run(tiny_gguf, orc):
 
 
 MODES = {"strict": {}, "fused": {}, "fused_graph": {"VKLLM_B200_DECODE": "graph"},
-         "fused_balanced": {"VKLLM_B200_PERSIST_BALANCE": "2"}, "fused_coarse": {"VKLLM_B200_PERSIST_FINE": "0"}}
+         "fused_balanced": {"VKLLM_B200_PERSIST_BALANCE": "2"}, "fused_fine": {"VKLLM_B200_PERSIST_FINE": "1"}}
 
 
 @pytest.mark.parametrize("mode", list(MODES))
