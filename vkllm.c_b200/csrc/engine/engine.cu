@@ -1036,13 +1036,19 @@ template <int HD>
 bool pf_attention_launch(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint32_t S, uint32_t p0,
                          __half *out, cudaStream_t s)
 {
-    static bool attr_set = false;
-    if (!attr_set)
+    static bool attr_set[64] = {}; // per device: the attribute is a property of the current device's function
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return false;
+    if (!attr_set[dev])
     {
         if (cudaFuncSetAttribute(k_pf_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PfSmem<HD>::kBytes) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
             return false;
-        attr_set = true;
+        }
+        attr_set[dev] = true;
     }
     dim3 grid((S + kPfBQ - 1) / kPfBQ, dd.H);
     k_pf_attention<HD><<<grid, kPfThreads, PfSmem<HD>::kBytes, s>>>(rq, lw.kcache, lw.vcache, dd.ctx, S, p0, dd.H,
