@@ -219,8 +219,11 @@ def prefill_gemm_roofline(vk, l, model, cfg, stream):
 
     D, F, V = cfg["embedding_length"], cfg["ffn_length"], cfg["vocab_size"]
     bw = model.block(0)
-    shapes = {"qkv/wo (4096x4096)": (bw.WQ, D, D), "up/gate (11008x4096)": (bw.WU, F, D),
-              "down (4096x11008)": (bw.WD, D, F), "logits (32000x4096)": (model.m.weights.output_weight, V, D)}
+    # The fused prefill runs Q/K/V and up/gate as one grouped GEMM each (N = 3 D and 2 F); a
+    # contiguous seeded B of that height stands in for the three (two) weight blocks, same tiles.
+    shapes = {"qkv grouped (12288x4096)": (None, 3 * D, D), "wo (4096x4096)": (bw.WO, D, D),
+              "up/gate grouped (22016x4096)": (None, 2 * F, D), "down (4096x11008)": (bw.WD, D, F),
+              "logits (32000x4096)": (model.m.weights.output_weight, V, D)}
     peak = 1656.1
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -232,7 +235,8 @@ def prefill_gemm_roofline(vk, l, model, cfg, stream):
     for name, (w, N, K) in shapes.items():
         A = (torch.rand((M, K), generator=g, device="cuda") * 0.2 - 0.1).half()
         Cm = torch.empty((M, N), device="cuda", dtype=torch.float16)
-        B = w.contents.data.dev
+        Bt = (torch.randn((N, K), generator=g, device="cuda") * 0.02).half() if w is None else None
+        B = Bt.data_ptr() if w is None else w.contents.data.dev
         args = (A.data_ptr(), B, Cm.data_ptr(), M, N, K, K, K, N, 1.0, 0, stream.cuda_stream)
         for _ in range(3):
             vk.check(l.vkllm_b200_gemm_f16(*args), "gemm")
