@@ -54,6 +54,8 @@ struct vkllm_b200_batch
     uint32_t tiled = 1;                                                  // GEMM operands in tile order
     uint32_t att_staged = 256; // threads of k_b_attention_staged (0: k_b_attention)
     uint32_t att_chunk = 64, att_ring = 3; // its rows per chunk and chunk buffers
+    // K splits and tiles (0: 128 x 128, 1: 128 x 256) of the QKV, up/gate and Wo / down GEMMs
+    uint32_t qkv_splits = 2, ug_splits = 3, proj_splits = 4, qkv_tile = 1, ug_tile = 1, proj_tile = 0;
     const float *out_norm = nullptr;
     void *ws = nullptr;
     __half *kv = nullptr; // [L][2][B][H][cap][hd]
@@ -74,9 +76,6 @@ namespace
 {
 
 constexpr int kBT = 256;
-constexpr uint32_t kProjSplits = 4; // K splits of the Wo / down GEMMs (M = sequences); <= kMaxPartSplits
-constexpr uint32_t kQkvSplits = 2;  // K splits of the QKV GEMM (128 x 256 tiles)
-constexpr uint32_t kUgSplits = 3;   // K splits of the up/gate GEMM (128 x 256 tiles)
 
 // Lets the next kernel in the stream, when it was launched as this one's programmatic dependent (the
 // batch's GEMMs), start its CTAs now; it still waits for this grid's completion before reading.
@@ -86,8 +85,7 @@ __device__ __forceinline__ void pdl_trigger()
 }
 
 constexpr uint32_t kMaxPartSplits = 4; // most split-K partials a consumer kernel sums
-static_assert(kProjSplits <= kMaxPartSplits && kQkvSplits <= kMaxPartSplits && kUgSplits <= kMaxPartSplits,
-              "the partial-summing kernels read at most kMaxPartSplits splits");
+
 
 // t[e] = sum over the splits (in split order, from 0) of the 8 fp32 partials at src + s * plane.
 // Every split's loads are issued before the first add, so the reads overlap (the partials were just
@@ -868,14 +866,16 @@ bool gemm_partials(const __half *A, const __half *W, uint32_t tiled, float *part
 }
 
 // The Wo / down projection with its residual add and the following RMSNORM (gains g) in one pass
-// over the rows when the GEMM can split K 4 ways into bt->part, else the three nodes separately.
+// over the rows when the GEMM can split K (bt->proj_splits ways) into bt->part, else the three nodes
+// separately.
 vkllm_err_t proj_residual_norm(vkllm_b200_batch *bt, const __half *in, const __half *w, uint32_t K, const float *g,
                                cudaStream_t s)
 {
     const BatchDims &dd = bt->dd;
     const uint32_t B = bt->B, D = dd.D;
     uint32_t used = 0;
-    if (gemm_partials(in, w, bt->tiled, bt->part, B, D, K, kProjSplits, &used, s))
+    if (bt->proj_splits > 1 && gemm_partials(in, w, bt->tiled, bt->part, B, D, K, bt->proj_splits, &used, s,
+                                             bt->proj_tile))
     {
         // a thread per 8 columns (up to 1024), so each thread's partial loads are issued at once
         const uint32_t threads = std::min(1024u, std::max(64u, (D / 8 + 31) & ~31u));
@@ -909,7 +909,8 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
             k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
         // QKV as split-K partials summed by the RoPE / KV-row kernel (else the GEMM's own reduction)
         uint32_t used = 0;
-        if (gemm_partials(bt->xn, w.wqkv, bt->tiled, bt->part, B, 3 * HD, D, kQkvSplits, &used, s, 1))
+        if (bt->qkv_splits > 1 &&
+            gemm_partials(bt->xn, w.wqkv, bt->tiled, bt->part, B, 3 * HD, D, bt->qkv_splits, &used, s, bt->qkv_tile))
             k_b_rope_kv_part<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->part, used, bt->qkv, HD, bt->pos, H, hd,
                                                                               bt->cap, dd.rope_base, kc, vc, B);
         else
@@ -931,7 +932,8 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
         _CHECK(proj_residual_norm(bt, bt->attn, w.wo_g, HD, w.ffn_norm, s));
         // up/gate as split-K partials summed by the gate kernel (else the GEMM's own reduction, with
         // SiLU on the gate half only)
-        if (gemm_partials(bt->xn, w.wug, bt->tiled, bt->part, B, 2 * F, D, kUgSplits, &used, s, 1))
+        if (bt->ug_splits > 1 &&
+            gemm_partials(bt->xn, w.wug, bt->tiled, bt->part, B, 2 * F, D, bt->ug_splits, &used, s, bt->ug_tile))
             k_b_gate_part<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->part, used, F, B);
         else
         {
@@ -1008,8 +1010,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     bt->ring_steps = 1024;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t kv_bytes = al((size_t)bt->L * 2 * B * dd.H * bt->cap * dd.hd * 2);
-    const size_t part_elems = (size_t)B * std::max({(size_t)kProjSplits * D, (size_t)kQkvSplits * 3 * HD,
-                                                    (size_t)kUgSplits * 2 * F});
+    const size_t part_elems = (size_t)B * kMaxPartSplits * std::max({(size_t)D, (size_t)3 * HD, (size_t)2 * F});
     const size_t act = al((size_t)B * D * 2) * 3 + al((size_t)B * 3 * HD * 2) + al((size_t)B * HD * 2) +
                        al((size_t)B * 2 * F * 2) + al((size_t)B * F * 2) + al((size_t)B * dd.V * 2) +
                        al(part_elems * 4);
@@ -1055,6 +1056,19 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     if (!(bt->att_staged == 128 || bt->att_staged == 256 || bt->att_staged == 512) || dd.hd % 8 || dd.hd > 128 ||
         att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_staged = 0;
+    // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0 / 1) of the QKV, up/gate
+    // and Wo / down GEMMs (defaults 2,3,4,1,1,0)
+    if (const char *ge = getenv("VKLLM_B200_BATCH_GEMM"))
+    {
+        unsigned v[6];
+        if (sscanf(ge, "%u,%u,%u,%u,%u,%u", &v[0], &v[1], &v[2], &v[3], &v[4], &v[5]) == 6 && v[0] >= 1 &&
+            v[0] <= kMaxPartSplits && v[1] >= 1 && v[1] <= kMaxPartSplits && v[2] >= 1 && v[2] <= kMaxPartSplits &&
+            v[3] <= 1 && v[4] <= 1 && v[5] <= 1)
+        {
+            bt->qkv_splits = v[0], bt->ug_splits = v[1], bt->proj_splits = v[2];
+            bt->qkv_tile = v[3], bt->ug_tile = v[4], bt->proj_tile = v[5];
+        }
+    }
     const char *tiled_env = getenv("VKLLM_B200_BATCH_TILED");
     bt->tiled = tiled_env && atoi(tiled_env) == 0 ? 0u : 1u;
     const size_t t_qkv = gemm_tiled_b_elems(3 * HD, D), t_ug = gemm_tiled_b_elems(2 * F, D),
