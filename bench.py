@@ -257,6 +257,42 @@ def prefill_gemm_roofline(vk, l, model, cfg, stream):
     return out
 
 
+def host_graph_cost(vk, ctx, model, pos, n=200):
+    """Host time per token of the reference loop's graph handling (tests/vkllm_test_infer_gguf.c:181-272)
+    without the device step: input tensor_new + graph_new + build_graph + graph_init, then graph_free,
+    with the structural graph cache on and off. Microseconds per token (median of 5 blocks of n),
+    measured around the ctypes calls (each adds ~0.1-0.3 us of Python overhead)."""
+    import ctypes as C
+
+    l = vk.lib()
+    out = {}
+    for on in (True, False):
+        ctx.set_graph_cache(on)
+        blocks = []
+        for _ in range(6):
+            t_build = t_free = 0
+            for i in range(n):
+                t0 = time.perf_counter_ns()
+                inp = vk.tensor_new(ctx, "input_toks", (1, 1, 1, 1), vk.U32, mapped=True)
+                g = C.POINTER(vk.Graph)()
+                vk.check(l.vkllm_graph_new(ctx.ptr, C.byref(g)), "graph_new")
+                vk.check(l.vkllm_models_llama2_build_graph(ctx.ptr, C.byref(model.m), inp, g, pos + i % 64),
+                         "build_graph")
+                vk.check(l.vkllm_graph_init(ctx.ptr, g), "graph_init")
+                t1 = time.perf_counter_ns()
+                l.vkllm_graph_free(ctx.ptr, g)
+                t2 = time.perf_counter_ns()
+                t_build += t1 - t0
+                t_free += t2 - t1
+            blocks.append((t_build / n / 1e3, t_free / n / 1e3))
+        blocks = sorted(blocks[1:], key=lambda b: b[0] + b[1])  # the first block warms the cache
+        b, f = blocks[len(blocks) // 2]
+        out["cache_on" if on else "cache_off"] = {"build_init_us": round(b, 2), "free_us": round(f, 2),
+                                                  "total_us": round(b + f, 2)}
+    ctx.set_graph_cache(True)
+    return out
+
+
 def batched_decode_leg(vk, model, args, world, rank, stream):
     """64 independent sequences with their own 128-token seeded prompts, greedy
     decode on the tensor-core GEMM path, sequences split evenly over the ranks (data parallel).
@@ -604,6 +640,9 @@ def run_ours(args, world, rank, local):
     if args.batch_seqs > 0:
         batched = batched_decode_leg(vk, model, args, world, rank, stream)
 
+    # ---- host cost of the per-token graph rebuild (no device work) ---------------------------------
+    host_cost = host_graph_cost(vk, ctx, model, PROMPT_LEN + W + K)
+
     # ---- e2e: reference token loop through the C API, host buffers --------------------------------
     pos = PROMPT_LEN + W + K
     tok = int(toks[-1])
@@ -684,7 +723,8 @@ def run_ours(args, world, rank, local):
                         "gemms": prefill_gemms},
             "batched": batched,
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                    "steps": n_e2e, "path": "reference token loop through the C API (graph rebuilt per token)"},
+                    "steps": n_e2e, "path": "reference token loop through the C API (graph rebuilt per token)",
+                    "host_graph_us_per_token": host_cost},
             "gpu_launches": int(launches if persistent else kps * K),
             "clocks": clk.summary(),
         }

@@ -111,6 +111,16 @@ enum
 extern vkllm_err_t vkllm_b200_set_exec_mode(struct vkllm_context *context, int mode);
 extern int vkllm_b200_get_exec_mode(struct vkllm_context *context);
 
+/* Structural graph cache (on by default; VKLLM_B200_GRAPH_CACHE=0 at context creation turns it off).
+ * vkllm_graph_free hands the nodes of a graph built by vkllm_models_llama2_build_graph to the
+ * context, and the next build for the same model, batch and token count takes them back, rewriting
+ * only the fields that follow the position (RoPE and softmax offsets, KV-slice rows, score columns).
+ * The graph the caller sees is the one a fresh build makes; node buffers stay attached between
+ * tokens. A caller that edits a built graph's nodes in place before freeing it turns the cache off.
+ * Turning it off (on = 0) frees the cached nodes; a model's entries go with vkllm_models_llama2_free,
+ * and all entries with a change of execution mode. */
+extern vkllm_err_t vkllm_b200_set_graph_cache(struct vkllm_context *context, int on);
+
 /* The context's CUDA stream (cudaStream_t); all graph work is enqueued on it. */
 extern void *vkllm_b200_context_stream(struct vkllm_context *context);
 extern int vkllm_b200_context_device(struct vkllm_context *context);

@@ -1224,8 +1224,11 @@ vkllm_err_t plan_run(vkllm_context *ctx, vkllm_graph *graph)
     return VKLLM_ERR_OK;
 }
 
-void plan_free(vkllm_graph *graph)
+void graph_cache_detach(vkllm_context *ctx, Plan *plan);
+
+void plan_free(vkllm_context *ctx, vkllm_graph *graph)
 {
+    graph_cache_detach(ctx, (Plan *)graph->b200_plan);
     free(graph->b200_plan);
     graph->b200_plan = nullptr;
 }

@@ -9,6 +9,8 @@ struct vkllm_tensor;
 namespace vkb
 {
 
+struct GraphCacheEntry;
+
 struct Plan
 {
     vkllm_models_llama2 *model;
@@ -17,6 +19,7 @@ struct Plan
     uint32_t offsets;         // position of the first token
     uint32_t seq_len;         // S
     size_t n_nodes;           // node count when built; a later edit disables the plan
+    GraphCacheEntry *cache_entry; // structural-cache entry whose nodes this graph holds (models/graph_cache.cpp)
 };
 
 } // namespace vkb

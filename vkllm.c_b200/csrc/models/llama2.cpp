@@ -26,6 +26,12 @@ vkllm_err_t fill_random_f16_shard(vkllm_context *ctx, void *dst, uint64_t rows, 
 vkllm_err_t fill_random_f16(vkllm_context *ctx, void *dst, uint64_t n, uint64_t seed, uint64_t tensor_id,
                             float std_dev);
 vkllm_err_t fill_const_f32(vkllm_context *ctx, void *dst, uint64_t n, float v);
+void plan_free(vkllm_context *ctx, vkllm_graph *graph);
+// Structural graph cache (graph_cache.cpp).
+bool graph_cache_take(vkllm_context *ctx, vkllm_models_llama2 *model, vkllm_tensor *input_toks, vkllm_graph *graph,
+                      uint32_t offsets, Plan *plan);
+void graph_cache_register(vkllm_context *ctx, vkllm_models_llama2 *model, vkllm_graph *graph, Plan *plan);
+void graph_cache_purge(vkllm_context *ctx, const vkllm_models_llama2 *model);
 } // namespace vkb
 
 namespace
@@ -437,6 +443,7 @@ extern "C" vkllm_err_t vkllm_b200_gguf_read_shard(const char *file, const char *
 extern "C" vkllm_err_t vkllm_models_llama2_free(struct vkllm_context *context, struct vkllm_models_llama2 *model)
 {
     _CHECK_ARGS(context && model);
+    vkb::graph_cache_purge(context, model);
     vkb::engine_destroy(context, model);
     vkb::tp_comm_free(model);
     if (model->meta.tokens)
@@ -474,6 +481,9 @@ extern "C" vkllm_err_t vkllm_models_llama2_free(struct vkllm_context *context, s
     return VKLLM_ERR_OK;
 }
 
+static vkllm_err_t build_graph_nodes(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                     struct vkllm_tensor *input_toks, struct vkllm_graph *graph, uint32_t offsets);
+
 extern "C" vkllm_err_t vkllm_models_llama2_build_graph(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                                        struct vkllm_tensor *input_toks, struct vkllm_graph *graph,
                                                        uint32_t offsets)
@@ -482,10 +492,45 @@ extern "C" vkllm_err_t vkllm_models_llama2_build_graph(struct vkllm_context *con
     _CHECK_ARGS(model->weights.tok_embed_weights && model->weights.output_norm_weight && model->weights.output_weight);
     _CHECK_ARGS(model->weights.blocks && model->weights.blocks->used_n > 0 && model->weights.kvcache);
     _CHECK_ARGS(input_toks->dtype == vkllm_dtype_uint32);
-    uint32_t B = input_toks->shapes[0], S = input_toks->shapes[3];
-    uint32_t D = model->meta.embedding_length, V = model->meta.vocab_size;
+    const uint32_t S = input_toks->shapes[3];
     _CHECK_ARGS((uint64_t)offsets + S <= model->meta.context_length);
 
+    // A plan left by an earlier build into this graph goes (its nodes stay in the graph).
+    vkb::plan_free(context, graph);
+    vkb::Plan *plan = (vkb::Plan *)calloc(1, sizeof(vkb::Plan));
+    if (!plan)
+        return VKLLM_ERR_ALLOC;
+    plan->model = model;
+    plan->input_toks = input_toks;
+    plan->offsets = offsets;
+    plan->seq_len = S;
+    if (graph->nodes->used_n == 0 && vkb::graph_cache_take(context, model, input_toks, graph, offsets, plan))
+    {
+        plan->output = graph->output_node;
+        plan->n_nodes = graph->nodes->used_n;
+        graph->b200_plan = plan;
+        return VKLLM_ERR_OK;
+    }
+    vkllm_err_t pe = build_graph_nodes(context, model, input_toks, graph, offsets);
+    if (pe != VKLLM_ERR_OK)
+    {
+        free(plan);
+        return pe;
+    }
+    plan->output = graph->output_node;
+    plan->n_nodes = graph->nodes->used_n;
+    graph->b200_plan = plan;
+    vkb::graph_cache_register(context, model, graph, plan);
+    return VKLLM_ERR_OK;
+}
+
+// The reference builder's node sequence (src/models/vkllm_models_llama2.c:488-602): the input, the
+// embedding, the transformer blocks, the output norm, the logits and the mapped ARG_MAX output.
+static vkllm_err_t build_graph_nodes(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                     struct vkllm_tensor *input_toks, struct vkllm_graph *graph, uint32_t offsets)
+{
+    uint32_t B = input_toks->shapes[0], S = input_toks->shapes[3];
+    uint32_t D = model->meta.embedding_length, V = model->meta.vocab_size;
     _CHECK(vkllm_graph_add_input(context, graph, input_toks));
     uint32_t eshape[4] = {B, 1, S, D};
     vkllm_tensor *esrcs[] = {input_toks, model->weights.tok_embed_weights};
@@ -542,19 +587,6 @@ extern "C" vkllm_err_t vkllm_models_llama2_build_graph(struct vkllm_context *con
                             &output));
     _CHECK(vkllm_graph_add_node(context, graph, output));
     _CHECK(vkllm_graph_set_output(context, graph, output));
-
-    vkb::Plan *plan = (vkb::Plan *)calloc(1, sizeof(vkb::Plan));
-    if (plan)
-    {
-        plan->model = model;
-        plan->input_toks = input_toks;
-        plan->output = output;
-        plan->offsets = offsets;
-        plan->seq_len = S;
-        plan->n_nodes = graph->nodes->used_n;
-        free(graph->b200_plan);
-        graph->b200_plan = plan;
-    }
     return VKLLM_ERR_OK;
 }
 

@@ -7,6 +7,11 @@
 #include "vkllm_kvcache.h"
 #include "vkllm_models_llama2.h"
 
+namespace vkb
+{
+void graph_cache_purge(vkllm_context *ctx, const vkllm_models_llama2 *model);
+}
+
 extern "C" const char *vkllm_b200_version(void)
 {
     return "vkllm-b200 0.1 (sm_100a)";
@@ -16,7 +21,18 @@ extern "C" vkllm_err_t vkllm_b200_set_exec_mode(struct vkllm_context *context, i
 {
     _CHECK_ARGS(context && context->runtime);
     _CHECK_ARGS(mode == VKLLM_B200_EXEC_FUSED || mode == VKLLM_B200_EXEC_STRICT);
+    if (context->runtime->exec_mode != mode) // cached nodes of one mode carry that mode's buffers
+        vkb::graph_cache_purge(context, nullptr);
     context->runtime->exec_mode = mode;
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_set_graph_cache(struct vkllm_context *context, int on)
+{
+    _CHECK_ARGS(context && context->runtime);
+    if (!on)
+        vkb::graph_cache_purge(context, nullptr);
+    context->runtime->graph_cache_on = on != 0;
     return VKLLM_ERR_OK;
 }
 

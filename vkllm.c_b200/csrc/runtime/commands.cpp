@@ -38,12 +38,23 @@ extern "C" vkllm_err_t vkllm_commands_new(struct vkllm_context *context, struct 
     // All commands objects of a context share its in-order stream, as every reference commands
     // object shares device queue 0 (src/core/vkllm_commands.c:87-94).
     p->stream = (void *)context->runtime->stream;
+    // The reference loop creates a commands object per token (with its graph); completion events
+    // are recycled through the context.
     cudaEvent_t ev;
-    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-    if (e != cudaSuccess)
+    auto &pool = context->runtime->event_pool;
+    if (!pool.empty())
     {
-        free(p);
-        return vkb::cuda_check(e, "cudaEventCreateWithFlags", __FILE__, __LINE__);
+        ev = (cudaEvent_t)pool.back();
+        pool.pop_back();
+    }
+    else
+    {
+        cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        if (e != cudaSuccess)
+        {
+            free(p);
+            return vkb::cuda_check(e, "cudaEventCreateWithFlags", __FILE__, __LINE__);
+        }
     }
     p->done = (void *)ev;
     vkllm_err_t err = vkllm_array_commands_task_new(&p->defer_tasks, 16);
@@ -66,9 +77,11 @@ extern "C" void vkllm_commands_free(struct vkllm_context *context, struct vkllm_
     for (size_t i = 0; i < commands->defer_tasks->used_n; ++i)
         commands->defer_tasks->data[i].func(&commands->defer_tasks->data[i]);
     vkllm_array_commands_task_free(commands->defer_tasks);
-    cudaEventDestroy((cudaEvent_t)commands->done);
+    if (context && context->runtime && context->runtime->event_pool.size() < 64)
+        context->runtime->event_pool.push_back(commands->done);
+    else
+        cudaEventDestroy((cudaEvent_t)commands->done);
     free(commands);
-    (void)context;
 }
 
 extern "C" vkllm_err_t vkllm_commands_begin(struct vkllm_context *context, struct vkllm_commands *commands)

@@ -51,6 +51,8 @@ extern "C" vkllm_err_t vkllm_context_new(uint32_t dev, struct vkllm_context **co
     rt->exec_mode = (strict && atoi(strict) != 0) ? VKLLM_EXEC_STRICT : VKLLM_EXEC_FUSED;
     const char *timing = getenv("VKLLM_NODE_TIMING");
     rt->node_timing = timing && atoi(timing) != 0;
+    const char *gc = getenv("VKLLM_B200_GRAPH_CACHE");
+    rt->graph_cache_on = !(gc && atoi(gc) == 0);
 
     vkllm_err_t err = vkllm_hashmap_new(&p->stats.node_time_cost, 1024);
     if (err != VKLLM_ERR_OK)
@@ -59,9 +61,12 @@ extern "C" vkllm_err_t vkllm_context_new(uint32_t dev, struct vkllm_context **co
     return VKLLM_ERR_OK;
 }
 
+struct vkllm_models_llama2;
+
 namespace vkb
 {
 void engine_release_all(vkllm_context *ctx);
+void graph_cache_purge(vkllm_context *ctx, const vkllm_models_llama2 *model);
 }
 
 extern "C" void vkllm_context_free(struct vkllm_context *p)
@@ -73,6 +78,7 @@ extern "C" void vkllm_context_free(struct vkllm_context *p)
     {
         if (rt->stream)
             cudaStreamSynchronize(rt->stream);
+        vkb::graph_cache_purge(p, nullptr); // cached nodes hold buffers of both allocators
         for (auto &kv : rt->pipelines)
         {
             if (kv.second->ev_start)
@@ -83,6 +89,8 @@ extern "C" void vkllm_context_free(struct vkllm_context *p)
         }
         for (void *b : rt->tensor_pool)
             free(b);
+        for (void *ev : rt->event_pool)
+            cudaEventDestroy((cudaEvent_t)ev);
         delete rt->dev_alloc;
         delete rt->host_alloc;
         if (rt->dev_error_word)

@@ -16,10 +16,12 @@
 
 namespace vkb
 {
-// Fused LLaMA-2 step for graphs carrying a plan (engine/fused_step.cpp). Returns VKLLM_ERR_ARGS
+// Fused LLaMA-2 step for graphs carrying a plan (engine/engine.cu). Returns VKLLM_ERR_ARGS
 // when the plan does not apply, in which case the graph runs node by node.
 vkllm_err_t plan_run(vkllm_context *ctx, vkllm_graph *graph);
-void plan_free(vkllm_graph *graph);
+void plan_free(vkllm_context *ctx, vkllm_graph *graph);
+// Structural graph cache (models/graph_cache.cpp): true when the nodes after the input went back to it.
+bool graph_cache_give(vkllm_context *ctx, vkllm_graph *graph);
 } // namespace vkb
 
 namespace
@@ -214,11 +216,12 @@ extern "C" vkllm_err_t vkllm_graph_free(struct vkllm_context *context, struct vk
 {
     _CHECK_ARGS(context && graph);
     vkllm_commands_free(context, graph->commands);
-    for (size_t i = 0; i < graph->nodes->used_n; i++)
+    const size_t n = vkb::graph_cache_give(context, graph) ? 1 : graph->nodes->used_n;
+    for (size_t i = 0; i < n; i++)
         vkllm_tensor_free(context, graph->nodes->data[i]);
     vkllm_array_tensor_free(graph->nodes);
     vkllm_array_tensor_free(graph->input_nodes);
-    vkb::plan_free(graph);
+    vkb::plan_free(context, graph);
     free(graph);
     return VKLLM_ERR_OK;
 }

@@ -33,6 +33,10 @@ struct vkllm_gpu_device
 namespace vkb
 {
 
+// Node set of a graph built by vkllm_models_llama2_build_graph, kept between vkllm_graph_free and the
+// next build for the same model and shapes (models/graph_cache.cpp).
+struct GraphCacheEntry;
+
 // Caching allocator: device memory and pinned, device-mapped host memory are recycled through
 // size-class free lists so that the reference's allocate-every-node-every-step pattern costs no
 // cudaMalloc/cudaFree (which would synchronise the device) after warm-up.
@@ -85,6 +89,9 @@ struct vkllm_b200_runtime
     bool node_timing = false;
     int* dev_error_word = nullptr; // device-side error flag written by kernels with bounded waits
     std::vector<void *> tensor_pool; // freed tensor structs of the pooled size (tensor.cpp)
+    std::vector<void *> event_pool;  // completion events of freed commands objects (commands.cpp)
+    bool graph_cache_on = true;      // VKLLM_B200_GRAPH_CACHE=0 turns the structural graph cache off
+    std::vector<vkb::GraphCacheEntry *> graph_cache;
 };
 
 namespace vkb

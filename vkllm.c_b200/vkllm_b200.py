@@ -152,6 +152,7 @@ _SIGS = {
                                                        C.c_uint64]),
     "vkllm_b200_random_f16_host": (None, [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p]),
     "vkllm_b200_set_exec_mode": (C.c_int, [C.c_void_p, C.c_int]),
+    "vkllm_b200_set_graph_cache": (C.c_int, [C.c_void_p, C.c_int]),
     "vkllm_b200_get_exec_mode": (C.c_int, [C.c_void_p]),
     "vkllm_b200_context_stream": (C.c_void_p, [C.c_void_p]),
     "vkllm_b200_context_device": (C.c_int, [C.c_void_p]),
@@ -258,6 +259,9 @@ class Context:
 
     def set_exec_mode(self, mode):
         check(lib().vkllm_b200_set_exec_mode(self.ptr, mode), "vkllm_b200_set_exec_mode")
+
+    def set_graph_cache(self, on):
+        check(lib().vkllm_b200_set_graph_cache(self.ptr, int(bool(on))), "vkllm_b200_set_graph_cache")
 
 
 def tensor_new(ctx, name, shape, dtype, op=OP_NONE, srcs=(), params=None, mapped=False):
