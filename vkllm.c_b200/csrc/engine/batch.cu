@@ -35,11 +35,15 @@ struct BatchLayer
 {
     const __half *wq, *wk, *wv, *wo, *wg, *wu, *wd;
     const float *attn_norm, *ffn_norm;
-    // The GEMM operands, the batch's own copies: [Wq; Wk; Wv] as [3 HD, D] and [Wup; Wgate] as
-    // [2 F, D], so that each is one GEMM with M = sequences (fewer, larger GEMMs fill the SMs without
-    // splitting K). With the tiled layout (the default) these and wo_g / wd_g are gemm_tile_b copies,
-    // whose B loads stream contiguous 16 KB tiles; otherwise wo_g / wd_g are the model's matrices.
+    // The GEMM operands: [Wq; Wk; Wv] as [3 HD, D] and [Wup; Wgate] as [2 F, D], so that each is one
+    // GEMM with M = sequences (fewer, larger GEMMs fill the SMs without splitting K). With the tiled
+    // layout (the default) these and wo_g / wd_g are the batch's gemm_tile_b copies, whose B loads
+    // stream contiguous 16 KB tiles. In place (tiled = 2) they are the model's own matrices, read as
+    // grouped B operands (wqkv, wqkv1, wqkv2 and wug, wug1, each group_* rows): no copy is made.
+    // Otherwise (tiled = 0) wqkv / wug are row-major concatenated copies and wo_g / wd_g the model's.
     const __half *wqkv, *wug, *wo_g, *wd_g;
+    const __half *wqkv1 = nullptr, *wqkv2 = nullptr, *wug1 = nullptr;
+    uint32_t group_qkv = 0, group_ug = 0;
 };
 } // namespace vkb
 
@@ -819,15 +823,36 @@ __global__ void k_b_check_pos(const uint32_t *pos, uint32_t cap, uint32_t B, uin
             atomicOr(err, 1u);
 }
 
-bool gemm(const __half *A, const __half *W, uint32_t tiled, __half *C, uint32_t M, uint32_t N, uint32_t K, int act,
+// B operand of a batch GEMM: W (tile-order copy when tiled == 1), or rows in `group` blocks from
+// W, W1, W2 (row-major, the model's matrices) when group > 0.
+struct BOp
+{
+    const __half *W, *W1, *W2;
+    uint32_t group;
+};
+
+inline BOp bop(const __half *W, const __half *W1 = nullptr, const __half *W2 = nullptr, uint32_t group = 0)
+{
+    return BOp{W, W1, W2, group};
+}
+
+void set_b(GemmArgs &g, const BOp &b, uint32_t tiled)
+{
+    g.B = b.W;
+    g.B1 = b.W1;
+    g.B2 = b.W2;
+    g.b_group_n = b.group;
+    g.b_tiled = b.group ? 0u : (tiled == 1 ? 1u : 0u);
+}
+
+bool gemm(const __half *A, const BOp &W, uint32_t tiled, __half *C, uint32_t M, uint32_t N, uint32_t K, int act,
           cudaStream_t s, uint32_t act_from = 0)
 {
     GemmArgs g{};
     g.act_from = act_from;
-    g.b_tiled = tiled;
+    set_b(g, W, tiled);
     g.pdl = 1;
     g.A = A;
-    g.B = W;
     g.C = C;
     g.M = M;
     g.N = N;
@@ -843,14 +868,13 @@ bool gemm(const __half *A, const __half *W, uint32_t tiled, __half *C, uint32_t 
 }
 
 // C = A . W^T as fp32 split-K partials in `part` (no reduction); false when the GEMM cannot split.
-bool gemm_partials(const __half *A, const __half *W, uint32_t tiled, float *part, uint32_t M, uint32_t N, uint32_t K,
+bool gemm_partials(const __half *A, const BOp &W, uint32_t tiled, float *part, uint32_t M, uint32_t N, uint32_t K,
                    uint32_t splits, uint32_t *used, cudaStream_t s, uint32_t tile = 0)
 {
     GemmArgs g{};
-    g.b_tiled = tiled;
+    set_b(g, W, tiled);
     g.pdl = 1;
     g.A = A;
-    g.B = W;
     g.C = nullptr;
     g.M = M;
     g.N = N;
@@ -874,7 +898,7 @@ vkllm_err_t proj_residual_norm(vkllm_b200_batch *bt, const __half *in, const __h
     const BatchDims &dd = bt->dd;
     const uint32_t B = bt->B, D = dd.D;
     uint32_t used = 0;
-    if (bt->proj_splits > 1 && gemm_partials(in, w, bt->tiled, bt->part, B, D, K, bt->proj_splits, &used, s,
+    if (bt->proj_splits > 1 && gemm_partials(in, bop(w), bt->tiled, bt->part, B, D, K, bt->proj_splits, &used, s,
                                              bt->proj_tile))
     {
         // a thread per 8 columns (up to 1024), so each thread's partial loads are issued at once
@@ -883,7 +907,7 @@ vkllm_err_t proj_residual_norm(vkllm_b200_batch *bt, const __half *in, const __h
         return VKLLM_ERR_OK;
     }
     (void)cudaGetLastError();
-    if (!gemm(in, w, bt->tiled, bt->t0, B, D, K, 0, s))
+    if (!gemm(in, bop(w), bt->tiled, bt->t0, B, D, K, 0, s))
         return VKLLM_ERR_VULKAN;
     k_b_bin8<<<grid_1d((uint64_t)B * D / 8, kBT), kBT, 0, s>>>(bt->x, bt->x, bt->t0, (uint64_t)B * D / 8, 0);
     k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, g, D, dd.eps, bt->xn);
@@ -909,14 +933,15 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
             k_b_rmsnorm<<<B, kBT, 0, s>>>(bt->x, w.attn_norm, D, dd.eps, bt->xn);
         // QKV as split-K partials summed by the RoPE / KV-row kernel (else the GEMM's own reduction)
         uint32_t used = 0;
+        const BOp b_qkv = bop(w.wqkv, w.wqkv1, w.wqkv2, w.group_qkv), b_ug = bop(w.wug, w.wug1, nullptr, w.group_ug);
         if (bt->qkv_splits > 1 &&
-            gemm_partials(bt->xn, w.wqkv, bt->tiled, bt->part, B, 3 * HD, D, bt->qkv_splits, &used, s, bt->qkv_tile))
+            gemm_partials(bt->xn, b_qkv, bt->tiled, bt->part, B, 3 * HD, D, bt->qkv_splits, &used, s, bt->qkv_tile))
             k_b_rope_kv_part<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(bt->part, used, bt->qkv, HD, bt->pos, H, hd,
                                                                               bt->cap, dd.rope_base, kc, vc, B);
         else
         {
             (void)cudaGetLastError();
-            if (!gemm(bt->xn, w.wqkv, bt->tiled, bt->qkv, B, 3 * HD, D, 0, s))
+            if (!gemm(bt->xn, b_qkv, bt->tiled, bt->qkv, B, 3 * HD, D, 0, s))
                 return VKLLM_ERR_VULKAN;
             k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(
                 bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
@@ -933,12 +958,12 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
         // up/gate as split-K partials summed by the gate kernel (else the GEMM's own reduction, with
         // SiLU on the gate half only)
         if (bt->ug_splits > 1 &&
-            gemm_partials(bt->xn, w.wug, bt->tiled, bt->part, B, 2 * F, D, bt->ug_splits, &used, s, bt->ug_tile))
+            gemm_partials(bt->xn, b_ug, bt->tiled, bt->part, B, 2 * F, D, bt->ug_splits, &used, s, bt->ug_tile))
             k_b_gate_part<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->part, used, F, B);
         else
         {
             (void)cudaGetLastError();
-            if (!gemm(bt->xn, w.wug, bt->tiled, bt->ug, B, 2 * F, D, 1, s, F))
+            if (!gemm(bt->xn, b_ug, bt->tiled, bt->ug, B, 2 * F, D, 1, s, F))
                 return VKLLM_ERR_VULKAN;
             k_b_gate<<<grid_1d((uint64_t)B * F / 8, kBT), kBT, 0, s>>>(bt->m, bt->ug, F, B);
         }
@@ -946,7 +971,7 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
         _CHECK(
             proj_residual_norm(bt, bt->m, w.wd_g, F, l + 1 < bt->L ? bt->layers[l + 1].attn_norm : bt->out_norm, s));
     }
-    if (!gemm(bt->xn, bt->wout_g, bt->tiled, bt->logits, B, dd.V, D, 0, s))
+    if (!gemm(bt->xn, bop(bt->wout_g), bt->tiled, bt->logits, B, dd.V, D, 0, s))
         return VKLLM_ERR_VULKAN;
     k_b_argmax<<<B, 1024, 0, s>>>(bt->logits, dd.V, bt->tok, bt->pos, bt->ring, bt->ring_steps, bt->err + 1, B);
     k_b_step_done<<<1, 1, 0, s>>>(bt->err + 1);
@@ -1069,13 +1094,19 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
             bt->qkv_tile = v[3], bt->ug_tile = v[4], bt->proj_tile = v[5];
         }
     }
+    // VKLLM_B200_BATCH_TILED: 1 (default) tile-order copies, 2 the model's matrices in place (grouped
+    // B operands; needs HD and F divisible by 256), 0 row-major concatenated copies.
     const char *tiled_env = getenv("VKLLM_B200_BATCH_TILED");
-    bt->tiled = tiled_env && atoi(tiled_env) == 0 ? 0u : 1u;
+    bt->tiled = tiled_env ? (uint32_t)atoi(tiled_env) : 1u;
+    if (bt->tiled > 2 || (bt->tiled == 2 && (HD % 256 != 0 || F % 256 != 0)))
+        bt->tiled = 1;
     const size_t t_qkv = gemm_tiled_b_elems(3 * HD, D), t_ug = gemm_tiled_b_elems(2 * F, D),
                  t_wo = gemm_tiled_b_elems(D, HD), t_wd = gemm_tiled_b_elems(D, F);
-    const size_t per_layer = bt->tiled ? t_qkv + t_ug + t_wo + t_wd : ((size_t)3 * HD + (size_t)2 * F) * D;
-    const size_t extra = bt->tiled ? gemm_tiled_b_elems(dd.V, D) : 0;
-    if (cudaMalloc(&bt->wcat, (per_layer * bt->L + extra) * sizeof(__half)) != cudaSuccess)
+    const size_t per_layer = bt->tiled == 1   ? t_qkv + t_ug + t_wo + t_wd
+                             : bt->tiled == 0 ? ((size_t)3 * HD + (size_t)2 * F) * D
+                                              : 0;
+    const size_t extra = bt->tiled == 1 ? gemm_tiled_b_elems(dd.V, D) : 0;
+    if (per_layer + extra > 0 && cudaMalloc(&bt->wcat, (per_layer * bt->L + extra) * sizeof(__half)) != cudaSuccess)
     {
         (void)cudaGetLastError();
         cudaFree(bt->ws);
@@ -1086,8 +1117,21 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     for (uint32_t l = 0; l < bt->L && copied; ++l)
     {
         BatchLayer &w = bt->layers[l];
+        if (bt->tiled == 2)
+        {
+            w.wqkv = w.wq;
+            w.wqkv1 = w.wk;
+            w.wqkv2 = w.wv;
+            w.group_qkv = HD;
+            w.wug = w.wu;
+            w.wug1 = w.wg;
+            w.group_ug = F;
+            w.wo_g = w.wo;
+            w.wd_g = w.wd;
+            continue;
+        }
         __half *qkv = bt->wcat + per_layer * l;
-        if (bt->tiled)
+        if (bt->tiled == 1)
         {
             __half *ug = qkv + t_qkv, *wo = ug + t_ug, *wd = wo + t_wo;
             copied = gemm_tile_b(TileSrcs{{w.wq, w.wk, w.wv}, {HD, HD, HD}, 3}, D, qkv, s) &&
@@ -1111,7 +1155,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         w.wo_g = w.wo;
         w.wd_g = w.wd;
     }
-    if (bt->tiled)
+    if (bt->tiled == 1)
     {
         __half *wo = bt->wcat + per_layer * bt->L;
         copied = copied && gemm_tile_b(TileSrcs{{bt->wout}, {dd.V}, 1}, D, wo, s);
