@@ -77,3 +77,35 @@ def test_batch_rejects_a_sequence_past_its_capacity(vk, ctx, tiny_gguf):
         if batch is not None:
             batch.free()
         model.free()
+
+
+def test_in_place_weights_match_tile_copies(vk, ctx, monkeypatch):
+    """VKLLM_B200_BATCH_TILED=2 reads the model's own matrices as grouped GEMM operands instead of the
+    batch's tile-order copies: the same GEMM tiles and K splits over the same values, so tokens and
+    logits are bit-identical. A random model whose Q/K/V and FFN row counts are multiples of 256 (the
+    in-place mode's requirement; the tiny model is not)."""
+    cfg = dict(block_count=2, context_length=256, embedding_length=512, head_count=4, ffn_length=1280,
+               vocab_size=4096, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(3, 4096, size=n, dtype=np.uint32) for n in (9, 3, 17, 1, 30, 6)]
+    runs = []
+    for tiled in ("1", "2"):
+        monkeypatch.setenv("VKLLM_B200_BATCH_TILED", tiled)
+        model = vk.Model(ctx).init_random(cfg, 77)
+        batch = None
+        try:
+            batch = vk.Batch(model, len(prompts), 64)
+            firsts = [batch.add_prompt(i, p) for i, p in enumerate(prompts)]
+            toks, logits = [], []
+            for _ in range(16):
+                toks.append(batch.decode(1)[0].copy())
+                logits.append(batch.logits().copy())
+        finally:
+            if batch is not None:
+                batch.free()
+            model.free()
+        runs.append((firsts, np.stack(toks), np.stack(logits)))
+    (f1, t1, l1), (f2, t2, l2) = runs
+    assert f1 == f2
+    assert np.array_equal(t1, t2)
+    assert np.array_equal(l1.view(np.uint16), l2.view(np.uint16))
