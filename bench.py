@@ -472,7 +472,7 @@ CFG_13B = dict(block_count=40, context_length=4096, embedding_length=5120, head_
                vocab_size=32000, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
 
 
-def tp13b_leg(vk, ctx, args, world, rank, stream):
+def tp13b_leg(vk, ctx, args, world, rank, stream, exchange="peer"):
     """LLaMA-2-13B, tensor parallel over the ranks (heads / FFN rows / vocabulary
     sharded; the Wo and down partial sums exchanged inside the persistent decode kernel over peer
     memory). Batch-1 greedy decode at positions 2048.. (the prompt length of the config); the KV rows
@@ -495,7 +495,10 @@ def tp13b_leg(vk, ctx, args, world, rank, stream):
             dist.all_gather_object(got, b)
             return got
 
-        m.tp_connect(gather)
+        if exchange == "nccl":
+            m.tp_connect_nccl(gather)
+        else:
+            m.tp_connect(gather)
     else:
         m.init_random(cfg, SEED)
     try:
@@ -525,7 +528,12 @@ def tp13b_leg(vk, ctx, args, world, rank, stream):
             "ms_per_token": round(ms_tok, 4), "positions": [P + W, P + W + K],
             "bytes_per_token_per_rank": int(w_rank + kv_rank),
             "hbm_frac_per_rank": round((w_rank + kv_rank) / (ms_tok * 1e-3) / 1e9 / peak, 4),
-            "allreduce": "fused in the decode kernel: per layer 2 x D fp32 row partials over NVLink peer memory" if world > 1 else "none (1 GPU)",
+            "exchange": exchange if world > 1 else "none",
+            "allreduce": ("none (1 GPU)" if world == 1 else
+                          "fused in the decode kernel: per layer 2 x D fp32 row partials over NVLink peer memory"
+                          if exchange == "peer" else
+                          "ncclAllReduce (fp32 sum, D rows) after Wo and after down, ncclAllGather of the argmax "
+                          "candidates, between the per-op kernels of a CUDA-graph step"),
             "path": "persistent kernel" if persistent else "graph", "kv": "zeroed cache below position 2048 (decode-only leg)"}
 
 
@@ -538,9 +546,10 @@ def run_ours(args, world, rank, local):
     if args.profile_tp:
         ctx = vk.Context(local)
         stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
-        tp = tp13b_leg(vk, ctx, args, world, rank, stream)
-        if rank == 0:
-            print(json.dumps({"profile_case": "tp13b", **tp}), flush=True)
+        for exchange in (("peer", "nccl") if world > 1 else ("peer",)):
+            tp = tp13b_leg(vk, ctx, args, world, rank, stream, exchange)
+            if rank == 0:
+                print(json.dumps({"profile_case": "tp13b", **tp}), flush=True)
         ctx.close()
         return None
     cfg = dict(CFG_7B)
@@ -758,6 +767,10 @@ def run_ours(args, world, rank, local):
         tp = tp13b_leg(vk, ctx, args, world, rank, stream)
         if result is not None:
             result["tp13b"] = tp
+        if world > 1:  # the NCCL exchange on the same shards, for comparison
+            tp = tp13b_leg(vk, ctx, args, world, rank, stream, "nccl")
+            if result is not None:
+                result["tp13b_nccl"] = tp
     ctx.close()
     return result
 

@@ -86,6 +86,19 @@ extern vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct vkll
 extern vkllm_err_t vkllm_b200_tp_connect(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                          const void *handles);
 
+/* NCCL exchange of a tensor-parallel model (the baseline the peer-memory exchange is measured
+ * against): the decode step runs the per-op kernels on the shards, with an ncclAllReduce (sum, fp32)
+ * of the Wo and down partial rows after each projection and an ncclAllGather of the argmax class
+ * candidates, all captured in one CUDA graph per step. One rank calls vkllm_b200_tp_nccl_unique_id
+ * (128 bytes); the caller hands those bytes to every rank, and every rank then calls
+ * vkllm_b200_tp_nccl_connect (collective over the ranks; before the first engine call).
+ * libnccl.so.2 is loaded at the first call (VKLLM_ERR_VULKAN when it cannot be). With only this
+ * exchange connected the engine uses it; with both, VKLLM_B200_TP_EXCHANGE=nccl at engine creation
+ * selects it (default: the peer-memory exchange). */
+extern vkllm_err_t vkllm_b200_tp_nccl_unique_id(void *id_out);
+extern vkllm_err_t vkllm_b200_tp_nccl_connect(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                              const void *id);
+
 /* The shard of a rows x cols matrix held by tensor-parallel rank tp_rank of tp_size: split 1 = rows
  * (Wq, Wk, Wv, Wgate, Wup, output), 2 = columns (Wo, Wdown), 0 = whole (embedding). out = {row0, rows,
  * col0, cols} of the shard in the unsharded matrix. Host only. */

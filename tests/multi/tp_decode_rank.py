@@ -1,7 +1,9 @@
 """One rank of a tensor-parallel decode run (launched by tests/test_tp_gpu.py under torchrun, one
-process per GPU): builds shard RANK of WORLD of a random model, connects the peer-memory exchange
-(handles gathered over gloo), decodes a prompt token by token and then greedily on the engine, and
-writes its tokens and its vocabulary shard of every generated step's logits to OUT/rank<r>.npz."""
+process per GPU): builds shard RANK of WORLD of a random model, connects the exchange (EXCHANGE:
+"peer", the peer-memory exchange inside the persistent kernel, handles gathered over gloo; or "nccl",
+the per-op kernels with NCCL collectives, the unique id gathered over gloo), decodes a prompt token
+by token and then greedily on the engine, and writes its tokens and its vocabulary shard of every
+generated step's logits to OUT/rank<r>.npz. Usage: tp_decode_rank.py OUT [EXCHANGE]."""
 import os
 import sys
 
@@ -17,7 +19,7 @@ CFG = dict(block_count=2, context_length=64, embedding_length=256, head_count=4,
 SEED, PROMPT, N_GEN = 7, [11, 22, 33, 44, 55], 8
 
 
-def main(out_dir):
+def main(out_dir, exchange):
     import ctypes as C
 
     dist.init_process_group("gloo", init_method="env://")
@@ -32,12 +34,17 @@ def main(out_dir):
             return got
 
         try:
-            model.tp_connect(gather)
+            if exchange == "nccl":
+                model.tp_connect_nccl(gather)
+            else:
+                model.tp_connect(gather)
             Vl = CFG["vocab_size"] // world
             logits = []
             for i, t in enumerate(PROMPT):  # teacher-forced prompt, one token per step
                 vk.check(l.vkllm_b200_engine_set_state(ctx.ptr, C.byref(model.m), t, i), "set_state")
                 vk.check(l.vkllm_b200_engine_decode_steps(ctx.ptr, C.byref(model.m), 1), "decode")
+            persistent = l.vkllm_b200_engine_is_persistent(ctx.ptr, C.byref(model.m))
+            assert bool(persistent) == (exchange != "nccl"), (exchange, persistent)
             buf = np.zeros(Vl, dtype=np.uint16)
             vk.check(l.vkllm_b200_engine_read_logits(ctx.ptr, C.byref(model.m), buf.ctypes.data, Vl), "logits")
             logits.append(buf.view(np.float16).copy())
@@ -55,4 +62,4 @@ def main(out_dir):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1])
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "peer")

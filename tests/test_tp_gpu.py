@@ -1,6 +1,7 @@
-"""Tensor-parallel decode (BASELINE configs[4] layout: heads, FFN rows and vocabulary sharded, the
-Wo / down partial sums exchanged inside the decode kernel over peer memory) on 2 GPUs, against the
-CPU oracle on the unsharded weights (the generator is counter-based, so the oracle rebuilds them).
+"""Tensor-parallel decode (BASELINE configs[4] layout: heads, FFN rows and vocabulary sharded) on 2
+GPUs, with either exchange of the Wo / down partial sums: inside the persistent decode kernel over peer
+memory ("peer"), or NCCL collectives between the per-op kernels ("nccl"), against the CPU oracle on
+the unsharded weights (the generator is counter-based, so the oracle rebuilds them).
 Each rank is a separate process (tests/multi/tp_decode_rank.py under torchrun). Bar: identical greedy
 tokens on every rank and equal to the oracle's; the ranks' logit shards, concatenated, within
 max-abs 2e-2 / mean-abs 2e-3 of the oracle's logits. Skipped with fewer than 2 GPUs."""
@@ -43,7 +44,8 @@ def oracle_weights(orc, cfg, seed):
     return w
 
 
-def test_tensor_parallel_decode_matches_the_oracle(orc, tmp_path):
+@pytest.mark.parametrize("exchange,port", [("peer", 29533), ("nccl", 29534)])
+def test_tensor_parallel_decode_matches_the_oracle(orc, tmp_path, exchange, port):
     import torch
 
     if torch.cuda.device_count() < 2:
@@ -53,7 +55,7 @@ def test_tensor_parallel_decode_matches_the_oracle(orc, tmp_path):
 
     env = dict(os.environ, MASTER_ADDR="127.0.0.1")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
-           "--master-port=29533", os.path.join(HERE, "multi", "tp_decode_rank.py"), str(tmp_path)]
+           f"--master-port={port}", os.path.join(HERE, "multi", "tp_decode_rank.py"), str(tmp_path), exchange]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     ranks = [np.load(os.path.join(tmp_path, f"rank{i}.npz")) for i in range(2)]

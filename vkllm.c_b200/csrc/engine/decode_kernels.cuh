@@ -397,6 +397,7 @@ struct WoOp
     DecodeDims dd;
     const __half *attn;
     __half *x;
+    float *part = nullptr; // tensor parallel: this rank's fp32 partial rows (summed over the ranks later)
     __device__ const __half *row_ptr(uint32_t u, uint32_t) const
     {
         return lw.wo + (uint64_t)u * dd.H * dd.hd;
@@ -407,7 +408,10 @@ struct WoOp
     }
     __device__ void epilogue(uint32_t u, const float *s) const
     {
-        x[u] = __float2half_rn(__half2float(x[u]) + round_f16(s[0]));
+        if (part)
+            part[u] = s[0];
+        else
+            x[u] = __float2half_rn(__half2float(x[u]) + round_f16(s[0]));
     }
     __device__ void finish() const
     {
@@ -449,6 +453,7 @@ struct DownOp
     DecodeDims dd;
     const __half *m;
     __half *x;
+    float *part = nullptr; // tensor parallel: this rank's fp32 partial rows (summed over the ranks later)
     __device__ const __half *row_ptr(uint32_t u, uint32_t) const
     {
         return lw.wd + (uint64_t)u * dd.F;
@@ -459,12 +464,48 @@ struct DownOp
     }
     __device__ void epilogue(uint32_t u, const float *s) const
     {
-        x[u] = __float2half_rn(__half2float(x[u]) + round_f16(s[0]));
+        if (part)
+            part[u] = s[0];
+        else
+            x[u] = __float2half_rn(__half2float(x[u]) + round_f16(s[0]));
     }
     __device__ void finish() const
     {
     }
 };
+
+// The end of the reference argmax (src/shaders/vkllm_arg_max.comp:77-90) for one warp holding the
+// 32 class winners (lane = class; idx 0xffffffff for an empty class): the 16/8/4/2/1 tree keeps the
+// left operand unless the right one is strictly greater; lane 0 then records the token in the step
+// state and the token ring and advances the position.
+__device__ __forceinline__ void argmax_tree_finish(float v, uint32_t idx, uint32_t lane, StepState *st,
+                                                   uint32_t *ring, uint32_t ring_len)
+{
+    if (idx == 0xffffffffu)
+    {
+        v = -FLT_MAX; // empty class (V < 32): the reference lane keeps -FLT_MAX and its own index
+        idx = lane;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float ov = __shfl_down_sync(0xffffffffu, v, o);
+        const uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
+        if ((int)lane < o && ov > v)
+        {
+            v = ov;
+            idx = oi;
+        }
+    }
+    if (lane == 0)
+    {
+        st->token = idx;
+        if (st->step < ring_len)
+            ring[st->step] = idx;
+        st->step += 1;
+        st->pos += 1;
+    }
+}
 
 // output_norm + logits + ARG_MAX. Every CTA stores its fp16 logits; the last CTA to finish computes
 // the argmax over all of them with the reference tie rule (src/shaders/vkllm_arg_max.comp:54-90):
@@ -483,6 +524,11 @@ struct LogitsOp
     StepState *st;
     uint32_t *ring;
     uint32_t ring_len;
+    // Tensor parallel: this rank's rows are vocabulary entries v0 .., and instead of finishing the
+    // argmax it writes its 32 class candidates to tp_cls ([32] values, then [32] indices) for the
+    // exchange (k_tp_argmax finishes).
+    uint32_t v0 = 0;
+    uint32_t *tp_cls = nullptr;
     __device__ const __half *row_ptr(uint32_t u, uint32_t) const
     {
         return wout + (uint64_t)u * dd.D;
@@ -513,13 +559,14 @@ struct LogitsOp
         const uint32_t V = dd.V;
         float bv = -FLT_MAX;
         uint32_t bi = 0xffffffffu;
-        for (uint32_t i = lane + 32 * warp; i < V; i += 32 * nw)
+        // class of a row = its vocabulary index (v0 + i) mod 32
+        for (uint32_t i = ((lane + 32 - (v0 & 31)) & 31) + 32 * warp; i < V; i += 32 * nw)
         {
             const float v = __half2float(__ldcg(logits + i));
             if (bi == 0xffffffffu || v > bv)
             {
                 bv = v;
-                bi = i;
+                bi = v0 + i;
             }
         }
         cls_v[warp][lane] = bv;
@@ -541,34 +588,53 @@ struct LogitsOp
                     idx = ci;
                 }
             }
-            if (idx == 0xffffffffu)
+            if (tp_cls)
             {
-                v = -FLT_MAX; // empty class (V < 32): the reference lane keeps -FLT_MAX and its own index
-                idx = lane;
+                tp_cls[lane] = __float_as_uint(v);
+                tp_cls[32 + lane] = idx;
+                if (lane == 0)
+                    *counter = 0;
+                return;
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-            {
-                const float ov = __shfl_down_sync(0xffffffffu, v, o);
-                const uint32_t oi = __shfl_down_sync(0xffffffffu, idx, o);
-                if ((int)lane < o && ov > v)
-                {
-                    v = ov;
-                    idx = oi;
-                }
-            }
+            argmax_tree_finish(v, idx, lane, st, ring, ring_len);
             if (lane == 0)
-            {
-                st->token = idx;
-                if (st->step < ring_len)
-                    ring[st->step] = idx;
-                st->step += 1;
-                st->pos += 1;
                 *counter = 0;
-            }
         }
     }
 };
+
+// Tensor parallel: x = fp16(x + fp16(sum)), sum = the ranks' Wo / down partial rows after the
+// allreduce (the projection node's rounding, then the residual add).
+__global__ void k_tp_residual(__half *__restrict__ x, const float *__restrict__ sum, uint32_t n)
+{
+    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < n; u += gridDim.x * blockDim.x)
+        x[u] = __float2half_rn(__half2float(x[u]) + round_f16(sum[u]));
+}
+
+// Tensor parallel: the argmax over the ranks' class candidates (cls: [world][64] words as LogitsOp
+// writes them, ranks in vocabulary order). Class c takes the largest value over the ranks, ties to
+// the smallest index (the lower rank, whose indices are smaller), as the reference's in-order scan
+// of one class does; then the tree. One warp.
+__global__ void k_tp_argmax(const uint32_t *__restrict__ cls, uint32_t world, StepState *st, uint32_t *ring,
+                            uint32_t ring_len)
+{
+    const uint32_t lane = threadIdx.x & 31;
+    float v = -FLT_MAX;
+    uint32_t idx = 0xffffffffu;
+    for (uint32_t q = 0; q < world; ++q)
+    {
+        const float cv = __uint_as_float(cls[q * 64 + lane]);
+        const uint32_t ci = cls[q * 64 + 32 + lane];
+        if (ci == 0xffffffffu)
+            continue;
+        if (idx == 0xffffffffu || cv > v || (cv == v && ci < idx))
+        {
+            v = cv;
+            idx = ci;
+        }
+    }
+    argmax_tree_finish(v, idx, lane, st, ring, ring_len);
+}
 
 __global__ void k_set_state(StepState *st, const uint32_t *tok_src, uint32_t token, uint32_t pos)
 {

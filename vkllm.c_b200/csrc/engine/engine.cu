@@ -10,6 +10,7 @@
 #include "../runtime/internal.h"
 #include "decode_kernels.cuh"
 #include "decode_persistent.cuh"
+#include "nccl_api.h"
 #include "plan.h"
 #include "prefill_kernels.cuh"
 #include "../kernels/kernels.h"
@@ -53,6 +54,9 @@ struct Engine
     uint32_t *am_idx = nullptr, *bar = nullptr; // bar[0] = barrier arrivals, then 2 x H attention counters
     uint32_t launches = 0;                      // kernel launches enqueued by the last decode call
     TpComm *tp = nullptr;                       // tensor-parallel exchange (shards only)
+    bool tp_nccl = false;                       // shards decode on the per-op kernels + NCCL collectives
+    float *tp_sum = nullptr;                    // [D] this rank's Wo / down partials, then their allreduce
+    uint32_t *tp_cls = nullptr, *tp_cls_all = nullptr; // argmax class candidates: [64], [world][64]
     __half *tiled = nullptr;                    // decode copy of the weights (persistent kernel's tile layout)
     void *d_tiled_ptrs = nullptr;               // [layer * 4 + phase] pointers into `tiled`
     float *rope_den = nullptr;                  // RoPE denominators of the persistent kernel
@@ -77,6 +81,7 @@ struct TpComm
     void *peer[kTpMax] = {};
     bool connected = false;
     uint32_t base[3] = {0, 0, 0}; // exchanges done per site (Wo, down, argmax)
+    ncclComm_t nccl = nullptr;    // the NCCL exchange's communicator (vkllm_b200_tp_nccl_connect)
 };
 
 struct TpLayout
@@ -124,7 +129,7 @@ QkvOp op_qkv(Engine *e, const LayerW &lw)
 }
 WoOp op_wo(Engine *e, const LayerW &lw)
 {
-    return WoOp{lw, e->dd, e->attn, e->x};
+    return WoOp{lw, e->dd, e->attn, e->x, e->tp_nccl ? e->tp_sum : nullptr};
 }
 UpGateOp op_upgate(Engine *e, const LayerW &lw)
 {
@@ -132,11 +137,27 @@ UpGateOp op_upgate(Engine *e, const LayerW &lw)
 }
 DownOp op_down(Engine *e, const LayerW &lw)
 {
-    return DownOp{lw, e->dd, e->m, e->x};
+    return DownOp{lw, e->dd, e->m, e->x, e->tp_nccl ? e->tp_sum : nullptr};
 }
 LogitsOp op_logits(Engine *e)
 {
-    return LogitsOp{e->wout, e->out_norm, e->dd, e->x, e->logits, e->logit_counter, e->state, e->ring, e->dd.ctx};
+    return LogitsOp{e->wout,  e->out_norm,  e->dd,  e->x, e->logits, e->logit_counter, e->state, e->ring, e->dd.ctx,
+                    e->pp.v0, e->tp_nccl ? e->tp_cls : nullptr};
+}
+
+// Tensor parallel (NCCL exchange): the ranks' partial rows summed in place (fp32), then the
+// projection's rounding and the residual add.
+cudaError_t tp_allreduce_residual(Engine *e, cudaStream_t s)
+{
+    const NcclApi *nc = nccl_api();
+    ncclResult_t r = nc->AllReduce(e->tp_sum, e->tp_sum, e->dd.D, ncclFloat32, ncclSum, e->tp->nccl, s);
+    if (r != ncclSuccess)
+    {
+        log_error("ncclAllReduce: %s", nc->GetErrorString(r));
+        return cudaErrorUnknown;
+    }
+    k_tp_residual<<<(e->dd.D + 255) / 256, 256, 0, s>>>(e->x, e->tp_sum, e->dd.D);
+    return cudaGetLastError();
 }
 
 template <class Op> cudaError_t launch_stream(Engine *e, const Op &op, const StreamGeom &g, cudaStream_t s)
@@ -148,7 +169,8 @@ template <class Op> cudaError_t launch_stream(Engine *e, const Op &op, const Str
 vkllm_err_t enqueue_step(Engine *e, cudaStream_t s)
 {
     const DecodeDims &dd = e->dd;
-    cudaError_t err = launch_pdl(k_dec_embed, dim3(e->grid_embed), dim3(256), 0, s, e->embed, dd.V, dd.D, e->unk,
+    // the embedding table is whole on every rank: ids below the full vocabulary size are valid
+    cudaError_t err = launch_pdl(k_dec_embed, dim3(e->grid_embed), dim3(256), 0, s, e->embed, e->pp.Vg, dd.D, e->unk,
                                  (const StepState *)e->state, e->x);
     dim3 agrid(dd.H, dd.nsplit);
     for (const LayerW &lw : e->layers)
@@ -163,13 +185,32 @@ vkllm_err_t enqueue_step(Engine *e, cudaStream_t s)
                              (const float2 *)e->part, e->opart, e->counters, e->attn, (const StepState *)e->state);
         if (err == cudaSuccess)
             err = launch_stream(e, op_wo(e, lw), e->g_wo, s);
+        if (err == cudaSuccess && e->tp_nccl)
+            err = tp_allreduce_residual(e, s);
         if (err == cudaSuccess)
             err = launch_stream(e, op_upgate(e, lw), e->g_upgate, s);
         if (err == cudaSuccess)
             err = launch_stream(e, op_down(e, lw), e->g_down, s);
+        if (err == cudaSuccess && e->tp_nccl)
+            err = tp_allreduce_residual(e, s);
     }
     if (err == cudaSuccess)
         err = launch_stream(e, op_logits(e), e->g_logits, s);
+    if (err == cudaSuccess && e->tp_nccl)
+    {
+        const NcclApi *nc = nccl_api();
+        ncclResult_t r = nc->AllGather(e->tp_cls, e->tp_cls_all, 64, ncclUint32, e->tp->nccl, s);
+        if (r != ncclSuccess)
+        {
+            log_error("ncclAllGather: %s", nc->GetErrorString(r));
+            err = cudaErrorUnknown;
+        }
+        else
+        {
+            k_tp_argmax<<<1, 32, 0, s>>>(e->tp_cls_all, e->tp->world, e->state, e->ring, dd.ctx);
+            err = cudaGetLastError();
+        }
+    }
     if (err == cudaSuccess)
         err = cudaGetLastError();
     if (err != cudaSuccess)
@@ -829,7 +870,8 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
            off_ring = off_lcnt + al(4), off_state = off_ring + al((size_t)dd.ctx * 4),
            off_amv = off_state + al(sizeof(StepState)), off_ami = off_amv + al((size_t)sms * 32 * 4),
            off_bar = off_ami + al((size_t)sms * 32 * 4),
-           total = off_bar + al(4 * (1 + 3 * (size_t)dd.H + kPersistMaxGrid)); // + per-CTA and per-head flags
+           off_tp = off_bar + al(4 * (1 + 3 * (size_t)dd.H + kPersistMaxGrid)), // + per-CTA and per-head flags
+           total = off_tp + al((size_t)dd.D * 4) + al(64 * 4) + al(64 * 4 * (size_t)kTpMax);
     if (cudaMalloc(&e->ws, total) != cudaSuccess)
     {
         (void)cudaGetLastError();
@@ -853,6 +895,9 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->am_val = (float *)(w + off_amv);
     e->am_idx = (uint32_t *)(w + off_ami);
     e->bar = (uint32_t *)(w + off_bar);
+    e->tp_sum = (float *)(w + off_tp);
+    e->tp_cls = (uint32_t *)(w + off_tp + al((size_t)dd.D * 4));
+    e->tp_cls_all = (uint32_t *)(w + off_tp + al((size_t)dd.D * 4) + al(64 * 4));
 
     // Streaming GEMV geometry: one CTA per SM; chunks of at most ~8 KB, one stage per warp and as
     // many warps (<= 32) as ~220 KB of shared memory holds next to the fp32 input vector.
@@ -897,15 +942,27 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->pp.tp_rank = tp > 1 ? model->b200.tp_rank : 0;
     e->pp.v0 = e->pp.tp_rank * dd.V;
     e->pp.Vg = dd.V * tp;
-    if (tp > 1)
+    TpComm *tpc = (TpComm *)model->b200.tp_comm;
+    const char *tp_x = getenv("VKLLM_B200_TP_EXCHANGE"); // "nccl": the NCCL exchange when both are connected
+    if (tp > 1 && tpc && tpc->nccl && (!tpc->connected || (tp_x && strcmp(tp_x, "nccl") == 0)))
     {
-        // Tensor-parallel shards decode only on the persistent kernel, whose Wo / down epilogues
-        // exchange the partial sums over peer memory.
-        TpComm *c = (TpComm *)model->b200.tp_comm;
+        // NCCL exchange: the per-op kernels of the graph path on the shards, with an ncclAllReduce of
+        // the Wo and down partial rows and an ncclAllGather of the argmax candidates, captured below.
+        e->persistent = false;
+        e->tp = tpc;
+        e->tp_nccl = true;
+        e->kernels_per_step += 2 * (uint32_t)e->layers.size() + 1; // residual adds and the argmax
+    }
+    else if (tp > 1)
+    {
+        // Tensor-parallel shards decode on the persistent kernel, whose Wo / down epilogues exchange
+        // the partial sums over peer memory.
+        TpComm *c = tpc;
         if (!e->persistent || !c || !c->connected || (uint32_t)sms > kTpCtas ||
             e->htab[PK_WO * ((size_t)sms + 1) + 1] > kTpRows || (dd.D + sms - 1) / sms > kTpRows)
         {
-            log_error("tensor-parallel decode needs the persistent kernel and vkllm_b200_tp_connect first");
+            log_error("tensor-parallel decode needs the persistent kernel and vkllm_b200_tp_connect, or "
+                      "vkllm_b200_tp_nccl_connect, first");
             if (e->d_layers)
                 cudaFree(e->d_layers);
             cudaFree(e->ws);
@@ -1733,18 +1790,73 @@ void tp_comm_free(vkllm_models_llama2 *model)
             cudaIpcCloseMemHandle(c->peer[q]);
     if (c->buf)
         cudaFree(c->buf);
+    if (c->nccl)
+        nccl_api()->CommDestroy(c->nccl);
     delete c;
     model->b200.tp_comm = nullptr;
 }
 } // namespace vkb
+
+extern "C" vkllm_err_t vkllm_b200_tp_nccl_unique_id(void *id_out)
+{
+    _CHECK_ARGS(id_out);
+    const NcclApi *nc = nccl_api();
+    if (!nc)
+        return VKLLM_ERR_VULKAN;
+    ncclUniqueId id;
+    ncclResult_t r = nc->GetUniqueId(&id);
+    if (r != ncclSuccess)
+    {
+        log_error("ncclGetUniqueId: %s", nc->GetErrorString(r));
+        return VKLLM_ERR_VULKAN;
+    }
+    static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+    memcpy(id_out, &id, sizeof(id));
+    return VKLLM_ERR_OK;
+}
+
+extern "C" vkllm_err_t vkllm_b200_tp_nccl_connect(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                                  const void *id)
+{
+    _CHECK_ARGS(context && model && id);
+    _CHECK_ARGS(model->b200.tp_size > 1 && model->b200.tp_size <= kTpMax && model->b200.tp_rank < model->b200.tp_size);
+    _CHECK_ARGS(!model->b200.engine);
+    TpComm *c = (TpComm *)model->b200.tp_comm;
+    _CHECK_ARGS(!c || !c->nccl);
+    const NcclApi *nc = nccl_api();
+    if (!nc)
+        return VKLLM_ERR_VULKAN;
+    VKB_CUDA(cudaSetDevice(context->device->ordinal));
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = nc->CommInitRank(&comm, (int)model->b200.tp_size, uid, (int)model->b200.tp_rank);
+    if (r != ncclSuccess)
+    {
+        log_error("ncclCommInitRank: %s", nc->GetErrorString(r));
+        return VKLLM_ERR_VULKAN;
+    }
+    if (!c)
+    {
+        c = new TpComm();
+        c->rank = model->b200.tp_rank;
+        c->world = model->b200.tp_size;
+        c->D = model->meta.embedding_length;
+        model->b200.tp_comm = c;
+    }
+    c->nccl = comm;
+    return VKLLM_ERR_OK;
+}
 
 extern "C" vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct vkllm_models_llama2 *model,
                                           void *handle_out)
 {
     _CHECK_ARGS(context && model && handle_out);
     _CHECK_ARGS(model->b200.tp_size > 1 && model->b200.tp_size <= kTpMax && model->b200.tp_rank < model->b200.tp_size);
-    _CHECK_ARGS(!model->b200.tp_comm && !model->b200.engine);
-    auto *c = new TpComm();
+    _CHECK_ARGS(!model->b200.engine);
+    _CHECK_ARGS(!model->b200.tp_comm || !((TpComm *)model->b200.tp_comm)->buf);
+    const bool fresh = !model->b200.tp_comm;
+    TpComm *c = fresh ? new TpComm() : (TpComm *)model->b200.tp_comm;
     c->rank = model->b200.tp_rank;
     c->world = model->b200.tp_size;
     c->D = model->meta.embedding_length;
@@ -1753,7 +1865,11 @@ extern "C" vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct 
     if (cudaMalloc(&c->buf, c->bytes) != cudaSuccess || cudaMemset(c->buf, 0, c->bytes) != cudaSuccess)
     {
         (void)cudaGetLastError();
-        delete c;
+        if (c->buf)
+            cudaFree(c->buf);
+        c->buf = nullptr;
+        if (fresh)
+            delete c;
         return VKLLM_ERR_ALLOC;
     }
     cudaIpcMemHandle_t h;
@@ -1761,7 +1877,9 @@ extern "C" vkllm_err_t vkllm_b200_tp_init(struct vkllm_context *context, struct 
     {
         (void)cudaGetLastError();
         cudaFree(c->buf);
-        delete c;
+        c->buf = nullptr;
+        if (fresh)
+            delete c;
         return VKLLM_ERR_VULKAN;
     }
     memcpy(handle_out, &h, sizeof(h));

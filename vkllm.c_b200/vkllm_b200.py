@@ -190,6 +190,8 @@ _SIGS = {
     "vkllm_b200_random_f16_host_shard": (None, [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint32, C.c_uint32,
                                                 C.c_uint32, C.c_uint32, C.c_void_p]),
     "vkllm_b200_tp_connect": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
+    "vkllm_b200_tp_nccl_unique_id": (C.c_int, [C.c_void_p]),
+    "vkllm_b200_tp_nccl_connect": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p]),
     "vkllm_b200_engine_bench_kernel": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_char_p, C.c_uint32,
                                                  C.POINTER(C.c_float), C.POINTER(C.c_uint64)]),
     "vkllm_b200_attention_decode_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
@@ -436,6 +438,16 @@ class Model:
         handles = all_gather(bytes(h))
         buf = (C.c_char * (64 * len(handles))).from_buffer_copy(b"".join(handles))
         check(lib().vkllm_b200_tp_connect(self.ctx.ptr, C.byref(self.m), buf), "tp_connect")
+
+    def tp_connect_nccl(self, all_gather):
+        """Sets up the NCCL exchange: rank 0's unique id reaches every rank through `all_gather(bytes)
+        -> list of bytes` (the caller's collective); then the communicator is created (collective)."""
+        uid = (C.c_char * 128)()
+        if self.m.b200.tp_rank == 0:
+            check(lib().vkllm_b200_tp_nccl_unique_id(uid), "tp_nccl_unique_id")
+        got = all_gather(bytes(uid))
+        root = (C.c_char * 128).from_buffer_copy(got[0])
+        check(lib().vkllm_b200_tp_nccl_connect(self.ctx.ptr, C.byref(self.m), root), "tp_nccl_connect")
 
     def free(self):
         if self.loaded:
