@@ -56,10 +56,12 @@ namespace
 constexpr size_t kMaxEntriesPerModel = 4;
 uint64_t g_use_clock = 0;
 
+// Frees an idle entry's nodes; their frees were counted when the graph holding them was freed.
 void free_entry_nodes(vkllm_context *ctx, GraphCacheEntry *e)
 {
     for (vkllm_tensor *t : e->nodes)
         vkllm_tensor_free(ctx, t);
+    ctx->stats.tensor_free_counts -= (int)e->nodes.size();
     e->nodes.clear();
 }
 
