@@ -19,6 +19,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <unordered_map>
 #include <mutex>
 #include <tuple>
 
@@ -468,10 +469,60 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
+// Encoded tensor maps, keyed by everything an encoding reads (a map holds an address and a shape,
+// so a key seen before gives the same map): prefill and the op path launch their GEMMs on the same
+// operands every step. Per thread, bounded (cleared when full).
+struct MapKey
+{
+    const void *ptr;
+    uint64_t v[9];
+    bool operator==(const MapKey &o) const
+    {
+        return ptr == o.ptr && memcmp(v, o.v, sizeof(v)) == 0;
+    }
+};
+struct MapKeyHash
+{
+    size_t operator()(const MapKey &k) const
+    {
+        uint64_t h = reinterpret_cast<uintptr_t>(k.ptr) * 1099511628211ull;
+        for (uint64_t x : k.v)
+            h = (h ^ x) * 1099511628211ull;
+        return (size_t)h;
+    }
+};
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> &map_cache()
+{
+    static thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> maps;
+    if (maps.size() > 4096)
+        maps.clear();
+    return maps;
+}
+
+bool encode_operand_uncached(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, uint64_t ld,
+                             uint32_t ext_c, uint64_t sc, uint32_t ext_b, uint64_t sb, uint32_t box_rows);
+
 // 4-D map {K, rows, C, B} of an fp16 operand (K innermost), box {64, box_rows, 1, 1}, 128-byte
 // swizzle, zero fill outside. Broadcast dimensions get extent 1.
 bool encode_operand(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, uint64_t ld, uint32_t ext_c,
                     uint64_t sc, uint32_t ext_b, uint64_t sb, uint32_t box_rows)
+{
+    const MapKey key{ptr, {K, rows, ld, ext_c, sc, ext_b, sb, box_rows, 0}};
+    auto &maps = map_cache();
+    auto it = maps.find(key);
+    if (it != maps.end())
+    {
+        *m = it->second;
+        return true;
+    }
+    if (!encode_operand_uncached(m, ptr, K, rows, ld, ext_c, sc, ext_b, sb, box_rows))
+        return false;
+    maps.emplace(key, *m);
+    return true;
+}
+
+bool encode_operand_uncached(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, uint64_t ld,
+                             uint32_t ext_c, uint64_t sc, uint32_t ext_b, uint64_t sb, uint32_t box_rows)
 {
     PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
     if (!fn)
@@ -494,6 +545,14 @@ bool encode_operand(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t rows, 
 // box_rows / 128) a contiguous run of box_rows * 128 bytes.
 bool encode_tiled_b(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t N, uint32_t box_rows)
 {
+    const MapKey key{ptr, {K, N, box_rows, 0, 0, 0, 0, 0, 1}};
+    auto &maps = map_cache();
+    auto it = maps.find(key);
+    if (it != maps.end())
+    {
+        *m = it->second;
+        return true;
+    }
     PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
     if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || box_rows % kTileRows)
         return false;
@@ -503,9 +562,12 @@ bool encode_tiled_b(CUtensorMap *m, const void *ptr, uint32_t K, uint32_t N, uin
     cuuint64_t strides[3] = {kBK * 2, tile_b, tile_b * kbs};
     cuuint32_t box[4] = {kBK, kTileRows, 1, box_rows / kTileRows};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    maps.emplace(key, *m);
+    return true;
 }
 
 uint32_t *error_word(int dev)
