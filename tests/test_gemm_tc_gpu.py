@@ -76,3 +76,15 @@ def test_gemm_rejects_unaligned_k(vk, torch_cuda):
     buf = torch_cuda.zeros(4096, device="cuda", dtype=torch_cuda.float16)
     p = buf.data_ptr()
     assert lib.vkllm_b200_gemm_f16(p, p, p, 4, 4, 12, 12, 12, 4, 1.0, 0, None) == vk.ARGS  # K % 8 != 0
+
+
+@pytest.mark.parametrize("tile,splits,M,N,K", [("256x192", "1", 512, 12288, 4096), ("256x192", "2", 300, 1000, 1032),
+                                               ("256x160", "1", 512, 2200, 512), ("256x160", "3", 700, 384, 960),
+                                               ("256x224", "1", 512, 3200, 512), ("256x224", "2", 260, 500, 264)])
+def test_gemm_wave_fitting_tiles(vk, torch_cuda, monkeypatch, tile, splits, M, N, K):
+    """The 256-row tiles of 192, 160 and 224 columns (two accumulators of 128 rows, tensor memory
+    rounded up to 512 columns), forced, with and without split K and with ragged M, N, K."""
+    monkeypatch.setenv("VKLLM_B200_GEMM_TILE", tile)
+    monkeypatch.setenv("VKLLM_B200_GEMM_SPLITS", splits)
+    got, ref, _, tol = run_gemm(vk, torch_cuda, M, N, K, seed=M + N + K + 1)
+    check(got, ref, tol)

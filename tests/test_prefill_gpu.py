@@ -97,3 +97,37 @@ def test_chunked_prefill_matches_oracle(vk, ctx, orc, tiny_gguf):
     finally:
         m.close()
         model.free()
+
+
+@pytest.mark.parametrize("tile", ["256x192", "256x160", "256x224", "128x256"])
+def test_grouped_prefill_gemm_tiles(vk, ctx, monkeypatch, tile):
+    """Fused prefill of a model whose Q/K/V and FFN row counts are multiples of 256, so that the Q/K/V
+    and up/gate projections run as grouped GEMMs over the model's own matrices. With the tile forced
+    to one whose width does not divide the group (4096 / 192, 1280 / 192, ...), B tiles straddle two
+    matrices and load in 32-row pieces. Every forced tile must give the prefill's tokens and, within
+    the logit bar, its logits with the tuner's own choices."""
+    import ctypes as C
+
+    cfg = dict(block_count=2, context_length=512, embedding_length=512, head_count=4, ffn_length=1280,
+               vocab_size=4096, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
+    rng = np.random.default_rng(3)
+    prompt = [int(t) for t in rng.integers(3, 4096, size=200)]
+    runs = []
+    for forced in (None, tile):
+        if forced:
+            monkeypatch.setenv("VKLLM_B200_GEMM_TILE", forced)
+        else:
+            monkeypatch.delenv("VKLLM_B200_GEMM_TILE", raising=False)
+        model = vk.Model(ctx).init_random(cfg, 21)
+        try:
+            tok = model.step(prompt, 0)
+            buf = np.zeros(cfg["vocab_size"], dtype=np.uint16)
+            vk.check(vk.lib().vkllm_b200_engine_read_logits(ctx.ptr, C.byref(model.m), buf.ctypes.data,
+                                                           cfg["vocab_size"]), "logits")
+            runs.append((tok, buf.view(np.float16).astype(np.float32)))
+        finally:
+            model.free()
+    (t0, l0), (t1, l1) = runs
+    d = np.abs(l0 - l1)
+    assert d.max() <= 2e-2 and d.mean() <= 2e-3, (tile, d.max(), d.mean())
+    assert t0 == t1 or abs(l0[t0] - l0[t1]) <= 2e-3, (tile, t0, t1)

@@ -102,7 +102,8 @@ template <int BM, int N> struct TileCfg
     static constexpr uint32_t kBBytes = (uint32_t)N * kBK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kStages = (200u * 1024u) / kStageBytes;
-    static constexpr uint32_t kTmemCols = kAcc * N;
+    // tensor-memory columns: a power of two >= 32 covering the accumulators
+    static constexpr uint32_t kTmemCols = kAcc * N <= 128 ? 128u : (kAcc * N <= 256 ? 256u : 512u);
     static constexpr uint32_t kSmem = 1024 /* alignment slack */ + kStages * kStageBytes + 256 /* barriers */;
 };
 
@@ -118,6 +119,8 @@ struct TcParams
     uint32_t act_from; // act applies to output columns >= act_from
     uint32_t b_tiled;  // B in 128-row x 64-column tiles (gemm_tile_b); its map is (64, 128, k-block, n-tile)
     uint32_t b_group_n; // > 0: B rows come from up to three matrices of b_group_n rows each (tmB, tmB1, tmB2)
+    uint32_t b_groups;  // their count
+    uint32_t b_piece;   // > 0: grouped B tiles load as pieces of this many rows (b_group_n % BN != 0)
     __half *C;
     uint32_t *err;
     // Split-K: `splits` CTAs share a tile, each over kb_per k-blocks, writing fp32 partials to
@@ -221,13 +224,24 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
         // Producer.
         const int32_t ca = p.a_cc ? 0 : (int32_t)zc, ba = p.a_bc ? 0 : (int32_t)zb;
         const int32_t cb = p.b_cc ? 0 : (int32_t)zc, bb = p.b_bc ? 0 : (int32_t)zb;
-        // grouped B: the tile's rows n0 .. n0 + BN - 1 lie in one group (b_group_n % BN == 0, host)
-        const uint32_t grp = p.b_group_n ? n0 / p.b_group_n : 0u;
+        // grouped B, whole tiles: the tile's rows n0 .. n0 + BN - 1 lie in one group (b_group_n % BN == 0)
+        const uint32_t grp = p.b_group_n && !p.b_piece ? n0 / p.b_group_n : 0u;
         const CUtensorMap *mapB = grp == 0 ? &tmB : (grp == 1 ? &tmB1 : &tmB2);
         const uint32_t nb0 = n0 - grp * p.b_group_n;
         auto load_b = [&](uint32_t kb, uint32_t sb, uint64_t *bar) {
             if (p.b_tiled) // BN / 128 consecutive tiles of the k-block: the same smem image as BN rows
                 tma_load_4d(sb, mapB, 0, 0, (int32_t)(kb_lo + kb), (int32_t)(nb0 / kTileRows), bar);
+            else if (p.b_piece)
+            {
+                // pieces of b_piece rows (128 B each in the swizzled image), each from its group's map;
+                // rows past N read the last group's map out of range (zero fill, same byte count)
+                for (uint32_t r = 0; r < (uint32_t)BN; r += p.b_piece)
+                {
+                    const uint32_t row = n0 + r, gi = min(row / p.b_group_n, p.b_groups - 1);
+                    tma_load_4d(sb + r * 128, gi == 0 ? &tmB : (gi == 1 ? &tmB1 : &tmB2), (int32_t)((kb_lo + kb) * kBK),
+                                (int32_t)(row - gi * p.b_group_n), 0, 0, bar);
+                }
+            }
             else
                 tma_load_4d(sb, mapB, (int32_t)((kb_lo + kb) * kBK), (int32_t)nb0, cb, bb, bar);
         };
@@ -620,29 +634,34 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
         return false;
     if (g.b_tiled)
     {
-        if (g.batch != 1 || !encode_tiled_b(&mb, g.B, g.K, g.N, BN))
+        if (g.batch != 1 || BN % kTileRows || !encode_tiled_b(&mb, g.B, g.K, g.N, BN))
             return false;
     }
     else if (!encode_operand(&mb, g.B, g.K, g.N, g.ldb, g.b_sc ? g.batch_c : 1, g.b_sc, g.b_sb ? batch_b : 1, g.b_sb,
                              BN))
         return false;
     CUtensorMap mb1 = mb, mb2 = mb;
-    uint32_t group_n = 0;
+    uint32_t group_n = 0, groups = 0, piece = 0;
     if (g.b_group_n)
     {
-        // grouped B: N = groups * b_group_n rows, group i from B, B1, B2
-        const uint32_t groups = g.N / g.b_group_n;
-        if (g.b_tiled || g.batch != 1 || g.b_group_n % BN || groups * g.b_group_n != g.N || groups < 1 || groups > 3)
+        // grouped B: N = groups * b_group_n rows, group i from B, B1, B2; a tile that may straddle two
+        // groups (b_group_n % BN != 0) loads in 32-row pieces, which never do (b_group_n % 32 == 0)
+        groups = g.N / g.b_group_n;
+        piece = g.b_group_n % BN ? 32u : 0u;
+        if (g.b_tiled || g.batch != 1 || (piece && g.b_group_n % piece) || groups * g.b_group_n != g.N ||
+            groups < 1 || groups > 3)
             return false;
         const void *src[3] = {g.B, g.B1, g.B2};
         CUtensorMap *dst[3] = {&mb, &mb1, &mb2};
         for (uint32_t i = 0; i < groups; ++i)
-            if (!src[i] || !encode_operand(dst[i], src[i], g.K, g.b_group_n, g.ldb, 1, 0, 1, 0, BN))
+            if (!src[i] || !encode_operand(dst[i], src[i], g.K, g.b_group_n, g.ldb, 1, 0, 1, 0, piece ? piece : BN))
                 return false;
         group_n = g.b_group_n;
     }
     TcParams p{};
     p.b_group_n = group_n;
+    p.b_groups = groups;
+    p.b_piece = piece;
     p.M = g.M;
     p.N = g.N;
     p.K = g.K;
@@ -764,16 +783,27 @@ bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool tran
 
 namespace
 {
-// A launch configuration: tile (0: 128 x 128, 1: 128 x 256, 2: 256 x 256) and K splits.
+// A launch configuration: tile (kTiles[tile]) and K splits. The 256-row tiles narrower than 256
+// columns let a shape's tile count fill the SMs in whole waves (e.g. 512 x 12288: 128 tiles of
+// 256 x 192 in one wave, against 96 of 256 x 256 or 192 of 128 x 256).
 struct TcChoice
 {
     uint8_t tile = 0, splits = 1;
 };
+constexpr uint32_t kNumTiles = 6;
+constexpr uint32_t kTileBM[kNumTiles] = {128, 128, 256, 256, 256, 256};
+constexpr uint32_t kTileBN[kNumTiles] = {128, 256, 256, 192, 160, 224};
 
 bool launch_choice(const GemmArgs &g, cudaStream_t s, TcChoice c)
 {
     switch (c.tile)
     {
+    case 5:
+        return launch_tc<256, 224>(g, s, c.splits);
+    case 4:
+        return launch_tc<256, 160>(g, s, c.splits);
+    case 3:
+        return launch_tc<256, 192>(g, s, c.splits);
     case 2:
         return launch_tc<256, 256>(g, s, c.splits);
     case 1:
@@ -852,12 +882,14 @@ TcChoice tune(const GemmArgs &g_in, cudaStream_t s, int sms, TcChoice model)
     const uint32_t kb_all = (g.K + kBK - 1) / kBK;
     float t_model = time_of(model), t_best = t_model;
     TcChoice best = model;
-    const uint32_t bms[3] = {128, 128, 256}, bns[3] = {128, 256, 256};
-    for (uint8_t t = 0; t < 3; ++t)
+    for (uint8_t t = 0; t < kNumTiles; ++t)
     {
-        if (t == 2 && g.M <= 128)
+        if (kTileBM[t] == 256 && g.M <= 128)
             continue;
-        const uint64_t n_tiles = (uint64_t)((g.N + bns[t] - 1) / bns[t]) * ((g.M + bms[t] - 1) / bms[t]) * g.batch;
+        if (g.b_tiled && kTileBN[t] % 128)
+            continue;
+        const uint64_t n_tiles =
+            (uint64_t)((g.N + kTileBN[t] - 1) / kTileBN[t]) * ((g.M + kTileBM[t] - 1) / kTileBM[t]) * g.batch;
         for (uint8_t sp : {1, 2, 3, 4, 6, 8})
         {
             if (sp > kb_all || (sp > 1 && n_tiles * sp > 2ull * (uint64_t)sms) || (t == model.tile && sp == model.splits))
@@ -887,6 +919,12 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
         const uint32_t sp = force_splits ? (uint32_t)atoi(force_splits) : 1u;
         if (!strcmp(force, "256x256"))
             return launch_tc<256, 256>(g, s, sp);
+        if (!strcmp(force, "256x192"))
+            return launch_tc<256, 192>(g, s, sp);
+        if (!strcmp(force, "256x160"))
+            return launch_tc<256, 160>(g, s, sp);
+        if (!strcmp(force, "256x224"))
+            return launch_tc<256, 224>(g, s, sp);
         if (!strcmp(force, "128x256"))
             return launch_tc<128, 256>(g, s, sp);
         if (!strcmp(force, "128x128"))
@@ -917,7 +955,7 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
             {
                 unsigned m, n, k, b, bt, t, sp;
                 while (fscanf(f, "%u %u %u %u %u %u %u", &m, &n, &k, &b, &bt, &t, &sp) == 7)
-                    if (bt <= 3 && t <= 2 && sp >= 1 && sp <= 8)
+                    if (bt <= 3 && t < kNumTiles && sp >= 1 && sp <= 8)
                         for (int d = 0; d < 64; ++d) // the file carries no device: it applies to each
                             cache[TuneKey{d, m, n, k, b, bt}] = TcChoice{(uint8_t)t, (uint8_t)sp};
                 fclose(f);
