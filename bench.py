@@ -659,20 +659,31 @@ def run_ours(args, world, rank, local):
     for _ in range(2):  # warm the per-step allocations
         tok = model.step([tok], pos)
         pos += 1
+    # (1) the loop in native code (vkllm_b200_token_loop: the reference loop's calls, one graph per
+    # token); (2) the same calls made one by one from Python through ctypes (Model.step)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
     e0.record(stream)
-    for _ in range(n_e2e):
-        tok = model.step([tok], pos)
-        pos += 1
+    toks_native, host_us = model.token_loop([tok], pos, n_e2e)
     e1.record(stream)
     e1.synchronize()
     wall_e2e = time.perf_counter() - w0
+    pos += n_e2e
+    tok = toks_native[-1]
     e2e_ms = max(e0.elapsed_time(e1), wall_e2e * 1000.0)
     e2e_max = max_over_ranks(world, e2e_ms)
     e2e_value = world * n_e2e / (e2e_max / 1000.0)
+    torch.cuda.synchronize()
+    barrier(world)
+    w0 = time.perf_counter()
+    for _ in range(n_e2e):
+        tok = model.step([tok], pos)
+        pos += 1
+    torch.cuda.synchronize()
+    e2e_py_max = max_over_ranks(world, (time.perf_counter() - w0) * 1000.0)
+    e2e_py_value = world * n_e2e / (e2e_py_max / 1000.0)
 
     result = None
     if rank == 0:
@@ -732,7 +743,12 @@ def run_ours(args, world, rank, local):
                         "gemms": prefill_gemms},
             "batched": batched,
             "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                    "steps": n_e2e, "path": "reference token loop through the C API (graph rebuilt per token)",
+                    "steps": n_e2e,
+                    "path": "reference token loop through the C API in native code (vkllm_b200_token_loop: "
+                            "tensor_new, graph_new, build_graph, init, upload, run, post_run, read, graph_free per token)",
+                    "host_us_per_token": round(host_us / n_e2e, 2),
+                    "python_ctypes_loop": {"value": round(e2e_py_value, 2), "unit": "tokens/s",
+                                           "path": "the same calls one by one from Python (ctypes)"},
                     "host_graph_us_per_token": host_cost},
             "gpu_launches": int(launches if persistent else kps * K),
             "clocks": clk.summary(),

@@ -205,6 +205,17 @@ extern vkllm_err_t vkllm_b200_gemm_f16(const void *A, const void *B, void *C, ui
  * bounded waits expired (the results of that launch are not valid). */
 extern uint32_t vkllm_b200_gemm_f16_error(void);
 
+/* The reference's token loop (tests/vkllm_test_infer_gguf.c:181-272) as one call, through the public
+ * entry points: for each of n_tokens iterations, a mapped u32 input tensor, vkllm_graph_new,
+ * vkllm_models_llama2_build_graph at `offset`, vkllm_graph_init, vkllm_commands_upload of the ids,
+ * vkllm_graph_run, vkllm_graph_post_run, the last row of the mapped argmax output and
+ * vkllm_graph_free. The first iteration feeds the n_prompt ids of `prompt` (the prefill), each later
+ * one the previous prediction; out_tokens[i] receives iteration i's prediction. When host_us is not
+ * NULL it receives the host time spent outside vkllm_graph_run (microseconds, all iterations). */
+extern vkllm_err_t vkllm_b200_token_loop(struct vkllm_context *context, struct vkllm_models_llama2 *model,
+                                         const uint32_t *prompt, uint32_t n_prompt, uint32_t offset,
+                                         uint32_t n_tokens, uint32_t *out_tokens, double *host_us);
+
 /* Batched greedy decode of independent sequences sharing the model's weights (no reference
  * counterpart; the reference decodes one sequence per graph). Each sequence has its own KV cache of
  * `kv_rows` rows per layer and head inside the batch. A step of all sequences runs the reference

@@ -176,3 +176,20 @@ def test_cache_lifetimes(vk, ctx, tiny_gguf):
         _free(vk, ctx, g5)
     finally:
         m.free()
+
+
+def test_native_token_loop_matches_the_python_loop(vk, ctx, tiny_gguf):
+    """vkllm_b200_token_loop (the reference loop's calls in native code) predicts what the same calls
+    made one by one from Python predict, prefill included."""
+    import gen_gguf
+
+    path, _ = tiny_gguf
+    prompt = gen_gguf.prompt(9, 12)
+    m = vk.Model(ctx).load(path)
+    try:
+        py = m.generate(prompt, 20)
+        native, host_us = m.token_loop(prompt, 0, 20)
+    finally:
+        m.free()
+    assert native == py
+    assert host_us > 0

@@ -173,6 +173,8 @@ _SIGS = {
     "vkllm_b200_gemm_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
                                       C.c_uint64, C.c_uint64, C.c_uint64, C.c_float, C.c_int, C.c_void_p]),
     "vkllm_b200_gemm_f16_error": (C.c_uint32, []),
+    "vkllm_b200_token_loop": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                        C.c_void_p, C.POINTER(C.c_double)]),
     "vkllm_b200_batch_new": (C.c_int, [C.c_void_p, C.POINTER(Llama2), C.c_uint32, C.c_uint32, C.POINTER(C.c_void_p)]),
     "vkllm_b200_batch_load_sequence": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32]),
     "vkllm_b200_batch_decode_steps": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32]),
@@ -503,6 +505,16 @@ class Model:
                     return fetch(self.ctx, t)[0, 0, -1].copy()
                 break
         return self.engine_logits().copy()
+
+    def token_loop(self, prompt, offset, n_tokens):
+        """The reference token loop in native code (vkllm_b200_token_loop): returns the n_tokens
+        predictions and the host microseconds spent outside vkllm_graph_run."""
+        p = np.asarray(prompt, dtype=np.uint32)
+        out = np.zeros(n_tokens, dtype=np.uint32)
+        host = C.c_double(0.0)
+        check(lib().vkllm_b200_token_loop(self.ctx.ptr, C.byref(self.m), p.ctypes.data, len(p), offset, n_tokens,
+                                          out.ctypes.data, C.byref(host)), "token_loop")
+        return [int(t) for t in out], host.value
 
     def generate(self, prompt, n_tokens, logits=None):
         """Greedy loop: prefill with `prompt`, then feed each prediction back; n_tokens predictions."""
