@@ -219,7 +219,9 @@ def lib():
             raise RuntimeError(f"{LIB_PATH} missing: run `python vkllm.c_b200/build.py` (or __graft_entry__.build())")
         l = C.CDLL(LIB_PATH)
         for name, (res, args) in _SIGS.items():
-            f = getattr(l, name)
+            f = getattr(l, name, None)
+            if f is None:  # a library older than this binding: calling the entry point raises
+                continue
             f.restype = res
             f.argtypes = args
         _lib = l
