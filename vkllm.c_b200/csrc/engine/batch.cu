@@ -59,7 +59,7 @@ struct vkllm_b200_batch
     uint32_t att_staged = 256; // threads of k_b_attention_staged (0: k_b_attention)
     uint32_t att_chunk = 64, att_ring = 3; // its rows per chunk and chunk buffers
     // K splits and tiles (0: 128 x 128, 1: 128 x 256) of the QKV, up/gate and Wo / down GEMMs
-    uint32_t qkv_splits = 2, ug_splits = 3, proj_splits = 4, qkv_tile = 1, ug_tile = 1, proj_tile = 0;
+    uint32_t qkv_splits = 3, ug_splits = 3, proj_splits = 4, qkv_tile = 1, ug_tile = 1, proj_tile = 0;
     const float *out_norm = nullptr;
     void *ws = nullptr;
     __half *kv = nullptr; // [L][2][B][H][cap][hd]
@@ -254,7 +254,9 @@ __global__ void k_b_rope_kv_part(const float *__restrict__ part, uint32_t splits
 }
 
 constexpr uint32_t kAttChunk = 64;    // key rows per staged chunk (staged attention), default
-constexpr uint32_t kAttStages = 3;    // chunk buffers in flight per CTA, default
+// chunk buffers in flight per CTA, default (7B, 64 sequences: 2 / 3 buffers of 64 rows 4.877 / 4.966 ms
+// per step; 4 / 6 of 32 rows 5.038 / 5.156)
+constexpr uint32_t kAttStages = 2;
 constexpr uint32_t kAttMaxStages = 8; // most chunk buffers
 constexpr uint32_t kAttThreads = 512; // most threads of the staged attention kernel
 constexpr uint32_t kErrAttTimeout = 2u; // batch error bit: a staged-attention copy wait expired
@@ -1082,7 +1084,8 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_staged = 0;
     // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0 / 1) of the QKV, up/gate
-    // and Wo / down GEMMs (defaults 2,3,4,1,1,0)
+    // and Wo / down GEMMs (defaults 3,3,4,1,1,0; 7B, 64 sequences: 2,3,4 / 3,3,4 / 4,3,4 / 3,2,4 splits
+    // 4.966 / 4.936 / 5.223 / 5.108 ms per step)
     if (const char *ge = getenv("VKLLM_B200_BATCH_GEMM"))
     {
         unsigned v[6];

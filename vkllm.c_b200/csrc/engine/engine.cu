@@ -220,7 +220,24 @@ vkllm_err_t enqueue_step(Engine *e, cudaStream_t s)
 
 template <class Op> void allow_smem(const StreamGeom &g)
 {
-    cudaFuncSetAttribute(k_gemv_stream<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stream_smem_bytes(g));
+    if (cudaFuncSetAttribute(k_gemv_stream<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)stream_smem_bytes(g)) != cudaSuccess)
+        log_error("streaming GEMV: %zu bytes of dynamic shared memory refused: %s", stream_smem_bytes(g),
+                  cudaGetErrorString(cudaGetLastError()));
+}
+
+// Dynamic shared memory a streaming GEMV of this op may use: `cap`, at most the opt-in limit less
+// the kernel's static shared memory (the logits op's argmax arrays take 8 KB of it).
+template <class Op> uint32_t stream_cap(vkllm_context *ctx, uint32_t cap)
+{
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, k_gemv_stream<Op>) != cudaSuccess)
+    {
+        (void)cudaGetLastError();
+        return cap;
+    }
+    const size_t limit = ctx->device->smem_optin > fa.sharedSizeBytes ? ctx->device->smem_optin - fa.sharedSizeBytes : 0;
+    return (uint32_t)(cap < limit ? cap : limit);
 }
 
 // Persistent decode geometry: every phase kind shares the block size and stage layout.
@@ -911,11 +928,11 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     const uint32_t kSmemCap = env_u32("VKLLM_B200_STREAM_SMEM_KB", 220) * 1024;
     const uint32_t kSpw = env_u32("VKLLM_B200_STREAM_SPW", 1);
     e->grid_stream = (unsigned)sms * env_u32("VKLLM_B200_STREAM_CTAS_PER_SM", 1);
-    e->g_qkv = make_stream_geom(3 * HD / 2, 2, dd.D, dd.D, kTarget, kSmemCap, kSpw);
-    e->g_wo = make_stream_geom(dd.D, 1, HD, HD, kTarget, kSmemCap, kSpw);
-    e->g_upgate = make_stream_geom(dd.F, 2, dd.D, dd.D, kTarget, kSmemCap, kSpw);
-    e->g_down = make_stream_geom(dd.D, 1, dd.F, dd.F, kTarget, kSmemCap, kSpw);
-    e->g_logits = make_stream_geom(dd.V, 1, dd.D, dd.D, kTarget, kSmemCap, kSpw);
+    e->g_qkv = make_stream_geom(3 * HD / 2, 2, dd.D, dd.D, kTarget, stream_cap<QkvOp>(ctx, kSmemCap), kSpw);
+    e->g_wo = make_stream_geom(dd.D, 1, HD, HD, kTarget, stream_cap<WoOp>(ctx, kSmemCap), kSpw);
+    e->g_upgate = make_stream_geom(dd.F, 2, dd.D, dd.D, kTarget, stream_cap<UpGateOp>(ctx, kSmemCap), kSpw);
+    e->g_down = make_stream_geom(dd.D, 1, dd.F, dd.F, kTarget, stream_cap<DownOp>(ctx, kSmemCap), kSpw);
+    e->g_logits = make_stream_geom(dd.V, 1, dd.D, dd.D, kTarget, stream_cap<LogitsOp>(ctx, kSmemCap), kSpw);
     for (const StreamGeom *g : {&e->g_qkv, &e->g_wo, &e->g_upgate, &e->g_down, &e->g_logits})
     {
         if (g->warps < 4 || stream_smem_bytes(*g) > ctx->device->smem_optin)
@@ -992,6 +1009,7 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
         return VKLLM_ERR_VULKAN;
     }
     cudaStreamSynchronize(ctx->runtime->stream);
+    (void)cudaGetLastError(); // errors of earlier calls were reported where they happened
     vkllm_err_t err = VKLLM_ERR_OK;
     if (cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
         err = VKLLM_ERR_VULKAN;
