@@ -82,8 +82,8 @@ def test_batch_rejects_a_sequence_past_its_capacity(vk, ctx, tiny_gguf):
 def test_in_place_weights_match_tile_copies(vk, ctx, monkeypatch):
     """VKLLM_B200_BATCH_TILED=2 reads the model's own matrices as grouped GEMM operands instead of the
     batch's tile-order copies: the same GEMM tiles and K splits over the same values, so tokens and
-    logits are bit-identical. A random model whose Q/K/V and FFN row counts are multiples of 256 (the
-    in-place mode's requirement; the tiny model is not)."""
+    logits are bit-identical. A random model whose Q/K/V and FFN row counts are multiples of 256, so
+    that whole B tiles lie in one matrix."""
     cfg = dict(block_count=2, context_length=256, embedding_length=512, head_count=4, ffn_length=1280,
                vocab_size=4096, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
     rng = np.random.default_rng(5)

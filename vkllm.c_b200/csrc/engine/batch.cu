@@ -1098,10 +1098,10 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         }
     }
     // VKLLM_B200_BATCH_TILED: 1 (default) tile-order copies, 2 the model's matrices in place (grouped
-    // B operands; needs HD and F divisible by 256), 0 row-major concatenated copies.
+    // B operands; HD and F multiples of 32), 0 row-major concatenated copies.
     const char *tiled_env = getenv("VKLLM_B200_BATCH_TILED");
     bt->tiled = tiled_env ? (uint32_t)atoi(tiled_env) : 1u;
-    if (bt->tiled > 2 || (bt->tiled == 2 && (HD % 256 != 0 || F % 256 != 0)))
+    if (bt->tiled > 2 || (bt->tiled == 2 && (HD % 32 != 0 || F % 32 != 0)))
         bt->tiled = 1;
     const size_t t_qkv = gemm_tiled_b_elems(3 * HD, D), t_ug = gemm_tiled_b_elems(2 * F, D),
                  t_wo = gemm_tiled_b_elems(D, HD), t_wd = gemm_tiled_b_elems(D, F);

@@ -1216,16 +1216,21 @@ vkllm_err_t prefill_run(Engine *e, const uint32_t *tok, uint32_t S, uint32_t p0,
     // up and gate side by side ([S][2F]) when grouped, else two [S][F] blocks; then m [S][F]
     __half *ug = (__half *)(w + 3 * sd + 5 * shd), *mm = (__half *)(w + 3 * sd + 5 * shd + 2 * sf);
     __half *lg = (__half *)(w + 3 * sd + 5 * shd + 3 * sf);
-    // the grouped GEMMs need every tile width (128, 256) to divide a group's rows
-    const bool grouped = HD % 256 == 0 && F % 256 == 0;
+    // grouped GEMMs load B tiles that straddle two matrices in 32-row pieces
+    const bool grouped = HD % 32 == 0 && F % 32 == 0;
     const uint32_t ldq = grouped ? 3 * HD : HD, ldu = grouped ? 2 * F : F;
     __half *q = qkv, *k = grouped ? qkv + HD : qkv + (uint64_t)S * HD, *v = grouped ? qkv + 2 * HD : qkv + 2ull * S * HD;
     __half *up = ug, *gt = grouped ? ug + F : ug + (uint64_t)S * F;
     k_pf_embed<<<S, 128, 0, s>>>(tok, e->embed, dd.V, D, e->unk, x);
     const uint64_t rope_threads = (uint64_t)S * HD / 8, gate_threads = (uint64_t)S * F / 8;
-    for (const LayerW &lw : e->layers)
+    // the residual adds and the RMSNORMs after them run as one pass per row (the next layer's attention
+    // norm comes with the down projection's residual, the output norm with the last one's)
+    if (!launch_rmsnorm_rows(x, e->layers[0].attn_norm, n, S, D, dd.eps, s))
+        return VKLLM_ERR_ARGS;
+    for (size_t li = 0; li < e->layers.size(); ++li)
     {
-        bool ok = launch_rmsnorm_rows(x, lw.attn_norm, n, S, D, dd.eps, s);
+        const LayerW &lw = e->layers[li];
+        bool ok = true;
         if (grouped)
             ok = ok && pf_gemm(n, lw.wq, qkv, S, 3 * HD, D, 0, s, lw.wk, lw.wv);
         else
@@ -1236,7 +1241,7 @@ vkllm_err_t prefill_run(Engine *e, const uint32_t *tok, uint32_t S, uint32_t p0,
         k_pf_rope_kv<<<(unsigned)((rope_threads + 255) / 256), 256, 0, s>>>(q, k, v, ldq, S, dd.H, dd.hd, p0, dd.ctx,
                                                                             dd.rope_base, rq, lw.kcache, lw.vcache);
         ok = pf_attention(rq, lw, dd, S, p0, att, s) && pf_gemm(att, lw.wo, y, S, D, HD, 0, s) &&
-             launch_bin_h(x, y, x, (uint64_t)S * D, 0, s) && launch_rmsnorm_rows(x, lw.ffn_norm, n, S, D, dd.eps, s);
+             launch_residual_rmsnorm_rows(x, y, lw.ffn_norm, n, S, D, dd.eps, s);
         if (grouped) // [up | silu(gate)]: SiLU from column F on
             ok = ok && pf_gemm(n, lw.wu, ug, S, 2 * F, D, 1, s, lw.wg, nullptr, F);
         else
@@ -1244,11 +1249,12 @@ vkllm_err_t prefill_run(Engine *e, const uint32_t *tok, uint32_t S, uint32_t p0,
         if (!ok)
             return VKLLM_ERR_ARGS;
         k_pf_gate_mul<<<(unsigned)((gate_threads + 255) / 256), 256, 0, s>>>(up, gt, ldu, S, F, mm);
-        ok = pf_gemm(mm, lw.wd, y, S, D, F, 0, s) && launch_bin_h(x, y, x, (uint64_t)S * D, 0, s);
+        const float *next_norm = li + 1 < e->layers.size() ? e->layers[li + 1].attn_norm : e->out_norm;
+        ok = pf_gemm(mm, lw.wd, y, S, D, F, 0, s) && launch_residual_rmsnorm_rows(x, y, next_norm, n, S, D, dd.eps, s);
         if (!ok)
             return VKLLM_ERR_ARGS;
     }
-    if (!launch_rmsnorm_rows(x, e->out_norm, n, S, D, dd.eps, s) || !pf_gemm(n, e->wout, lg, S, V, D, 0, s) ||
+    if (!pf_gemm(n, e->wout, lg, S, V, D, 0, s) ||
         !launch_argmax_rows(lg, S, V, out, s))
         return VKLLM_ERR_ARGS;
     VKB_CUDA(cudaMemcpyAsync(e->logits, lg + (uint64_t)(S - 1) * V, (size_t)V * 2, cudaMemcpyDeviceToDevice, s));

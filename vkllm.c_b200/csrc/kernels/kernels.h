@@ -80,6 +80,9 @@ uint32_t gemm_tcgen05_error(int dev);
 bool launch_rmsnorm_rows(const __half *x, const float *g, __half *y, uint32_t rows, uint32_t W, float eps,
                          cudaStream_t s);
 bool launch_bin_h(const __half *a, const __half *b, __half *out, uint64_t n, int op, cudaStream_t s);
+// x = fp16(x + y) (the residual BIN), then n = RMSNORM(x) with gains g, per row of W.
+bool launch_residual_rmsnorm_rows(__half *x, const __half *y, const float *g, __half *n, uint32_t rows, uint32_t W,
+                                  float eps, cudaStream_t s);
 bool launch_argmax_rows(const __half *x, uint32_t rows, uint32_t W, uint32_t *out, cudaStream_t s);
 
 } // namespace vkb

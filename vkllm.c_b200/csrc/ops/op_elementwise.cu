@@ -135,6 +135,70 @@ __global__ void k_rmsnorm_vec(const __half *x, Desc4 dx, const float *g, __half 
     }
 }
 
+// The residual BIN (op 0, fp16(float(x) + float(y)), src/shaders/vkllm_bin_op.comp:43-72) and the
+// RMSNORM of its result (as k_rmsnorm_vec) in one pass over a dense row: x = x + y, n = rmsnorm(x).
+__global__ void k_residual_rmsnorm_vec(__half *__restrict__ x, const __half *__restrict__ y, const float *g,
+                                       __half *__restrict__ n, uint32_t W, float eps)
+{
+    __shared__ float red[32];
+    const uint64_t row = blockIdx.x;
+    uint4 *xr = reinterpret_cast<uint4 *>(x + row * W);
+    const uint4 *yr = reinterpret_cast<const uint4 *>(y + row * W);
+    uint4 *nr = reinterpret_cast<uint4 *>(n + row * W);
+    const uint32_t n8 = W / 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < n8)
+    {
+        const uint4 a = xr[threadIdx.x], b = yr[threadIdx.x];
+        const __half2 *ah = reinterpret_cast<const __half2 *>(&a), *bh = reinterpret_cast<const __half2 *>(&b);
+        __half2 *vh = reinterpret_cast<__half2 *>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 fa = __half22float2(ah[e]), fb = __half22float2(bh[e]);
+            vh[e] = __floats2half2_rn(fa.x + fb.x, fa.y + fb.y);
+        }
+        xr[threadIdx.x] = v;
+    }
+    const __half2 *vh = reinterpret_cast<const __half2 *>(&v);
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+    {
+        const float2 f = __half22float2(vh[e]);
+        s = fmaf(f.x, f.x, s);
+        s = fmaf(f.y, f.y, s);
+    }
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32)
+    {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0)
+            red[0] = t;
+    }
+    __syncthreads();
+    const float alpha = rsqrtf(red[0] / (float)W + eps);
+    if (threadIdx.x < n8)
+    {
+        const float4 ga = reinterpret_cast<const float4 *>(g)[2 * threadIdx.x];
+        const float4 gb = reinterpret_cast<const float4 *>(g)[2 * threadIdx.x + 1];
+        const float gg[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+        uint4 o;
+        __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+        {
+            const float2 f = __half22float2(vh[e]);
+            oh[e] = __floats2half2_rn((f.x * gg[2 * e]) * alpha, (f.y * gg[2 * e + 1]) * alpha);
+        }
+        nr[threadIdx.x] = o;
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // ROPE (src/shaders/vkllm_rope.comp:39-79): one thread per rotated pair.
 template <typename T>
@@ -1093,6 +1157,16 @@ bool launch_rmsnorm_rows(const __half *x, const float *g, __half *y, uint32_t ro
     Desc4 d{{1, 1, rows, W}, {0, 0, W, 1}};
     const unsigned threads = ((W / 8 + 31) / 32) * 32;
     k_rmsnorm_vec<<<rows, threads < 32 ? 32 : threads, 0, s>>>(x, d, g, y, d, eps);
+    return true;
+}
+
+bool launch_residual_rmsnorm_rows(__half *x, const __half *y, const float *g, __half *n, uint32_t rows, uint32_t W,
+                                  float eps, cudaStream_t s)
+{
+    if (W % 8 != 0 || W / 8 > 1024 || (((uintptr_t)x | (uintptr_t)y | (uintptr_t)n | (uintptr_t)g) & 15))
+        return false;
+    const unsigned threads = ((W / 8 + 31) / 32) * 32;
+    k_residual_rmsnorm_vec<<<rows, threads < 32 ? 32 : threads, 0, s>>>(x, y, g, n, W, eps);
     return true;
 }
 
