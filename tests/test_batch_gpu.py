@@ -21,9 +21,10 @@ N_STEPS = 32
 
 # the batch's kernel choices (read when the batch is created): the default (bulk-copy staged
 # attention, tile-order GEMM operands), the register-loading attention kernel, the staged kernel
-# with 128 threads, and row-major GEMM operands
+# with 128 threads, row-major GEMM operands, and GEMM tiles that load 64 rows of A per stage
 VARIANTS = {"default": {}, "att_registers": {"VKLLM_B200_BATCH_ATT_STAGED": "0"},
-            "att_staged_128": {"VKLLM_B200_BATCH_ATT_STAGED": "128"}, "rowmajor_b": {"VKLLM_B200_BATCH_TILED": "0"}}
+            "att_staged_128": {"VKLLM_B200_BATCH_ATT_STAGED": "128"}, "rowmajor_b": {"VKLLM_B200_BATCH_TILED": "0"},
+            "a64_tiles": {"VKLLM_B200_BATCH_GEMM": "3,3,4,3,3,2"}}
 
 
 @pytest.mark.parametrize("variant", list(VARIANTS))

@@ -88,3 +88,15 @@ def test_gemm_wave_fitting_tiles(vk, torch_cuda, monkeypatch, tile, splits, M, N
     monkeypatch.setenv("VKLLM_B200_GEMM_SPLITS", splits)
     got, ref, _, tol = run_gemm(vk, torch_cuda, M, N, K, seed=M + N + K + 1)
     check(got, ref, tol)
+
+
+@pytest.mark.parametrize("tile,splits,M,N,K", [("128x256a64", "1", 64, 4096, 4096), ("128x256a64", "3", 64, 12288, 4096),
+                                               ("128x128a64", "2", 33, 1000, 1032), ("128x128a64", "1", 1, 512, 512),
+                                               ("128x256a64", "4", 48, 700, 11008)])
+def test_gemm_tiles_loading_64_rows_of_a(vk, torch_cuda, monkeypatch, tile, splits, M, N, K):
+    """128-row tiles that load only 64 rows of A per stage (M <= 64: batched decode), forced, with and
+    without split K; the MMA's upper 64 rows read other staged data and are never stored."""
+    monkeypatch.setenv("VKLLM_B200_GEMM_TILE", tile)
+    monkeypatch.setenv("VKLLM_B200_GEMM_SPLITS", splits)
+    got, ref, _, tol = run_gemm(vk, torch_cuda, M, N, K, seed=M + N + K + 2)
+    check(got, ref, tol)

@@ -1083,7 +1083,8 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     if (!(bt->att_staged == 128 || bt->att_staged == 256 || bt->att_staged == 512) || dd.hd % 8 || dd.hd > 128 ||
         att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_staged = 0;
-    // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0 / 1) of the QKV, up/gate
+    // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0: 128 x 128, 1: 128 x 256;
+    // 2, 3: the same loading 64 rows of A per stage, for up to 64 sequences) of the QKV, up/gate
     // and Wo / down GEMMs (defaults 3,3,4,1,1,0; 7B, 64 sequences: 2,3,4 / 3,3,4 / 4,3,4 / 3,2,4 splits
     // 4.966 / 4.936 / 5.223 / 5.108 ms per step)
     if (const char *ge = getenv("VKLLM_B200_BATCH_GEMM"))
@@ -1091,7 +1092,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         unsigned v[6];
         if (sscanf(ge, "%u,%u,%u,%u,%u,%u", &v[0], &v[1], &v[2], &v[3], &v[4], &v[5]) == 6 && v[0] >= 1 &&
             v[0] <= kMaxPartSplits && v[1] >= 1 && v[1] <= kMaxPartSplits && v[2] >= 1 && v[2] <= kMaxPartSplits &&
-            v[3] <= 1 && v[4] <= 1 && v[5] <= 1)
+            v[3] <= 3 && v[4] <= 3 && v[5] <= 3)
         {
             bt->qkv_splits = v[0], bt->ug_splits = v[1], bt->proj_splits = v[2];
             bt->qkv_tile = v[3], bt->ug_tile = v[4], bt->proj_tile = v[5];

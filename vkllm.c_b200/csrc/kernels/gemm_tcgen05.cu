@@ -94,11 +94,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map
 }
 
 // Tile BM x N: BM = 128 (one accumulator) or 256 (two M = 128 accumulators side by side in tensor
-// memory, sharing each B tile, which halves the operand bytes per flop of a 128 x N tile).
-template <int BM, int N> struct TileCfg
+// memory, sharing each B tile, which halves the operand bytes per flop of a 128 x N tile). AR: rows
+// of A loaded per stage. AR = 64 < BM = 128 serves M <= 64 (batched decode): the stage keeps 8 KB of
+// A instead of 16, so one more stage of B fits in flight; the MMA still reads 128 rows, the upper 64
+// from the start of the stage's B region (in bounds), and those accumulator rows are never stored.
+template <int BM, int N, int AR = BM> struct TileCfg
 {
     static constexpr uint32_t kAcc = BM / 128;
-    static constexpr uint32_t kABytes = (uint32_t)BM * kBK * 2;
+    static constexpr uint32_t kABytes = (uint32_t)AR * kBK * 2;
     static constexpr uint32_t kBBytes = (uint32_t)N * kBK * 2;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kStages = (200u * 1024u) / kStageBytes;
@@ -172,13 +175,14 @@ __device__ __forceinline__ void store_row32(__half *crow, uint32_t nb, const uin
     }
 }
 
-template <int BM, int BN>
+template <int BM, int BN, int AR = BM>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                      const __grid_constant__ CUtensorMap tmB,
                                                      const __grid_constant__ CUtensorMap tmB1,
                                                      const __grid_constant__ CUtensorMap tmB2, TcParams p)
 {
-    using Cfg = TileCfg<BM, BN>;
+    static_assert(AR == BM || (BM == 128 && AR == 64), "A rows per stage: the tile's, or 64 of a 128-row tile");
+    using Cfg = TileCfg<BM, BN, AR>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t base = (su32(smem_raw) + 1023u) & ~1023u; // 1024-B aligned stages (swizzle atoms)
     unsigned char *smem = smem_raw + (base - su32(smem_raw));
@@ -604,11 +608,13 @@ uint32_t *error_word(int dev)
 
 // ws_ext / splits_out: when given, the split-K partials go to the caller's buffer ([splits][batch][M]
 // [N] fp32, splits > 1) and no reduction is launched; *splits_out receives the split count used.
-template <int BM, int BN>
+template <int BM, int BN, int AR = BM>
 bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws_ext = nullptr,
                uint32_t *splits_out = nullptr)
 {
-    using Cfg = TileCfg<BM, BN>;
+    using Cfg = TileCfg<BM, BN, AR>;
+    if (AR < BM && g.M > (uint32_t)AR)
+        return false;
     int dev = 0, cc = 0, optin = 0;
     if (cudaGetDevice(&dev) != cudaSuccess)
         return false;
@@ -619,8 +625,8 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
     static bool attr_set[64] = {};
     if (dev < 64 && !attr_set[dev])
     {
-        if (cudaFuncSetAttribute(k_gemm_tc<BM, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemm_tc<BM, BN, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)Cfg::kSmem) != cudaSuccess)
         {
             (void)cudaGetLastError();
             return false;
@@ -630,7 +636,7 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
     const uint32_t batch_b = g.batch / g.batch_c;
     CUtensorMap ma, mb;
     // broadcast dimensions (stride 0) are described with extent 1 and indexed 0 by the kernel
-    if (!encode_operand(&ma, g.A, g.K, g.M, g.lda, g.a_sc ? g.batch_c : 1, g.a_sc, g.a_sb ? batch_b : 1, g.a_sb, BM))
+    if (!encode_operand(&ma, g.A, g.K, g.M, g.lda, g.a_sc ? g.batch_c : 1, g.a_sc, g.a_sb ? batch_b : 1, g.a_sb, AR))
         return false;
     if (g.b_tiled)
     {
@@ -718,11 +724,11 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
         at[0].val.programmaticStreamSerializationAllowed = 1;
         lc.attrs = at;
         lc.numAttrs = 1;
-        if (cudaLaunchKernelEx(&lc, k_gemm_tc<BM, BN>, ma, mb, mb1, mb2, p) != cudaSuccess)
+        if (cudaLaunchKernelEx(&lc, k_gemm_tc<BM, BN, AR>, ma, mb, mb1, mb2, p) != cudaSuccess)
             return false;
     }
     else
-        k_gemm_tc<BM, BN><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, mb1, mb2, p);
+        k_gemm_tc<BM, BN, AR><<<grid, 192, Cfg::kSmem, s>>>(ma, mb, mb1, mb2, p);
     if (p.splits > 1 && !ws_ext)
     {
         const uint64_t work = (uint64_t)g.batch * g.M * ((g.N + 7) / 8);
@@ -790,14 +796,20 @@ struct TcChoice
 {
     uint8_t tile = 0, splits = 1;
 };
-constexpr uint32_t kNumTiles = 6;
-constexpr uint32_t kTileBM[kNumTiles] = {128, 128, 256, 256, 256, 256};
-constexpr uint32_t kTileBN[kNumTiles] = {128, 256, 256, 192, 160, 224};
+// Tiles 6 and 7 are 128 x 256 and 128 x 128 loading 64 rows of A per stage (M <= 64).
+constexpr uint32_t kNumTiles = 8;
+constexpr uint32_t kTileBM[kNumTiles] = {128, 128, 256, 256, 256, 256, 128, 128};
+constexpr uint32_t kTileBN[kNumTiles] = {128, 256, 256, 192, 160, 224, 256, 128};
+constexpr uint32_t kTileAR[kNumTiles] = {128, 128, 256, 256, 256, 256, 64, 64};
 
 bool launch_choice(const GemmArgs &g, cudaStream_t s, TcChoice c)
 {
     switch (c.tile)
     {
+    case 7:
+        return launch_tc<128, 128, 64>(g, s, c.splits);
+    case 6:
+        return launch_tc<128, 256, 64>(g, s, c.splits);
     case 5:
         return launch_tc<256, 224>(g, s, c.splits);
     case 4:
@@ -884,7 +896,7 @@ TcChoice tune(const GemmArgs &g_in, cudaStream_t s, int sms, TcChoice model)
     TcChoice best = model;
     for (uint8_t t = 0; t < kNumTiles; ++t)
     {
-        if (kTileBM[t] == 256 && g.M <= 128)
+        if ((kTileBM[t] == 256 && g.M <= 128) || g.M > kTileAR[t])
             continue;
         if (g.b_tiled && kTileBN[t] % 128)
             continue;
@@ -919,6 +931,10 @@ bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s)
         const uint32_t sp = force_splits ? (uint32_t)atoi(force_splits) : 1u;
         if (!strcmp(force, "256x256"))
             return launch_tc<256, 256>(g, s, sp);
+        if (!strcmp(force, "128x256a64"))
+            return launch_tc<128, 256, 64>(g, s, sp);
+        if (!strcmp(force, "128x128a64"))
+            return launch_tc<128, 128, 64>(g, s, sp);
         if (!strcmp(force, "256x192"))
             return launch_tc<256, 192>(g, s, sp);
         if (!strcmp(force, "256x160"))
@@ -994,8 +1010,17 @@ bool gemm_tcgen05_partials(const GemmArgs &g, cudaStream_t s, uint32_t splits, f
 {
     if (g.batch == 0 || g.batch_c == 0 || !ws || !splits_used || splits < 2)
         return false;
-    return tile == 1 ? launch_tc<128, 256>(g, s, splits, ws, splits_used)
-                     : launch_tc<128, 128>(g, s, splits, ws, splits_used);
+    switch (tile)
+    {
+    case 3:
+        return launch_tc<128, 256, 64>(g, s, splits, ws, splits_used);
+    case 2:
+        return launch_tc<128, 128, 64>(g, s, splits, ws, splits_used);
+    case 1:
+        return launch_tc<128, 256>(g, s, splits, ws, splits_used);
+    default:
+        return launch_tc<128, 128>(g, s, splits, ws, splits_used);
+    }
 }
 
 namespace

@@ -65,7 +65,8 @@ bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool tran
 // Enqueues the tcgen05 GEMM; returns false when it cannot run on this device / shape.
 bool gemm_tcgen05_launch(const GemmArgs &g, cudaStream_t s);
 
-// The tcgen05 GEMM (tile 0: 128 x 128, 1: 128 x 256) with K split `splits` ways, writing its fp32
+// The tcgen05 GEMM (tile 0: 128 x 128, 1: 128 x 256; 2, 3: the same loading 64 rows of A per stage,
+// for M <= 64) with K split `splits` ways, writing its fp32
 // partial sums [splits][batch][M][N] to `ws` instead of C (no reduction is launched; the caller sums
 // the partials in split order, then applies scale / act / fp16 as the plain GEMM would).
 // *splits_used receives the split count (<= splits: every split gets at least one 64-deep k-block).
