@@ -8,8 +8,9 @@ reference's shape-only MATMUL predicate reads V transposed (quirk Q1,
 src/core/vkllm_op_matmul.c:14-30); and a prompt prefilled in two chunks, the second at a nonzero
 position over the cache the first wrote. Compared: the argmax of EVERY row of the graph's output
 (the reference computes all S rows, src/models/vkllm_models_llama2.c:569-587) and the last row's
-fp16 logits, within the north_star bar (max-abs 2e-2, mean-abs 2e-3); the node-by-node path
-(VKLLM_B200_PREFILL=0) must agree with the oracle the same way."""
+fp16 logits, within the north_star bar (max-abs 2e-2, mean-abs 2e-3); the attention kernel's single-CTA
+form (VKLLM_B200_PF_ATT_PAIR=0; the default splits the key blocks over a cluster of two CTAs) and the
+node-by-node path (VKLLM_B200_PREFILL=0) must agree with the oracle the same way."""
 import ctypes as C
 
 import numpy as np
@@ -58,12 +59,14 @@ def check_rows(ids, logits, ref_ids, ref_all):
 
 
 @pytest.mark.parametrize("n", [5, 47, 48, 49, 130])
-@pytest.mark.parametrize("path", ["fused", "nodes"])
+@pytest.mark.parametrize("path", ["fused", "fused_single_cta", "nodes"])
 def test_prefill_matches_oracle(vk, ctx, orc, tiny_gguf, n, path, monkeypatch):
     import gen_gguf
 
     if path == "nodes":
         monkeypatch.setenv("VKLLM_B200_PREFILL", "0")
+    if path == "fused_single_cta":  # attention without the CTA-pair key split
+        monkeypatch.setenv("VKLLM_B200_PF_ATT_PAIR", "0")
     path_, weights = tiny_gguf
     prompt = gen_gguf.prompt(100 + n, n)
     model = vk.Model(ctx).load(path_)

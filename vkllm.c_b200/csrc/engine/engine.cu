@@ -1107,7 +1107,7 @@ void engine_destroy(vkllm_context *ctx, vkllm_models_llama2 *model)
 namespace
 {
 
-template <int HD>
+template <int HD, bool PAIR>
 bool pf_attention_launch(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint32_t S, uint32_t p0,
                          __half *out, cudaStream_t s)
 {
@@ -1117,7 +1117,7 @@ bool pf_attention_launch(const __half *rq, const LayerW &lw, const DecodeDims &d
         return false;
     if (!attr_set[dev])
     {
-        if (cudaFuncSetAttribute(k_pf_attention<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(k_pf_attention<HD, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PfSmem<HD>::kBytes) != cudaSuccess)
         {
             (void)cudaGetLastError();
@@ -1125,10 +1125,38 @@ bool pf_attention_launch(const __half *rq, const LayerW &lw, const DecodeDims &d
         }
         attr_set[dev] = true;
     }
-    dim3 grid((S + kPfBQ - 1) / kPfBQ, dd.H);
-    k_pf_attention<HD><<<grid, kPfThreads, PfSmem<HD>::kBytes, s>>>(rq, lw.kcache, lw.vcache, dd.ctx, S, p0, dd.H,
-                                                                    dd.scale, out);
+    const uint32_t tiles = (S + kPfBQ - 1) / kPfBQ;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(PAIR ? 2 * tiles : tiles, dd.H);
+    lc.blockDim = dim3(kPfThreads);
+    lc.dynamicSmemBytes = PfSmem<HD>::kBytes;
+    lc.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = PAIR ? 2 : 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    lc.attrs = at;
+    lc.numAttrs = PAIR ? 1 : 0;
+    if (cudaLaunchKernelEx(&lc, k_pf_attention<HD, PAIR>, rq, (const __half *)lw.kcache, (const __half *)lw.vcache,
+                           dd.ctx, S, p0, dd.H, dd.scale, out) != cudaSuccess)
+    {
+        log_error("prefill attention launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return false;
+    }
     return true;
+}
+
+// VKLLM_B200_PF_ATT_PAIR=0: one CTA per (query tile, head) instead of a cluster of two that split the
+// key blocks.
+template <int HD>
+bool pf_attention_hd(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint32_t S, uint32_t p0, __half *out,
+                     cudaStream_t s)
+{
+    const char *v = getenv("VKLLM_B200_PF_ATT_PAIR");
+    const bool pair = !(v && atoi(v) == 0);
+    return pair ? pf_attention_launch<HD, true>(rq, lw, dd, S, p0, out, s)
+                : pf_attention_launch<HD, false>(rq, lw, dd, S, p0, out, s);
 }
 
 bool pf_attention(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint32_t S, uint32_t p0, __half *out,
@@ -1137,17 +1165,17 @@ bool pf_attention(const __half *rq, const LayerW &lw, const DecodeDims &dd, uint
     switch (dd.hd)
     {
     case 32:
-        return pf_attention_launch<32>(rq, lw, dd, S, p0, out, s);
+        return pf_attention_hd<32>(rq, lw, dd, S, p0, out, s);
     case 48:
-        return pf_attention_launch<48>(rq, lw, dd, S, p0, out, s);
+        return pf_attention_hd<48>(rq, lw, dd, S, p0, out, s);
     case 64:
-        return pf_attention_launch<64>(rq, lw, dd, S, p0, out, s);
+        return pf_attention_hd<64>(rq, lw, dd, S, p0, out, s);
     case 80:
-        return pf_attention_launch<80>(rq, lw, dd, S, p0, out, s);
+        return pf_attention_hd<80>(rq, lw, dd, S, p0, out, s);
     case 96:
-        return pf_attention_launch<96>(rq, lw, dd, S, p0, out, s);
+        return pf_attention_hd<96>(rq, lw, dd, S, p0, out, s);
     case 128:
-        return pf_attention_launch<128>(rq, lw, dd, S, p0, out, s);
+        return pf_attention_hd<128>(rq, lw, dd, S, p0, out, s);
     default:
         return false;
     }

@@ -247,6 +247,29 @@ __device__ __forceinline__ void pf_scores(const uint32_t (&qa)[HD / 16][4], cons
             s[nt][e] = pf_round16(s[nt][e] * scale);
 }
 
+// Cluster helpers of the CTA-pair form of k_pf_attention: this CTA's rank in its cluster, a barrier
+// over the cluster (release / acquire), and a float load from the peer CTA's shared memory.
+__device__ __forceinline__ uint32_t pf_cluster_rank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void pf_cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float pf_peer_ld(const float *local, uint32_t peer)
+{
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(pf_smem(local)), "r"(peer));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
 // Attention of one head over keys 0 .. Lk - 1 (Lk = p0 + S) for query rows q0 .. q0 + 63 of the S new
 // tokens, in two passes over the cache: (1) scores of every key block to get each row's max over
 // all Lk entries (masked ones included, as the reference shader) and its sum of exp(s - max) over
@@ -254,7 +277,11 @@ __device__ __forceinline__ void pf_scores(const uint32_t (&qa)[HD / 16][4], cons
 // where masked), and p . V summed in fp32; the result rounded to fp16 into out[s][h * HD + d].
 // When Lk == HD the reference's shape-only predicate reads the V slice as [HD, Lk]
 // (src/core/vkllm_op_matmul.c:14-30): the product is then out[i][w] = sum_j p_ij V[w][j].
-template <int HD>
+// PAIR: a cluster of two CTAs shares the query tile, CTA r taking the key blocks b with b % 2 == r in
+// both passes; they combine their row statistics (max, then the sums rescaled to it) and then their
+// fp32 partial outputs through distributed shared memory, and CTA 0 stores the rows. Twice the CTAs
+// (and half the serial key blocks per CTA) for the same work; only fp32 summation orders change.
+template <int HD, bool PAIR>
 __global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(const __half *__restrict__ rq, const __half *__restrict__ kc,
                                                              const __half *__restrict__ vc, uint32_t ctx, uint32_t S,
                                                              uint32_t p0, uint32_t H, float scale,
@@ -262,11 +289,14 @@ __global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(
 {
     using SM = PfSmem<HD>;
     constexpr int LD = SM::LD, LDT = SM::LDT;
+    constexpr uint32_t step = PAIR ? 2u : 1u;
     extern __shared__ __align__(16) unsigned char pf_sm[];
+    __shared__ float st_m[kPfBQ], st_l[kPfBQ]; // PAIR: this CTA's row statistics for the peer
     __half *sq = reinterpret_cast<__half *>(pf_sm);
     // key buffer b at sk0 + b * kK; value buffer 0 at sv0, value buffer 1 where the Q tile was
     __half *const sk0 = sq + SM::kQV, *const sv0 = sq + SM::kQV + 2 * SM::kK;
-    const uint32_t h = blockIdx.y, q0 = blockIdx.x * kPfBQ;
+    const uint32_t r = PAIR ? pf_cluster_rank() : 0u;
+    const uint32_t h = blockIdx.y, q0 = (PAIR ? blockIdx.x >> 1 : blockIdx.x) * kPfBQ;
     const uint32_t Lk = p0 + S;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const bool q1 = Lk == (uint32_t)HD;
@@ -285,25 +315,30 @@ __global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(
     const uint32_t i0 = q0 + 16 * warp + g, i1 = i0 + 8;
     float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
     const uint32_t nkb = (Lk + kPfBK - 1) / kPfBK;
+    // this CTA's key blocks: r, r + step, ...
+    const uint32_t nb1 = nkb > r ? (nkb - r + step - 1) / step : 0u;
     float s[kPfBK / 8][4];
 
     // ---- pass 1: row max over every key, row sum over the unmasked keys (rescaled online). Key
-    // tiles are double-buffered: block kb + 1 is in flight while block kb is scored.
-    pf_async_rows<HD, LD>(sk0, kb, HD, 0, kPfBK, Lk);
-    pf_cp_commit();
-    for (uint32_t kb_i = 0; kb_i < nkb; ++kb_i)
+    // tiles are double-buffered: the next block is in flight while one is scored.
+    if (nb1 > 0)
     {
-        const uint32_t j0 = kb_i * kPfBK;
-        if (kb_i + 1 < nkb)
+        pf_async_rows<HD, LD>(sk0, kb, HD, r * kPfBK, kPfBK, Lk);
+        pf_cp_commit();
+    }
+    for (uint32_t it = 0; it < nb1; ++it)
+    {
+        const uint32_t j0 = (r + it * step) * kPfBK;
+        if (it + 1 < nb1)
         {
-            pf_async_rows<HD, LD>(sk0 + ((kb_i + 1) & 1) * SM::kK, kb, HD, j0 + kPfBK, kPfBK, Lk);
+            pf_async_rows<HD, LD>(sk0 + ((it + 1) & 1) * SM::kK, kb, HD, j0 + step * kPfBK, kPfBK, Lk);
             pf_cp_commit();
             pf_cp_wait<1>();
         }
         else
             pf_cp_wait<0>();
         __syncthreads();
-        pf_scores<HD, LD>(qa, sk0 + (kb_i & 1) * SM::kK, scale, s);
+        pf_scores<HD, LD>(qa, sk0 + (it & 1) * SM::kK, scale, s);
         float bm0 = -FLT_MAX, bm1 = -FLT_MAX;
 #pragma unroll
         for (int nt = 0; nt < kPfBK / 8; ++nt)
@@ -349,36 +384,60 @@ __global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(
         __syncthreads(); // every warp is done with this buffer before it is refilled
     }
 
-    // ---- pass 2: probabilities and p . V over the key blocks that hold an unmasked key
+    if constexpr (PAIR)
+    {
+        // the pair's row statistics: max of the two, sums rescaled to it (the same bits in both CTAs:
+        // fp32 addition commutes)
+        if (c == 0)
+        {
+            st_m[16 * warp + g] = m0;
+            st_l[16 * warp + g] = l0;
+            st_m[16 * warp + g + 8] = m1;
+            st_l[16 * warp + g + 8] = l1;
+        }
+        pf_cluster_sync();
+        const float pm0 = pf_peer_ld(&st_m[16 * warp + g], r ^ 1u), pl0 = pf_peer_ld(&st_l[16 * warp + g], r ^ 1u);
+        const float pm1 = pf_peer_ld(&st_m[16 * warp + g + 8], r ^ 1u),
+                    pl1 = pf_peer_ld(&st_l[16 * warp + g + 8], r ^ 1u);
+        const float M0 = fmaxf(m0, pm0), M1 = fmaxf(m1, pm1);
+        l0 = l0 * expf(m0 - M0) + pl0 * expf(pm0 - M0);
+        l1 = l1 * expf(m1 - M1) + pl1 * expf(pm1 - M1);
+        m0 = M0;
+        m1 = M1;
+    }
+
+    // ---- pass 2: probabilities and p . V over this CTA's key blocks that hold an unmasked key
     float o[HD / 8][4];
 #pragma unroll
     for (int nt = 0; nt < HD / 8; ++nt)
         o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
     const uint32_t last_row = min(q0 + kPfBQ, S) - 1;
     const uint32_t nkb2 = min(nkb, (p0 + last_row) / kPfBK + 1);
-    // K and V tiles of block kb + 1 are in flight while block kb is used
-    auto issue_kv = [&](uint32_t blk) {
+    const uint32_t nb2 = nkb2 > r ? (nkb2 - r + step - 1) / step : 0u;
+    // K and V tiles of the next block are in flight while one is used (buffer = iteration parity)
+    auto issue_kv = [&](uint32_t blk, uint32_t buf) {
         const uint32_t jb = blk * kPfBK;
-        pf_async_rows<HD, LD>(sk0 + (blk & 1) * SM::kK, kb, HD, jb, kPfBK, Lk);
+        pf_async_rows<HD, LD>(sk0 + buf * SM::kK, kb, HD, jb, kPfBK, Lk);
         if (!q1)
-            pf_async_rows<HD, LD>(((blk & 1) ? sq : sv0), vb, HD, jb, kPfBK, Lk);
+            pf_async_rows<HD, LD>((buf ? sq : sv0), vb, HD, jb, kPfBK, Lk);
         else
-            pf_async_vt<HD, LDT>(((blk & 1) ? sq : sv0), vb, jb);
+            pf_async_vt<HD, LDT>((buf ? sq : sv0), vb, jb);
         pf_cp_commit();
     };
-    issue_kv(0);
-    for (uint32_t kb_i = 0; kb_i < nkb2; ++kb_i)
+    if (nb2 > 0)
+        issue_kv(r, 0);
+    for (uint32_t it = 0; it < nb2; ++it)
     {
-        const uint32_t j0 = kb_i * kPfBK;
-        if (kb_i + 1 < nkb2)
+        const uint32_t j0 = (r + it * step) * kPfBK;
+        if (it + 1 < nb2)
         {
-            issue_kv(kb_i + 1);
+            issue_kv(r + (it + 1) * step, (it + 1) & 1);
             pf_cp_wait<1>();
         }
         else
             pf_cp_wait<0>();
         __syncthreads();
-        const __half *sk = sk0 + (kb_i & 1) * SM::kK, *sv = ((kb_i & 1) ? sq : sv0);
+        const __half *sk = sk0 + (it & 1) * SM::kK, *sv = ((it & 1) ? sq : sv0);
         pf_scores<HD, LD>(qa, sk, scale, s);
         // p = fp16(exp(s - max) / sum) where unmasked, else 0 (the softmax node)
 #pragma unroll
@@ -420,6 +479,41 @@ __global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(
             }
         }
         __syncthreads(); // every warp is done with these buffers before they are refilled
+    }
+    if constexpr (PAIR)
+    {
+        // CTA 1 publishes its fp32 partial rows (in the K buffers, free after the loop's last barrier);
+        // CTA 0 adds them to its own and stores; the last barrier keeps CTA 1's shared memory alive
+        // until CTA 0 has read it
+        float *so = reinterpret_cast<float *>(sk0); // [64][HD]
+        if (r == 1)
+        {
+#pragma unroll
+            for (int nt = 0; nt < HD / 8; ++nt)
+            {
+                const uint32_t d = nt * 8 + 2 * c;
+                so[(16 * warp + g) * HD + d] = o[nt][0];
+                so[(16 * warp + g) * HD + d + 1] = o[nt][1];
+                so[(16 * warp + g + 8) * HD + d] = o[nt][2];
+                so[(16 * warp + g + 8) * HD + d + 1] = o[nt][3];
+            }
+        }
+        pf_cluster_sync();
+        if (r == 0)
+        {
+#pragma unroll
+            for (int nt = 0; nt < HD / 8; ++nt)
+            {
+                const uint32_t d = nt * 8 + 2 * c;
+                o[nt][0] += pf_peer_ld(&so[(16 * warp + g) * HD + d], 1);
+                o[nt][1] += pf_peer_ld(&so[(16 * warp + g) * HD + d + 1], 1);
+                o[nt][2] += pf_peer_ld(&so[(16 * warp + g + 8) * HD + d], 1);
+                o[nt][3] += pf_peer_ld(&so[(16 * warp + g + 8) * HD + d + 1], 1);
+            }
+        }
+        pf_cluster_sync();
+        if (r != 0)
+            return;
     }
     // ---- store: out[i][h * HD + d] = fp16(o)
     const uint64_t row_pitch = (uint64_t)H * HD;
