@@ -296,7 +296,10 @@ __global__ void __launch_bounds__(kPfThreads, HD == 128 ? 3 : 2) k_pf_attention(
     // key buffer b at sk0 + b * kK; value buffer 0 at sv0, value buffer 1 where the Q tile was
     __half *const sk0 = sq + SM::kQV, *const sv0 = sq + SM::kQV + 2 * SM::kK;
     const uint32_t r = PAIR ? pf_cluster_rank() : 0u;
-    const uint32_t h = blockIdx.y, q0 = (PAIR ? blockIdx.x >> 1 : blockIdx.x) * kPfBQ;
+    // heaviest query tiles (most unmasked key blocks) first: with twice the CTAs the grid exceeds one
+    // wave, and the tail should hold the light ones
+    const uint32_t h = blockIdx.y,
+                   q0 = (PAIR ? (gridDim.x >> 1) - 1 - (blockIdx.x >> 1) : blockIdx.x) * kPfBQ;
     const uint32_t Lk = p0 + S;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const bool q1 = Lk == (uint32_t)HD;
