@@ -105,3 +105,40 @@ def test_noalloc_attention_rejects_misaligned_caches(vk, ctx):
     assert lib.vkllm_b200_attention_decode_noalloc(ok, ok, odd2, 8, 128, 64, 4, 1.0, ok, None) == vk.ARGS
     assert lib.vkllm_b200_attention_decode_noalloc(odd1, ok, ok, 8, 128, 64, 4, 1.0, ok, None) == vk.ARGS
     assert lib.vkllm_b200_attention_decode_noalloc(ok, ok, ok, 8, 128, 64, 4, 1.0, odd1, None) == vk.ARGS
+
+
+def test_noalloc_attention_under_stream_capture(vk, ctx):
+    """The use the entry point exists for: recorded into a CUDA graph by stream capture (where a device
+    allocation is an error that invalidates the capture) and replayed. After one eager call (which
+    resolves the scratch array's address), the captured call records without error, and its replays
+    give the eager call's bits."""
+    import torch
+
+    lib = vk.lib()
+    H, hd, rows, n = 8, 128, 512, 300
+    g = torch.Generator(device="cuda").manual_seed(7)
+    q = (torch.rand((H, hd), generator=g, device="cuda") * 2 - 1).half()
+    kc = (torch.rand((H, rows, hd), generator=g, device="cuda") * 2 - 1).half()
+    vc = (torch.rand((H, rows, hd), generator=g, device="cuda") * 2 - 1).half()
+    out_eager = torch.zeros((H, hd), device="cuda", dtype=torch.float16)
+    out_graph = torch.full((H, hd), float("nan"), device="cuda", dtype=torch.float16)
+    scale = 1.0 / np.sqrt(hd)
+    s = torch.cuda.Stream()
+
+    def call(out):
+        return lib.vkllm_b200_attention_decode_noalloc(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), H, hd, rows, n,
+                                                       scale, out.data_ptr(), C.c_void_p(s.cuda_stream))
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        assert call(out_eager) == vk.OK
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        err = call(out_graph)
+    assert err == vk.OK
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out_graph, out_eager)
+    del graph
