@@ -132,7 +132,7 @@ struct PersistParams
     // rows and V / N vocabulary rows (from v0); the Wo and down outputs are partial sums that every
     // rank writes, per output row, into every peer's receive area, then raises a flag per CTA.
     uint32_t tp_size, tp_rank, v0, Vg;
-    float *tp_x[kTpMax];          // rank q's receive area [2 sites][N ranks][kTpCtas][kTpRows] fp32
+    uint64_t *tp_x[kTpMax];       // rank q's receive slots [2 sites][N ranks][kTpCtas][kTpRows]: epoch, fp32
     uint32_t *tp_flag[kTpMax];    // rank q's flags [3 sites][kTpCtas][N ranks]
     float *tp_amv[kTpMax];        // rank q's argmax class slots [N ranks][32]
     uint32_t *tp_ami[kTpMax];
@@ -229,6 +229,20 @@ __device__ __forceinline__ void st_relaxed_sys_u32(uint32_t *p, uint32_t v)
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// 8-byte slots of the tensor-parallel exchange: (epoch << 32) | fp32 bits, written and read as one
+// aligned 64-bit access, so a reader that sees the epoch sees the value with it.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t *p, uint64_t v)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *p)
+{
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 struct UnitRange
 {
     uint32_t u0, count;
@@ -247,66 +261,62 @@ __device__ __forceinline__ UnitRange cta_units(uint32_t kind)
 __shared__ __align__(16) float s_tp_stage[kTpRows];
 
 // Tensor-parallel allreduce of this CTA's output rows of the Wo (site 0) or down (site 1) phase:
-// the CTA's staged row partials go to the same CTA slot of every rank's receive area as one
-// contiguous block of 16-byte stores (NVLink carries full-width writes instead of 4-byte ones); then
-// thread 0 publishes a flag to the same CTA index of every rank and waits (bounded) for theirs; then
-// each row is summed over the ranks in rank order (fp32), rounded to fp16 (the projection node) and
-// added to the residual: x = fp16(x + fp16(sum)). Returns false on a timed-out wait or a reported
-// error.
+// each staged row partial goes to the same CTA slot of every rank as one 8-byte store carrying the
+// exchange's epoch with the value (no fence and no separate flag: a slot showing the epoch holds
+// the value). Then each row waits (bounded) for every rank's slot to show the epoch, sums the
+// partials in rank order (fp32, so every rank computes the same bits), rounds to fp16 (the
+// projection node) and adds the residual: x = fp16(x + fp16(sum)). A slot is rewritten only after
+// its reader has used it: the writer's next exchange at this site needs the reader's contribution
+// to the exchange in between. Returns false on a timed-out wait or a reported error.
 __device__ __forceinline__ bool tp_allreduce_rows(const PersistParams &P, uint32_t site, uint32_t epoch)
 {
-    __shared__ uint32_t ok_s;
-    __syncthreads();
+    __syncthreads(); // the staged rows are complete
+    const UnitRange r = cta_units(site == 0 ? PK_WO : PK_DOWN);
     {
-        const uint32_t n4 = (cta_units(site == 0 ? PK_WO : PK_DOWN).count + 3) / 4;
         const uint64_t blk = (((uint64_t)site * P.tp_size + P.tp_rank) * kTpCtas + blockIdx.x) * kTpRows;
-        for (uint32_t t = threadIdx.x; t < n4 * P.tp_size; t += blockDim.x)
+        const uint64_t tag = (uint64_t)epoch << 32;
+        for (uint32_t t = threadIdx.x; t < r.count * P.tp_size; t += blockDim.x)
         {
-            const uint32_t q = t / n4, i = t % n4;
-            reinterpret_cast<float4 *>(P.tp_x[q] + blk)[i] = reinterpret_cast<const float4 *>(s_tp_stage)[i];
+            const uint32_t q = t / r.count, i = t % r.count;
+            st_relaxed_sys_u64(P.tp_x[q] + blk + i, tag | __float_as_uint(s_tp_stage[i]));
         }
     }
-    __syncthreads();
-    if (threadIdx.x == 0)
+    bool ok = true;
+    const uint64_t *rx = P.tp_x[P.tp_rank] + ((uint64_t)site * P.tp_size * kTpCtas + blockIdx.x) * kTpRows;
+    for (uint32_t i = threadIdx.x; i < r.count && ok; i += blockDim.x)
     {
-        __threadfence_system(); // this CTA's partial stores to the peers precede the flags
-        const uint32_t slot = (site * kTpCtas + blockIdx.x) * kTpMax + P.tp_rank;
-        for (uint32_t q = 0; q < P.tp_size; ++q)
-            st_relaxed_sys_u32(P.tp_flag[q] + slot, epoch);
-        bool ok = true;
-        const uint32_t *mine = P.tp_flag[P.tp_rank] + (site * kTpCtas + blockIdx.x) * kTpMax;
-        const uint64_t t0 = global_ns();
+        float t = 0.f;
         for (uint32_t q = 0; q < P.tp_size && ok; ++q)
-            while (ld_acquire_sys_u32(mine + q) < epoch)
+        {
+            const uint64_t *slot = rx + (uint64_t)q * kTpCtas * kTpRows + i;
+            uint64_t v = ld_relaxed_sys_u64(slot);
+            if ((uint32_t)(v >> 32) != epoch)
             {
-                if (ld_acquire_u32(P.err) != 0)
+                const uint64_t t0 = global_ns();
+                while ((uint32_t)((v = ld_relaxed_sys_u64(slot)) >> 32) != epoch)
                 {
-                    ok = false;
-                    break;
-                }
-                if (global_ns() - t0 > kWaitLimitNs)
-                {
-                    atomicOr(P.err, kErrPeerTimeout);
-                    ok = false;
-                    break;
+                    if (ld_acquire_u32(P.err) != 0)
+                    {
+                        ok = false;
+                        break;
+                    }
+                    if (global_ns() - t0 > kWaitLimitNs)
+                    {
+                        atomicOr(P.err, kErrPeerTimeout);
+                        ok = false;
+                        break;
+                    }
                 }
             }
-        ok_s = ok ? 1u : 0u;
+            t += __uint_as_float((uint32_t)v);
+        }
+        if (ok)
+        {
+            const uint32_t u = r.u0 + i;
+            P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(t));
+        }
     }
-    __syncthreads();
-    if (!ok_s)
-        return false;
-    const UnitRange r = cta_units(site == 0 ? PK_WO : PK_DOWN);
-    const float *rx = P.tp_x[P.tp_rank] + ((uint64_t)site * P.tp_size * kTpCtas + blockIdx.x) * kTpRows;
-    for (uint32_t i = threadIdx.x; i < r.count; i += blockDim.x)
-    {
-        const uint32_t u = r.u0 + i;
-        float t = 0.f;
-        for (uint32_t q = 0; q < P.tp_size; ++q)
-            t += __ldcg(rx + (uint64_t)q * kTpCtas * kTpRows + i);
-        P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(t));
-    }
-    return true;
+    return __syncthreads_and(ok) != 0;
 }
 
 // Producer cursor of one warp over its chunk sequence (step, layer, kind, k).

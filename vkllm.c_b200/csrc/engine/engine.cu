@@ -95,7 +95,7 @@ inline TpLayout tp_layout(uint32_t world, uint32_t D)
     TpLayout t;
     t.x = 0;
     (void)D;
-    t.flag = t.x + al((size_t)2 * world * kTpCtas * kTpRows * 4);
+    t.flag = t.x + al((size_t)2 * world * kTpCtas * kTpRows * 8); // 8-byte (epoch, value) slots
     t.amv = t.flag + al((size_t)3 * kTpCtas * kTpMax * 4);
     t.ami = t.amv + al((size_t)kTpMax * 32 * 4);
     t.total = t.ami + al((size_t)kTpMax * 32 * 4);
@@ -990,7 +990,7 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
         for (uint32_t q = 0; q < c->world; ++q)
         {
             char *b = (char *)c->peer[q];
-            e->pp.tp_x[q] = (float *)(b + t.x);
+            e->pp.tp_x[q] = (uint64_t *)(b + t.x);
             e->pp.tp_flag[q] = (uint32_t *)(b + t.flag);
             e->pp.tp_amv[q] = (float *)(b + t.amv);
             e->pp.tp_ami[q] = (uint32_t *)(b + t.ami);
