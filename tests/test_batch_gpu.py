@@ -21,10 +21,11 @@ N_STEPS = 32
 
 # the batch's kernel choices (read when the batch is created): the default (bulk-copy staged
 # attention, tile-order GEMM operands), the register-loading attention kernel, the staged kernel
-# with 128 threads, row-major GEMM operands, and GEMM tiles that load 64 rows of A per stage
+# with 128 threads, row-major GEMM operands, and GEMM tiles that stage all 128 rows of A (up to 32
+# sequences the default tiles stage 64)
 VARIANTS = {"default": {}, "att_registers": {"VKLLM_B200_BATCH_ATT_STAGED": "0"},
             "att_staged_128": {"VKLLM_B200_BATCH_ATT_STAGED": "128"}, "rowmajor_b": {"VKLLM_B200_BATCH_TILED": "0"},
-            "a64_tiles": {"VKLLM_B200_BATCH_GEMM": "3,3,4,3,3,2"}}
+            "full_a_tiles": {"VKLLM_B200_BATCH_GEMM": "3,3,4,1,1,0"}}
 
 
 @pytest.mark.parametrize("variant", list(VARIANTS))
