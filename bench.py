@@ -784,7 +784,10 @@ def run_ours(args, world, rank, local):
         if result is not None:
             result["tp13b"] = tp
         if world > 1:  # the NCCL exchange on the same shards, for comparison
-            tp = tp13b_leg(vk, ctx, args, world, rank, stream, "nccl")
+            try:
+                tp = tp13b_leg(vk, ctx, args, world, rank, stream, "nccl")
+            except Exception as e:  # the comparison arm must not void the line
+                tp = {"error": str(e)[:200]}
             if result is not None:
                 result["tp13b_nccl"] = tp
     ctx.close()
