@@ -21,7 +21,7 @@ N_STEPS = 32
 
 # the batch's kernel choices (read when the batch is created): the default (bulk-copy staged
 # attention, tile-order GEMM operands), the register-loading attention kernel, the staged kernel
-# with 128 threads, row-major GEMM operands, and GEMM tiles that stage all 128 rows of A (up to 32
+# with 128 threads, row-major GEMM operands, and GEMM tiles that stage all 128 rows of A (up to 8
 # sequences the default tiles stage 64)
 VARIANTS = {"default": {}, "att_registers": {"VKLLM_B200_BATCH_ATT_STAGED": "0"},
             "att_staged_128": {"VKLLM_B200_BATCH_ATT_STAGED": "128"}, "rowmajor_b": {"VKLLM_B200_BATCH_TILED": "0"},

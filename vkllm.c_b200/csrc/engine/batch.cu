@@ -1086,10 +1086,10 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0: 128 x 128, 1: 128 x 256;
     // 2, 3: the same loading 64 rows of A per stage, for up to 64 sequences) of the QKV, up/gate
     // and Wo / down GEMMs (defaults 3,3,4,1,1,0; 7B, 64 sequences: 2,3,4 / 3,3,4 / 4,3,4 / 3,2,4 splits
-    // 4.966 / 4.936 / 5.223 / 5.108 ms per step). Up to 32 sequences the tiles that stage 64 rows of A
-    // keep one more weight stage in flight: 8 sequences 3.52 against 3.74 ms per step (64: 4.93
-    // against 4.87, so not there).
-    if (B <= 32)
+    // 4.966 / 4.936 / 5.223 / 5.108 ms per step). Up to 8 sequences the tiles that stage 64 rows of A
+    // keep one more weight stage in flight: 8 sequences 3.52 against 3.74 ms per step (16: 3.66
+    // against 3.63, 64: 4.93 against 4.87, so not there).
+    if (B <= 8)
         bt->qkv_tile = 3, bt->ug_tile = 3, bt->proj_tile = 2;
     if (const char *ge = getenv("VKLLM_B200_BATCH_GEMM"))
     {
