@@ -100,6 +100,58 @@ __global__ void k_gemv(const T *a, Desc4 da, const T *w, Desc4 dw, T *out, Desc4
     }
 }
 
+// k_gemv for one input row (A [1, 1, 1, K], W rows contiguous, every output in one row): the row is
+// staged once per block in shared memory, and each lane keeps 16 weight chunks of 16 bytes in flight
+// instead of 8, so a 4096-wide row is one round trip to HBM. Each lane adds its chunks in the same
+// order as k_gemv (i, i + 32, ...), then the same warp sum: the same bits.
+constexpr uint32_t kGemvWideMaxK = 16384; // halves of the staged input row (32 KB)
+
+// ldg_stream without `volatile`, so that the compiler may issue a whole group of these loads before
+// the arithmetic that uses the first (a volatile load orders after the preceding dot products).
+__device__ __forceinline__ uint4 ldg_stream_sched(const void *p)
+{
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+
+__global__ void __launch_bounds__(256) k_gemv_row(const __half *__restrict__ a, const __half *__restrict__ w,
+                                                  uint64_t ldw, __half *__restrict__ out, uint32_t N, uint32_t K,
+                                                  float scale, int act)
+{
+    __shared__ __align__(16) uint4 xs[kGemvWideMaxK / 8];
+    const uint32_t nchunk = K / 8, lane = threadIdx.x & 31;
+    for (uint32_t i = threadIdx.x; i < nchunk; i += blockDim.x)
+        xs[i] = reinterpret_cast<const uint4 *>(a)[i];
+    __syncthreads();
+    const uint32_t warps = (gridDim.x * blockDim.x) >> 5;
+    for (uint32_t n = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; n < N; n += warps)
+    {
+        const uint4 *wp = reinterpret_cast<const uint4 *>(w + (uint64_t)n * ldw);
+        float acc = 0.f;
+        uint32_t i = lane;
+        for (; i + 32 * 15 < nchunk; i += 32 * 16)
+        {
+            uint4 wv[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                wv[u] = ldg_stream_sched(wp + i + 32 * u);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+                acc = dot8_f16(xs[i + 32 * u], wv[u], acc);
+        }
+        for (; i < nchunk; i += 32)
+            acc = dot8_f16(xs[i], ldg_stream_sched(wp + i), acc);
+        acc = warp_sum(acc) * scale;
+        if (act == 1)
+            acc = silu_f32(acc);
+        if (lane == 0)
+            out[n] = __float2half_rn(acc);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------
 // CUDA-core GEMM for any strides / broadcast / layout (src/shaders/vkllm_matmul_t0.comp,
 // vkllm_matmul_t1.comp): 64x64 output tile per 256-thread block, 4x4 per thread, fp32 accumulation.
@@ -343,7 +395,25 @@ extern "C" vkllm_err_t vkllm_op_matmul_run(vkllm_context *context, vkllm_command
         bool vec_ok = f16 && da.stride[3] == 1 && db.stride[3] == 1 && da.shape[3] % 8 == 0 &&
                       da.stride[1] % 8 == 0 && da.stride[2] % 8 == 0 && db.stride[1] % 8 == 0 &&
                       db.stride[2] % 8 == 0 && ((uintptr_t)a & 15) == 0 && ((uintptr_t)b & 15) == 0;
-        if (f16 && vec_ok)
+        const bool one_row = n_out == dc.shape[3] && dc.stride[3] == 1 && da.shape[3] <= kGemvWideMaxK;
+        if (f16 && vec_ok && one_row)
+        {
+            static int per_sm[64] = {};
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (dev >= 0 && dev < 64 && per_sm[dev] == 0 &&
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], k_gemv_row, 256, 0) != cudaSuccess)
+            {
+                (void)cudaGetLastError();
+                per_sm[dev] = 1;
+            }
+            const uint64_t rows_grid = (n_out + 7) / 8;
+            const uint64_t resident = (uint64_t)context->device->sm_count * (uint64_t)(per_sm[dev] > 0 ? per_sm[dev] : 1);
+            k_gemv_row<<<(unsigned)(rows_grid < resident ? rows_grid : resident), 256, 0, s>>>(
+                (const __half *)a, (const __half *)b, db.stride[2], (__half *)c, dc.shape[3], da.shape[3], p->scale,
+                p->act);
+        }
+        else if (f16 && vec_ok)
             k_gemv<__half, true><<<grid, 256, 0, s>>>((const __half *)a, da, (const __half *)b, db, (__half *)c, dc,
                                                        p->scale, p->act);
         else if (f16)
