@@ -57,6 +57,9 @@ def lib():
             "oracle_op_embedding": (C.c_int, [V, V, V, C.c_uint32, C.c_int]),
             "oracle_op_arg_max": (C.c_int, [V, C.c_void_p, C.POINTER(C.c_uint32)]),
             "oracle_op_ffn_up_gate": (C.c_int, [V, V, V, V]),
+            "oracle_round16": (None, [C.c_void_p, C.c_void_p, C.c_uint64]),
+            "oracle_f32_to_f16": (None, [C.c_void_p, C.c_void_p, C.c_uint64]),
+            "oracle_f16_to_f32": (None, [C.c_void_p, C.c_void_p, C.c_uint64]),
             "oracle_random_f16": (None, [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, C.c_uint64, C.c_void_p]),
             "oracle_llama2_new": (C.c_void_p, [C.POINTER(_Cfg), C.c_void_p, C.c_void_p, C.c_void_p,
                                                C.POINTER(C.c_void_p)]),
@@ -158,6 +161,22 @@ def arg_max(x):
 def ffn_up_gate(x, wu, wg, out_dtype):
     out = np.zeros(x.shape[:3] + (wu.shape[2],), dtype=out_dtype)
     lib().oracle_op_ffn_up_gate(C.byref(_view(x)), C.byref(_view(wu)), C.byref(_view(wg)), C.byref(_view(out)))
+    return out
+
+
+def round16(x):
+    """One fp16 rounding of each fp32 value, as the fp16 arithmetic mode applies it after every op."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().oracle_round16(x.ctypes.data, out.ctypes.data, x.size)
+    return out
+
+
+def f32_to_f16_bits(x):
+    """The oracle's software fp32 -> fp16 conversion (storage rounding), as raw bits."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().oracle_f32_to_f16(x.ctypes.data, out.ctypes.data, x.size)
     return out
 
 

@@ -35,6 +35,8 @@
 #include <memory>
 #include <vector>
 
+#include <immintrin.h>
+
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -110,9 +112,17 @@ inline uint16_t f2h(float f)
     return (uint16_t)h;
 }
 
+// One fp16 rounding of an fp32 value (the value of f2h followed by h2f): the F16C conversion, which
+// is IEEE round-to-nearest-even with fp16 subnormals and overflow to infinity, part of the x86-64-v3
+// baseline this library is built for. round16x8 rounds eight lanes the same way.
 inline float round16(float f)
 {
-    return h2f(f2h(f));
+    return _cvtsh_ss(_cvtss_sh(f, _MM_FROUND_TO_NEAREST_INT));
+}
+
+inline __m256 round16x8(__m256 v)
+{
+    return _mm256_cvtph_ps(_mm256_cvtps_ph(v, _MM_FROUND_TO_NEAREST_INT));
 }
 
 int g_arith16 = 0; // 1: the shaderFloat16 variants (oracle_set_arith)
@@ -261,7 +271,8 @@ void gemv(const View &a, const View &w, const View &out, float scale, int act)
 // an odd K padded by a zero pair. The loops below compute 8-32 columns of a row at once (a panel of
 // B converted to fp32 and laid out k-major per block of columns), which the compiler vectorises
 // across columns; each column still sees exactly that sequence of operations.
-constexpr uint32_t kGemmNB = 32; // columns per panel
+constexpr uint32_t kGemmNB = 32; // columns per panel (a multiple of the 8 lanes of round16x8)
+static_assert(kGemmNB % 8 == 0, "panel width");
 constexpr uint32_t kGemmMB = 4;  // rows per register block
 
 void gemm(const View &a, const View &bm, const View &out, bool trans_b, float scale, int act)
@@ -314,8 +325,13 @@ void gemm(const View &a, const View &bm, const View &out, bool trans_b, float sc
                         const float a0 = r < mm ? A[(size_t)(m0 + r) * Kp + k] : 0.f;
                         const float a1 = r < mm ? A[(size_t)(m0 + r) * Kp + k + 1] : 0.f;
                         if (g_arith16) // f16f16f16: float(dot(f16vec2, f16vec2)), the dot in fp16
-                            for (uint32_t j = 0; j < kGemmNB; ++j)
-                                acc[r][j] += round16(round16(a0 * b0[j]) + round16(a1 * b1[j]));
+                            for (uint32_t j = 0; j < kGemmNB; j += 8)
+                            {
+                                const __m256 p0 = round16x8(_mm256_mul_ps(_mm256_set1_ps(a0), _mm256_loadu_ps(b0 + j)));
+                                const __m256 p1 = round16x8(_mm256_mul_ps(_mm256_set1_ps(a1), _mm256_loadu_ps(b1 + j)));
+                                _mm256_storeu_ps(&acc[r][j], _mm256_add_ps(_mm256_loadu_ps(&acc[r][j]),
+                                                                           round16x8(_mm256_add_ps(p0, p1))));
+                            }
                         else
                             for (uint32_t j = 0; j < kGemmNB; ++j)
                                 acc[r][j] += a0 * b0[j] + a1 * b1[j];
@@ -579,6 +595,13 @@ void oracle_f32_to_f16(const float *in, uint16_t *out, uint64_t n)
 {
     for (uint64_t i = 0; i < n; ++i)
         out[i] = f2h(in[i]);
+}
+
+// round16 over an array (lets a test compare the F16C rounding with f2h/h2f and with numpy).
+void oracle_round16(const float *in, float *out, uint64_t n)
+{
+    for (uint64_t i = 0; i < n; ++i)
+        out[i] = round16(in[i]);
 }
 
 void oracle_f16_to_f32(const uint16_t *in, float *out, uint64_t n)

@@ -143,3 +143,24 @@ def test_planted_error_is_caught(orc, g):
     got = orc.matmul(a, b, ref.shape, 1.0, 0).astype(np.float32) * np.float32(1.01)
     with pytest.raises(AssertionError):
         close(got, ref, 1e-2)
+
+
+def test_fp16_arithmetic_rounding_is_round_to_nearest_even(orc):
+    """The fp16 arithmetic mode rounds after every operation with the F16C conversion; the storage
+    conversion is the software f2h. Both must be IEEE round-to-nearest-even: compared with numpy's
+    float32 -> float16 cast on every fp32 value next to each fp16 number and halfway point (ties),
+    the subnormal range, the overflow edge, signed zeros, infinities and a random sweep."""
+    h = np.arange(0, 0x7C00, dtype=np.uint16).view(np.float16).astype(np.float32)  # every finite positive fp16
+    mids = ((h[:-1].astype(np.float64) + h[1:]) / 2).astype(np.float32)  # exact ties in fp32
+    near = np.concatenate([np.nextafter(v, np.float32(np.inf)) for v in (h, mids)] +
+                          [np.nextafter(v, np.float32(0)) for v in (h, mids)])
+    edge = np.array([65504, 65519.996, 65520, 65536, 1e30, np.inf, 0.0, 2.0 ** -25, 2.0 ** -25 * 1.0001,
+                     2.0 ** -24, 3 * 2.0 ** -26, 1e-40, 5.96e-8], dtype=np.float32)
+    rnd = np.random.default_rng(1).standard_normal(1 << 20).astype(np.float32) * np.float32(100)
+    x = np.concatenate([h, mids, near, edge, rnd])
+    x = np.concatenate([x, -x])
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16)
+    got = orc.round16(x)
+    np.testing.assert_array_equal(got.view(np.uint32), want.astype(np.float32).view(np.uint32))
+    np.testing.assert_array_equal(orc.f32_to_f16_bits(x), want.view(np.uint16))

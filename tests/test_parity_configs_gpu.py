@@ -47,6 +47,35 @@ def download_weights(vk, ctx, model, cfg):
     return w
 
 
+def oracle_with_bars(orc, cfg, weights, prompt, n_tokens, oracle_ctx):
+    """The oracle's greedy run in both arithmetic modes. Returns the fp32arith tokens and logits (the
+    parity target) and per-step max-abs / mean-abs bars: north_star's, widened to the fp16arith vs
+    fp32arith spread. The spread is measured at the steps whose inputs agree in both modes; a later
+    step (after the two modes' greedy tokens parted) takes the largest spread measured before it."""
+    ocfg = dict(D=cfg["embedding_length"], H=cfg["head_count"], F=cfg["ffn_length"], V=cfg["vocab_size"],
+                L=cfg["block_count"], ctx=oracle_ctx, eps=cfg["rms_eps"], rope_base=cfg["rope_freq_base"])
+    orc.threads(0)
+    runs = {}
+    for mode in ("fp16", "fp32"):
+        prev = orc.set_arith(mode)
+        try:
+            m = orc.Llama2(ocfg, weights, ctx=oracle_ctx)
+            runs[mode] = m.generate(list(prompt), n_tokens)
+            m.close()
+        finally:
+            orc.set_arith(prev)
+    ref_toks, ref_logits = runs["fp32"]
+    t16, l16 = runs["fp16"]
+    max_bar, mean_bar, seen_max, seen_mean = [], [], 2e-2, 2e-3
+    for i in range(n_tokens):
+        if t16[:i] == ref_toks[:i]:
+            spread = np.abs(l16[i].astype(np.float32) - ref_logits[i].astype(np.float32))
+            seen_max, seen_mean = max(seen_max, float(spread.max())), max(seen_mean, float(spread.mean()))
+        max_bar.append(seen_max)
+        mean_bar.append(seen_mean)
+    return ref_toks, ref_logits, max_bar, mean_bar
+
+
 def run_pair(vk, ctx, orc, cfg, seed, prompt_len, n_tokens, oracle_ctx):
     prompt = list(np.random.default_rng(seed).integers(3, cfg["vocab_size"], size=prompt_len, dtype=np.uint32))
     model = vk.Model(ctx).init_random(cfg, seed)
@@ -57,29 +86,7 @@ def run_pair(vk, ctx, orc, cfg, seed, prompt_len, n_tokens, oracle_ctx):
         weights = download_weights(vk, ctx, model, cfg)
     finally:
         model.free()
-    ocfg = dict(D=cfg["embedding_length"], H=cfg["head_count"], F=cfg["ffn_length"], V=cfg["vocab_size"],
-                L=cfg["block_count"], ctx=oracle_ctx, eps=cfg["rms_eps"], rope_base=cfg["rope_freq_base"])
-    orc.threads(0)
-    runs = {}
-    for mode in ("fp16", "fp32"):
-        prev = orc.set_arith(mode)
-        try:
-            m = orc.Llama2(ocfg, weights, ctx=oracle_ctx)
-            runs[mode] = m.generate(prompt, n_tokens)
-            m.close()
-        finally:
-            orc.set_arith(prev)
-    ref_toks, ref_logits = runs["fp32"]
-    t16, l16 = runs["fp16"]
-    # The reference-internal spread is measured at the steps whose inputs agree in both modes; a later
-    # step (after the two modes' greedy tokens parted) takes the largest spread measured before it.
-    max_bar, mean_bar, seen_max, seen_mean = [], [], 2e-2, 2e-3
-    for i in range(n_tokens):
-        if t16[:i] == ref_toks[:i]:
-            spread = np.abs(l16[i].astype(np.float32) - ref_logits[i].astype(np.float32))
-            seen_max, seen_mean = max(seen_max, float(spread.max())), max(seen_mean, float(spread.mean()))
-        max_bar.append(seen_max)
-        mean_bar.append(seen_mean)
+    ref_toks, ref_logits, max_bar, mean_bar = oracle_with_bars(orc, cfg, weights, prompt, n_tokens, oracle_ctx)
     return toks, logits, ref_toks, ref_logits, persistent, max_bar, mean_bar
 
 
@@ -106,3 +113,36 @@ def test_13b_geometry_decode_parity(vk, ctx, orc):
     toks, logits, ref_toks, ref_logits, persistent, mb, ab = run_pair(vk, ctx, orc, cfg, 33, 40, 5, 512)
     assert persistent
     compare_greedy(toks, logits, ref_toks, ref_logits, mb, ab, "13b geometry, 2 layers")
+
+
+def test_7b_geometry_batched_decode_at_bench_shape(vk, ctx, orc):
+    """The batched decode at the benchmark's own shape: 64 sequences in one batch,
+    each with its own 128-token prompt, KV rows for 384 positions, decoding positions 128..131 on two
+    layers of the 7B geometry. M = 64 selects the benchmark's GEMM tiles and K splits and the staged
+    attention at the same key counts. Eight slots spread over the batch (first, last and six between)
+    are checked against the oracle run on that sequence alone, with the per-step bars of the other
+    tests here (north_star's, widened to the reference-internal spread on that sequence)."""
+    cfg = dict(CFG_7B, block_count=2, context_length=512)
+    n_seqs, P, cap, n_steps = 64, 128, 384, 4
+    rng = np.random.default_rng(34)
+    prompts = [rng.integers(3, cfg["vocab_size"], size=P, dtype=np.uint32) for _ in range(n_seqs)]
+    model = vk.Model(ctx).init_random(cfg, 34)
+    batch = None
+    try:
+        batch = vk.Batch(model, n_seqs, cap)
+        firsts = [batch.add_prompt(i, p) for i, p in enumerate(prompts)]
+        toks, logits = [], []
+        for _ in range(n_steps):
+            toks.append(batch.decode(1)[0].copy())
+            logits.append(batch.logits().copy())
+        toks = np.stack(toks)
+        weights = download_weights(vk, ctx, model, cfg)
+    finally:
+        if batch is not None:
+            batch.free()
+        model.free()
+    for i in (0, 9, 18, 27, 36, 45, 54, 63):
+        ref_toks, ref_logits, mb, ab = oracle_with_bars(orc, cfg, weights, prompts[i], n_steps + 1, cap)
+        assert firsts[i] == ref_toks[0], f"sequence {i}: prefill token"
+        compare_greedy([int(t) for t in toks[:, i]], [logits[s][i] for s in range(n_steps)], ref_toks[1:],
+                       ref_logits[1:], mb[1:], ab[1:], f"batched 7b geometry, sequence {i}")
