@@ -38,3 +38,20 @@ def compare_greedy(toks, logits, ref_toks, ref_logits, max_bar, mean_bar, what="
             warnings.warn("greedy divergence at a reference tie: " + msg)
             return i + 1
     return n
+
+
+def download_weights(vk, ctx, model, cfg):
+    """A random-initialised model's weights as the oracle's GGUF-named numpy arrays."""
+    w = {}
+    m = model.m.weights
+    w["token_embd.weight"] = vk.fetch(ctx, m.tok_embed_weights).reshape(cfg["vocab_size"], -1)
+    w["output.weight"] = vk.fetch(ctx, m.output_weight).reshape(cfg["vocab_size"], -1)
+    w["output_norm.weight"] = vk.fetch(ctx, m.output_norm_weight).reshape(-1)
+    names = {"attn_norm_weight": "attn_norm", "ffn_norm_weight": "ffn_norm", "WQ": "attn_q", "WK": "attn_k",
+             "WV": "attn_v", "WO": "attn_output", "WG": "ffn_gate", "WU": "ffn_up", "WD": "ffn_down"}
+    for l in range(cfg["block_count"]):
+        bw = model.block(l)
+        for f, n in names.items():
+            a = vk.fetch(ctx, getattr(bw, f))
+            w[f"blk.{l}.{n}.weight"] = a.reshape(-1) if "norm" in n else a.reshape(a.shape[2], a.shape[3])
+    return w

@@ -111,3 +111,56 @@ def test_in_place_weights_match_tile_copies(vk, ctx, monkeypatch):
     assert f1 == f2
     assert np.array_equal(t1, t2)
     assert np.array_equal(l1.view(np.uint16), l2.view(np.uint16))
+
+
+# (head size, heads, prompt lengths): ragged key counts (tails of 1..15 rows past a 16-key block),
+# a one-token prompt, and one sequence that passes Lk == hd (quirk Q1) during the steps
+TC_MODELS = {64: (8, (1, 17, 40, 56, 9, 33)), 128: (4, (1, 17, 120, 70, 9, 100))}
+# chunk rows : ring buffers of the tensor-core attention (read when the batch is created)
+TC_CHUNKS = ["64:2", "16:4", "128:2", "48:3"]
+
+
+@pytest.mark.parametrize("chunk", TC_CHUNKS)
+@pytest.mark.parametrize("hd", sorted(TC_MODELS))
+def test_tensor_core_attention_matches_each_sequence_alone(vk, ctx, orc, hd, chunk, monkeypatch):
+    """k_b_attention_tc (mma.sync over TMA-swizzled K/V chunks) at head sizes 64 and 128 and several
+    chunk / ring shapes: every sequence of a batch of 6 decodes what the oracle decodes on it alone
+    (logits within north_star's bar at every step, greedy ids identical except at a reference tie).
+    Prompts of 1 to 120 tokens put the last key block's tail at every remainder; one sequence per
+    model crosses Lk == hd, where the kernel runs the reference's transposed-V reading."""
+    from parity import download_weights
+
+    c, r = chunk.split(":")
+    monkeypatch.setenv("VKLLM_B200_BATCH_ATT_CHUNK", c)
+    monkeypatch.setenv("VKLLM_B200_BATCH_ATT_RING", r)
+    H, lens = TC_MODELS[hd]
+    cfg = dict(block_count=2, context_length=256, embedding_length=H * hd, head_count=H, ffn_length=1280,
+               vocab_size=4096, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
+    rng = np.random.default_rng(hd)
+    prompts = [rng.integers(3, cfg["vocab_size"], size=n, dtype=np.uint32) for n in lens]
+    n_steps, cap = 24, 192
+    model = vk.Model(ctx).init_random(cfg, 40 + hd)
+    batch = None
+    try:
+        batch = vk.Batch(model, len(prompts), cap)
+        firsts = [batch.add_prompt(i, p) for i, p in enumerate(prompts)]
+        toks, logits = [], []
+        for _ in range(n_steps):
+            toks.append(batch.decode(1)[0].copy())
+            logits.append(batch.logits().copy())
+        toks = np.stack(toks)
+        weights = download_weights(vk, ctx, model, cfg)
+    finally:
+        if batch is not None:
+            batch.free()
+        model.free()
+    ocfg = dict(D=cfg["embedding_length"], H=H, F=cfg["ffn_length"], V=cfg["vocab_size"], L=cfg["block_count"],
+                ctx=cap, eps=cfg["rms_eps"], rope_base=cfg["rope_freq_base"])
+    orc.threads(0)
+    for i, p in enumerate(prompts):
+        m = orc.Llama2(ocfg, weights, ctx=cap)
+        ref_toks, ref_logits = m.generate(list(p), n_steps + 1)
+        m.close()
+        assert firsts[i] == ref_toks[0]
+        compare_greedy([int(t) for t in toks[:, i]], [logits[s][i] for s in range(n_steps)], ref_toks[1:],
+                       ref_logits[1:], 2e-2, 2e-3, f"hd {hd} chunk {chunk} sequence {i}")

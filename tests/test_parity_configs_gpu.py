@@ -21,7 +21,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from parity import compare_greedy
+from parity import compare_greedy, download_weights
 
 pytestmark = pytest.mark.gpu
 
@@ -29,22 +29,6 @@ CFG_7B = dict(block_count=32, context_length=4096, embedding_length=4096, head_c
               vocab_size=32000, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
 CFG_13B = dict(block_count=40, context_length=4096, embedding_length=5120, head_count=40, ffn_length=13824,
                vocab_size=32000, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)
-
-
-def download_weights(vk, ctx, model, cfg):
-    w = {}
-    m = model.m.weights
-    w["token_embd.weight"] = vk.fetch(ctx, m.tok_embed_weights).reshape(cfg["vocab_size"], -1)
-    w["output.weight"] = vk.fetch(ctx, m.output_weight).reshape(cfg["vocab_size"], -1)
-    w["output_norm.weight"] = vk.fetch(ctx, m.output_norm_weight).reshape(-1)
-    names = {"attn_norm_weight": "attn_norm", "ffn_norm_weight": "ffn_norm", "WQ": "attn_q", "WK": "attn_k",
-             "WV": "attn_v", "WO": "attn_output", "WG": "ffn_gate", "WU": "ffn_up", "WD": "ffn_down"}
-    for l in range(cfg["block_count"]):
-        bw = model.block(l)
-        for f, n in names.items():
-            a = vk.fetch(ctx, getattr(bw, f))
-            w[f"blk.{l}.{n}.weight"] = a.reshape(-1) if "norm" in n else a.reshape(a.shape[2], a.shape[3])
-    return w
 
 
 def oracle_with_bars(orc, cfg, weights, prompt, n_tokens, oracle_ctx):

@@ -58,6 +58,7 @@ struct vkllm_b200_batch
     uint32_t tiled = 1;                                                  // GEMM operands in tile order
     uint32_t att_staged = 256; // threads of k_b_attention_staged (0: k_b_attention)
     uint32_t att_chunk = 64, att_ring = 3; // its rows per chunk and chunk buffers
+    uint32_t att_tc = 1;                   // k_b_attention_tc (tensor-core attention; hd 64 or 128)
     // K splits and tiles (0: 128 x 128, 1: 128 x 256) of the QKV, up/gate and Wo / down GEMMs
     uint32_t qkv_splits = 3, ug_splits = 3, proj_splits = 4, qkv_tile = 1, ug_tile = 1, proj_tile = 0;
     const float *out_norm = nullptr;
@@ -452,6 +453,282 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
         for (uint32_t w = 0; w < nw; ++w)
             v += acc[w * hd + d];
         o[d] = __float2half_rn(v);
+    }
+}
+
+constexpr uint32_t kAttTcThreads = 256; // 8 warps
+
+// Dynamic shared memory of k_b_attention_tc: 1 KB of alignment slack, the chunk ring (each buffer
+// hd / 64 swizzled boxes of chunk x 128 bytes), the mbarriers, the fp16 scores and probabilities
+// over the cap rounded up to whole chunks, the second key half's output slices (hd < 128) and q.
+__host__ __device__ constexpr size_t att_tc_smem(uint32_t hd, uint32_t cap, uint32_t chunk, uint32_t stages)
+{
+    return 1024 + (size_t)stages * chunk * hd * 2 + 8 * stages + 2 * 2 * ((size_t)(cap + chunk - 1) / chunk * chunk + 16) +
+           4 * (size_t)hd + 2 * (size_t)hd;
+}
+
+__device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap *map, int32_t c0, int32_t c1, int32_t c2,
+                                              int32_t c3, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+                 "%4, %5}], [%6];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void att_ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void att_ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// d += A (16 x 16, fp16, row-major fragment) . B (16 x 8, fp16, column fragment), fp32 accumulation
+__device__ __forceinline__ void att_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory address of 16-byte piece `dc` (0 .. hd / 8 - 1) of row r of a chunk buffer: piece dc
+// lies in box dc / 8 (64 fp16 columns each, chunk x 128 bytes), swizzled by the TMA's 128-byte
+// pattern (piece c of a box row r at c ^ (r & 7)).
+__device__ __forceinline__ uint32_t att_piece(uint32_t buf, uint32_t chunk, uint32_t r, uint32_t dc)
+{
+    return buf + (dc >> 3) * chunk * 128 + r * 128 + (((dc & 7) ^ (r & 7)) << 4);
+}
+
+// Attention of one (head, sequence) on the tensor cores: the same nodes as k_b_attention_staged
+// (scores s_j = fp16(scale * q.k_j), p_j = fp16(exp(s_j - max) / sum), output fp16(sum_j p_j v_j)),
+// with the sums of products on mma.sync m16n8k16 (fp16 operands, whose products are exact, fp32
+// accumulation) instead of per-lane FMAs and shuffles. The sequence's key rows, then its value rows,
+// arrive as `chunk`-row TMA boxes (128-byte swizzle) in a ring of `stages` buffers.
+//  * Scores: warp w takes 16-key blocks w, w + 8, ... of a chunk; A = the block's key rows (ldmatrix),
+//    B = q in all 8 columns, so every column of D holds the block's 16 scores.
+//  * Output: warp w owns output columns [16 (w % S), 16 (w % S) + 16) for S = hd / 16 slices and
+//    the key blocks of its key part w / S; A = the probabilities in all 16 rows, B = the value rows
+//    (ldmatrix.trans), so every row of D holds p . V for 16 columns. Key rows past Lk in the last
+//    value chunk are zeroed before use (their probabilities are 0, and 0 times a stale value must stay 0).
+// At Lk == hd the reference reads V as [hd, Lk] (src/core/vkllm_op_matmul.c:14-30); that step runs a
+// scalar path from global memory. Each mbarrier wait is bounded; on expiry the CTA sets kErrAttTimeout
+// in *err, waits (bounded) for its copies in flight and returns.
+template <uint32_t HD>
+__global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __grid_constant__ CUtensorMap kmap,
+                                                                const __grid_constant__ CUtensorMap vmap,
+                                                                const __half *__restrict__ q, uint32_t q_stride,
+                                                                const __half *__restrict__ kc,
+                                                                const __half *__restrict__ vc,
+                                                                const uint32_t *__restrict__ pos, uint32_t H,
+                                                                uint32_t cap, float scale, __half *__restrict__ out,
+                                                                uint32_t *err, uint32_t chunk, uint32_t stages)
+{
+    static_assert(HD % 64 == 0 && HD <= 128, "head size");
+    constexpr uint32_t kSlices = HD / 16, kParts = 8 / kSlices;
+    pdl_trigger();
+    extern __shared__ unsigned char att_tc_sm[];
+    __shared__ float red[32];
+    const uint32_t h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (pos[b] >= cap)
+        return; // flagged by k_b_check_pos
+    const uint32_t Lk = pos[b] + 1;
+    const __half *qv = q + (uint64_t)b * q_stride + h * HD;
+    __half *o = out + (uint64_t)b * H * HD + h * HD;
+    const uint32_t capr = (cap + chunk - 1) / chunk * chunk + 16;
+    const uint32_t base = (smem_u32(att_tc_sm) + 1023u) & ~1023u; // swizzled boxes need 1 KB alignment
+    unsigned char *sm = att_tc_sm + (base - smem_u32(att_tc_sm));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)stages * chunk * HD * 2);
+    __half *sc = reinterpret_cast<__half *>(bars + stages); // [capr] scores
+    __half *ph = sc + capr;                                  // [capr] probabilities, 0 past Lk
+    float *acc = reinterpret_cast<float *>(ph + capr);       // [HD] the second key part's output, then q
+    if (Lk == HD)
+    {
+        // quirk Q1, scalar from global memory: o[w] = sum_k p_k V[w][k] with V read as [hd, Lk]
+        const __half *kb = kc + ((uint64_t)b * H + h) * cap * HD;
+        const __half *vb = vc + ((uint64_t)b * H + h) * cap * HD;
+        float mx = -FLT_MAX;
+        for (uint32_t j = tid; j < Lk; j += blockDim.x)
+        {
+            float a = 0.f;
+#pragma unroll 4
+            for (uint32_t d = 0; d < HD; ++d)
+                a = fmaf(__half2float(qv[d]), __half2float(kb[(uint64_t)j * HD + d]), a);
+            const float s = round_f16(a * scale);
+            sc[j] = __float2half_rn(s);
+            mx = fmaxf(mx, s);
+        }
+        mx = warp_max(mx);
+        if (lane == 0)
+            red[warp] = mx;
+        __syncthreads();
+        float m = -FLT_MAX;
+        for (uint32_t w = 0; w < (blockDim.x >> 5); ++w)
+            m = fmaxf(m, red[w]);
+        __syncthreads();
+        float l = 0.f;
+        for (uint32_t j = tid; j < Lk; j += blockDim.x)
+            l += expf(__half2float(sc[j]) - m);
+        l = bsum(l, red);
+        for (uint32_t j = tid; j < Lk; j += blockDim.x)
+            ph[j] = __float2half_rn(expf(__half2float(sc[j]) - m) / l);
+        __syncthreads();
+        for (uint32_t w = tid; w < HD; w += blockDim.x)
+        {
+            float v = 0.f;
+            for (uint32_t k = 0; k < Lk; ++k)
+                v = fmaf(__half2float(ph[k]), __half2float(vb[(uint64_t)w * Lk + k]), v);
+            o[w] = __float2half_rn(v);
+        }
+        return;
+    }
+    const uint32_t nk = (Lk + chunk - 1) / chunk, total = 2 * nk, buf_bytes = chunk * HD * 2;
+    // chunk c < nk: key rows [chunk c, ...); c >= nk: value rows [chunk (c - nk), ...); buffer c % stages
+    auto issue = [&](uint32_t c) {
+        const uint32_t st = c % stages;
+        const int32_t r0 = (int32_t)((c < nk ? c : c - nk) * chunk);
+        mbar_arrive_expect_tx(&bars[st], buf_bytes);
+#pragma unroll
+        for (uint32_t bx = 0; bx < HD / 64; ++bx)
+            tma_load_rows(base + st * buf_bytes + bx * chunk * 128, c < nk ? &kmap : &vmap, (int32_t)(bx * 64), r0,
+                          (int32_t)h, (int32_t)b, &bars[st]);
+    };
+    if (tid == 0)
+    {
+        for (uint32_t st = 0; st < stages; ++st)
+            mbar_init(&bars[st], 1);
+        fence_barrier_init();
+        for (uint32_t c = 0; c < stages && c < total; ++c)
+            issue(c);
+    }
+    // q as fp16 pairs in shared memory: the scores' B fragments (every column) are the pairs
+    // k = 16 ks + 2 (lane & 3) + {0, 1} and the same + 8
+    uint32_t *qs2 = reinterpret_cast<uint32_t *>(acc + HD);
+    for (uint32_t i = tid; i < HD / 2; i += kAttTcThreads)
+        qs2[i] = reinterpret_cast<const uint32_t *>(qv)[i];
+    __syncthreads(); // mbarrier initialisation and q visible to every thread
+    const uint32_t mi = lane >> 3, lrow = (lane & 7) + 8 * (mi & 1); // this lane's ldmatrix row and piece
+    const uint32_t slice = warp % kSlices, part = warp / kSlices;
+    float mx = -FLT_MAX;
+    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t c = 0; c < total; ++c)
+    {
+        const uint32_t st = c % stages;
+        const bool timed_out = !mbar_wait_bounded(&bars[st], (c / stages) & 1u, kWaitLimitNs);
+        if (__syncthreads_or(timed_out))
+        {
+            if (tid == 0)
+            {
+                atomicOr(err, kErrAttTimeout);
+                for (uint32_t k = c; k < total && k < c + stages; ++k)
+                    (void)mbar_wait_bounded(&bars[k % stages], (k / stages) & 1u, kWaitLimitNs / 4);
+            }
+            return;
+        }
+        const uint32_t buf = base + st * buf_bytes;
+        const uint32_t r0 = (c < nk ? c : c - nk) * chunk, rows = min(chunk, Lk - r0), nkb = (rows + 15) / 16;
+        if (c < nk)
+        {
+            for (uint32_t kb = warp; kb < nkb; kb += kAttTcThreads / 32)
+            {
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+                for (uint32_t ks = 0; ks < HD / 16; ++ks)
+                {
+                    uint32_t a0, a1, a2, a3;
+                    att_ldsm_x4(att_piece(buf, chunk, kb * 16 + lrow, 2 * ks + (mi >> 1)), a0, a1, a2, a3);
+                    att_mma(d, a0, a1, a2, a3, qs2[8 * ks + (lane & 3)], qs2[8 * ks + 4 + (lane & 3)]);
+                }
+                if ((lane & 3) == 0) // d[0]: key 16 kb + lane / 4, d[2]: that + 8
+#pragma unroll
+                    for (uint32_t e = 0; e < 2; ++e)
+                    {
+                        const uint32_t r = kb * 16 + (lane >> 2) + 8 * e;
+                        if (r < rows)
+                        {
+                            const float s = round_f16(d[2 * e] * scale);
+                            sc[r0 + r] = __float2half_rn(s);
+                            mx = fmaxf(mx, s);
+                        }
+                    }
+            }
+            if (c + 1 == nk)
+            {
+                // softmax over the whole row: max, sum of exp, p_j = fp16(exp(s_j - max) / sum), 0 past Lk
+                mx = warp_max(mx);
+                if (lane == 0)
+                    red[warp] = mx;
+                __syncthreads();
+                float m = -FLT_MAX;
+                for (uint32_t w = 0; w < kAttTcThreads / 32; ++w)
+                    m = fmaxf(m, red[w]);
+                __syncthreads();
+                float l = 0.f;
+                for (uint32_t j = tid; j < Lk; j += kAttTcThreads)
+                    l += expf(__half2float(sc[j]) - m);
+                l = bsum(l, red);
+                for (uint32_t j = tid; j < nk * chunk; j += kAttTcThreads)
+                    ph[j] = j < Lk ? __float2half_rn(expf(__half2float(sc[j]) - m) / l) : __float2half_rn(0.f);
+            }
+        }
+        else
+        {
+            const uint32_t padded = nkb * 16;
+            if (rows < padded) // the last value chunk: zero its rows past Lk that the key blocks read
+            {
+                const uint32_t per_row = HD / 8, n = (padded - rows) * per_row;
+                for (uint32_t i = tid; i < n; i += kAttTcThreads)
+                {
+                    const uint32_t r = rows + i / per_row, dc = i % per_row;
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(att_piece(buf, chunk, r, dc)), "r"(0u)
+                                 : "memory");
+                }
+                __syncthreads();
+            }
+            for (uint32_t kb = part; kb < nkb; kb += kParts)
+            {
+                uint32_t b00, b01, b10, b11;
+                att_ldsm_x4_t(att_piece(buf, chunk, kb * 16 + lrow, 2 * slice + (mi >> 1)), b00, b01, b10, b11);
+                const uint32_t k0 = r0 + kb * 16 + 2 * (lane & 3);
+                const uint32_t pa = *reinterpret_cast<const uint32_t *>(ph + k0);
+                const uint32_t pb = *reinterpret_cast<const uint32_t *>(ph + k0 + 8);
+                att_mma(o0, pa, pa, pb, pb, b00, b01);
+                att_mma(o1, pa, pa, pb, pb, b10, b11);
+            }
+        }
+        __syncthreads(); // buffer st is free (and, after the last key chunk, the probabilities are set)
+        if (tid == 0 && c + stages < total)
+        {
+            fence_proxy_async();
+            issue(c + stages);
+        }
+    }
+    // o0 / o1: columns 16 slice + 2 (lane & 3) + {0, 1} and the same + 8 (every row of D is equal)
+    const uint32_t col = 16 * slice + 2 * (lane & 3);
+    if (kParts > 1)
+    {
+        if (part == 1 && lane < 4)
+        {
+            acc[col] = o0[0], acc[col + 1] = o0[1], acc[col + 8] = o1[0], acc[col + 9] = o1[1];
+        }
+        __syncthreads();
+        if (part == 0 && lane < 4)
+        {
+            o0[0] += acc[col], o0[1] += acc[col + 1], o1[0] += acc[col + 8], o1[1] += acc[col + 9];
+        }
+    }
+    if (part == 0 && lane < 4)
+    {
+        *reinterpret_cast<__half2 *>(o + col) = __floats2half2_rn(o0[0], o0[1]);
+        *reinterpret_cast<__half2 *>(o + col + 8) = __floats2half2_rn(o1[0], o1[1]);
     }
 }
 
@@ -948,7 +1225,21 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
             k_b_rope_kv<<<dim3(H, B), (hd / 2 + 31) / 32 * 32, 0, s>>>(
                 bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
         }
-        if (bt->att_staged)
+        CUtensorMap km, vm;
+        if (bt->att_tc && encode_kv_rows_map(&km, kc, hd, bt->cap, H, B, bt->att_chunk) &&
+            encode_kv_rows_map(&vm, vc, hd, bt->cap, H, B, bt->att_chunk))
+        {
+            const size_t smem = att_tc_smem(hd, bt->cap, bt->att_chunk, bt->att_ring);
+            if (hd == 128)
+                k_b_attention_tc<128><<<dim3(H, B), kAttTcThreads, smem, s>>>(km, vm, bt->qkv, 3 * HD, kc, vc, bt->pos, H,
+                                                                              bt->cap, dd.scale, bt->attn, bt->err,
+                                                                              bt->att_chunk, bt->att_ring);
+            else
+                k_b_attention_tc<64><<<dim3(H, B), kAttTcThreads, smem, s>>>(km, vm, bt->qkv, 3 * HD, kc, vc, bt->pos, H,
+                                                                             bt->cap, dd.scale, bt->attn, bt->err,
+                                                                             bt->att_chunk, bt->att_ring);
+        }
+        else if (bt->att_staged)
             k_b_attention_staged<<<dim3(H, B), bt->att_staged,
                                    att_staged_smem(hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring), s>>>(
                 bt->qkv, 3 * HD, kc, vc, bt->pos, H, hd, bt->cap, dd.scale, bt->attn, bt->err, bt->att_chunk,
@@ -1083,6 +1374,13 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     if (!(bt->att_staged == 128 || bt->att_staged == 256 || bt->att_staged == 512) || dd.hd % 8 || dd.hd > 128 ||
         att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_staged = 0;
+    // VKLLM_B200_BATCH_ATT_TC=0 selects the FMA kernels above instead of the tensor-core attention,
+    // which needs hd 64 or 128 and whole 16-row key blocks per chunk
+    const char *tc_env = getenv("VKLLM_B200_BATCH_ATT_TC");
+    bt->att_tc = (tc_env && atoi(tc_env) == 0) ? 0u : 1u;
+    if ((dd.hd != 64 && dd.hd != 128) || bt->att_chunk % 16 ||
+        att_tc_smem(dd.hd, bt->cap, bt->att_chunk, bt->att_ring) > 200 * 1024)
+        bt->att_tc = 0;
     // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0: 128 x 128, 1: 128 x 256;
     // 2, 3: the same loading 64 rows of A per stage, for up to 64 sequences) of the QKV, up/gate
     // and Wo / down GEMMs (defaults 3,3,4,1,1,0; 7B, 64 sequences: 2,3,4 / 3,3,4 / 4,3,4 / 3,2,4 splits
@@ -1173,6 +1471,9 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         bt->wout_g = bt->wout;
     if (!copied || cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
+        (bt->att_tc && cudaFuncSetAttribute(dd.hd == 128 ? k_b_attention_tc<128> : k_b_attention_tc<64>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)att_tc_smem(dd.hd, bt->cap, bt->att_chunk, bt->att_ring)) != cudaSuccess) ||
         (bt->att_staged && cudaFuncSetAttribute(k_b_attention_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 (int)att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk,
                                                                      bt->att_ring)) != cudaSuccess) ||

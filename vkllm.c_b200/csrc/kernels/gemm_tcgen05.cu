@@ -740,6 +740,13 @@ bool launch_tc(const GemmArgs &g, cudaStream_t s, uint32_t splits = 1, float *ws
 
 } // namespace
 
+bool encode_kv_rows_map(CUtensorMap *m, const __half *base, uint32_t hd, uint32_t cap, uint32_t heads, uint32_t seqs,
+                        uint32_t box_rows)
+{
+    return hd % kBK == 0 && box_rows >= 8 && box_rows <= 256 && box_rows % 8 == 0 &&
+           encode_operand(m, base, hd, cap, hd, heads, (uint64_t)cap * hd, seqs, (uint64_t)heads * cap * hd, box_rows);
+}
+
 bool make_gemm_args(const Desc4 &da, const Desc4 &db, const Desc4 &dc, bool trans_b, const void *a, const void *b,
                     void *c, float scale, int act, GemmArgs *g)
 {

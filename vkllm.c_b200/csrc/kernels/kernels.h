@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -85,5 +86,11 @@ bool launch_bin_h(const __half *a, const __half *b, __half *out, uint64_t n, int
 bool launch_residual_rmsnorm_rows(__half *x, const __half *y, const float *g, __half *n, uint32_t rows, uint32_t W,
                                   float eps, cudaStream_t s);
 bool launch_argmax_rows(const __half *x, uint32_t rows, uint32_t W, uint32_t *out, cudaStream_t s);
+// Tensor map over a KV cache laid out [seqs][heads][cap][hd] fp16: dims {hd, cap, heads, seqs}, box
+// {64, box_rows, 1, 1} with 128-byte swizzle (16-byte piece c of box row r stored at piece c ^ (r & 7)),
+// zero fill past cap. Needs hd a multiple of 64 and box_rows a multiple of 8 up to 256. Cached per
+// (address, shape).
+bool encode_kv_rows_map(CUtensorMap *m, const __half *base, uint32_t hd, uint32_t cap, uint32_t heads, uint32_t seqs,
+                        uint32_t box_rows);
 
 } // namespace vkb
