@@ -512,7 +512,7 @@ __device__ __forceinline__ uint32_t att_piece(uint32_t buf, uint32_t chunk, uint
 // (scores s_j = fp16(scale * q.k_j), p_j = fp16(exp(s_j - max) / sum), output fp16(sum_j p_j v_j)),
 // with the sums of products on mma.sync m16n8k16 (fp16 operands, whose products are exact, fp32
 // accumulation) instead of per-lane FMAs and shuffles. The sequence's key rows, then its value rows,
-// arrive as `chunk`-row TMA boxes (128-byte swizzle) in a ring of `stages` buffers.
+// arrive as `chunk`-row chunks of 16-row TMA boxes (128-byte swizzle) in a ring of `stages` buffers.
 //  * Scores: warp w takes 16-key blocks w, w + 8, ... of a chunk; A = the block's key rows (ldmatrix),
 //    B = q in all 8 columns, so every column of D holds the block's 16 scores.
 //  * Output: warp w owns output columns [16 (w % S), 16 (w % S) + 16) for S = hd / 16 slices and
@@ -591,15 +591,18 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
         return;
     }
     const uint32_t nk = (Lk + chunk - 1) / chunk, total = 2 * nk, buf_bytes = chunk * HD * 2;
-    // chunk c < nk: key rows [chunk c, ...); c >= nk: value rows [chunk (c - nk), ...); buffer c % stages
+    // chunk c < nk: key rows [chunk c, ...); c >= nk: value rows [chunk (c - nk), ...); buffer c % stages.
+    // The maps' boxes are 16 rows, so a chunk fetches only the 16-key blocks that hold keys below Lk;
+    // each lands at its row offset (a multiple of 8) of the chunk's boxes, in the same swizzled layout.
     auto issue = [&](uint32_t c) {
-        const uint32_t st = c % stages;
-        const int32_t r0 = (int32_t)((c < nk ? c : c - nk) * chunk);
-        mbar_arrive_expect_tx(&bars[st], buf_bytes);
+        const uint32_t st = c % stages, r0 = (c < nk ? c : c - nk) * chunk;
+        const uint32_t nb = (min(chunk, Lk - r0) + 15) / 16;
+        mbar_arrive_expect_tx(&bars[st], nb * 16 * HD * 2);
+        for (uint32_t i = 0; i < nb; ++i)
 #pragma unroll
-        for (uint32_t bx = 0; bx < HD / 64; ++bx)
-            tma_load_rows(base + st * buf_bytes + bx * chunk * 128, c < nk ? &kmap : &vmap, (int32_t)(bx * 64), r0,
-                          (int32_t)h, (int32_t)b, &bars[st]);
+            for (uint32_t bx = 0; bx < HD / 64; ++bx)
+                tma_load_rows(base + st * buf_bytes + bx * chunk * 128 + i * 16 * 128, c < nk ? &kmap : &vmap,
+                              (int32_t)(bx * 64), (int32_t)(r0 + 16 * i), (int32_t)h, (int32_t)b, &bars[st]);
     };
     if (tid == 0)
     {
@@ -1226,8 +1229,8 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
                 bt->qkv, bt->qkv + HD, bt->qkv + 2 * HD, 3 * HD, bt->pos, H, hd, bt->cap, dd.rope_base, kc, vc, B);
         }
         CUtensorMap km, vm;
-        if (bt->att_tc && encode_kv_rows_map(&km, kc, hd, bt->cap, H, B, bt->att_chunk) &&
-            encode_kv_rows_map(&vm, vc, hd, bt->cap, H, B, bt->att_chunk))
+        if (bt->att_tc && encode_kv_rows_map(&km, kc, hd, bt->cap, H, B, 16) &&
+            encode_kv_rows_map(&vm, vc, hd, bt->cap, H, B, 16))
         {
             const size_t smem = att_tc_smem(hd, bt->cap, bt->att_chunk, bt->att_ring);
             if (hd == 128)
