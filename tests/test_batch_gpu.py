@@ -116,23 +116,25 @@ def test_in_place_weights_match_tile_copies(vk, ctx, monkeypatch):
 # (head size, heads, prompt lengths): ragged key counts (tails of 1..15 rows past a 16-key block),
 # a one-token prompt, and one sequence that passes Lk == hd (quirk Q1) during the steps
 TC_MODELS = {64: (8, (1, 17, 40, 56, 9, 33)), 128: (4, (1, 17, 120, 70, 9, 100))}
-# chunk rows : ring buffers of the tensor-core attention (read when the batch is created)
-TC_CHUNKS = ["64:2", "16:4", "128:2", "48:3"]
+# chunk rows : ring buffers : threads per CTA of the tensor-core attention (read when the batch is
+# created); threads 0 runs the FMA staged kernel on the same models
+TC_CHUNKS = ["48:2:128", "64:2:256", "16:4:128", "128:2:256", "48:3:128", "32:2:128", "64:2:0"]
 
 
 @pytest.mark.parametrize("chunk", TC_CHUNKS)
 @pytest.mark.parametrize("hd", sorted(TC_MODELS))
 def test_tensor_core_attention_matches_each_sequence_alone(vk, ctx, orc, hd, chunk, monkeypatch):
-    """k_b_attention_tc (mma.sync over TMA-swizzled K/V chunks) at head sizes 64 and 128 and several
-    chunk / ring shapes: every sequence of a batch of 6 decodes what the oracle decodes on it alone
+    """k_b_attention_tc (mma.sync over TMA-swizzled K/V chunks) at head sizes 64 and 128, 4 and 8
+    warps per CTA and several chunk / ring shapes: every sequence of a batch of 6 decodes what the oracle decodes on it alone
     (logits within north_star's bar at every step, greedy ids identical except at a reference tie).
     Prompts of 1 to 120 tokens put the last key block's tail at every remainder; one sequence per
     model crosses Lk == hd, where the kernel runs the reference's transposed-V reading."""
     from parity import download_weights
 
-    c, r = chunk.split(":")
+    c, r, t = chunk.split(":")
     monkeypatch.setenv("VKLLM_B200_BATCH_ATT_CHUNK", c)
     monkeypatch.setenv("VKLLM_B200_BATCH_ATT_RING", r)
+    monkeypatch.setenv("VKLLM_B200_BATCH_ATT_TC", t)
     H, lens = TC_MODELS[hd]
     cfg = dict(block_count=2, context_length=256, embedding_length=H * hd, head_count=H, ffn_length=1280,
                vocab_size=4096, rope_freq_base=10000.0, rms_eps=1e-5, init_std=0.02)

@@ -58,7 +58,7 @@ struct vkllm_b200_batch
     uint32_t tiled = 1;                                                  // GEMM operands in tile order
     uint32_t att_staged = 256; // threads of k_b_attention_staged (0: k_b_attention)
     uint32_t att_chunk = 64, att_ring = 3; // its rows per chunk and chunk buffers
-    uint32_t att_tc = 1;                   // k_b_attention_tc (tensor-core attention; hd 64 or 128)
+    uint32_t att_tc = 128;                 // threads of k_b_attention_tc (tensor-core attention; 0: off)
     // K splits and tiles (0: 128 x 128, 1: 128 x 256) of the QKV, up/gate and Wo / down GEMMs
     uint32_t qkv_splits = 3, ug_splits = 3, proj_splits = 4, qkv_tile = 1, ug_tile = 1, proj_tile = 0;
     const float *out_norm = nullptr;
@@ -255,6 +255,8 @@ __global__ void k_b_rope_kv_part(const float *__restrict__ part, uint32_t splits
 }
 
 constexpr uint32_t kAttChunk = 64;    // key rows per staged chunk (staged attention), default
+constexpr uint32_t kAttTcChunk = 48;   // key rows per chunk of the tensor-core attention, default
+constexpr uint32_t kAttTcThreads = 128; // threads per CTA of the tensor-core attention, default
 // chunk buffers in flight per CTA, default (7B, 64 sequences: 2 / 3 buffers of 64 rows 4.877 / 4.966 ms
 // per step; 4 / 6 of 32 rows 5.038 / 5.156)
 constexpr uint32_t kAttStages = 2;
@@ -456,7 +458,6 @@ __global__ void __launch_bounds__(kAttThreads) k_b_attention_staged(const __half
     }
 }
 
-constexpr uint32_t kAttTcThreads = 256; // 8 warps
 
 // Dynamic shared memory of k_b_attention_tc: 1 KB of alignment slack, the chunk ring (each buffer
 // hd / 64 swizzled boxes of chunk x 128 bytes), the mbarriers, the fp16 scores and probabilities
@@ -515,15 +516,16 @@ __device__ __forceinline__ uint32_t att_piece(uint32_t buf, uint32_t chunk, uint
 // arrive as `chunk`-row chunks of 16-row TMA boxes (128-byte swizzle) in a ring of `stages` buffers.
 //  * Scores: warp w takes 16-key blocks w, w + 8, ... of a chunk; A = the block's key rows (ldmatrix),
 //    B = q in all 8 columns, so every column of D holds the block's 16 scores.
-//  * Output: warp w owns output columns [16 (w % S), 16 (w % S) + 16) for S = hd / 16 slices and
-//    the key blocks of its key part w / S; A = the probabilities in all 16 rows, B = the value rows
+//  * Output: the hd / 16 slices of 16 output columns are dealt to the warps (several per warp when
+//    they outnumber the warps; with more warps than slices, the key blocks are split in two parts
+//    summed at the end); A = the probabilities in all 16 rows, B = the value rows
 //    (ldmatrix.trans), so every row of D holds p . V for 16 columns. Key rows past Lk in the last
 //    value chunk are zeroed before use (their probabilities are 0, and 0 times a stale value must stay 0).
 // At Lk == hd the reference reads V as [hd, Lk] (src/core/vkllm_op_matmul.c:14-30); that step runs a
 // scalar path from global memory. Each mbarrier wait is bounded; on expiry the CTA sets kErrAttTimeout
 // in *err, waits (bounded) for its copies in flight and returns.
-template <uint32_t HD>
-__global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __grid_constant__ CUtensorMap kmap,
+template <uint32_t HD, uint32_t NT>
+__global__ void __launch_bounds__(NT, NT == 256 ? 5 : 10) k_b_attention_tc(const __grid_constant__ CUtensorMap kmap,
                                                                 const __grid_constant__ CUtensorMap vmap,
                                                                 const __half *__restrict__ q, uint32_t q_stride,
                                                                 const __half *__restrict__ kc,
@@ -532,8 +534,12 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
                                                                 uint32_t cap, float scale, __half *__restrict__ out,
                                                                 uint32_t *err, uint32_t chunk, uint32_t stages)
 {
-    static_assert(HD % 64 == 0 && HD <= 128, "head size");
-    constexpr uint32_t kSlices = HD / 16, kParts = 8 / kSlices;
+    static_assert(HD % 64 == 0 && HD <= 128 && (NT == 128 || NT == 256), "head size, threads");
+    // output slices of 16 columns: G groups of warps own kSPW slices each (slices g, g + G, ...);
+    // with more warps than slices the key blocks are split into kParts parts
+    constexpr uint32_t kWarps = NT / 32, kSlices = HD / 16, kG = kSlices < kWarps ? kSlices : kWarps;
+    constexpr uint32_t kSPW = kSlices / kG, kParts = kWarps / kG;
+    static_assert(kParts <= 2, "key parts");
     pdl_trigger();
     extern __shared__ unsigned char att_tc_sm[];
     __shared__ float red[32];
@@ -542,7 +548,7 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
         return; // flagged by k_b_check_pos
     const uint32_t Lk = pos[b] + 1;
     const __half *qv = q + (uint64_t)b * q_stride + h * HD;
-    __half *o = out + (uint64_t)b * H * HD + h * HD;
+    __half *o_out = out + (uint64_t)b * H * HD + h * HD;
     const uint32_t capr = (cap + chunk - 1) / chunk * chunk + 16;
     const uint32_t base = (smem_u32(att_tc_sm) + 1023u) & ~1023u; // swizzled boxes need 1 KB alignment
     unsigned char *sm = att_tc_sm + (base - smem_u32(att_tc_sm));
@@ -586,7 +592,7 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
             float v = 0.f;
             for (uint32_t k = 0; k < Lk; ++k)
                 v = fmaf(__half2float(ph[k]), __half2float(vb[(uint64_t)w * Lk + k]), v);
-            o[w] = __float2half_rn(v);
+            o_out[w] = __float2half_rn(v);
         }
         return;
     }
@@ -615,13 +621,13 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
     // q as fp16 pairs in shared memory: the scores' B fragments (every column) are the pairs
     // k = 16 ks + 2 (lane & 3) + {0, 1} and the same + 8
     uint32_t *qs2 = reinterpret_cast<uint32_t *>(acc + HD);
-    for (uint32_t i = tid; i < HD / 2; i += kAttTcThreads)
+    for (uint32_t i = tid; i < HD / 2; i += NT)
         qs2[i] = reinterpret_cast<const uint32_t *>(qv)[i];
     __syncthreads(); // mbarrier initialisation and q visible to every thread
     const uint32_t mi = lane >> 3, lrow = (lane & 7) + 8 * (mi & 1); // this lane's ldmatrix row and piece
-    const uint32_t slice = warp % kSlices, part = warp / kSlices;
+    const uint32_t grp = warp % kG, part = warp / kG;
     float mx = -FLT_MAX;
-    float o0[4] = {0.f, 0.f, 0.f, 0.f}, o1[4] = {0.f, 0.f, 0.f, 0.f};
+    float o[kSPW][2][4] = {};
     for (uint32_t c = 0; c < total; ++c)
     {
         const uint32_t st = c % stages;
@@ -640,7 +646,7 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
         const uint32_t r0 = (c < nk ? c : c - nk) * chunk, rows = min(chunk, Lk - r0), nkb = (rows + 15) / 16;
         if (c < nk)
         {
-            for (uint32_t kb = warp; kb < nkb; kb += kAttTcThreads / 32)
+            for (uint32_t kb = warp; kb < nkb; kb += kWarps)
             {
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
@@ -671,14 +677,14 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
                     red[warp] = mx;
                 __syncthreads();
                 float m = -FLT_MAX;
-                for (uint32_t w = 0; w < kAttTcThreads / 32; ++w)
+                for (uint32_t w = 0; w < kWarps; ++w)
                     m = fmaxf(m, red[w]);
                 __syncthreads();
                 float l = 0.f;
-                for (uint32_t j = tid; j < Lk; j += kAttTcThreads)
+                for (uint32_t j = tid; j < Lk; j += NT)
                     l += expf(__half2float(sc[j]) - m);
                 l = bsum(l, red);
-                for (uint32_t j = tid; j < nk * chunk; j += kAttTcThreads)
+                for (uint32_t j = tid; j < nk * chunk; j += NT)
                     ph[j] = j < Lk ? __float2half_rn(expf(__half2float(sc[j]) - m) / l) : __float2half_rn(0.f);
             }
         }
@@ -688,7 +694,7 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
             if (rows < padded) // the last value chunk: zero its rows past Lk that the key blocks read
             {
                 const uint32_t per_row = HD / 8, n = (padded - rows) * per_row;
-                for (uint32_t i = tid; i < n; i += kAttTcThreads)
+                for (uint32_t i = tid; i < n; i += NT)
                 {
                     const uint32_t r = rows + i / per_row, dc = i % per_row;
                     asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(att_piece(buf, chunk, r, dc)), "r"(0u)
@@ -698,13 +704,18 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
             }
             for (uint32_t kb = part; kb < nkb; kb += kParts)
             {
-                uint32_t b00, b01, b10, b11;
-                att_ldsm_x4_t(att_piece(buf, chunk, kb * 16 + lrow, 2 * slice + (mi >> 1)), b00, b01, b10, b11);
                 const uint32_t k0 = r0 + kb * 16 + 2 * (lane & 3);
                 const uint32_t pa = *reinterpret_cast<const uint32_t *>(ph + k0);
                 const uint32_t pb = *reinterpret_cast<const uint32_t *>(ph + k0 + 8);
-                att_mma(o0, pa, pa, pb, pb, b00, b01);
-                att_mma(o1, pa, pa, pb, pb, b10, b11);
+#pragma unroll
+                for (uint32_t j = 0; j < kSPW; ++j)
+                {
+                    uint32_t b00, b01, b10, b11;
+                    att_ldsm_x4_t(att_piece(buf, chunk, kb * 16 + lrow, 2 * (grp + kG * j) + (mi >> 1)), b00, b01, b10,
+                                  b11);
+                    att_mma(o[j][0], pa, pa, pb, pb, b00, b01);
+                    att_mma(o[j][1], pa, pa, pb, pb, b10, b11);
+                }
             }
         }
         __syncthreads(); // buffer st is free (and, after the last key chunk, the probabilities are set)
@@ -714,25 +725,41 @@ __global__ void __launch_bounds__(kAttTcThreads, 5) k_b_attention_tc(const __gri
             issue(c + stages);
         }
     }
-    // o0 / o1: columns 16 slice + 2 (lane & 3) + {0, 1} and the same + 8 (every row of D is equal)
-    const uint32_t col = 16 * slice + 2 * (lane & 3);
+    // o[j][0] / o[j][1]: columns 16 (grp + kG j) + 2 (lane & 3) + {0, 1} and the same + 8 (every row of
+    // D is equal); with two key parts, part 1 hands its sums to part 0 through shared memory
+#pragma unroll
+    for (uint32_t j = 0; j < kSPW; ++j)
+    {
+        const uint32_t col = 16 * (grp + kG * j) + 2 * (lane & 3);
+        if (kParts > 1 && part == 1 && lane < 4)
+        {
+            acc[col] = o[j][0][0], acc[col + 1] = o[j][0][1], acc[col + 8] = o[j][1][0], acc[col + 9] = o[j][1][1];
+        }
+    }
     if (kParts > 1)
-    {
-        if (part == 1 && lane < 4)
-        {
-            acc[col] = o0[0], acc[col + 1] = o0[1], acc[col + 8] = o1[0], acc[col + 9] = o1[1];
-        }
         __syncthreads();
-        if (part == 0 && lane < 4)
-        {
-            o0[0] += acc[col], o0[1] += acc[col + 1], o1[0] += acc[col + 8], o1[1] += acc[col + 9];
-        }
-    }
     if (part == 0 && lane < 4)
-    {
-        *reinterpret_cast<__half2 *>(o + col) = __floats2half2_rn(o0[0], o0[1]);
-        *reinterpret_cast<__half2 *>(o + col + 8) = __floats2half2_rn(o1[0], o1[1]);
-    }
+#pragma unroll
+        for (uint32_t j = 0; j < kSPW; ++j)
+        {
+            const uint32_t col = 16 * (grp + kG * j) + 2 * (lane & 3);
+            float v[4] = {o[j][0][0], o[j][0][1], o[j][1][0], o[j][1][1]};
+            if (kParts > 1)
+                v[0] += acc[col], v[1] += acc[col + 1], v[2] += acc[col + 8], v[3] += acc[col + 9];
+            *reinterpret_cast<__half2 *>(o_out + col) = __floats2half2_rn(v[0], v[1]);
+            *reinterpret_cast<__half2 *>(o_out + col + 8) = __floats2half2_rn(v[2], v[3]);
+        }
+}
+
+using AttTcKernel = void (*)(CUtensorMap, CUtensorMap, const __half *, uint32_t, const __half *, const __half *,
+                            const uint32_t *, uint32_t, uint32_t, float, __half *, uint32_t *, uint32_t, uint32_t);
+
+// The instantiation for head size hd (64 or 128) and `threads` per CTA (128 or 256).
+AttTcKernel att_tc_kernel(uint32_t hd, uint32_t threads)
+{
+    if (hd == 128)
+        return threads == 128 ? k_b_attention_tc<128, 128> : k_b_attention_tc<128, 256>;
+    return threads == 128 ? k_b_attention_tc<64, 128> : k_b_attention_tc<64, 256>;
 }
 
 // Attention of one (head, sequence): scores s_j = fp16(scale * q.k_j) over the sequence's Lk = pos + 1
@@ -1233,14 +1260,9 @@ vkllm_err_t enqueue_batch_step(vkllm_b200_batch *bt, cudaStream_t s)
             encode_kv_rows_map(&vm, vc, hd, bt->cap, H, B, 16))
         {
             const size_t smem = att_tc_smem(hd, bt->cap, bt->att_chunk, bt->att_ring);
-            if (hd == 128)
-                k_b_attention_tc<128><<<dim3(H, B), kAttTcThreads, smem, s>>>(km, vm, bt->qkv, 3 * HD, kc, vc, bt->pos, H,
-                                                                              bt->cap, dd.scale, bt->attn, bt->err,
-                                                                              bt->att_chunk, bt->att_ring);
-            else
-                k_b_attention_tc<64><<<dim3(H, B), kAttTcThreads, smem, s>>>(km, vm, bt->qkv, 3 * HD, kc, vc, bt->pos, H,
-                                                                             bt->cap, dd.scale, bt->attn, bt->err,
-                                                                             bt->att_chunk, bt->att_ring);
+            auto kern = att_tc_kernel(hd, bt->att_tc);
+            kern<<<dim3(H, B), bt->att_tc, smem, s>>>(km, vm, bt->qkv, 3 * HD, kc, vc, bt->pos, H, bt->cap, dd.scale,
+                                                      bt->attn, bt->err, bt->att_chunk, bt->att_ring);
         }
         else if (bt->att_staged)
             k_b_attention_staged<<<dim3(H, B), bt->att_staged,
@@ -1366,22 +1388,28 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
     // GEMM operand copies, per layer [Wq; Wk; Wv] then [Wup; Wgate] (then Wo and Wdown when tiled)
     const char *att_env = getenv("VKLLM_B200_BATCH_ATT_STAGED");
     bt->att_staged = att_env ? (uint32_t)atoi(att_env) : 256u;
+    // VKLLM_B200_BATCH_ATT_TC = 0 selects the FMA kernels below instead of the tensor-core attention
+    // (which needs hd 64 or 128 and whole 16-row key blocks per chunk), 128 / 256 its threads per CTA.
+    // 7B, 64 sequences, one box (chunk / ring / threads): 48/2/128 4.733, 64/2/128 4.810, 32/3/128
+    // 4.818, 64/2/256 4.849-4.865 ms per step; the FMA kernel 64/2/256 4.862.
+    const char *tc_env = getenv("VKLLM_B200_BATCH_ATT_TC");
+    bt->att_tc = tc_env ? (uint32_t)atoi(tc_env) : kAttTcThreads;
+    if (bt->att_tc != 128 && bt->att_tc != 256)
+        bt->att_tc = 0;
+    const bool tc_shape = dd.hd == 64 || dd.hd == 128;
+    const uint32_t chunk_default = bt->att_tc && tc_shape ? kAttTcChunk : kAttChunk;
     const char *chunk_env = getenv("VKLLM_B200_BATCH_ATT_CHUNK"), *ring_env = getenv("VKLLM_B200_BATCH_ATT_RING");
-    bt->att_chunk = chunk_env ? (uint32_t)atoi(chunk_env) : kAttChunk;
+    bt->att_chunk = chunk_env ? (uint32_t)atoi(chunk_env) : chunk_default;
     bt->att_ring = ring_env ? (uint32_t)atoi(ring_env) : kAttStages;
     if (bt->att_chunk < 8 || bt->att_chunk > 256 || bt->att_chunk % 8 || bt->att_ring < 2 || bt->att_ring > kAttMaxStages)
     {
-        bt->att_chunk = kAttChunk;
+        bt->att_chunk = chunk_default;
         bt->att_ring = kAttStages;
     }
     if (!(bt->att_staged == 128 || bt->att_staged == 256 || bt->att_staged == 512) || dd.hd % 8 || dd.hd > 128 ||
         att_staged_smem(dd.hd, bt->cap, bt->att_staged, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_staged = 0;
-    // VKLLM_B200_BATCH_ATT_TC=0 selects the FMA kernels above instead of the tensor-core attention,
-    // which needs hd 64 or 128 and whole 16-row key blocks per chunk
-    const char *tc_env = getenv("VKLLM_B200_BATCH_ATT_TC");
-    bt->att_tc = (tc_env && atoi(tc_env) == 0) ? 0u : 1u;
-    if ((dd.hd != 64 && dd.hd != 128) || bt->att_chunk % 16 ||
+    if (!tc_shape || bt->att_chunk % 16 ||
         att_tc_smem(dd.hd, bt->cap, bt->att_chunk, bt->att_ring) > 200 * 1024)
         bt->att_tc = 0;
     // VKLLM_B200_BATCH_GEMM="qs,us,ps,qt,ut,pt": K splits (1..4) and tiles (0: 128 x 128, 1: 128 x 256;
@@ -1474,7 +1502,7 @@ extern "C" vkllm_err_t vkllm_b200_batch_new(struct vkllm_context *ctx, struct vk
         bt->wout_g = bt->wout;
     if (!copied || cudaMemsetAsync(bt->ws, 0, kv_bytes + act + small, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_b_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024) != cudaSuccess ||
-        (bt->att_tc && cudaFuncSetAttribute(dd.hd == 128 ? k_b_attention_tc<128> : k_b_attention_tc<64>,
+        (bt->att_tc && cudaFuncSetAttribute(att_tc_kernel(dd.hd, bt->att_tc),
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)att_tc_smem(dd.hd, bt->cap, bt->att_chunk, bt->att_ring)) != cudaSuccess) ||
         (bt->att_staged && cudaFuncSetAttribute(k_b_attention_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
