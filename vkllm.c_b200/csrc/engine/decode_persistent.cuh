@@ -460,6 +460,7 @@ __device__ __forceinline__ void prefetch_slice(const PersistParams &P, uint32_t 
 }
 
 // Epilogue of one unit of a GEMV phase (executed by one lane).
+template <bool TP>
 __device__ __forceinline__ void persist_epilogue(const PersistParams &P, uint32_t kind, const LayerW &lw, uint32_t u,
                                                  const float *s, uint32_t pos)
 {
@@ -492,7 +493,7 @@ __device__ __forceinline__ void persist_epilogue(const PersistParams &P, uint32_
     }
     case PK_WO:
     case PK_DOWN:
-        if (P.tp_size > 1) // partial over this rank's K slice, staged for tp_allreduce_rows
+        if constexpr (TP) // partial over this rank's K slice, staged for tp_allreduce_rows
             s_tp_stage[u - cta_units(kind).u0] = s[0];
         else
             P.x[u] = __float2half_rn(__half2float(__ldcg(P.x + u)) + round_f16(s[0]));
@@ -607,7 +608,7 @@ __device__ __forceinline__ bool fine_segment(const PersistParams &P, uint32_t ks
 // One GEMV phase: consumes this warp's tiles (partials to `part`), then the CTA sums the partials
 // of each of its units in segment order and runs the epilogue. Returns false when a wait timed out
 // in any warp of the CTA.
-template <int NM, bool GATED = false>
+template <int NM, bool TP, bool TRACE, bool GATED = false>
 __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t kind, uint32_t layer, WarpPipe &wp,
                                              const __half *xs, float *part, uint32_t pos, SyncState &tr,
                                              uint32_t gate_epoch = 0)
@@ -619,7 +620,7 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
     const uint32_t T = groups * g.Ks;
     const uint32_t nk = T > warp ? (T - warp + P.warps - 1) / P.warps : 0;
     const LayerW &lw = P.layers[kind == PK_LOGITS ? 0 : layer];
-    const bool wt = P.wtrace && blockIdx.x == 0 && lane == 0;
+    const bool wt = TRACE && P.wtrace && blockIdx.x == 0 && lane == 0; // per-warp pipeline accounting
     unsigned long long t_wait = 0, t_cons = 0, t_comp = 0;
     bool ok = true;
     uint32_t grp = warp / g.Ks, ks = warp % g.Ks; // tile t = warp + warps * k = grp * Ks + ks
@@ -737,7 +738,7 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
                 a += part[ks * pitch + ul * NM + m];
             sums[m] = a;
         }
-        persist_epilogue(P, kind, lw, r.u0 + ul, sums, pos);
+        persist_epilogue<TP>(P, kind, lw, r.u0 + ul, sums, pos);
     }
     return true;
 }
@@ -751,6 +752,7 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
 // [hd, Lk] (src/core/vkllm_op_matmul.c:14-30): split 0 then computes o[w] = sum_k p_k V[w][k] from
 // the stored scores and the other splits contribute 0. `aepoch` counts the attention phases of
 // this launch. Returns false on a timed-out wait or a reported error.
+template <bool FINE>
 __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32_t layer, uint32_t pos,
                                                   uint32_t aepoch, float *scratch, float *red)
 {
@@ -1007,7 +1009,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
                 P.attn[h * hd + d] = __float2half_rn(o);
             }
         __syncthreads();
-        if (flag_s && tid == 0 && P.fine) // the head's output is complete: the Wo tiles reading it may start
+        if (FINE && flag_s && tid == 0) // the head's output is complete: the Wo tiles reading it may start
         {
             __threadfence();
             st_release_gpu_u32(P.head_flag + h, aepoch + 1);
@@ -1077,6 +1079,10 @@ __device__ __forceinline__ void stage_copy_h(const __half *__restrict__ x, uint3
     __syncthreads();
 }
 
+// TP: tensor parallelism (P.tp_size > 1); FINE: the fine-grained Wo and down phases (P.fine); TRACE:
+// the per-warp pipeline accounting (P.wtrace). Each combination is its own instantiation, so the
+// kernel a launch runs holds no code of the others (their branches cost time in the tile loops).
+template <bool TP, bool FINE, bool TRACE>
 __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(PersistParams P)
 {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -1166,7 +1172,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
             else
                 stage_rmsnorm_h(P.x, lw.attn_norm, dd.D, dd.eps, xs, sred);
             trace_mark(P, tr);
-            ok = persist_gemv<2>(P, PK_QKV, l, wp, xs, part, pos, tr);
+            ok = persist_gemv<2, TP, TRACE>(P, PK_QKV, l, wp, xs, part, pos, tr);
             if (threadIdx.x == 0)
                 prefetch_slice(P, PK_WO, l);
             if (!__syncthreads_and(ok) || !grid_sync(P, tr))
@@ -1174,10 +1180,10 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 ok = false;
                 break;
             }
-            if (P.fine)
+            if constexpr (FINE)
             {
                 // Wo tiles wait only for the heads their input columns span
-                if (!persist_attention(P, l, pos, step * P.L + l, scratch, sred))
+                if (!persist_attention<FINE>(P, l, pos, step * P.L + l, scratch, sred))
                 {
                     ok = false;
                     break;
@@ -1186,22 +1192,22 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                     s_seg[threadIdx.x] = 0;
                 __syncthreads();
                 trace_mark(P, tr);
-                ok = persist_gemv<1, true>(P, PK_WO, l, wp, xs, part, pos, tr, step * P.L + l + 1);
+                ok = persist_gemv<1, TP, TRACE, true>(P, PK_WO, l, wp, xs, part, pos, tr, step * P.L + l + 1);
             }
             else
             {
-                if (!persist_attention(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
+                if (!persist_attention<FINE>(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
                 {
                     ok = false;
                     break;
                 }
                 stage_copy_h(P.attn, dd.H * dd.hd, xs);
                 trace_mark(P, tr);
-                ok = persist_gemv<1>(P, PK_WO, l, wp, xs, part, pos, tr);
+                ok = persist_gemv<1, TP, TRACE>(P, PK_WO, l, wp, xs, part, pos, tr);
             }
             if (threadIdx.x == 0)
                 prefetch_slice(P, PK_UPGATE, l);
-            if (P.tp_size > 1 && __syncthreads_and(ok))
+            if (TP && __syncthreads_and(ok))
                 ok = tp_allreduce_rows(P, 0, P.tp_base[0] + step * P.L + l + 1);
             if (!__syncthreads_and(ok) || !grid_sync(P, tr))
             {
@@ -1210,10 +1216,10 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
             }
             stage_rmsnorm_h(P.x, lw.ffn_norm, dd.D, dd.eps, xs, sred);
             trace_mark(P, tr);
-            ok = persist_gemv<2>(P, PK_UPGATE, l, wp, xs, part, pos, tr);
+            ok = persist_gemv<2, TP, TRACE>(P, PK_UPGATE, l, wp, xs, part, pos, tr);
             if (threadIdx.x == 0)
                 prefetch_slice(P, PK_DOWN, l);
-            if (P.fine)
+            if constexpr (FINE)
             {
                 // publish this CTA's up/gate rows, then stage the down input segment by segment
                 const uint32_t fe = step * P.L + l + 1;
@@ -1231,7 +1237,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                     s_seg[threadIdx.x] = 0;
                 __syncthreads();
                 trace_mark(P, tr);
-                ok = persist_gemv<1, true>(P, PK_DOWN, l, wp, xs, part, pos, tr, fe);
+                ok = persist_gemv<1, TP, TRACE, true>(P, PK_DOWN, l, wp, xs, part, pos, tr, fe);
             }
             else
             {
@@ -1242,11 +1248,11 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                 }
                 stage_copy_h(P.m, dd.F, xs);
                 trace_mark(P, tr);
-                ok = persist_gemv<1>(P, PK_DOWN, l, wp, xs, part, pos, tr);
+                ok = persist_gemv<1, TP, TRACE>(P, PK_DOWN, l, wp, xs, part, pos, tr);
             }
             if (threadIdx.x == 0)
                 prefetch_slice(P, l + 1 < P.L ? PK_QKV : PK_LOGITS, l + 1 < P.L ? l + 1 : 0);
-            if (P.tp_size > 1 && __syncthreads_and(ok))
+            if (TP && __syncthreads_and(ok))
                 ok = tp_allreduce_rows(P, 1, P.tp_base[1] + step * P.L + l + 1);
             if (!__syncthreads_and(ok) || !grid_sync(P, tr))
             {
@@ -1258,7 +1264,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
             break;
         stage_rmsnorm_h(P.x, P.out_norm, dd.D, dd.eps, xs, sred);
         trace_mark(P, tr);
-        ok = persist_gemv<1>(P, PK_LOGITS, 0, wp, xs, part, pos, tr);
+        ok = persist_gemv<1, TP, TRACE>(P, PK_LOGITS, 0, wp, xs, part, pos, tr);
         if (threadIdx.x == 0 && step + 1 < P.n_steps)
             prefetch_slice(P, PK_QKV, 0);
         if (!__syncthreads_and(ok))
@@ -1336,7 +1342,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
                         idx = ci;
                     }
                 }
-                if (P.tp_size > 1)
+                if constexpr (TP)
                 {
                     // this rank's class results -> every rank (CTA 0 sends), then every CTA combines the
                     // ranks' results per class with the same rule (indices grow with the rank)
@@ -1441,6 +1447,22 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
     for (uint32_t gi = wp.consumed; gi < wp.issued; ++gi)
         (void)mbar_wait_bounded(&wp.bar[gi % P.spw], (gi / P.spw) & 1u, kWaitLimitNs / 4);
     __syncwarp();
+}
+
+using PersistKernel = void (*)(PersistParams);
+
+// The instantiation for tensor parallelism `tp`, the fine-grained phases `fine` and tracing `trace`.
+inline PersistKernel persist_kernel(bool tp, bool fine, bool trace)
+{
+    if (trace)
+    {
+        if (tp)
+            return fine ? k_decode_persistent<true, true, true> : k_decode_persistent<true, false, true>;
+        return fine ? k_decode_persistent<false, true, true> : k_decode_persistent<false, false, true>;
+    }
+    if (tp)
+        return fine ? k_decode_persistent<true, true, false> : k_decode_persistent<true, false, false>;
+    return fine ? k_decode_persistent<false, true, false> : k_decode_persistent<false, false, false>;
 }
 
 } // namespace vkb

@@ -472,12 +472,18 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
     }
     if (dd.hd % 8 != 0 || dd.hd > 256)
         return;
-    // dynamic shared memory may use the opt-in limit minus the kernel's static shared memory
+    // dynamic shared memory may use the opt-in limit minus the kernel's static shared memory (the
+    // largest over the instantiations: tensor parallelism is configured after this setup)
     cudaFuncAttributes fa{};
-    if (cudaFuncGetAttributes(&fa, k_decode_persistent) != cudaSuccess)
+    for (int v = 0; v < 8; ++v)
     {
-        (void)cudaGetLastError();
-        return;
+        cudaFuncAttributes fv{};
+        if (cudaFuncGetAttributes(&fv, persist_kernel(v & 1, v & 2, v & 4)) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            return;
+        }
+        fa.sharedSizeBytes = fv.sharedSizeBytes > fa.sharedSizeBytes ? fv.sharedSizeBytes : fa.sharedSizeBytes;
     }
     const size_t optin = ctx->device->smem_optin > fa.sharedSizeBytes ? ctx->device->smem_optin - fa.sharedSizeBytes : 0;
     const size_t fixed = kStreamBarBytes + P.xs_bytes + P.part_bytes;
@@ -516,16 +522,18 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
             P.wtrace = nullptr;
         }
     }
-    if (cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->pp_smem) !=
-        cudaSuccess)
+    int blocks = 1;
+    for (int v = 0; v < 8 && blocks >= 1; ++v)
     {
-        (void)cudaGetLastError();
-        return;
+        int bv = 0;
+        if (cudaFuncSetAttribute(persist_kernel(v & 1, v & 2, v & 4), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)e->pp_smem) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bv, persist_kernel(v & 1, v & 2, v & 4), 32 * warps,
+                                                          e->pp_smem) != cudaSuccess)
+            bv = 0;
+        blocks = bv < blocks ? bv : blocks;
     }
-    int blocks = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_decode_persistent, 32 * warps, e->pp_smem) !=
-            cudaSuccess ||
-        blocks < 1)
+    if (blocks < 1)
     {
         (void)cudaGetLastError();
         return;
@@ -615,7 +623,7 @@ vkllm_err_t run_persistent(Engine *e, uint32_t n, cudaStream_t s)
         attr[0].val.cooperative = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        VKB_CUDA(cudaLaunchKernelEx(&cfg, k_decode_persistent, P));
+        VKB_CUDA(cudaLaunchKernelEx(&cfg, persist_kernel(P.tp_size > 1, P.fine != 0, P.wtrace != nullptr), P));
         e->launches += 1;
         n -= k;
     }
