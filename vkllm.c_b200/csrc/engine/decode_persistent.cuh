@@ -102,7 +102,8 @@ struct PersistParams
     uint32_t att_groups;    // key groups of the attention phase (bounded by the scratch)
     uint32_t *err;
     TileGeom tg[PK_COUNT];
-    uint32_t spw, warps;    // stages per warp, warps per CTA
+    uint32_t spw, warps;    // stages per warp (a power of two), warps per CTA
+    uint32_t spw_shift;     // log2(spw): stage and phase of chunk i are i & (spw - 1), (i >> spw_shift) & 1
     uint32_t xs_bytes;      // fp16 input staging (>= 2 * max K)
     uint32_t part_bytes;    // tile partials; xs + part also serve as the attention scratch
     uint32_t n_steps;
@@ -432,8 +433,8 @@ struct WarpPipe
 // Issues the next tile into its stage.
 __device__ __forceinline__ void pipe_advance(const PersistParams &P, WarpPipe &wp, uint32_t warp)
 {
-    cursor_issue(P, wp.cur, warp, wp.stage + (size_t)(wp.issued % P.spw) * kTileBytes, &wp.bar[wp.issued % P.spw],
-                 wp.policy);
+    const uint32_t slot = wp.issued & (P.spw - 1);
+    cursor_issue(P, wp.cur, warp, wp.stage + (size_t)slot * kTileBytes, &wp.bar[slot], wp.policy);
     ++wp.issued;
     ++wp.cur.k;
     tile_step(wp.cur.grp, wp.cur.ks, wp.cur.Ks, P.warps);
@@ -642,9 +643,9 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
                 break;
             }
         }
-        const uint32_t gi = wp.consumed, s = gi % P.spw;
+        const uint32_t gi = wp.consumed, s = gi & (P.spw - 1);
         const long long c0 = wt ? clock64() : 0;
-        const bool okw = mbar_wait_bounded(&wp.bar[s], (gi / P.spw) & 1u, kWaitLimitNs);
+        const bool okw = mbar_wait_bounded(&wp.bar[s], (gi >> P.spw_shift) & 1u, kWaitLimitNs);
         if (__any_sync(0xffffffffu, !okw))
         {
             ok = false;

@@ -451,6 +451,10 @@ void setup_persistent(Engine *e, vkllm_context *ctx, uint32_t att_split, uint32_
         part_floats = need > part_floats ? need : part_floats;
     }
     P.spw = spw < 1 ? 1 : (spw > kStreamMaxSpw ? kStreamMaxSpw : spw);
+    P.spw_shift = 0; // a power of two (rounded down), so the kernel finds stages with masks and shifts
+    while ((2u << P.spw_shift) <= P.spw)
+        ++P.spw_shift;
+    P.spw = 1u << P.spw_shift;
     P.xs_bytes = (maxk * 2 + 127) / 128 * 128;
     P.part_bytes = (uint32_t)((part_floats * 4 + 127) / 128 * 128);
     // Attention scratch (aliases xs + part): q, the split's scores, and per key-group partial
