@@ -753,7 +753,7 @@ __device__ __forceinline__ bool persist_gemv(const PersistParams &P, uint32_t ki
 // [hd, Lk] (src/core/vkllm_op_matmul.c:14-30): split 0 then computes o[w] = sum_k p_k V[w][k] from
 // the stored scores and the other splits contribute 0. `aepoch` counts the attention phases of
 // this launch. Returns false on a timed-out wait or a reported error.
-template <bool FINE>
+template <bool FINE, bool TRACE>
 __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32_t layer, uint32_t pos,
                                                   uint32_t aepoch, float *scratch, float *red)
 {
@@ -775,7 +775,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
     // tracing: CTA 0's thread 0 stamps the sub-steps of each item in shared memory (no live registers)
     __shared__ long long att_ts[kAttTraceSlots];
     auto amark = [&](uint32_t k) {
-        if (P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
+        if (TRACE && P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
             att_ts[k] = clock64();
     };
     for (uint32_t it = blockIdx.x; it < dd.H * ns; it += gridDim.x)
@@ -1016,7 +1016,7 @@ __device__ __forceinline__ bool persist_attention(const PersistParams &P, uint32
             st_release_gpu_u32(P.head_flag + h, aepoch + 1);
         }
         amark(7);
-        if (P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
+        if (TRACE && P.wtrace && blockIdx.x == 0 && threadIdx.x == 0)
         {
             for (uint32_t k = 0; k + 1 < kAttTraceSlots; ++k)
                 atomicAdd(P.wtrace + kAttTraceBase + k, (unsigned long long)(att_ts[k + 1] - att_ts[k]));
@@ -1184,7 +1184,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
             if constexpr (FINE)
             {
                 // Wo tiles wait only for the heads their input columns span
-                if (!persist_attention<FINE>(P, l, pos, step * P.L + l, scratch, sred))
+                if (!persist_attention<FINE, TRACE>(P, l, pos, step * P.L + l, scratch, sred))
                 {
                     ok = false;
                     break;
@@ -1197,7 +1197,7 @@ __global__ void __launch_bounds__(kPersistMaxWarps * 32, 1) k_decode_persistent(
             }
             else
             {
-                if (!persist_attention<FINE>(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
+                if (!persist_attention<FINE, TRACE>(P, l, pos, step * P.L + l, scratch, sred) || !grid_sync(P, tr))
                 {
                     ok = false;
                     break;
