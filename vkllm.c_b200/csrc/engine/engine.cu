@@ -964,9 +964,10 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
     e->kernels_per_step = 2 + 6 * (uint32_t)e->layers.size();
     // Persistent kernel: VKLLM_B200_PERSIST_SPW overrides the weight-tile stages per warp,
     // VKLLM_B200_PERSIST_L2_KB the next-phase weights per CTA prefetched into L2 at each barrier
-    // (64 KB measured best at 7B: 0 -> 2.99, 64 -> 2.90, 128 -> 2.93, 256 -> 2.98 ms/token).
+    // (80 KB measured best at 7B: 0 -> 2.891, 32 -> 2.846, 48 -> 2.814, 64 -> 2.803, 80 -> 2.787,
+    // 96 -> 2.788, 128 -> 2.810 ms/token on one box; 64 / 80 / 96 -> 2.813 / 2.810 / 2.813 on another).
     const char *l2kb = getenv("VKLLM_B200_PERSIST_L2_KB"); // "0" turns it off
-    setup_persistent(e, ctx, att_split, env_u32("VKLLM_B200_PERSIST_SPW", 1), l2kb ? (uint32_t)atoi(l2kb) : 64u);
+    setup_persistent(e, ctx, att_split, env_u32("VKLLM_B200_PERSIST_SPW", 1), l2kb ? (uint32_t)atoi(l2kb) : 80u);
     e->pp.tp_size = tp;
     e->pp.tp_rank = tp > 1 ? model->b200.tp_rank : 0;
     e->pp.v0 = e->pp.tp_rank * dd.V;
