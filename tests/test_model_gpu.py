@@ -5,11 +5,11 @@ the CPU oracle's restatement of the reference graph on the same weights and prom
 
 Bar: greedy token ids identical for the first 32 steps; fp16 logits within
 max-abs 2e-2 and mean-abs 2e-3 at every step whose inputs agree. Every execution path is checked:
-node by node (STRICT, the reference's own DAG), the persistent decode kernel (FUSED, the default),
+node by node (STRICT, the reference's own DAG), the persistent decode kernel (FUSED, the default, its row partition calibrated at engine creation),
 the CUDA-graph decode path that runs when cooperative launch is unavailable (VKLLM_B200_DECODE=graph),
-the persistent kernel with its row partition calibrated at engine creation
-(VKLLM_B200_PERSIST_BALANCE=2), and the persistent kernel whose Wo and down tiles wait per input
-segment for its producers instead of at grid barriers (VKLLM_B200_PERSIST_FINE=1)."""
+the persistent kernel with equal row shares (VKLLM_B200_PERSIST_BALANCE=0), and the persistent
+kernel whose Wo and down tiles wait per input segment for its producers instead of at grid barriers
+(VKLLM_B200_PERSIST_FINE=1)."""
 import numpy as np
 import pytest
 
@@ -32,7 +32,7 @@ def reference_run(tiny_gguf, orc):
 
 
 MODES = {"strict": {}, "fused": {}, "fused_graph": {"VKLLM_B200_DECODE": "graph"},
-         "fused_balanced": {"VKLLM_B200_PERSIST_BALANCE": "2"}, "fused_fine": {"VKLLM_B200_PERSIST_FINE": "1"}}
+         "fused_equal_shares": {"VKLLM_B200_PERSIST_BALANCE": "0"}, "fused_fine": {"VKLLM_B200_PERSIST_FINE": "1"}}
 
 
 @pytest.mark.parametrize("mode", list(MODES))

@@ -1045,12 +1045,13 @@ vkllm_err_t engine_create(vkllm_context *ctx, vkllm_models_llama2 *model, Engine
         delete e;
         return err;
     }
-    // VKLLM_B200_PERSIST_BALANCE: calibration rounds of the row partition (default 0, equal shares;
-    // 7B on one B200: 0 -> 2.857, 3 -> 2.869, 6 -> 2.864 ms/token, although the per-CTA spread of
-    // the up/gate phase shrank from 5.5 to 3.9 us: the phases stream at the HBM rate and the CTAs that
-    // finish first keep HBM busy with the next phase's tiles)
+    // VKLLM_B200_PERSIST_BALANCE: calibration rounds of the row partition (default 8; 0 keeps equal
+    // shares). 7B, same box: 0 -> 2.791, 5 -> 2.760, 8 -> 2.755-2.757, 12 -> 2.751-2.756 ms/token.
+    // (With the slower kernel of before, 0 -> 2.857, 3 -> 2.869, 6 -> 2.864: the CTAs that finished
+    // a phase first kept HBM busy with the next phase's tiles; with fewer instructions per tile the
+    // slowest CTA at each barrier is what the step waits for.)
     const char *bal = getenv("VKLLM_B200_PERSIST_BALANCE");
-    balance_persistent(e, bal ? (uint32_t)atoi(bal) : 0u);
+    balance_persistent(e, bal ? (uint32_t)atoi(bal) : 8u);
     *out = e;
     return VKLLM_ERR_OK;
 }
